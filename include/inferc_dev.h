@@ -1,0 +1,211 @@
+/* libinferc_b200 — C ABI of the B200 (sm_100a) device executor for inferc's
+ * fused-op hot path.
+ *
+ * This is the boundary the reference's runtime would bind in place of its CPU
+ * kernels. The reference dispatches on the op_type string inside
+ * Executor::Run (src/runtime/executor.cc:123-343) to free functions
+ * `rt::Tensor Op(const rt::Tensor&..., attrs)` that throw std::runtime_error;
+ * each entry point below replaces one of those functions (cited per entry)
+ * and keeps its argument meaning, its attribute defaults and its checks, but
+ * takes raw device pointers and sizes and returns a status code instead of
+ * throwing.
+ *
+ * Conventions
+ *   - Return value: INFERC_OK (0) or an INFERC_ERR_* code; the message is
+ *     available from inferc_dev_last_error_string() on the calling thread.
+ *   - Tensor pointers are DEVICE addresses (cudaMalloc / inferc_dev_alloc)
+ *     of dense row-major fp32 data unless stated; "host" marks the
+ *     exceptions. Leading dims of the reference's [..., M, K] inputs are
+ *     flattened into M by the caller (as the reference kernels do).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Every op
+ *     is asynchronous with respect to the host.
+ *   - No entry point falls back to the CPU: without a usable CUDA device they
+ *     return INFERC_ERR_CUDA.
+ */
+#ifndef INFERC_DEV_H_
+#define INFERC_DEV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "inferc_models.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  INFERC_OK = 0,
+  INFERC_ERR_INVALID = 1, /* bad shape / argument (reference: runtime_error) */
+  INFERC_ERR_CUDA = 2,    /* CUDA runtime or launch failure */
+  INFERC_ERR_OOM = 3,     /* device or host allocation failed */
+  INFERC_ERR_TIMEOUT = 4, /* a bounded device wait gave up */
+  INFERC_ERR_RANGE = 5    /* index out of range found on the device */
+};
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Message of the last failed call on this host thread (never NULL). */
+const char* inferc_dev_last_error_string(void);
+
+/* Library version string, e.g. "inferc_b200 0.1 sm_100a". */
+const char* inferc_dev_version(void);
+
+/* Device buffers (replace rt::Tensor's host storage, src/runtime/tensor.cc:53-75). */
+int inferc_dev_alloc(void** ptr, size_t bytes);
+int inferc_dev_free(void* ptr);
+int inferc_dev_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int inferc_dev_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int inferc_dev_stream_synchronize(void* stream);
+
+/* ------------------------------------------------------------- fused ops */
+
+/* FusedLayerNorm (rt::LayerNorm, src/kernels/activation.cc:103-150; executor
+ * attribute `epsilon`, default 1e-5, executor.cc:213-217). y = (x-mean) *
+ * (1/sqrtf(var+eps)) * gamma + beta over each row of `feat` elements, biased
+ * variance. x and y may alias. */
+int inferc_dev_layernorm(const float* x, const float* gamma, const float* beta,
+                         float* y, int64_t rows, int64_t feat, float eps,
+                         void* stream);
+
+/* FusedMatMulAddGELU (src/kernels/fused_matmul_add_gelu.cc:13-80):
+ * Y[M,N] = erfGELU(X[M,K] W[K,N] + b[N]). */
+int inferc_dev_fused_matmul_add_gelu(const float* x, const float* w,
+                                     const float* b, float* y, int64_t M,
+                                     int64_t K, int64_t N, void* stream);
+
+/* FusedQKV (rt::FusedQKVProjection, src/kernels/attention.cc:102-141):
+ * q = X Wq + bq, k = X Wk + bk, v = X Wv + bv; X [M,K], Wi [K,N], outputs
+ * [M,N]. */
+int inferc_dev_fused_qkv(const float* x, const float* wq, const float* bq,
+                         const float* wk, const float* bk, const float* wv,
+                         const float* bv, float* q, float* k, float* v,
+                         int64_t M, int64_t K, int64_t N, void* stream);
+
+/* FusedAttention (src/kernels/attention.cc:32-100; attributes head_dim,
+ * default 64, and fill, default -3.0e38, executor.cc:218-224).
+ * q, k, v, out: [B,S,H], head h at columns [h*head_dim, (h+1)*head_dim).
+ * mask: optional bool bytes (DEVICE), true = masked (score REPLACED by fill),
+ * of shape mask_shape[0..mask_rank) (HOST array) right-aligned and broadcast
+ * to [B, H/head_dim, S, S]; NULL / rank 0 = no mask. head_dim <= 128. */
+int inferc_dev_fused_attention(const float* q, const float* k, const float* v,
+                               const uint8_t* mask, const int64_t* mask_shape,
+                               int mask_rank, int64_t B, int64_t S, int64_t H,
+                               int64_t head_dim, float fill, float* out,
+                               void* stream);
+
+/* ONNX Gemm (rt::Gemm, src/kernels/matmul.cc:161-228): Y[M,N] =
+ * alpha*op(A) op(B) + beta*C. c may be NULL; c_len is M*N (full), N (row
+ * broadcast) or 1 (scalar); other lengths are rejected. M == 1 runs the
+ * split-K GEMV kernel (the reference's decode shape). */
+int inferc_dev_gemm(const float* a, const float* b, const float* c,
+                    int64_t c_len, float* y, int64_t M, int64_t K, int64_t N,
+                    float alpha, float beta, int trans_a, int trans_b,
+                    void* stream);
+
+/* 2-D MatMul (rt::MatMul, src/kernels/matmul.cc:63-159, batch_count == 1):
+ * Y[M,N] = A[M,K] B[K,N]. */
+int inferc_dev_matmul(const float* a, const float* b, float* y, int64_t M,
+                      int64_t K, int64_t N, void* stream);
+
+/* Gelu / GeluTanh (src/kernels/activation.cc:15-50), elementwise over n. */
+int inferc_dev_gelu(const float* x, float* y, int64_t n, void* stream);
+int inferc_dev_gelu_tanh(const float* x, float* y, int64_t n, void* stream);
+
+/* Softmax over the last axis (src/kernels/activation.cc:52-101). */
+int inferc_dev_softmax(const float* x, float* y, int64_t rows, int64_t cols,
+                       void* stream);
+
+/* ------------------------------------------------------------ decode ops */
+
+/* Batch-1 fp32 GEMV with the Gemm epilogue, y[N] = act(x[K] W[K,N] + b[N]
+ * (+ resid[N])); act 0 none, 1 erf GELU, 2 tanh GELU, 3 ReLU. The M==1
+ * Gemm of the decode graphs (src/kernels/matmul.cc:202-226). b / resid may
+ * be NULL; resid may alias y. Split-K with a deterministic reduction. */
+int inferc_dev_gemv(const float* x, const float* w, const float* b,
+                    const float* resid, float* y, int64_t K, int64_t N,
+                    int act, void* stream);
+
+/* int4 per-row-scale GEMV (bench/amx/int4_gemv_amx.cc:258-271): y[r] =
+ * sum_k (scales[r]*(q[r,k]-8)) x[k]; W [N, K/2] bytes, byte r*(K/2)+k/2
+ * holds even k in the low nibble, odd k in the high nibble. K must be even.
+ * Accumulates in fp32. */
+int inferc_dev_gemv_int4_rowscale(const uint8_t* w, const float* scales,
+                                  const float* x, float* y, int64_t N,
+                                  int64_t K, void* stream);
+
+/* Many int4 GEMVs in one launch (the decode step's 4 matrices x layers +
+ * LM head). descs is a HOST array of `count` descriptors with DEVICE
+ * pointers. */
+typedef struct InfercInt4Gemv {
+  const uint8_t* w;
+  const float* scales;
+  const float* x;
+  float* y;
+  int64_t n, k;
+} InfercInt4Gemv;
+int inferc_dev_gemv_int4_batched(const InfercInt4Gemv* descs, int count,
+                                 void* stream);
+
+/* Greedy argmax with the first maximum winning (src/cli/main.cpp:823-829):
+ * writes the index (int64, DEVICE) of the first largest of x[0..n). */
+int inferc_dev_argmax(const float* x, int64_t n, int64_t* out_index,
+                      void* stream);
+
+/* KV-cache append in place, replacing the with-past graph's
+ * Concat(past, new) (src/kernels/movement.cc:142-189): copies `n` new rows of
+ * K and V (each [n, heads*head_dim], row stride ld_new) into the cache
+ * k_cache / v_cache [heads, max_len, head_dim] at positions [pos, pos+n). */
+int inferc_dev_kv_append(const float* k_new, const float* v_new,
+                         int64_t ld_new, float* k_cache, float* v_cache,
+                         int64_t heads, int64_t head_dim, int64_t max_len,
+                         int64_t pos, int64_t n, void* stream);
+
+/* Single-query attention over the first L cached positions (the decode
+ * step's MatMul, Div(sqrt(head_dim)), Softmax, MatMul): q [heads*head_dim],
+ * out [heads*head_dim]. */
+int inferc_dev_decode_attention(const float* q, const float* k_cache,
+                                const float* v_cache, float* out,
+                                int64_t heads, int64_t head_dim,
+                                int64_t max_len, int64_t L, void* stream);
+
+/* ------------------------------------------------------------------ plans */
+
+/* A prepared DistilBERT-architecture encoder (the `inferc optimize` plan run
+ * by `inferc run`, src/cli/main.cpp:324-420). create copies the weights
+ * (HOST pointers in `w`) to the current device once; run executes one
+ * forward as a replayed CUDA graph per (B,S). */
+typedef struct InfercEncoderPlan* inferc_encoder_t;
+int inferc_dev_encoder_create(const InfercEncoderWeights* w, int64_t max_batch,
+                              int64_t max_seq, inferc_encoder_t* out);
+/* ids, mask: int64 [B,S] DEVICE; logits: [B, n_classes] DEVICE. */
+int inferc_dev_encoder_run(inferc_encoder_t plan, const int64_t* ids,
+                           const int64_t* mask, int64_t B, int64_t S,
+                           float* logits, void* stream);
+/* Same with HOST ids / mask / logits: copies in, runs, copies out, syncs. */
+int inferc_dev_encoder_run_host(inferc_encoder_t plan, const int64_t* ids,
+                                const int64_t* mask, int64_t B, int64_t S,
+                                float* logits);
+void inferc_dev_encoder_destroy(inferc_encoder_t plan);
+
+/* A prepared GPT-2 greedy decoder (`inferc decode`, src/cli/main.cpp:700-945)
+ * with a device-resident KV cache of max_len positions. */
+typedef struct InfercDecoderPlan* inferc_decoder_t;
+int inferc_dev_decoder_create(const InfercGpt2Weights* w, int64_t max_len,
+                              inferc_decoder_t* out);
+/* Greedy decode: prompt (HOST int64 [n_prompt]) -> tokens_out (HOST int64
+ * [max_tokens]): the prefill token followed by max_tokens-1 single-token
+ * steps, as `inferc decode --max-tokens` does. step_ms_out (HOST, may be NULL)
+ * receives the mean device time per single-token step in milliseconds. */
+int inferc_dev_decode(inferc_decoder_t plan, const int64_t* prompt,
+                      int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
+                      double* step_ms_out);
+/* Device logits [vocab] of the most recent step (valid after decode). */
+const float* inferc_dev_decoder_logits(inferc_decoder_t plan);
+void inferc_dev_decoder_destroy(inferc_decoder_t plan);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INFERC_DEV_H_ */

@@ -1,0 +1,249 @@
+// extern "C" op entry points of libinferc_b200 (declared in
+// include/inferc_dev.h). Each keeps the argument checks of the reference
+// kernel it replaces and reports them as INFERC_ERR_INVALID instead of
+// throwing across the ABI.
+#include <cstring>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace inferc_dev {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+// The tensor-core GEMM (gemm_tc.cu) when it accepts the shape, else the
+// CUDA-core kernel. Defined in gemm_dispatch.cu.
+void launch_gemm(const float* A, int64_t lda, bool ta, const float* B, int64_t ldb, bool tb,
+                 float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
+                 cudaStream_t st);
+
+}  // namespace inferc_dev
+
+using namespace inferc_dev;
+
+extern "C" {
+
+const char* inferc_dev_last_error_string(void) { return g_last_error.c_str(); }
+
+const char* inferc_dev_version(void) { return "inferc_b200 0.1 sm_100a"; }
+
+int inferc_dev_alloc(void** ptr, size_t bytes) {
+  return guard([&] {
+    IDEV_CHECK_ARG(ptr != nullptr, "alloc: null out pointer");
+    *ptr = nullptr;
+    if (bytes == 0) return;
+    const cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaErrorMemoryAllocation) {
+      cudaGetLastError();
+      throw Error(INFERC_ERR_OOM, "alloc: out of device memory (" + std::to_string(bytes) + " B)");
+    }
+    IDEV_CUDA(e);
+  });
+}
+
+int inferc_dev_free(void* ptr) {
+  return guard([&] {
+    if (ptr) IDEV_CUDA(cudaFree(ptr));
+  });
+}
+
+int inferc_dev_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream) {
+  return guard([&] {
+    IDEV_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, as_stream(stream)));
+  });
+}
+
+int inferc_dev_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream) {
+  return guard([&] {
+    IDEV_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, as_stream(stream)));
+  });
+}
+
+int inferc_dev_stream_synchronize(void* stream) {
+  return guard([&] { IDEV_CUDA(cudaStreamSynchronize(as_stream(stream))); });
+}
+
+int inferc_dev_layernorm(const float* x, const float* gamma, const float* beta, float* y,
+                         int64_t rows, int64_t feat, float eps, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(rows >= 0 && feat > 0, "LayerNorm: bad shape");
+    IDEV_CHECK_ARG(rows == 0 || (x && gamma && beta && y), "LayerNorm: null pointer");
+    launch_layernorm(x, gamma, beta, y, rows, feat, eps, as_stream(stream));
+  });
+}
+
+int inferc_dev_fused_matmul_add_gelu(const float* x, const float* w, const float* b, float* y,
+                                     int64_t M, int64_t K, int64_t N, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(M >= 0 && K > 0 && N > 0, "FusedMatMulAddGELU: bad shape");
+    IDEV_CHECK_ARG(M == 0 || (x && w && b && y), "FusedMatMulAddGELU: null pointer");
+    Epilogue ep;
+    ep.bias = b;
+    ep.bias_mode = 1;
+    ep.act = ACT_GELU_ERF;
+    launch_gemm(x, K, false, w, N, false, y, N, M, N, K, ep, as_stream(stream));
+  });
+}
+
+int inferc_dev_fused_qkv(const float* x, const float* wq, const float* bq, const float* wk,
+                         const float* bk, const float* wv, const float* bv, float* q, float* k,
+                         float* v, int64_t M, int64_t K, int64_t N, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(M >= 0 && K > 0 && N > 0, "FusedQKV: bad shape");
+    const float* ws[3] = {wq, wk, wv};
+    const float* bs[3] = {bq, bk, bv};
+    float* os[3] = {q, k, v};
+    for (int i = 0; i < 3; ++i) {
+      IDEV_CHECK_ARG(M == 0 || (x && ws[i] && bs[i] && os[i]), "FusedQKV: null pointer");
+      Epilogue ep;
+      ep.bias = bs[i];
+      ep.bias_mode = 1;
+      launch_gemm(x, K, false, ws[i], N, false, os[i], N, M, N, K, ep, as_stream(stream));
+    }
+  });
+}
+
+int inferc_dev_fused_attention(const float* q, const float* k, const float* v,
+                               const uint8_t* mask, const int64_t* mask_shape, int mask_rank,
+                               int64_t B, int64_t S, int64_t H, int64_t head_dim, float fill,
+                               float* out, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(B >= 0 && S >= 0 && H > 0, "FusedAttention: expect [B,S,H]");
+    IDEV_CHECK_ARG(head_dim > 0 && H % head_dim == 0,
+                   "FusedAttention: H not divisible by head_dim");
+    AttnArgs a{};
+    a.q = q; a.k = k; a.v = v; a.out = out;
+    a.ldq = a.ldk = a.ldv = a.ldo = H;
+    a.bstride_q = a.bstride_k = a.bstride_v = a.bstride_o = S * H;
+    a.B = B; a.S = S; a.nH = H / head_dim; a.hd = head_dim;
+    a.scale = 1.0f / std::sqrt((float)head_dim);
+    a.fill = fill;
+    a.causal = 0;
+    if (mask != nullptr && mask_rank > 0) {
+      IDEV_CHECK_ARG(mask_shape != nullptr && mask_rank <= 4,
+                     "FusedAttention: mask rank must be 1..4 with a shape");
+      // Right-aligned broadcast strides over [B, nH, S, S] (MaskStrides,
+      // src/kernels/attention.cc:17-29); each mask axis must be 1 or match.
+      const int64_t full[4] = {B, a.nH, S, S};
+      int64_t st = 1;
+      for (int i = mask_rank - 1; i >= 0; --i) {
+        const int od = 4 - (mask_rank - i);
+        IDEV_CHECK_ARG(mask_shape[i] == 1 || mask_shape[i] == full[od],
+                       "FusedAttention: mask shape does not broadcast to [B,nH,S,S]");
+        a.ms[od] = mask_shape[i] == 1 ? 0 : st;
+        st *= mask_shape[i];
+      }
+      a.mask = mask;
+    }
+    launch_attention(a, as_stream(stream));
+  });
+}
+
+int inferc_dev_gemm(const float* a, const float* b, const float* c, int64_t c_len, float* y,
+                    int64_t M, int64_t K, int64_t N, float alpha, float beta, int trans_a,
+                    int trans_b, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(M >= 0 && K > 0 && N >= 0, "Gemm: bad shape");
+    const bool use_c = c != nullptr && beta != 0.0f;
+    if (use_c)
+      IDEV_CHECK_ARG(c_len == M * N || c_len == N || c_len == 1,
+                     "Gemm: unsupported C shape for broadcast");
+    cudaStream_t st = as_stream(stream);
+    if (M == 1 && !trans_b && (!use_c || c_len == N)) {
+      GemvArgs g{};
+      g.x = a; g.w = b; g.y = y; g.K = K; g.N = N;
+      g.alpha = alpha; g.beta = beta;
+      g.bias = use_c ? c : nullptr;
+      g.act = ACT_NONE;
+      launch_gemv(g, st);
+      return;
+    }
+    Epilogue ep;
+    ep.alpha = alpha;
+    ep.beta = beta;
+    if (use_c) {
+      ep.bias = c;
+      ep.bias_mode = c_len == M * N ? 3 : c_len == N ? 1 : 2;
+      ep.ldbias = N;
+    }
+    launch_gemm(a, trans_a ? M : K, trans_a != 0, b, trans_b ? K : N, trans_b != 0, y, N, M, N,
+                K, ep, st);
+  });
+}
+
+int inferc_dev_matmul(const float* a, const float* b, float* y, int64_t M, int64_t K, int64_t N,
+                      void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(M >= 0 && K > 0 && N >= 0, "MatMul: bad shape");
+    Epilogue ep;
+    launch_gemm(a, K, false, b, N, false, y, N, M, N, K, ep, as_stream(stream));
+  });
+}
+
+int inferc_dev_gelu(const float* x, float* y, int64_t n, void* stream) {
+  return guard([&] { launch_act(x, y, n, ACT_GELU_ERF, as_stream(stream)); });
+}
+
+int inferc_dev_gelu_tanh(const float* x, float* y, int64_t n, void* stream) {
+  return guard([&] { launch_act(x, y, n, ACT_GELU_TANH, as_stream(stream)); });
+}
+
+int inferc_dev_softmax(const float* x, float* y, int64_t rows, int64_t cols, void* stream) {
+  return guard([&] { launch_softmax(x, y, rows, cols, as_stream(stream)); });
+}
+
+int inferc_dev_gemv(const float* x, const float* w, const float* b, const float* resid, float* y,
+                    int64_t K, int64_t N, int act, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(K > 0 && N >= 0, "GEMV: bad shape");
+    IDEV_CHECK_ARG(act >= 0 && act <= 3, "GEMV: unknown activation");
+    GemvArgs g{};
+    g.x = x; g.w = w; g.bias = b; g.resid = resid; g.y = y; g.K = K; g.N = N;
+    g.alpha = 1.0f; g.beta = 1.0f; g.act = act;
+    launch_gemv(g, as_stream(stream));
+  });
+}
+
+int inferc_dev_gemv_int4_rowscale(const uint8_t* w, const float* scales, const float* x, float* y,
+                                  int64_t N, int64_t K, void* stream) {
+  return guard([&] {
+    InfercInt4Gemv d{w, scales, x, y, N, K};
+    launch_gemv_int4(&d, 1, as_stream(stream));
+  });
+}
+
+int inferc_dev_gemv_int4_batched(const InfercInt4Gemv* descs, int count, void* stream) {
+  return guard([&] { launch_gemv_int4(descs, count, as_stream(stream)); });
+}
+
+int inferc_dev_argmax(const float* x, int64_t n, int64_t* out_index, void* stream) {
+  return guard([&] { launch_argmax(x, n, out_index, as_stream(stream)); });
+}
+
+int inferc_dev_kv_append(const float* k_new, const float* v_new, int64_t ld_new, float* k_cache,
+                         float* v_cache, int64_t heads, int64_t head_dim, int64_t max_len,
+                         int64_t pos, int64_t n, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(pos >= 0 && n >= 0 && pos + n <= max_len,
+                   "kv_append: positions beyond the cache");
+    launch_kv_append(k_new, v_new, ld_new, k_cache, v_cache, heads, head_dim, max_len, nullptr,
+                     pos, n, as_stream(stream));
+  });
+}
+
+int inferc_dev_decode_attention(const float* q, const float* k_cache, const float* v_cache,
+                                float* out, int64_t heads, int64_t head_dim, int64_t max_len,
+                                int64_t L, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(L >= 1 && L <= max_len, "decode_attention: L must be in [1, max_len]");
+    launch_decode_attention(q, nullptr, nullptr, const_cast<float*>(k_cache),
+                            const_cast<float*>(v_cache), out, heads, head_dim, max_len, nullptr,
+                            L, as_stream(stream));
+  });
+}
+
+}  // extern "C"

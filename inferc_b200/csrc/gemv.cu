@@ -1,0 +1,429 @@
+// Batch-1 decode GEMVs (HBM-bound: every weight byte is read exactly once).
+//
+//  * gemv_kn: y[N] = act(alpha * x[K] W[K,N] + beta*b + resid) for the
+//    [K,N] weights of the decode graph's M==1 Gemm nodes
+//    (src/kernels/matmul.cc:202-226). A CTA owns 128 columns (one float4 per
+//    lane, coalesced 512-byte row segments) and a slice of K; the K slices
+//    of one column tile are spread over CTAs (split-K) so that ~2 CTAs per SM
+//    stream weights. Partial sums go to a workspace and the last CTA to
+//    finish a column tile adds them in split order, so the result does not
+//    depend on CTA scheduling. An optional LayerNorm prologue normalises x
+//    in shared memory (the decode graph's FusedLayerNorm feeding the Gemm).
+//  * row_gemv: y[N] = W[N,K] x for row-major [N,K] weights (the tied LM head
+//    MatMul(x, wte^T)), one warp per row, with optional LayerNorm prologue
+//    and a fused greedy argmax (first maximum wins, src/cli/main.cpp:870-875).
+#include "kernels.cuh"
+
+#include <mutex>
+#include <vector>
+
+namespace inferc_dev {
+
+void Workspace::allocate(size_t floats, size_t n) {
+  IDEV_CUDA(cudaMalloc(&partials, floats * sizeof(float)));
+  IDEV_CUDA(cudaMalloc(&counters, n * sizeof(unsigned int)));
+  IDEV_CUDA(cudaMemset(counters, 0, n * sizeof(unsigned int)));
+  partial_floats = floats;
+  n_counters = n;
+  owned = true;
+}
+
+void Workspace::release() {
+  if (owned) {
+    cudaFree(partials);
+    cudaFree(counters);
+  }
+  partials = nullptr;
+  counters = nullptr;
+  owned = false;
+}
+
+Workspace& workspace_for_current_device() {
+  static std::mutex mu;
+  static std::vector<Workspace> per_dev;
+  int dev = 0;
+  IDEV_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
+  Workspace& ws = per_dev[dev];
+  if (!ws.owned) ws.allocate(size_t(4) << 20, 8192);  // 16 MB of partials
+  return ws;
+}
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kColsPerCta = 128;  // 32 lanes x float4
+constexpr int kMaxK = 8192;       // shared-memory copy of x
+
+// Normalised (or plain) copy of x[k0:k1) into xs[0:k1-k0). With LN, the
+// mean and biased variance of the full x[0:K) are computed first (two
+// passes, like rt::LayerNorm).
+__device__ void stage_x(const float* __restrict__ x, const float* __restrict__ g,
+                        const float* __restrict__ b, float eps, int64_t K, int64_t k0, int64_t k1,
+                        float* xs, float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (g == nullptr) {
+    for (int64_t k = k0 + tid; k < k1; k += kThreads) xs[k - k0] = x[k];
+    __syncthreads();
+    return;
+  }
+  float s = 0.f;
+  for (int64_t k = tid; k < K; k += kThreads) s += x[k];
+  s = warp_sum(s);
+  if (lane == 0) red[wid] = s;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < kWarps; ++w) tot += red[w];
+  const float mean = tot / (float)K;
+  __syncthreads();
+  float sq = 0.f;
+  for (int64_t k = tid; k < K; k += kThreads) {
+    const float d = x[k] - mean;
+    sq += d * d;
+  }
+  sq = warp_sum(sq);
+  if (lane == 0) red[wid] = sq;
+  __syncthreads();
+  float tsq = 0.f;
+  for (int w = 0; w < kWarps; ++w) tsq += red[w];
+  const float inv = 1.0f / sqrtf(tsq / (float)K + eps);
+  for (int64_t k = k0 + tid; k < k1; k += kThreads) xs[k - k0] = ((x[k] - mean) * inv) * g[k] + b[k];
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads)
+    gemv_kn_kernel(GemvArgs a, int64_t k_per_split, int splits, float* partials,
+                   unsigned int* counters) {
+  __shared__ float xs[kMaxK];
+  __shared__ float red[kWarps];
+  __shared__ float4 wsum[kWarps][32];
+  __shared__ bool last;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t n0 = (int64_t)blockIdx.x * kColsPerCta;
+  const int split = blockIdx.y;
+  const int64_t k0 = split * k_per_split;
+  const int64_t k1 = min(a.K, k0 + k_per_split);
+  stage_x(a.x, a.ln_gamma, a.ln_beta, a.ln_eps, a.K, k0, k1, xs, red);
+
+  const int64_t col = n0 + lane * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (col < a.N) {
+    const float* wp = a.w + col;
+    int64_t k = k0 + wid;
+    // 4 independent 128-bit loads in flight per lane.
+    for (; k + 3 * kWarps < k1; k += 4 * kWarps) {
+      float4 w0 = __ldg(reinterpret_cast<const float4*>(wp + (k)*a.N));
+      float4 w1 = __ldg(reinterpret_cast<const float4*>(wp + (k + kWarps) * a.N));
+      float4 w2 = __ldg(reinterpret_cast<const float4*>(wp + (k + 2 * kWarps) * a.N));
+      float4 w3 = __ldg(reinterpret_cast<const float4*>(wp + (k + 3 * kWarps) * a.N));
+      const float x0 = xs[k - k0], x1 = xs[k + kWarps - k0], x2 = xs[k + 2 * kWarps - k0],
+                  x3 = xs[k + 3 * kWarps - k0];
+      acc.x = fmaf(x0, w0.x, acc.x); acc.y = fmaf(x0, w0.y, acc.y);
+      acc.z = fmaf(x0, w0.z, acc.z); acc.w = fmaf(x0, w0.w, acc.w);
+      acc.x = fmaf(x1, w1.x, acc.x); acc.y = fmaf(x1, w1.y, acc.y);
+      acc.z = fmaf(x1, w1.z, acc.z); acc.w = fmaf(x1, w1.w, acc.w);
+      acc.x = fmaf(x2, w2.x, acc.x); acc.y = fmaf(x2, w2.y, acc.y);
+      acc.z = fmaf(x2, w2.z, acc.z); acc.w = fmaf(x2, w2.w, acc.w);
+      acc.x = fmaf(x3, w3.x, acc.x); acc.y = fmaf(x3, w3.y, acc.y);
+      acc.z = fmaf(x3, w3.z, acc.z); acc.w = fmaf(x3, w3.w, acc.w);
+    }
+    for (; k < k1; k += kWarps) {
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(wp + k * a.N));
+      const float x0 = xs[k - k0];
+      acc.x = fmaf(x0, w0.x, acc.x); acc.y = fmaf(x0, w0.y, acc.y);
+      acc.z = fmaf(x0, w0.z, acc.z); acc.w = fmaf(x0, w0.w, acc.w);
+    }
+  }
+  wsum[wid][lane] = acc;
+  __syncthreads();
+  // Warps 0..3 each finish 32 columns: sum the 8 warp partials in order.
+  float part = 0.f;
+  int64_t c = -1;
+  if (tid < kColsPerCta) {
+    const int l = tid >> 2, e = tid & 3;
+    for (int w = 0; w < kWarps; ++w) {
+      const float4 v = wsum[w][l];
+      part += e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
+    }
+    c = n0 + tid;
+  }
+  auto finish = [&](float total, int64_t cc) {
+    float v = a.alpha * total;
+    if (a.bias) v += a.beta * a.bias[cc];
+    if (a.resid) v += a.resid[cc];
+    a.y[cc] = apply_act(v, a.act);
+  };
+  if (splits == 1) {
+    if (c >= 0 && c < a.N) finish(part, c);
+    return;
+  }
+  if (c >= 0 && c < a.N) partials[(int64_t)split * a.N + c] = part;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&counters[blockIdx.x], 1u);
+    last = (prev == (unsigned)splits - 1);
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (c >= 0 && c < a.N) {
+    float total = 0.f;
+    for (int s = 0; s < splits; ++s) total += __ldcg(&partials[(int64_t)s * a.N + c]);
+    finish(total, c);
+  }
+  if (tid == 0) counters[blockIdx.x] = 0u;  // ready for the next launch
+}
+
+// Scalar fallback for odd N / unaligned pointers: one thread per column.
+__global__ void gemv_kn_scalar_kernel(GemvArgs a) {
+  __shared__ float xs[kMaxK];
+  __shared__ float red[kWarps];
+  stage_x(a.x, a.ln_gamma, a.ln_beta, a.ln_eps, a.K, 0, a.K, xs, red);
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= a.N) return;
+  float acc = 0.f;
+  for (int64_t k = 0; k < a.K; ++k) acc = fmaf(xs[k], a.w[k * a.N + c], acc);
+  float v = a.alpha * acc;
+  if (a.bias) v += a.beta * a.bias[c];
+  if (a.resid) v += a.resid[c];
+  a.y[c] = apply_act(v, a.act);
+}
+
+// ---------------------------------------------------------------- row gemv
+
+struct BestIdx {
+  float v;
+  int64_t i;
+};
+// First maximum wins: larger value, or equal value at a smaller index.
+__device__ __forceinline__ bool better(float v, int64_t i, float bv, int64_t bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+__device__ __forceinline__ void warp_best(float& v, int64_t& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (better(ov, oi, v, i)) { v = ov; i = oi; }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    row_gemv_kernel(RowGemvArgs a, float* best_v, int64_t* best_i, unsigned int* counter) {
+  __shared__ __align__(16) float xs[kMaxK];
+  __shared__ float red[kWarps];
+  __shared__ float sv[kWarps];
+  __shared__ int64_t si[kWarps];
+  __shared__ bool last;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  stage_x(a.x, a.ln_gamma, a.ln_beta, a.ln_eps, a.K, 0, a.K, xs, red);
+  const int64_t K4 = a.K / 4;
+  const float4* x4 = reinterpret_cast<const float4*>(xs);
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + wid; r < a.N; r += stride) {
+    const float4* w4 = reinterpret_cast<const float4*>(a.w + r * a.K);
+    float acc = 0.f;
+    for (int64_t k = lane; k < K4; k += 32) {
+      const float4 w = __ldg(w4 + k), xv = x4[k];
+      acc = fmaf(xv.x, w.x, acc);
+      acc = fmaf(xv.y, w.y, acc);
+      acc = fmaf(xv.z, w.z, acc);
+      acc = fmaf(xv.w, w.w, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) a.y[r] = acc;
+    if (better(acc, r, bv, bi)) { bv = acc; bi = r; }
+  }
+  if (a.argmax_out == nullptr) return;
+  // bv/bi are identical across the lanes of a warp (warp_sum broadcasts).
+  if (lane == 0) { sv[wid] = bv; si[wid] = bi; }
+  __syncthreads();
+  if (tid == 0) {
+    float v = sv[0];
+    int64_t i = si[0];
+    for (int w = 1; w < kWarps; ++w)
+      if (better(sv[w], si[w], v, i)) { v = sv[w]; i = si[w]; }
+    best_v[blockIdx.x] = v;
+    best_i[blockIdx.x] = i;
+    __threadfence();
+    last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (wid == 0) {
+    float v = -INFINITY;
+    int64_t i = INT64_MAX;
+    for (int64_t b = lane; b < gridDim.x; b += 32) {
+      const float ov = __ldcg(&best_v[b]);
+      const int64_t oi = __ldcg(&best_i[b]);
+      if (better(ov, oi, v, i)) { v = ov; i = oi; }
+    }
+    warp_best(v, i);
+    if (lane == 0) {
+      *a.argmax_out = i;
+      if (a.pos_counter) {
+        const int64_t pos = *a.pos_counter;
+        if (a.token_log) a.token_log[pos - a.log_base] = i;
+        *a.pos_counter = pos + 1;
+      }
+      *counter = 0u;
+    }
+  }
+}
+
+__global__ void argmax_kernel(const float* __restrict__ x, int64_t n, int64_t* out, float* best_v,
+                              int64_t* best_i, unsigned int* counter) {
+  __shared__ float sv[kWarps];
+  __shared__ int64_t si[kWarps];
+  __shared__ bool last;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + tid; i < n; i += (int64_t)gridDim.x * kThreads)
+    if (better(x[i], i, bv, bi)) { bv = x[i]; bi = i; }
+  warp_best(bv, bi);
+  if (lane == 0) { sv[wid] = bv; si[wid] = bi; }
+  __syncthreads();
+  if (tid == 0) {
+    float v = sv[0];
+    int64_t i = si[0];
+    for (int w = 1; w < kWarps; ++w)
+      if (better(sv[w], si[w], v, i)) { v = sv[w]; i = si[w]; }
+    best_v[blockIdx.x] = v;
+    best_i[blockIdx.x] = i;
+    __threadfence();
+    last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last || wid != 0) return;
+  __threadfence();
+  float v = -INFINITY;
+  int64_t i = INT64_MAX;
+  for (int64_t b = lane; b < gridDim.x; b += 32) {
+    const float ov = __ldcg(&best_v[b]);
+    const int64_t oi = __ldcg(&best_i[b]);
+    if (better(ov, oi, v, i)) { v = ov; i = oi; }
+  }
+  warp_best(v, i);
+  if (lane == 0) {
+    // All-NaN input: report index 0, as the reference's scan would.
+    *out = (i == INT64_MAX) ? 0 : i;
+    *counter = 0u;
+  }
+}
+
+__global__ void decode_embed_kernel(const int64_t* tok, const int64_t* pos, const float* wte,
+                                    const float* wpe, float* x, int64_t H, int64_t vocab,
+                                    int64_t max_pos, int* err) {
+  const int64_t t = *tok, p = *pos - 1;
+  if (t < 0 || t >= vocab || p < 0 || p >= max_pos) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(err, 1);
+    return;
+  }
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < H;
+       c += (int64_t)gridDim.x * blockDim.x)
+    x[c] = wte[t * H + c] + wpe[p * H + c];
+}
+
+__global__ void rows_embed_kernel(const int64_t* ids, int64_t n, int64_t pos0, const float* wte,
+                                  const float* wpe, float* x, int64_t H, int64_t vocab, int* err) {
+  const int64_t r = blockIdx.x;
+  if (r >= n) return;
+  const int64_t t = ids[r];
+  if (t < 0 || t >= vocab) {
+    if (threadIdx.x == 0) atomicExch(err, 1);
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) x[r * H + c] = 0.f;
+    return;
+  }
+  for (int64_t c = threadIdx.x; c < H; c += blockDim.x)
+    x[r * H + c] = wte[t * H + c] + wpe[(pos0 + r) * H + c];
+}
+
+int sm_count() {
+  static int n = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  return n;
+}
+
+}  // namespace
+
+void launch_gemv(const GemvArgs& g, cudaStream_t st) {
+  if (g.N <= 0) return;
+  IDEV_CHECK_ARG(g.K > 0 && g.K <= kMaxK, "GEMV: K must be in [1, 8192]");
+  Workspace& ws = g.ws ? *g.ws : workspace_for_current_device();
+  const bool vec = g.N % 4 == 0 && aligned16(g.w);
+  if (!vec) {
+    gemv_kn_scalar_kernel<<<(unsigned)((g.N + kThreads - 1) / kThreads), kThreads, 0, st>>>(g);
+    IDEV_LAUNCHED();
+    return;
+  }
+  const int64_t tiles = (g.N + kColsPerCta - 1) / kColsPerCta;
+  const int64_t target = 2 * (int64_t)sm_count();
+  int64_t splits = std::max<int64_t>(1, target / tiles);
+  splits = std::min<int64_t>(splits, std::max<int64_t>(1, g.K / (2 * kWarps)));
+  while (splits > 1 && (size_t)(splits * g.N) > ws.partial_floats) --splits;
+  if ((size_t)tiles + 2 > ws.n_counters) splits = 1;  // last two slots: argmax
+  int64_t kps = (g.K + splits - 1) / splits;
+  splits = (g.K + kps - 1) / kps;
+  dim3 grid((unsigned)tiles, (unsigned)splits);
+  gemv_kn_kernel<<<grid, kThreads, 0, st>>>(g, kps, (int)splits, ws.partials, ws.counters);
+  IDEV_LAUNCHED();
+}
+
+void launch_row_gemv(const RowGemvArgs& g, cudaStream_t st) {
+  if (g.N <= 0) return;
+  IDEV_CHECK_ARG(g.K > 0 && g.K <= kMaxK && g.K % 4 == 0 && aligned16(g.w),
+                 "row GEMV: K must be a multiple of 4 in [4, 8192], W 16-byte aligned");
+  Workspace& ws = g.ws ? *g.ws : workspace_for_current_device();
+  const int64_t want = std::min<int64_t>(4 * (int64_t)sm_count(), (g.N + kWarps - 1) / kWarps);
+  const int blocks = (int)std::max<int64_t>(1, want);
+  IDEV_CHECK_ARG((size_t)blocks * 3 <= ws.partial_floats && ws.n_counters >= 1,
+                 "row GEMV: workspace too small");
+  // best values / indices live in the partials buffer: [blocks] floats then
+  // [blocks] int64 (8-byte aligned offset).
+  float* best_v = ws.partials;
+  int64_t* best_i = reinterpret_cast<int64_t*>(ws.partials + ((blocks + 1) & ~1));
+  row_gemv_kernel<<<blocks, kThreads, 0, st>>>(g, best_v, best_i,
+                                               ws.counters + ws.n_counters - 1);
+  IDEV_LAUNCHED();
+}
+
+void launch_argmax(const float* x, int64_t n, int64_t* out, cudaStream_t st) {
+  IDEV_CHECK_ARG(n > 0, "argmax: empty input");
+  Workspace& ws = workspace_for_current_device();
+  const int blocks = (int)std::min<int64_t>(2 * sm_count(), (n + kThreads - 1) / kThreads);
+  float* best_v = ws.partials;
+  int64_t* best_i = reinterpret_cast<int64_t*>(ws.partials + ((blocks + 1) & ~1));
+  argmax_kernel<<<blocks, kThreads, 0, st>>>(x, n, out, best_v, best_i,
+                                             ws.counters + ws.n_counters - 2);
+  IDEV_LAUNCHED();
+}
+
+void launch_decode_embed(const int64_t* tok, const int64_t* pos, const float* wte,
+                         const float* wpe, float* x, int64_t H, int64_t vocab, int64_t max_pos,
+                         int* err, cudaStream_t st) {
+  decode_embed_kernel<<<(unsigned)((H + 255) / 256), 256, 0, st>>>(tok, pos, wte, wpe, x, H,
+                                                                    vocab, max_pos, err);
+  IDEV_LAUNCHED();
+}
+
+void launch_rows_embed(const int64_t* ids, int64_t n, int64_t pos0, const float* wte,
+                       const float* wpe, float* x, int64_t H, int64_t vocab, int* err,
+                       cudaStream_t st) {
+  if (n <= 0) return;
+  rows_embed_kernel<<<(unsigned)n, 256, 0, st>>>(ids, n, pos0, wte, wpe, x, H, vocab, err);
+  IDEV_LAUNCHED();
+}
+
+}  // namespace inferc_dev

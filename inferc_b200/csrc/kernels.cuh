@@ -1,0 +1,128 @@
+// Host-side launchers of the device kernels (one .cu per kernel family).
+#pragma once
+
+#include "common.cuh"
+
+namespace inferc_dev {
+
+// ---- layernorm.cu
+void launch_layernorm(const float* x, const float* gamma, const float* beta, float* y,
+                      int64_t rows, int64_t feat, float eps, cudaStream_t st);
+// Encoder embedding: y[b,s,:] = LN(word[ids[b,s]] + pos[s]); cond[b,s] =
+// (mask[b,s] == 0). Out-of-range ids set *err_flag (device int) to 1 and
+// produce a zero row.
+void launch_embed_layernorm(const int64_t* ids, const int64_t* mask, const float* word,
+                            const float* pos, int64_t vocab, const float* gamma,
+                            const float* beta, float* y, uint8_t* cond, int64_t B,
+                            int64_t S, int64_t H, float eps, int* err_flag, cudaStream_t st);
+
+// ---- gemm_simt.cu : C[M,N] = epilogue(op(A) op(B)) on CUDA cores (fp32 FMA).
+void launch_gemm_simt(const float* A, int64_t lda, bool trans_a, const float* B, int64_t ldb,
+                      bool trans_b, float* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                      const Epilogue& ep, cudaStream_t st);
+
+// ---- elementwise.cu
+void launch_act(const float* x, float* y, int64_t n, int act, cudaStream_t st);
+void launch_softmax(const float* x, float* y, int64_t rows, int64_t cols, cudaStream_t st);
+void launch_fill_rows(float* y, const float* c, int64_t c_len, int64_t M, int64_t N,
+                      cudaStream_t st);
+
+// ---- attention.cu
+struct AttnArgs {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* out;
+  int64_t ldq, ldk, ldv, ldo;  // row strides (elements) of the [B*S, *] views
+  int64_t bstride_q, bstride_k, bstride_v, bstride_o;  // batch strides (elements)
+  const uint8_t* mask;         // bool, true = masked; may be null
+  int64_t ms[4];               // mask element strides over [B, nH, S, S]
+  int64_t B, S, nH, hd;
+  float scale, fill;
+  int causal;                  // 1: additionally mask j > i (prefill)
+};
+void launch_attention(const AttnArgs& a, cudaStream_t st);
+
+void launch_kv_append(const float* k_new, const float* v_new, int64_t ld_new, float* kc,
+                      float* vc, int64_t heads, int64_t hd, int64_t max_len,
+                      const int64_t* pos_dev, int64_t pos_host, int64_t n, cudaStream_t st);
+// Decode attention; L (number of visible keys) either from *len_dev (device,
+// when non-null) or len_host. When k_new/v_new are given, the kernel first
+// writes them at position L-1 of the cache (fused KV append).
+void launch_decode_attention(const float* q, const float* k_new, const float* v_new,
+                             float* kc, float* vc, float* out, int64_t heads, int64_t hd,
+                             int64_t max_len, const int64_t* len_dev, int64_t len_host,
+                             cudaStream_t st);
+
+// ---- gemv.cu
+struct Workspace;
+
+struct GemvArgs {
+  Workspace* ws = nullptr;  // split-K scratch; null = the device's shared one
+  const float* x;       // [K] input (raw residual stream when ln_gamma is set)
+  const float* ln_gamma;  // optional LayerNorm prologue on x
+  const float* ln_beta;
+  float ln_eps;
+  const float* w;       // [K, N] row-major
+  const float* bias;    // [N] or null
+  const float* resid;   // [N] or null, may alias y
+  float* y;             // [N]
+  int64_t K, N;
+  float alpha, beta;    // y = act(alpha*acc + beta*bias + resid)
+  int act;
+};
+// Split-K over CTAs; partial sums go to the workspace and the last CTA of
+// each column tile reduces them in a fixed order (deterministic).
+void launch_gemv(const GemvArgs& g, cudaStream_t st);
+
+// Row-dot GEMV y[N] = W[N,K] x (W rows contiguous), optional LN prologue on x,
+// optional fused greedy argmax (first max wins) into *argmax_out; when
+// pos_counter is non-null the last block also increments it after writing
+// the token to tokens[*pos_counter - base] (decode loop bookkeeping).
+struct RowGemvArgs {
+  Workspace* ws = nullptr;  // scratch for the fused argmax; null = shared
+  const float* x;
+  const float* ln_gamma;
+  const float* ln_beta;
+  float ln_eps;
+  const float* w;  // [N, K]
+  float* y;        // [N]
+  int64_t K, N;
+  int64_t* argmax_out;  // optional
+  int64_t* pos_counter; // optional
+  int64_t* token_log;   // optional, token_log[*pos_counter - log_base] = argmax
+  int64_t log_base;
+};
+void launch_row_gemv(const RowGemvArgs& g, cudaStream_t st);
+
+void launch_argmax(const float* x, int64_t n, int64_t* out, cudaStream_t st);
+
+// ---- gemv_int4.cu
+void launch_gemv_int4(const InfercInt4Gemv* descs_host, int count, cudaStream_t st);
+
+// ---- decode embedding (gemv.cu): x = wte[*tok] + wpe[*pos - 1]
+void launch_decode_embed(const int64_t* tok, const int64_t* pos, const float* wte,
+                         const float* wpe, float* x, int64_t H, int64_t vocab,
+                         int64_t max_pos, int* err_flag, cudaStream_t st);
+
+// Rows embedding for prefill: x[i] = wte[ids[i]] + wpe[pos0 + i].
+void launch_rows_embed(const int64_t* ids, int64_t n, int64_t pos0, const float* wte,
+                       const float* wpe, float* x, int64_t H, int64_t vocab, int* err_flag,
+                       cudaStream_t st);
+
+// Workspace management (per device), used by split-K reductions.
+// Scratch for split-K / cross-CTA reductions. Counters must start at zero;
+// every kernel that uses them returns them to zero before it exits. Kernels
+// that share one Workspace must be ordered on the device (one stream).
+struct Workspace {
+  float* partials = nullptr;
+  size_t partial_floats = 0;
+  unsigned int* counters = nullptr;
+  size_t n_counters = 0;
+  bool owned = false;
+  void allocate(size_t floats, size_t counters);
+  void release();
+};
+Workspace& workspace_for_current_device();
+
+}  // namespace inferc_dev

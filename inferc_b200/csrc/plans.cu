@@ -1,0 +1,564 @@
+// Prepared plans: the DistilBERT-architecture encoder (`inferc run` on the
+// optimized plan, src/cli/main.cpp:324-420) and the GPT-2 greedy decoder
+// (`inferc decode`, src/cli/main.cpp:700-945), executed entirely on the
+// device as replayed CUDA graphs.
+//
+// Encoder node sequence per layer (the optimized plan's order):
+//   FusedQKV -> FusedAttention -> MatMul+Add(bias)+Add(residual)
+//   -> FusedLayerNorm -> FusedMatMulAddGELU -> MatMul+Add+Add -> FusedLayerNorm
+// mapped onto 7 kernels: QKV GEMM (one N=3H GEMM over the concatenated
+// weights), attention, out-proj GEMM with bias+residual epilogue, LayerNorm,
+// FFN1 GEMM with bias+erf-GELU epilogue, FFN2 GEMM with bias+residual,
+// LayerNorm. Embedding Gather+Add+LayerNorm is one kernel; the CLS Gather is
+// folded into the head GEMM's row stride.
+//
+// Decoder: prefill with batched kernels (causal attention), then each token
+// step is one CUDA graph: embedding, per layer [LN-prologue QKV GEMV, fused
+// KV-append + attention, out-proj GEMV + residual, LN-prologue FC GEMV +
+// tanh-GELU, proj GEMV + residual], LN-prologue LM-head GEMV with fused
+// argmax. The step reads its position and token from device memory and
+// advances them itself, so successive replays need no host work.
+#include <cfloat>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <utility>
+#include <vector>
+
+#include "kernels.cuh"
+
+namespace inferc_dev {
+void launch_gemm(const float* A, int64_t lda, bool ta, const float* B, int64_t ldb, bool tb,
+                 float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
+                 cudaStream_t st);
+}
+
+using namespace inferc_dev;
+
+namespace {
+
+// Owns every device allocation of a plan.
+struct DevArena {
+  std::vector<void*> ptrs;
+  ~DevArena() {
+    for (void* p : ptrs) cudaFree(p);
+  }
+  template <typename T>
+  T* alloc(size_t n) {
+    void* p = nullptr;
+    const size_t bytes = std::max<size_t>(n, 1) * sizeof(T);
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw Error(e == cudaErrorMemoryAllocation ? INFERC_ERR_OOM : INFERC_ERR_CUDA,
+                  "plan allocation of " + std::to_string(bytes) + " B failed: " +
+                      cudaGetErrorString(e));
+    }
+    ptrs.push_back(p);
+    return static_cast<T*>(p);
+  }
+  float* upload(const float* host, size_t n, const char* what) {
+    IDEV_CHECK_ARG(host != nullptr, std::string("plan: missing weight ") + what);
+    float* d = alloc<float>(n);
+    IDEV_CUDA(cudaMemcpy(d, host, n * sizeof(float), cudaMemcpyHostToDevice));
+    return d;
+  }
+};
+
+struct Graph {
+  cudaGraphExec_t exec = nullptr;
+  ~Graph() {
+    if (exec) cudaGraphExecDestroy(exec);
+  }
+};
+
+template <typename Fn>
+std::unique_ptr<Graph> capture(cudaStream_t st, Fn&& body) {
+  IDEV_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  try {
+    body();
+  } catch (...) {
+    cudaGraph_t g = nullptr;
+    cudaStreamEndCapture(st, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  cudaGraph_t g = nullptr;
+  IDEV_CUDA(cudaStreamEndCapture(st, &g));
+  auto out = std::make_unique<Graph>();
+  const cudaError_t e = cudaGraphInstantiate(&out->exec, g, 0);
+  cudaGraphDestroy(g);
+  IDEV_CUDA(e);
+  return out;
+}
+
+}  // namespace
+
+// ======================================================================
+// Encoder
+// ======================================================================
+
+struct InfercEncoderPlan {
+  int64_t L, H, nH, F, V, P, C, maxB, maxS;
+  float eps, fill;
+  DevArena mem;
+  cudaStream_t stream = nullptr;
+  int device = 0;
+  // weights
+  float *word, *pos, *eln_g, *eln_b;
+  std::vector<float*> wqkv, bqkv, wo, bo, ln1g, ln1b, w1, b1, w2, b2, ln2g, ln2b;
+  float *pre_w, *pre_b, *cls_w, *cls_b;
+  // activations
+  int64_t *ids, *mask;
+  uint8_t* cond;
+  float *x, *qkv, *ctx, *t, *hf, *pre, *logits;
+  int* err;
+  std::map<std::pair<int64_t, int64_t>, std::unique_ptr<Graph>> graphs;
+
+  ~InfercEncoderPlan() {
+    graphs.clear();
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  void forward(int64_t B, int64_t S, cudaStream_t st) {
+    const int64_t M = B * S;
+    launch_embed_layernorm(ids, mask, word, pos, V, eln_g, eln_b, x, cond, B, S, H, eps, err, st);
+    for (int64_t l = 0; l < L; ++l) {
+      Epilogue e_qkv;
+      e_qkv.bias = bqkv[l];
+      e_qkv.bias_mode = 1;
+      launch_gemm(x, H, false, wqkv[l], 3 * H, false, qkv, 3 * H, M, 3 * H, H, e_qkv, st);
+      AttnArgs a{};
+      a.q = qkv; a.k = qkv + H; a.v = qkv + 2 * H; a.out = ctx;
+      a.ldq = a.ldk = a.ldv = 3 * H;
+      a.ldo = H;
+      a.bstride_q = a.bstride_k = a.bstride_v = S * 3 * H;
+      a.bstride_o = S * H;
+      a.mask = cond;  // [B,1,1,S]
+      a.ms[0] = S; a.ms[1] = 0; a.ms[2] = 0; a.ms[3] = 1;
+      a.B = B; a.S = S; a.nH = nH; a.hd = H / nH;
+      a.scale = 1.0f / std::sqrt((float)(H / nH));
+      a.fill = fill;
+      launch_attention(a, st);
+      Epilogue e_o;
+      e_o.bias = bo[l];
+      e_o.bias_mode = 1;
+      e_o.resid = x;
+      e_o.ldr = H;
+      launch_gemm(ctx, H, false, wo[l], H, false, t, H, M, H, H, e_o, st);
+      launch_layernorm(t, ln1g[l], ln1b[l], x, M, H, eps, st);
+      Epilogue e_1;
+      e_1.bias = b1[l];
+      e_1.bias_mode = 1;
+      e_1.act = ACT_GELU_ERF;
+      launch_gemm(x, H, false, w1[l], F, false, hf, F, M, F, H, e_1, st);
+      Epilogue e_2;
+      e_2.bias = b2[l];
+      e_2.bias_mode = 1;
+      e_2.resid = x;
+      e_2.ldr = H;
+      launch_gemm(hf, F, false, w2[l], H, false, t, H, M, H, F, e_2, st);
+      launch_layernorm(t, ln2g[l], ln2b[l], x, M, H, eps, st);
+    }
+    // Gather(CLS) -> Gemm(transB=1) + Relu -> Gemm(transB=1): the CLS rows
+    // are rows b*S of x, read through lda = S*H.
+    Epilogue e_p;
+    e_p.bias = pre_b;
+    e_p.bias_mode = 1;
+    e_p.act = ACT_RELU;
+    launch_gemm_simt(x, S * H, false, pre_w, H, true, pre, H, B, H, H, e_p, st);
+    Epilogue e_c;
+    e_c.bias = cls_b;
+    e_c.bias_mode = 1;
+    launch_gemm_simt(pre, H, false, cls_w, H, true, logits, C, B, C, H, e_c, st);
+  }
+
+  Graph& graph_for(int64_t B, int64_t S) {
+    auto key = std::make_pair(B, S);
+    auto it = graphs.find(key);
+    if (it != graphs.end()) return *it->second;
+    // Eager run first: configures kernel attributes outside the capture and
+    // surfaces launch errors with a clear message.
+    forward(B, S, stream);
+    IDEV_CUDA(cudaStreamSynchronize(stream));
+    auto g = capture(stream, [&] { forward(B, S, stream); });
+    Graph& ref = *g;
+    graphs[key] = std::move(g);
+    return ref;
+  }
+
+  void check_shape(int64_t B, int64_t S) const {
+    IDEV_CHECK_ARG(B >= 1 && S >= 1, "encoder: empty batch");
+    IDEV_CHECK_ARG(B <= maxB && S <= maxS, "encoder: batch/sequence beyond the plan's maximum");
+    IDEV_CHECK_ARG(S <= P, "encoder: sequence longer than the position table");
+  }
+
+  // Inputs already in plan buffers `ids`, `mask`; runs on `st` after the plan
+  // stream's previous work.
+  void run_graph(int64_t B, int64_t S, cudaStream_t st) {
+    Graph& g = graph_for(B, S);
+    IDEV_CUDA(cudaGraphLaunch(g.exec, st));
+  }
+};
+
+static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t maxS,
+                           InfercEncoderPlan* p) {
+  IDEV_CHECK_ARG(w != nullptr, "encoder_create: null weights");
+  IDEV_CHECK_ARG(w->layers >= 1 && w->layers <= INFERC_MAX_LAYERS, "encoder: bad layer count");
+  IDEV_CHECK_ARG(w->hidden > 0 && w->heads > 0 && w->hidden % w->heads == 0,
+                 "encoder: hidden not divisible by heads");
+  IDEV_CHECK_ARG(maxB >= 1 && maxS >= 1 && maxS <= w->max_pos, "encoder: bad plan maxima");
+  IDEV_CUDA(cudaGetDevice(&p->device));
+  p->L = w->layers; p->H = w->hidden; p->nH = w->heads; p->F = w->ffn; p->V = w->vocab;
+  p->P = w->max_pos; p->C = w->n_classes; p->maxB = maxB; p->maxS = maxS;
+  p->eps = w->ln_eps; p->fill = w->attn_fill;
+  const int64_t H = p->H, F = p->F, M = maxB * maxS;
+  DevArena& m = p->mem;
+  p->word = m.upload(w->word_emb, (size_t)p->V * H, "word_emb");
+  p->pos = m.upload(w->pos_emb, (size_t)p->P * H, "pos_emb");
+  p->eln_g = m.upload(w->emb_ln_g, H, "emb_ln_g");
+  p->eln_b = m.upload(w->emb_ln_b, H, "emb_ln_b");
+  std::vector<float> cat((size_t)H * 3 * H), bcat((size_t)3 * H);
+  for (int64_t l = 0; l < p->L; ++l) {
+    const float* parts[3] = {w->wq[l], w->wk[l], w->wv[l]};
+    const float* bparts[3] = {w->bq[l], w->bk[l], w->bv[l]};
+    for (int i = 0; i < 3; ++i) {
+      IDEV_CHECK_ARG(parts[i] && bparts[i], "encoder: missing QKV weight");
+      for (int64_t k = 0; k < H; ++k)
+        std::memcpy(&cat[(size_t)(k * 3 * H + i * H)], parts[i] + k * H, H * sizeof(float));
+      std::memcpy(&bcat[(size_t)(i * H)], bparts[i], H * sizeof(float));
+    }
+    p->wqkv.push_back(m.upload(cat.data(), cat.size(), "wqkv"));
+    p->bqkv.push_back(m.upload(bcat.data(), bcat.size(), "bqkv"));
+    p->wo.push_back(m.upload(w->wo[l], (size_t)H * H, "wo"));
+    p->bo.push_back(m.upload(w->bo[l], H, "bo"));
+    p->ln1g.push_back(m.upload(w->ln1_g[l], H, "ln1_g"));
+    p->ln1b.push_back(m.upload(w->ln1_b[l], H, "ln1_b"));
+    p->w1.push_back(m.upload(w->w1[l], (size_t)H * F, "w1"));
+    p->b1.push_back(m.upload(w->b1[l], F, "b1"));
+    p->w2.push_back(m.upload(w->w2[l], (size_t)F * H, "w2"));
+    p->b2.push_back(m.upload(w->b2[l], H, "b2"));
+    p->ln2g.push_back(m.upload(w->ln2_g[l], H, "ln2_g"));
+    p->ln2b.push_back(m.upload(w->ln2_b[l], H, "ln2_b"));
+  }
+  p->pre_w = m.upload(w->pre_w, (size_t)H * H, "pre_w");
+  p->pre_b = m.upload(w->pre_b, H, "pre_b");
+  p->cls_w = m.upload(w->cls_w, (size_t)p->C * H, "cls_w");
+  p->cls_b = m.upload(w->cls_b, p->C, "cls_b");
+  p->ids = m.alloc<int64_t>(M);
+  p->mask = m.alloc<int64_t>(M);
+  p->cond = m.alloc<uint8_t>(M);
+  p->x = m.alloc<float>((size_t)M * H);
+  p->qkv = m.alloc<float>((size_t)M * 3 * H);
+  p->ctx = m.alloc<float>((size_t)M * H);
+  p->t = m.alloc<float>((size_t)M * H);
+  p->hf = m.alloc<float>((size_t)M * F);
+  p->pre = m.alloc<float>((size_t)maxB * H);
+  p->logits = m.alloc<float>((size_t)maxB * p->C);
+  p->err = m.alloc<int>(1);
+  IDEV_CUDA(cudaMemset(p->err, 0, sizeof(int)));
+  IDEV_CUDA(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
+}
+
+// ======================================================================
+// GPT-2 decoder
+// ======================================================================
+
+struct InfercDecoderPlan {
+  int64_t L, H, nH, hd, F, V, P, max_len;
+  float eps;
+  DevArena mem;
+  Workspace ws;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float *wte, *wpe, *lnf_g, *lnf_b;
+  std::vector<float*> ln1g, ln1b, attn_w, attn_b, proj_w, proj_b, ln2g, ln2b, fc_w, fc_b, fp_w,
+      fp_b;
+  std::vector<float*> kc, vc;  // per layer [nH, max_len, hd]
+  // prefill rows (up to max_len) and single-token buffers
+  int64_t* ids;
+  float *xr, *hr, *qkvr, *ctxr, *fr;
+  float *x, *qkv, *ctx, *f, *logits;
+  int64_t *len, *tok, *token_log;
+  int* err;
+  std::unique_ptr<Graph> step_graph;
+
+  ~InfercDecoderPlan() {
+    step_graph.reset();
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+    ws.release();
+  }
+
+  // Prefill over n prompt tokens already in `ids`: fills the cache at
+  // positions [0, n), writes the first generated token to tok and
+  // token_log[0], and sets len = n + 1.
+  void prefill(int64_t n, cudaStream_t st) {
+    launch_rows_embed(ids, n, 0, wte, wpe, xr, H, V, err, st);
+    for (int64_t l = 0; l < L; ++l) {
+      launch_layernorm(xr, ln1g[l], ln1b[l], hr, n, H, eps, st);
+      Epilogue e;
+      e.bias = attn_b[l];
+      e.bias_mode = 1;
+      launch_gemm(hr, H, false, attn_w[l], 3 * H, false, qkvr, 3 * H, n, 3 * H, H, e, st);
+      launch_kv_append(qkvr + H, qkvr + 2 * H, 3 * H, kc[l], vc[l], nH, hd, max_len, nullptr, 0,
+                       n, st);
+      AttnArgs a{};
+      a.q = qkvr; a.k = qkvr + H; a.v = qkvr + 2 * H; a.out = ctxr;
+      a.ldq = a.ldk = a.ldv = 3 * H;
+      a.ldo = H;
+      a.bstride_q = a.bstride_k = a.bstride_v = n * 3 * H;
+      a.bstride_o = n * H;
+      a.B = 1; a.S = n; a.nH = nH; a.hd = hd;
+      a.scale = 1.0f / std::sqrt((float)hd);
+      a.fill = -FLT_MAX;  // Where(causal, scores, finfo(float32).min)
+      a.causal = 1;
+      launch_attention(a, st);
+      Epilogue ep;
+      ep.bias = proj_b[l];
+      ep.bias_mode = 1;
+      ep.resid = xr;
+      ep.ldr = H;
+      launch_gemm(ctxr, H, false, proj_w[l], H, false, xr, H, n, H, H, ep, st);
+      launch_layernorm(xr, ln2g[l], ln2b[l], hr, n, H, eps, st);
+      Epilogue e1;
+      e1.bias = fc_b[l];
+      e1.bias_mode = 1;
+      e1.act = ACT_GELU_TANH;
+      launch_gemm(hr, H, false, fc_w[l], F, false, fr, F, n, F, H, e1, st);
+      Epilogue e2;
+      e2.bias = fp_b[l];
+      e2.bias_mode = 1;
+      e2.resid = xr;
+      e2.ldr = H;
+      launch_gemm(fr, F, false, fp_w[l], H, false, xr, H, n, H, F, e2, st);
+    }
+    IDEV_CUDA(cudaMemcpyAsync(len, &n_host_scratch, sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    RowGemvArgs r{};
+    r.ws = &ws;
+    r.x = xr + (n - 1) * H;
+    r.ln_gamma = lnf_g; r.ln_beta = lnf_b; r.ln_eps = eps;
+    r.w = wte; r.y = logits; r.K = H; r.N = V;
+    r.argmax_out = tok; r.pos_counter = len; r.token_log = token_log; r.log_base = n;
+    launch_row_gemv(r, st);
+  }
+  int64_t n_host_scratch = 0;  // source of the len upload (must outlive the copy)
+
+  // One single-token step (captured once into step_graph).
+  void step(cudaStream_t st) {
+    launch_decode_embed(tok, len, wte, wpe, x, H, V, P, err, st);
+    for (int64_t l = 0; l < L; ++l) {
+      GemvArgs g{};
+      g.ws = &ws;
+      g.x = x; g.ln_gamma = ln1g[l]; g.ln_beta = ln1b[l]; g.ln_eps = eps;
+      g.w = attn_w[l]; g.bias = attn_b[l]; g.y = qkv; g.K = H; g.N = 3 * H;
+      g.alpha = 1.f; g.beta = 1.f; g.act = ACT_NONE;
+      launch_gemv(g, st);
+      launch_decode_attention(qkv, qkv + H, qkv + 2 * H, kc[l], vc[l], ctx, nH, hd, max_len, len,
+                              0, st);
+      GemvArgs o{};
+      o.ws = &ws;
+      o.x = ctx; o.w = proj_w[l]; o.bias = proj_b[l]; o.resid = x; o.y = x; o.K = H; o.N = H;
+      o.alpha = 1.f; o.beta = 1.f; o.act = ACT_NONE;
+      launch_gemv(o, st);
+      GemvArgs u{};
+      u.ws = &ws;
+      u.x = x; u.ln_gamma = ln2g[l]; u.ln_beta = ln2b[l]; u.ln_eps = eps;
+      u.w = fc_w[l]; u.bias = fc_b[l]; u.y = f; u.K = H; u.N = F;
+      u.alpha = 1.f; u.beta = 1.f; u.act = ACT_GELU_TANH;
+      launch_gemv(u, st);
+      GemvArgs d{};
+      d.ws = &ws;
+      d.x = f; d.w = fp_w[l]; d.bias = fp_b[l]; d.resid = x; d.y = x; d.K = F; d.N = H;
+      d.alpha = 1.f; d.beta = 1.f; d.act = ACT_NONE;
+      launch_gemv(d, st);
+    }
+    RowGemvArgs r{};
+    r.ws = &ws;
+    r.x = x; r.ln_gamma = lnf_g; r.ln_beta = lnf_b; r.ln_eps = eps;
+    r.w = wte; r.y = logits; r.K = H; r.N = V;
+    r.argmax_out = tok; r.pos_counter = len; r.token_log = token_log; r.log_base = log_base;
+    launch_row_gemv(r, st);
+  }
+  int64_t log_base = 0;  // n_prompt of the current decode; baked into the step graph
+
+  void decode(const int64_t* prompt, int64_t n, int64_t max_tokens, int64_t* out,
+              double* step_ms) {
+    IDEV_CHECK_ARG(prompt != nullptr && out != nullptr, "decode: null prompt or output");
+    IDEV_CHECK_ARG(n >= 1 && max_tokens >= 1, "decode: empty prompt or max_tokens <= 0");
+    IDEV_CHECK_ARG(n + max_tokens - 1 <= std::min(P, max_len),
+                   "decode: prompt + new tokens exceed the context / cache length");
+    for (int64_t i = 0; i < n; ++i)
+      IDEV_CHECK_ARG(prompt[i] >= 0 && prompt[i] < V, "decode: prompt token id out of range");
+    cudaStream_t st = stream;
+    IDEV_CUDA(cudaMemcpyAsync(ids, prompt, n * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    n_host_scratch = n;
+    prefill(n, st);
+    if (max_tokens > 1) {
+      if (!step_graph || log_base != n) {
+        // The graph bakes log_base; (re)capture when the prompt length
+        // changes. The first capture is preceded by nothing eager: every
+        // kernel of the step has already run in prefill or is plain.
+        IDEV_CUDA(cudaStreamSynchronize(st));
+        log_base = n;
+        step_graph.reset();
+        step_graph = capture(st, [&] { step(st); });
+      }
+      IDEV_CUDA(cudaEventRecord(ev0, st));
+      for (int64_t s = 1; s < max_tokens; ++s) IDEV_CUDA(cudaGraphLaunch(step_graph->exec, st));
+      IDEV_CUDA(cudaEventRecord(ev1, st));
+    }
+    IDEV_CUDA(cudaMemcpyAsync(out, token_log, max_tokens * sizeof(int64_t),
+                              cudaMemcpyDeviceToHost, st));
+    int herr = 0;
+    IDEV_CUDA(cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    IDEV_CUDA(cudaStreamSynchronize(st));
+    if (herr) {
+      IDEV_CUDA(cudaMemset(err, 0, sizeof(int)));
+      throw Error(INFERC_ERR_RANGE, "decode: token or position out of range on the device");
+    }
+    if (step_ms) {
+      float ms = 0.f;
+      if (max_tokens > 1) IDEV_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
+      *step_ms = max_tokens > 1 ? ms / double(max_tokens - 1) : 0.0;
+    }
+  }
+};
+
+static void decoder_create(const InfercGpt2Weights* w, int64_t max_len, InfercDecoderPlan* p) {
+  IDEV_CHECK_ARG(w != nullptr, "decoder_create: null weights");
+  IDEV_CHECK_ARG(w->layers >= 1 && w->layers <= INFERC_MAX_LAYERS, "decoder: bad layer count");
+  IDEV_CHECK_ARG(w->hidden > 0 && w->heads > 0 && w->hidden % w->heads == 0,
+                 "decoder: hidden not divisible by heads");
+  IDEV_CHECK_ARG(max_len >= 1 && max_len <= 8192, "decoder: max_len must be in [1, 8192]");
+  p->L = w->layers; p->H = w->hidden; p->nH = w->heads; p->hd = w->hidden / w->heads;
+  p->F = w->ffn; p->V = w->vocab; p->P = w->max_pos; p->max_len = max_len; p->eps = w->ln_eps;
+  const int64_t H = p->H, F = p->F;
+  DevArena& m = p->mem;
+  p->wte = m.upload(w->wte, (size_t)p->V * H, "wte");
+  p->wpe = m.upload(w->wpe, (size_t)p->P * H, "wpe");
+  p->lnf_g = m.upload(w->lnf_g, H, "lnf_g");
+  p->lnf_b = m.upload(w->lnf_b, H, "lnf_b");
+  for (int64_t l = 0; l < p->L; ++l) {
+    p->ln1g.push_back(m.upload(w->ln1_g[l], H, "ln1_g"));
+    p->ln1b.push_back(m.upload(w->ln1_b[l], H, "ln1_b"));
+    p->attn_w.push_back(m.upload(w->attn_w[l], (size_t)H * 3 * H, "attn_w"));
+    p->attn_b.push_back(m.upload(w->attn_b[l], 3 * H, "attn_b"));
+    p->proj_w.push_back(m.upload(w->proj_w[l], (size_t)H * H, "proj_w"));
+    p->proj_b.push_back(m.upload(w->proj_b[l], H, "proj_b"));
+    p->ln2g.push_back(m.upload(w->ln2_g[l], H, "ln2_g"));
+    p->ln2b.push_back(m.upload(w->ln2_b[l], H, "ln2_b"));
+    p->fc_w.push_back(m.upload(w->fc_w[l], (size_t)H * F, "fc_w"));
+    p->fc_b.push_back(m.upload(w->fc_b[l], F, "fc_b"));
+    p->fp_w.push_back(m.upload(w->fcproj_w[l], (size_t)F * H, "fcproj_w"));
+    p->fp_b.push_back(m.upload(w->fcproj_b[l], H, "fcproj_b"));
+    p->kc.push_back(m.alloc<float>((size_t)p->nH * max_len * p->hd));
+    p->vc.push_back(m.alloc<float>((size_t)p->nH * max_len * p->hd));
+  }
+  p->ids = m.alloc<int64_t>(max_len);
+  p->xr = m.alloc<float>((size_t)max_len * H);
+  p->hr = m.alloc<float>((size_t)max_len * H);
+  p->qkvr = m.alloc<float>((size_t)max_len * 3 * H);
+  p->ctxr = m.alloc<float>((size_t)max_len * H);
+  p->fr = m.alloc<float>((size_t)max_len * F);
+  p->x = m.alloc<float>(H);
+  p->qkv = m.alloc<float>(3 * H);
+  p->ctx = m.alloc<float>(H);
+  p->f = m.alloc<float>(F);
+  p->logits = m.alloc<float>(p->V);
+  p->len = m.alloc<int64_t>(1);
+  p->tok = m.alloc<int64_t>(1);
+  p->token_log = m.alloc<int64_t>(max_len + 1);
+  p->err = m.alloc<int>(1);
+  IDEV_CUDA(cudaMemset(p->err, 0, sizeof(int)));
+  p->ws.allocate(size_t(1) << 20, 1024);
+  IDEV_CUDA(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
+  IDEV_CUDA(cudaEventCreate(&p->ev0));
+  IDEV_CUDA(cudaEventCreate(&p->ev1));
+}
+
+// ======================================================================
+// C ABI
+// ======================================================================
+
+extern "C" {
+
+int inferc_dev_encoder_create(const InfercEncoderWeights* w, int64_t max_batch, int64_t max_seq,
+                              inferc_encoder_t* out) {
+  return guard([&] {
+    IDEV_CHECK_ARG(out != nullptr, "encoder_create: null out");
+    *out = nullptr;
+    auto p = std::make_unique<InfercEncoderPlan>();
+    encoder_create(w, max_batch, max_seq, p.get());
+    const int64_t M = max_batch * max_seq;
+    IDEV_CUDA(cudaMemset(p->ids, 0, M * sizeof(int64_t)));
+    IDEV_CUDA(cudaMemset(p->mask, 0, M * sizeof(int64_t)));
+    *out = p.release();
+  });
+}
+
+int inferc_dev_encoder_run(inferc_encoder_t p, const int64_t* ids, const int64_t* mask,
+                           int64_t B, int64_t S, float* logits, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(p != nullptr, "encoder_run: null plan");
+    p->check_shape(B, S);
+    cudaStream_t st = as_stream(stream);
+    p->graph_for(B, S);
+    IDEV_CUDA(cudaMemcpyAsync(p->ids, ids, B * S * sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
+    IDEV_CUDA(cudaMemcpyAsync(p->mask, mask, B * S * sizeof(int64_t), cudaMemcpyDeviceToDevice,
+                              st));
+    p->run_graph(B, S, st);
+    IDEV_CUDA(cudaMemcpyAsync(logits, p->logits, B * p->C * sizeof(float),
+                              cudaMemcpyDeviceToDevice, st));
+  });
+}
+
+int inferc_dev_encoder_run_host(inferc_encoder_t p, const int64_t* ids, const int64_t* mask,
+                                int64_t B, int64_t S, float* logits) {
+  return guard([&] {
+    IDEV_CHECK_ARG(p != nullptr, "encoder_run_host: null plan");
+    p->check_shape(B, S);
+    cudaStream_t st = p->stream;
+    p->graph_for(B, S);
+    IDEV_CUDA(cudaMemcpyAsync(p->ids, ids, B * S * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    IDEV_CUDA(cudaMemcpyAsync(p->mask, mask, B * S * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    p->run_graph(B, S, st);
+    IDEV_CUDA(cudaMemcpyAsync(logits, p->logits, B * p->C * sizeof(float),
+                              cudaMemcpyDeviceToHost, st));
+    int herr = 0;
+    IDEV_CUDA(cudaMemcpyAsync(&herr, p->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    IDEV_CUDA(cudaStreamSynchronize(st));
+    if (herr) {
+      IDEV_CUDA(cudaMemset(p->err, 0, sizeof(int)));
+      throw Error(INFERC_ERR_RANGE, "encoder: Gather index out of range");
+    }
+  });
+}
+
+void inferc_dev_encoder_destroy(inferc_encoder_t p) { delete p; }
+
+int inferc_dev_decoder_create(const InfercGpt2Weights* w, int64_t max_len, inferc_decoder_t* out) {
+  return guard([&] {
+    IDEV_CHECK_ARG(out != nullptr, "decoder_create: null out");
+    *out = nullptr;
+    auto p = std::make_unique<InfercDecoderPlan>();
+    decoder_create(w, max_len, p.get());
+    *out = p.release();
+  });
+}
+
+int inferc_dev_decode(inferc_decoder_t p, const int64_t* prompt, int64_t n_prompt,
+                      int64_t max_tokens, int64_t* tokens_out, double* step_ms_out) {
+  return guard([&] {
+    IDEV_CHECK_ARG(p != nullptr, "decode: null plan");
+    p->decode(prompt, n_prompt, max_tokens, tokens_out, step_ms_out);
+  });
+}
+
+const float* inferc_dev_decoder_logits(inferc_decoder_t p) { return p ? p->logits : nullptr; }
+
+void inferc_dev_decoder_destroy(inferc_decoder_t p) { delete p; }
+
+}  // extern "C"
