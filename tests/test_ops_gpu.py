@@ -20,7 +20,7 @@ def T(a):
     return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
 
 
-def N(t):
+def host(t):
     torch.cuda.synchronize()
     return t.detach().cpu().numpy()
 
@@ -44,14 +44,14 @@ def test_layernorm(port, rows, feat):
     x = rng.standard_normal((rows, feat), dtype=np.float32) * 3 + 1
     g = rng.standard_normal(feat, dtype=np.float32)
     b = rng.standard_normal(feat, dtype=np.float32)
-    y = N(ops.LayerNorm(T(x), T(g), T(b), 1e-5))
+    y = host(ops.LayerNorm(T(x), T(g), T(b), 1e-5))
     if rows:
         np.testing.assert_allclose(y, port.layernorm(x, g, b, 1e-5), atol=1e-5, rtol=1e-5)
 
 
 def test_layernorm_golden(gold):
     g, i = gold
-    y = N(ops.LayerNorm(T(i["ln_x"]), T(i["ln_g"]), T(i["ln_b"]), 1e-12))
+    y = host(ops.LayerNorm(T(i["ln_x"]), T(i["ln_g"]), T(i["ln_b"]), 1e-12))
     np.testing.assert_allclose(y, g["ln_y"], atol=1e-5)
 
 
@@ -72,14 +72,14 @@ def test_fused_matmul_add_gelu(port, M, K, N):
     x = rng.standard_normal((M, K), dtype=np.float32)
     w = (rng.standard_normal((K, N), dtype=np.float32) * 0.02).astype(np.float32)
     b = rng.standard_normal(N, dtype=np.float32) * 0.1
-    y = N(ops.FusedMatMulAddGELU(T(x), T(w), T(b)))
+    y = host(ops.FusedMatMulAddGELU(T(x), T(w), T(b)))
     if M:
         np.testing.assert_allclose(y, port.fused_matmul_add_gelu(x, w, b), atol=2e-5, rtol=1e-5)
 
 
 def test_fused_matmul_add_gelu_golden_and_errors(gold):
     g, i = gold
-    y = N(ops.FusedMatMulAddGELU(T(i["mmg_x"]), T(i["mmg_w"]), T(i["mmg_b"])))
+    y = host(ops.FusedMatMulAddGELU(T(i["mmg_x"]), T(i["mmg_w"]), T(i["mmg_b"])))
     np.testing.assert_allclose(y, g["mmg_y"], atol=2e-5)
     with pytest.raises(RuntimeError, match="K mismatch"):
         ops.FusedMatMulAddGELU(torch.zeros(2, 5, device=DEV), torch.zeros(4, 3, device=DEV),
@@ -91,7 +91,7 @@ def test_fused_qkv_golden(gold):
     outs = ops.FusedQKVProjection(T(i["mmg_x"]), *[T(i["qkv_" + n]) for n in
                                                    ("wq", "bq", "wk", "bk", "wv", "bv")])
     for o, n in zip(outs, ("qkv_q", "qkv_k", "qkv_v")):
-        np.testing.assert_allclose(N(o), g[n], atol=2e-5)
+        np.testing.assert_allclose(host(o), g[n], atol=2e-5)
 
 
 @pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
@@ -104,16 +104,16 @@ def test_gemm_variants(port, ta, tb, clen):
     c = {"none": None, "row": rng.standard_normal(Nn, dtype=np.float32),
          "full": rng.standard_normal((M, Nn), dtype=np.float32),
          "scalar": np.array([0.75], np.float32)}[clen]
-    y = N(ops.Gemm(T(a), T(b), None if c is None else T(c), 0.5, 2.0, ta, tb))
+    y = host(ops.Gemm(T(a), T(b), None if c is None else T(c), 0.5, 2.0, ta, tb))
     ref = port.gemm(a, b, None if c is None else c.ravel(), 0.5, 2.0, ta, tb)
     np.testing.assert_allclose(y, ref, atol=1e-4, rtol=1e-5)
 
 
 def test_gemm_m1_golden_and_bad_c(gold):
     g, i = gold
-    y = N(ops.Gemm(T(i["gemv_a"]), T(i["gemv_b"]), T(i["gemv_c"])))
+    y = host(ops.Gemm(T(i["gemv_a"]), T(i["gemv_b"]), T(i["gemv_c"])))
     np.testing.assert_allclose(y, g["gemv_y"], atol=1e-5)
-    y = N(ops.Gemm(T(i["gemm_a"]), T(i["gemm_b"]), T(i["gemm_c"]), 0.5, 2.0, False, True))
+    y = host(ops.Gemm(T(i["gemm_a"]), T(i["gemm_b"]), T(i["gemm_c"]), 0.5, 2.0, False, True))
     np.testing.assert_allclose(y, g["gemm_y"], atol=1e-4)
     with pytest.raises(RuntimeError, match="C shape"):
         ops.Gemm(torch.zeros(3, 4, device=DEV), torch.zeros(4, 5, device=DEV),
@@ -124,7 +124,7 @@ def test_matmul_matches_torch_fp64():
     rng = np.random.default_rng(9)
     a = rng.standard_normal((129, 257), dtype=np.float32)
     b = rng.standard_normal((257, 131), dtype=np.float32)
-    y = N(ops.MatMul(T(a), T(b)))
+    y = host(ops.MatMul(T(a), T(b)))
     ref = a.astype(np.float64) @ b.astype(np.float64)
     np.testing.assert_allclose(y, ref, atol=1e-3, rtol=1e-5)
 
@@ -142,14 +142,14 @@ def _attn_case(B, S, H, hd, lens, seed):
 def test_fused_attention_padding_mask(port, B, S):
     lens = np.random.default_rng(B * S).integers(min(16, S), S + 1, size=B)
     q, k, v, m = _attn_case(B, S, 768, 64, lens, B + S)
-    y = N(ops.FusedAttention(T(q), T(k), T(v), T(m), 64, -3.4028234663852886e38))
+    y = host(ops.FusedAttention(T(q), T(k), T(v), T(m), 64, -3.4028234663852886e38))
     np.testing.assert_allclose(y, port.fused_attention(q, k, v, m, 64, -3.4028234663852886e38),
                                atol=2e-5)
 
 
 def test_fused_attention_golden(gold):
     g, i = gold
-    y = N(ops.FusedAttention(T(i["attn_q"]), T(i["attn_k"]), T(i["attn_v"]),
+    y = host(ops.FusedAttention(T(i["attn_q"]), T(i["attn_k"]), T(i["attn_v"]),
                              T(i["attn_mask"]), 64, -3.0e38))
     np.testing.assert_allclose(y, g["attn_o"], atol=2e-5)
 
@@ -158,10 +158,10 @@ def test_fused_attention_known_answers():
     # kernels_test.cc:222-253 (head_dim 2: generic kernel)
     q = T(np.array([[[1, 0], [0, 1]]], np.float32))
     v = T(np.array([[[1, 2], [3, 4]]], np.float32))
-    y = N(ops.FusedAttention(q, q.clone(), v, None, 2, -1e30)).ravel()
+    y = host(ops.FusedAttention(q, q.clone(), v, None, 2, -1e30)).ravel()
     np.testing.assert_allclose(y, [1.6604, 2.6604, 2.3396, 3.3396], atol=1e-3)
     m = T(np.array([0, 1], np.uint8).reshape(1, 1, 1, 2))
-    y = N(ops.FusedAttention(q, q.clone(), v, m, 2, -1e30)).ravel()
+    y = host(ops.FusedAttention(q, q.clone(), v, m, 2, -1e30)).ravel()
     np.testing.assert_allclose(y, [1, 2, 1, 2], atol=1e-3)
 
 
@@ -171,7 +171,7 @@ def test_fused_attention_full_mask_broadcasts_and_fully_masked_rows(port):
     q, k, v = [rng.standard_normal((B, S, H), dtype=np.float32) for _ in range(3)]
     m = (rng.random((B, 2, S, S)) < 0.3).astype(np.uint8)  # per-head, per-query mask
     m[1, 0, 5, :] = 1  # fully masked row -> uniform weights
-    y = N(ops.FusedAttention(T(q), T(k), T(v), T(m), 64, -3.0e38))
+    y = host(ops.FusedAttention(T(q), T(k), T(v), T(m), 64, -3.0e38))
     np.testing.assert_allclose(y, port.fused_attention(q, k, v, m, 64, -3.0e38), atol=2e-5)
     with pytest.raises(RuntimeError, match="broadcast"):
         ops.FusedAttention(T(q), T(k), T(v), T(np.zeros((3, 1, 1, S), np.uint8)), 64, -3.0e38)
@@ -179,7 +179,7 @@ def test_fused_attention_full_mask_broadcasts_and_fully_masked_rows(port):
 
 def test_fused_attention_head_dim_32_generic(port):
     q, k, v, m = _attn_case(2, 40, 96, 32, [40, 20], 3)
-    y = N(ops.FusedAttention(T(q), T(k), T(v), T(m), 32, -3.0e38))
+    y = host(ops.FusedAttention(T(q), T(k), T(v), T(m), 32, -3.0e38))
     np.testing.assert_allclose(y, port.fused_attention(q, k, v, m, 32, -3.0e38), atol=2e-5)
 
 
@@ -187,11 +187,11 @@ def test_fused_attention_head_dim_32_generic(port):
 
 def test_gelu_gelu_tanh_softmax_golden(gold):
     g, i = gold
-    np.testing.assert_allclose(N(ops.GeluTanh(T(i["gt_x"]))), g["gt_y"], atol=1e-6)
-    np.testing.assert_allclose(N(ops.Gelu(T(i["gt_x"]))), g["ge_y"], atol=1e-6)
-    np.testing.assert_allclose(N(ops.Softmax(T(i["sm_x"]))), g["sm_y"], atol=1e-7)
+    np.testing.assert_allclose(host(ops.GeluTanh(T(i["gt_x"]))), g["gt_y"], atol=1e-6)
+    np.testing.assert_allclose(host(ops.Gelu(T(i["gt_x"]))), g["ge_y"], atol=1e-6)
+    np.testing.assert_allclose(host(ops.Softmax(T(i["sm_x"]))), g["sm_y"], atol=1e-7)
     x = T(np.array([[1000, 1001, 999, 1002]], np.float32))
-    y = N(ops.Softmax(x))
+    y = host(ops.Softmax(x))
     assert np.isfinite(y).all() and abs(y.sum() - 1) < 1e-5
 
 
@@ -207,7 +207,7 @@ def test_gemv_kn(port, K, Nn, act):
     b = rng.standard_normal(Nn, dtype=np.float32) * 0.1
     r = rng.standard_normal(Nn, dtype=np.float32)
     for _ in range(2):  # second call checks the split-K counters were reset
-        y = N(ops.Gemv(T(x), T(w), T(b), T(r), act))
+        y = host(ops.Gemv(T(x), T(w), T(b), T(r), act))
     ref = port.gemm(x[None], w, b) + r
     if act == "gelu_tanh":
         ref = port.gelu_tanh(ref)
@@ -220,7 +220,7 @@ def test_gemv_is_deterministic():
     rng = np.random.default_rng(0)
     x = T(rng.standard_normal(3072, dtype=np.float32))
     w = T(rng.standard_normal((3072, 768), dtype=np.float32))
-    outs = [N(ops.Gemv(x, w)) for _ in range(5)]
+    outs = [host(ops.Gemv(x, w)) for _ in range(5)]
     for o in outs[1:]:
         np.testing.assert_array_equal(o, outs[0])
 
@@ -239,7 +239,7 @@ def test_argmax_first_max_wins():
 def test_int4_rowscale(port, n, k):
     rng = np.random.default_rng(n + k)
     m = synth.int4_matrix(n, k, rng)
-    y = N(ops.Int4GemvRowScale(T(m.w), T(m.scales), T(m.x)))
+    y = host(ops.Int4GemvRowScale(T(m.w), T(m.scales), T(m.x)))
     ref = port.int4_gemv_rowscale(m.w, m.scales, m.x)
     tol = 1e-6 * np.abs(m.scales).max() * np.abs(m.x).sum() * 8 + 1e-6
     np.testing.assert_allclose(y, ref, atol=tol, rtol=1e-5)
@@ -251,7 +251,7 @@ def test_int4_reference_fixture(port):
     w = np.array([(i * 31) & 0xFF for i in range(N_ * K // 2)], np.uint8).reshape(N_, K // 2)
     x = np.sin(0.07 * np.arange(K)).astype(np.float32)
     s = np.array([0.05 + 0.01 * (i % 7) for i in range(N_)], np.float32)
-    y = N(ops.Int4GemvRowScale(T(w), T(s), T(x)))
+    y = host(ops.Int4GemvRowScale(T(w), T(s), T(x)))
     np.testing.assert_allclose(y, port.int4_gemv_rowscale(w, s, x), atol=1e-4)
 
 
@@ -261,4 +261,4 @@ def test_int4_batched_gpt2_set(port):
     ops.Int4GemvBatched(dev)
     for m, d in zip(mats, dev):
         ref = port.int4_gemv_rowscale(m.w, m.scales, m.x)
-        np.testing.assert_allclose(N(d[3]), ref, atol=1e-4, rtol=1e-5)
+        np.testing.assert_allclose(host(d[3]), ref, atol=1e-4, rtol=1e-5)
