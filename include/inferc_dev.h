@@ -126,6 +126,22 @@ int inferc_dev_gemv(const float* x, const float* w, const float* b,
                     const float* resid, float* y, int64_t K, int64_t N,
                     int act, void* stream);
 
+/* Allocation-free variant of inferc_dev_gemv, with the same arguments and
+ * result. No counterpart in the reference: it exists for callers that may not
+ * allocate device memory (a host framework that owns the device heap, an
+ * allocator-less runtime, a real-time loop), whereas inferc_dev_gemv
+ * allocates its split-K scratch on first use. Its scratch is a fixed 1 MiB
+ * array built into the library (held on every device that loads it until the
+ * process exits), so N is limited to 262144 columns and K to 8192; larger
+ * sizes return INFERC_ERR_INVALID. The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress) with the device current;
+ * make that first call before any stream capture. All calls share the one
+ * array, so calls that overlap on the GPU (different streams, or different
+ * host threads on one device) race; order them on one stream. */
+int inferc_dev_gemv_noalloc(const float* x, const float* w, const float* b,
+                            const float* resid, float* y, int64_t K, int64_t N,
+                            int act, void* stream);
+
 /* int4 per-row-scale GEMV (bench/amx/int4_gemv_amx.cc:258-271): y[r] =
  * sum_k (scales[r]*(q[r,k]-8)) x[k]; W [N, K/2] bytes, byte r*(K/2)+k/2
  * holds even k in the low nibble, odd k in the high nibble. K must be even.

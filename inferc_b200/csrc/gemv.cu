@@ -427,3 +427,90 @@ void launch_rows_embed(const int64_t* ids, int64_t n, int64_t pos0, const float*
 }
 
 }  // namespace inferc_dev
+
+// ======================================================================
+// Allocation-free GEMV entry point.
+//
+// Some callers cannot allocate device memory at all: code that runs inside a
+// host framework which owns the whole device heap and forbids cudaMalloc
+// during inference, allocator-less embedded runtimes, and real-time loops
+// where an allocation (and the device synchronisation it can imply) is not
+// allowed. inferc_dev_gemv needs a split-K scratch buffer that the library
+// allocates lazily on first use; this variant instead takes its scratch from a
+// fixed array compiled into the library, so a call allocates nothing.
+// ======================================================================
+
+namespace inferc_dev {
+namespace {
+
+constexpr size_t kNoAllocPartials = size_t(1) << 18;  // 256 Ki floats = 1 MiB
+constexpr size_t kNoAllocCounters = 1024;
+
+// Lives on every device that loads this library, until the process exits.
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocPartials];
+static __device__ __align__(256) unsigned int g_noalloc_counters[kNoAllocCounters];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_partials_ptr[kMaxDevices] = {};
+unsigned int* g_noalloc_counters_ptr[kMaxDevices] = {};
+
+// Device addresses of the two arrays for the current device. The array names
+// are host-side stand-ins in host code, so the real addresses are looked up
+// once per device, with that device current.
+void noalloc_scratch(float** partials, unsigned int** counters) {
+  int dev = 0;
+  IDEV_CUDA(cudaGetDevice(&dev));
+  IDEV_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "gemv_noalloc: device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_partials_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    void* c = nullptr;
+    IDEV_CUDA(cudaGetSymbolAddress(&p, g_noalloc_partials));
+    IDEV_CUDA(cudaGetSymbolAddress(&c, g_noalloc_counters));
+    g_noalloc_partials_ptr[dev] = static_cast<float*>(p);
+    g_noalloc_counters_ptr[dev] = static_cast<unsigned int*>(c);
+  }
+  *partials = g_noalloc_partials_ptr[dev];
+  *counters = g_noalloc_counters_ptr[dev];
+}
+
+}  // namespace
+}  // namespace inferc_dev
+
+extern "C" int inferc_dev_gemv_noalloc(const float* x, const float* w, const float* b,
+                                       const float* resid, float* y, int64_t K, int64_t N,
+                                       int act, void* stream) {
+  using namespace inferc_dev;
+  return guard([&] {
+    IDEV_CHECK_ARG(K > 0 && K <= kMaxK, "gemv_noalloc: K must be in [1, 8192]");
+    IDEV_CHECK_ARG(N >= 0 && (size_t)N <= kNoAllocPartials,
+                   "gemv_noalloc: N exceeds the built-in scratch (max 262144 columns)");
+    IDEV_CHECK_ARG(act >= 0 && act <= 3, "gemv_noalloc: unknown activation");
+    if (N == 0) return;
+    cudaStream_t st = as_stream(stream);
+    GemvArgs g{};
+    g.x = x; g.w = w; g.bias = b; g.resid = resid; g.y = y; g.K = K; g.N = N;
+    g.alpha = 1.0f; g.beta = 1.0f; g.act = act;
+    if (!(N % 4 == 0 && aligned16(w))) {  // scalar path: needs no scratch
+      gemv_kn_scalar_kernel<<<(unsigned)((N + kThreads - 1) / kThreads), kThreads, 0, st>>>(g);
+      IDEV_LAUNCHED();
+      return;
+    }
+    float* partials = nullptr;
+    unsigned int* counters = nullptr;
+    noalloc_scratch(&partials, &counters);
+    const int64_t tiles = (N + kColsPerCta - 1) / kColsPerCta;
+    int64_t splits = std::max<int64_t>(1, 2 * (int64_t)sm_count() / tiles);
+    splits = std::min<int64_t>(splits, std::max<int64_t>(1, K / (2 * kWarps)));
+    while (splits > 1 && (size_t)(splits * N) > kNoAllocPartials) --splits;
+    if ((size_t)tiles > kNoAllocCounters) splits = 1;
+    int64_t kps = (K + splits - 1) / splits;
+    splits = (K + kps - 1) / kps;
+    if (splits > 1)  // the reduction counters must start at zero
+      IDEV_CUDA(cudaMemsetAsync(counters, 0, (size_t)tiles * sizeof(unsigned int), st));
+    dim3 grid((unsigned)tiles, (unsigned)splits);
+    gemv_kn_kernel<<<grid, kThreads, 0, st>>>(g, kps, (int)splits, partials, counters);
+    IDEV_LAUNCHED();
+  });
+}
