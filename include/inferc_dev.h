@@ -48,6 +48,8 @@ enum {
 /* Message of the last failed call on this host thread (never NULL). */
 const char* inferc_dev_last_error_string(void);
 
+/* Waits for the stream; also reports INFERC_ERR_TIMEOUT when a bounded
+ * device wait of an earlier tensor-core GEMM gave up (then cleared). */
 /* Library version string, e.g. "inferc_b200 0.1 sm_100a". */
 const char* inferc_dev_version(void);
 
@@ -115,6 +117,25 @@ int inferc_dev_gelu_tanh(const float* x, float* y, int64_t n, void* stream);
 /* Softmax over the last axis (src/kernels/activation.cc:52-101). */
 int inferc_dev_softmax(const float* x, float* y, int64_t rows, int64_t cols,
                        void* stream);
+
+/* Weight preparation for the tensor-core path: splits fp32 w[n] into
+ * big = w rounded to tf32 and small = w - big (both fp32 arrays of n). An
+ * executor does this once per initializer, as the reference copies each
+ * initializer once per Executor (src/runtime/executor.cc:89-96). */
+int inferc_dev_tf32_split(const float* w, float* big, float* small, int64_t n,
+                          void* stream);
+
+/* Prepared-weight GEMM with the fused epilogue of FusedMatMulAddGELU / Gemm:
+ * Y[M,N] = act(A[M,K] (B_big + B_small)[K,N] + bias[N] + resid[M,N]) with A
+ * and Y row strides lda / ldy and resid row stride ldr; bias / resid may be
+ * NULL; act as for inferc_dev_gemv. Runs the tcgen05 3xTF32 kernel when
+ * M >= 256 and operands are 16-byte aligned, else the CUDA-core kernel on
+ * B_big + B_small. */
+int inferc_dev_gemm_tf32x3(const float* a, int64_t lda, const float* b_big,
+                           const float* b_small, int64_t ldb, const float* bias,
+                           const float* resid, int64_t ldr, float* y,
+                           int64_t ldy, int64_t M, int64_t N, int64_t K,
+                           int act, void* stream);
 
 /* ------------------------------------------------------------ decode ops */
 

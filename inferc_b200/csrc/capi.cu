@@ -15,6 +15,15 @@ thread_local std::string g_last_error;
 
 void set_last_error(const std::string& msg) { g_last_error = msg; }
 
+int read_and_clear_tc_error();
+void launch_split_tf32(const float* x, float* big, float* small, int64_t n, cudaStream_t st);
+bool gemm_use_tc(int64_t M, int64_t N, int64_t K);
+bool gemm_tc_supported(const float* A, int64_t lda, const float* Bb, const float* Bs,
+                       int64_t ldb, int64_t M, int64_t N, int64_t K);
+void launch_gemm_tc(const float* A, int64_t lda, const float* Bb, const float* Bs, int64_t ldb,
+                    float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
+                    cudaStream_t st);
+
 // The tensor-core GEMM (gemm_tc.cu) when it accepts the shape, else the
 // CUDA-core kernel. Defined in gemm_dispatch.cu.
 void launch_gemm(const float* A, int64_t lda, bool ta, const float* B, int64_t ldb, bool tb,
@@ -64,7 +73,11 @@ int inferc_dev_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream
 }
 
 int inferc_dev_stream_synchronize(void* stream) {
-  return guard([&] { IDEV_CUDA(cudaStreamSynchronize(as_stream(stream))); });
+  return guard([&] {
+    IDEV_CUDA(cudaStreamSynchronize(as_stream(stream)));
+    if (read_and_clear_tc_error())
+      throw Error(INFERC_ERR_TIMEOUT, "a tensor-core GEMM wait timed out (results invalid)");
+  });
 }
 
 int inferc_dev_layernorm(const float* x, const float* gamma, const float* beta, float* y,
@@ -194,6 +207,46 @@ int inferc_dev_gelu_tanh(const float* x, float* y, int64_t n, void* stream) {
 
 int inferc_dev_softmax(const float* x, float* y, int64_t rows, int64_t cols, void* stream) {
   return guard([&] { launch_softmax(x, y, rows, cols, as_stream(stream)); });
+}
+
+int inferc_dev_tf32_split(const float* w, float* big, float* small, int64_t n, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(n >= 0 && (n == 0 || (w && big && small)), "tf32_split: bad arguments");
+    launch_split_tf32(w, big, small, n, as_stream(stream));
+  });
+}
+
+int inferc_dev_gemm_tf32x3(const float* a, int64_t lda, const float* b_big, const float* b_small,
+                           int64_t ldb, const float* bias, const float* resid, int64_t ldr,
+                           float* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
+                           void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(M >= 0 && N >= 0 && K > 0 && lda >= K && ldb >= N && ldy >= N,
+                   "gemm_tf32x3: bad shape / leading dimensions");
+    IDEV_CHECK_ARG(act >= 0 && act <= 3, "gemm_tf32x3: unknown activation");
+    if (M == 0 || N == 0) return;
+    Epilogue ep;
+    ep.bias = bias;
+    ep.bias_mode = bias ? 1 : 0;
+    ep.resid = resid;
+    ep.ldr = ldr;
+    ep.act = act;
+    cudaStream_t st = as_stream(stream);
+    if (gemm_use_tc(M, N, K) && gemm_tc_supported(a, lda, b_big, b_small, ldb, M, N, K)) {
+      launch_gemm_tc(a, lda, b_big, b_small, ldb, y, ldy, M, N, K, ep, st);
+      return;
+    }
+    // CUDA-core path (small M / unaligned): big + small is the original
+    // weight exactly, so y = act(A big + resid) then y = act(A small + y + bias).
+    Epilogue first;  // y = A big + resid (resid may alias y: same element, same thread)
+    first.resid = resid;
+    first.ldr = ldr;
+    launch_gemm_simt(a, lda, false, b_big, ldb, false, y, ldy, M, N, K, first, st);
+    Epilogue second = ep;
+    second.resid = y;
+    second.ldr = ldy;
+    launch_gemm_simt(a, lda, false, b_small, ldb, false, y, ldy, M, N, K, second, st);
+  });
 }
 
 int inferc_dev_gemv(const float* x, const float* w, const float* b, const float* resid, float* y,

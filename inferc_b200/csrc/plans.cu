@@ -29,6 +29,10 @@
 #include "kernels.cuh"
 
 namespace inferc_dev {
+void launch_split_tf32(const float* x, float* big, float* small, int64_t n, cudaStream_t st);
+void launch_gemm_presplit(const float* A, int64_t lda, const float* W, const float* Wb,
+                          const float* Ws, int64_t ldb, float* C, int64_t ldc, int64_t M,
+                          int64_t N, int64_t K, const Epilogue& ep, cudaStream_t st);
 void launch_gemm(const float* A, int64_t lda, bool ta, const float* B, int64_t ldb, bool tb,
                  float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
                  cudaStream_t st);
@@ -65,6 +69,24 @@ struct DevArena {
     return d;
   }
 };
+
+// A GEMM weight held three ways: fp32 (CUDA-core path) and its tf32
+// big/small split (tensor-core 3xTF32 path), all [K,N] row-major.
+struct SplitWeight {
+  float* w = nullptr;
+  float* big = nullptr;
+  float* small = nullptr;
+};
+
+SplitWeight split_weight(DevArena& m, float* w, size_t n) {
+  SplitWeight s;
+  s.w = w;
+  s.big = m.alloc<float>(n);
+  s.small = m.alloc<float>(n);
+  launch_split_tf32(w, s.big, s.small, (int64_t)n, nullptr);
+  IDEV_CUDA(cudaDeviceSynchronize());
+  return s;
+}
 
 struct Graph {
   cudaGraphExec_t exec = nullptr;
@@ -107,7 +129,8 @@ struct InfercEncoderPlan {
   int device = 0;
   // weights
   float *word, *pos, *eln_g, *eln_b;
-  std::vector<float*> wqkv, bqkv, wo, bo, ln1g, ln1b, w1, b1, w2, b2, ln2g, ln2b;
+  std::vector<float*> bqkv, bo, ln1g, ln1b, b1, b2, ln2g, ln2b;
+  std::vector<SplitWeight> wqkv, wo, w1, w2;
   float *pre_w, *pre_b, *cls_w, *cls_b;
   // activations
   int64_t *ids, *mask;
@@ -121,6 +144,12 @@ struct InfercEncoderPlan {
     if (stream) cudaStreamDestroy(stream);
   }
 
+  static void gemm(const float* A, int64_t lda, const SplitWeight& w, int64_t ldb, float* C,
+                   int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
+                   cudaStream_t st) {
+    launch_gemm_presplit(A, lda, w.w, w.big, w.small, ldb, C, ldc, M, N, K, ep, st);
+  }
+
   void forward(int64_t B, int64_t S, cudaStream_t st) {
     const int64_t M = B * S;
     launch_embed_layernorm(ids, mask, word, pos, V, eln_g, eln_b, x, cond, B, S, H, eps, err, st);
@@ -128,7 +157,7 @@ struct InfercEncoderPlan {
       Epilogue e_qkv;
       e_qkv.bias = bqkv[l];
       e_qkv.bias_mode = 1;
-      launch_gemm(x, H, false, wqkv[l], 3 * H, false, qkv, 3 * H, M, 3 * H, H, e_qkv, st);
+      gemm(x, H, wqkv[l], 3 * H, qkv, 3 * H, M, 3 * H, H, e_qkv, st);
       AttnArgs a{};
       a.q = qkv; a.k = qkv + H; a.v = qkv + 2 * H; a.out = ctx;
       a.ldq = a.ldk = a.ldv = 3 * H;
@@ -146,19 +175,19 @@ struct InfercEncoderPlan {
       e_o.bias_mode = 1;
       e_o.resid = x;
       e_o.ldr = H;
-      launch_gemm(ctx, H, false, wo[l], H, false, t, H, M, H, H, e_o, st);
+      gemm(ctx, H, wo[l], H, t, H, M, H, H, e_o, st);
       launch_layernorm(t, ln1g[l], ln1b[l], x, M, H, eps, st);
       Epilogue e_1;
       e_1.bias = b1[l];
       e_1.bias_mode = 1;
       e_1.act = ACT_GELU_ERF;
-      launch_gemm(x, H, false, w1[l], F, false, hf, F, M, F, H, e_1, st);
+      gemm(x, H, w1[l], F, hf, F, M, F, H, e_1, st);
       Epilogue e_2;
       e_2.bias = b2[l];
       e_2.bias_mode = 1;
       e_2.resid = x;
       e_2.ldr = H;
-      launch_gemm(hf, F, false, w2[l], H, false, t, H, M, H, F, e_2, st);
+      gemm(hf, F, w2[l], H, t, H, M, H, F, e_2, st);
       launch_layernorm(t, ln2g[l], ln2b[l], x, M, H, eps, st);
     }
     // Gather(CLS) -> Gemm(transB=1) + Relu -> Gemm(transB=1): the CLS rows
@@ -229,15 +258,15 @@ static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t 
         std::memcpy(&cat[(size_t)(k * 3 * H + i * H)], parts[i] + k * H, H * sizeof(float));
       std::memcpy(&bcat[(size_t)(i * H)], bparts[i], H * sizeof(float));
     }
-    p->wqkv.push_back(m.upload(cat.data(), cat.size(), "wqkv"));
+    p->wqkv.push_back(split_weight(m, m.upload(cat.data(), cat.size(), "wqkv"), cat.size()));
     p->bqkv.push_back(m.upload(bcat.data(), bcat.size(), "bqkv"));
-    p->wo.push_back(m.upload(w->wo[l], (size_t)H * H, "wo"));
+    p->wo.push_back(split_weight(m, m.upload(w->wo[l], (size_t)H * H, "wo"), (size_t)H * H));
     p->bo.push_back(m.upload(w->bo[l], H, "bo"));
     p->ln1g.push_back(m.upload(w->ln1_g[l], H, "ln1_g"));
     p->ln1b.push_back(m.upload(w->ln1_b[l], H, "ln1_b"));
-    p->w1.push_back(m.upload(w->w1[l], (size_t)H * F, "w1"));
+    p->w1.push_back(split_weight(m, m.upload(w->w1[l], (size_t)H * F, "w1"), (size_t)H * F));
     p->b1.push_back(m.upload(w->b1[l], F, "b1"));
-    p->w2.push_back(m.upload(w->w2[l], (size_t)F * H, "w2"));
+    p->w2.push_back(split_weight(m, m.upload(w->w2[l], (size_t)F * H, "w2"), (size_t)F * H));
     p->b2.push_back(m.upload(w->b2[l], H, "b2"));
     p->ln2g.push_back(m.upload(w->ln2_g[l], H, "ln2_g"));
     p->ln2b.push_back(m.upload(w->ln2_b[l], H, "ln2_b"));
