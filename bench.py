@@ -64,7 +64,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
@@ -255,9 +255,9 @@ def main():
             dist.barrier()
         return float(ms.item())
 
-    for _ in range(args.warmup):
-        step()
     with ClockSampler(torch.cuda.current_device()) as clocks:
+        for _ in range(args.warmup):
+            step()
         ms = timed(step, args.steps)
     value = GLOBAL_BATCH * args.steps / (ms / 1e3)
     for _ in range(args.warmup):

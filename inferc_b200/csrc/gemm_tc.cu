@@ -12,10 +12,13 @@
 // in HBM (split_tf32_kernel); A (the activation) is split in shared memory by
 // the converter warps as each tile arrives.
 //
-// CTA tile 128 x BN x 32 (K), STAGES-deep TMA ring. Warp roles (192 threads):
+// Persistent kernel (one CTA per SM striding over 128 x BN output tiles),
+// STAGES-deep TMA ring, two TMEM accumulators so the epilogue of one tile
+// overlaps the MMAs of the next. Warp roles (320 threads):
 //   warp 0      TMA producer (one lane): A tile, B_big tile, B_small tile
 //   warp 1      TMEM allocation + MMA issuer (one lane)
-//   warps 2..5  converter (A -> A_big in place + A_small) and epilogue
+//   warps 2..5  converter (A -> A_big in place + A_small)
+//   warps 6..9  epilogue
 //               (tcgen05.ld of the 128 x BN fp32 accumulator, bias / GELU /
 //               residual, stores to global).
 // Shared-memory layouts are the canonical SWIZZLE_128B UMMA layouts that TMA
@@ -27,6 +30,7 @@
 // error flag, stops issuing work, frees its TMEM and exits.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -35,8 +39,9 @@ namespace inferc_dev {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BK = 32;  // fp32 elements per 128-byte swizzle row
-constexpr int kThreadsTc = 192;
+constexpr int kConvThreads = 128;  // warps 2..5
+constexpr int kEpiThreads = 256;   // warps 6..13 (two per TMEM lane quarter)
+constexpr int kThreadsTc = 64 + kConvThreads + kEpiThreads;
 constexpr uint32_t kSpinLimit = 1u << 22;
 
 // ------------------------------------------------------------ PTX helpers
@@ -166,33 +171,75 @@ __device__ int g_tc_error;  // set to 1 by a CTA whose barrier wait timed out
 
 namespace {
 
-template <int BN, int STAGES>
+// BK = 32 (128-byte A rows, SWIZZLE_128B) or 16 (64-byte A rows, SWIZZLE_64B).
+template <int BN, int BK, int STAGES>
 struct TcShape {
-  static constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KiB
-  static constexpr uint32_t B_BYTES = BK * BN * 4;  // BN x 128 B
+  static constexpr uint32_t A_BYTES = BM * BK * 4;
+  static constexpr uint32_t B_BYTES = BK * BN * 4;
+  static constexpr uint32_t B_GROUP = BK * 128;  // one 32-column group of B
+  static constexpr uint32_t A_LAYOUT = BK == 32 ? 2 : 4;  // SWIZZLE_128B / _64B
+  static constexpr uint32_t A_SBO = 8 * BK * 4;           // 8-row atom
+  static_assert(BK == 32 || BK == 16, "BK must be 16 or 32");
   static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32,256]");
 };
 
-template <int BN, int STAGES>
+// Epilogue kinds compiled into the kernel (the generic kind evaluates the
+// runtime Epilogue description element by element).
+enum EpiKind : int { EPI_GENERIC = 0, EPI_BIAS = 1, EPI_BIAS_GELU = 2, EPI_BIAS_RESID = 3 };
+
+template <int EPI>
+__device__ __forceinline__ void epilogue16(const Epilogue& ep, const float (&v)[16], int64_t row,
+                                           int64_t col0, int N, float* __restrict__ dst,
+                                           bool vec_ok) {
+  if (EPI != EPI_GENERIC && vec_ok && col0 + 16 <= N) {
+    float b[16], r[16];
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(ep.bias + col0 + i));
+      b[i] = t.x; b[i + 1] = t.y; b[i + 2] = t.z; b[i + 3] = t.w;
+      if (EPI == EPI_BIAS_RESID) {
+        const float4 u = *reinterpret_cast<const float4*>(ep.resid + row * ep.ldr + col0 + i);
+        r[i] = u.x; r[i + 1] = u.y; r[i + 2] = u.z; r[i + 3] = u.w;
+      }
+    }
+    float o[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float t = ep.alpha * v[i] + ep.beta * b[i];
+      if (EPI == EPI_BIAS_RESID) t += r[i];
+      if (EPI == EPI_BIAS_GELU) t = gelu_erf(t);
+      o[i] = t;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i += 4)
+      *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+    return;
+  }
+  for (int i = 0; i < 16; ++i)
+    if (col0 + i < N) dst[i] = epilogue_apply(ep, v[i], row, col0 + i);
+}
+
+template <int BN, int BK, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreadsTc, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmBb,
                        const __grid_constant__ CUtensorMap tmBs, float* __restrict__ C,
                        int64_t ldc, int M, int N, int K, Epilogue ep) {
-  using S = TcShape<BN, STAGES>;
+  using S = TcShape<BN, BK, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES], conv_bar[STAGES], empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t accum_bar;
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   const int ktiles = (K + BK - 1) / BK;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int total = ((M + BM - 1) / BM) * tiles_n;
   auto stage_a = [&](int s) { return smem + (size_t)s * S::STAGE_BYTES; };
   auto stage_as = [&](int s) { return stage_a(s) + S::A_BYTES; };
   auto stage_bb = [&](int s) { return stage_a(s) + 2 * S::A_BYTES; };
@@ -205,17 +252,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&conv_bar[s], 128);
+      mbar_init(&conv_bar[s], kConvThreads);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], kEpiThreads);
+    }
     abort_sh = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == 1) {  // two accumulators of BN columns each
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&tmem_base_sh)),
-                 "r"((uint32_t)BN));
+                 "r"((uint32_t)(2 * BN)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -225,96 +275,117 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // ---------------- TMA producer
-      for (int it = 0; it < ktiles && !abort_sh; ++it) {
-        const int s = it % STAGES, r = it / STAGES;
-        if (it >= STAGES && !mbar_wait(&empty_bar[s], (r - 1) & 1)) {
-          fail();
-          break;
-        }
-        mbar_expect_tx(&full_bar[s], S::A_BYTES + 2 * S::B_BYTES);
-        tma_load_2d(stage_a(s), &tmA, &full_bar[s], it * BK, m0);
+      int g = 0;  // k-iteration counter across tiles (stage ring position)
+      for (int tile = blockIdx.x; tile < total && !abort_sh; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+        for (int it = 0; it < ktiles && !abort_sh; ++it, ++g) {
+          const int s = g % STAGES, r = g / STAGES;
+          if (g >= STAGES && !mbar_wait(&empty_bar[s], (r - 1) & 1)) {
+            fail();
+            break;
+          }
+          mbar_expect_tx(&full_bar[s], S::A_BYTES + 2 * S::B_BYTES);
+          tma_load_2d(stage_a(s), &tmA, &full_bar[s], it * BK, m0);
 #pragma unroll
-        for (int g = 0; g < BN / 32; ++g) {
-          tma_load_2d(stage_bb(s) + g * 4096, &tmBb, &full_bar[s], n0 + g * 32, it * BK);
-          tma_load_2d(stage_bs(s) + g * 4096, &tmBs, &full_bar[s], n0 + g * 32, it * BK);
+          for (int gi = 0; gi < BN / 32; ++gi) {
+            tma_load_2d(stage_bb(s) + gi * S::B_GROUP, &tmBb, &full_bar[s], n0 + gi * 32, it * BK);
+            tma_load_2d(stage_bs(s) + gi * S::B_GROUP, &tmBs, &full_bar[s], n0 + gi * 32, it * BK);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_tf32(BM, BN);
-      for (int it = 0; it < ktiles && !abort_sh; ++it) {
-        const int s = it % STAGES, r = it / STAGES;
-        if (!mbar_wait(&conv_bar[s], r & 1)) {
+      int g = 0, tl = 0;  // k-iteration counter, local tile counter
+      for (int tile = blockIdx.x; tile < total && !abort_sh; tile += gridDim.x, ++tl) {
+        const int acc = tl & 1;
+        if (tl >= 2 && !mbar_wait(&tempty_bar[acc], ((tl >> 1) - 1) & 1)) {
           fail();
           break;
         }
         tc_fence_after();
-        const uint32_t a = smem_u32(stage_a(s)), as = smem_u32(stage_as(s));
-        const uint32_t bb = smem_u32(stage_bb(s)), bs = smem_u32(stage_bs(s));
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int it = 0; it < ktiles && !abort_sh; ++it, ++g) {
+          const int s = g % STAGES, r = g / STAGES;
+          if (!mbar_wait(&conv_bar[s], r & 1)) {
+            fail();
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(stage_a(s)), as = smem_u32(stage_as(s));
+          const uint32_t bb = smem_u32(stage_bb(s)), bs = smem_u32(stage_bs(s));
 #pragma unroll
-        for (int j = 0; j < BK / 8; ++j) {
-          // A: K-major, k-step of 8 tf32 = 32 bytes inside the 128-byte row.
-          const uint64_t da = smem_desc(a + j * 32, 16, 1024, 2);
-          const uint64_t das = smem_desc(as + j * 32, 16, 1024, 2);
-          // B: MN-major, 128-byte rows of 32 columns in 4-row (512 B) swizzle
-          // atoms; a k-step of 8 rows advances 1 KiB; 32-column groups are
-          // 4 KiB apart.
-          const uint64_t dbb = smem_desc(bb + j * 1024, 4096, 512, 1);
-          const uint64_t dbs = smem_desc(bs + j * 1024, 4096, 512, 1);
-          mma_tf32(tmem, das, dbb, idesc, (it | j) != 0);
-          mma_tf32(tmem, da, dbs, idesc, 1);
-          mma_tf32(tmem, da, dbb, idesc, 1);
+          for (int j = 0; j < BK / 8; ++j) {
+            // A: K-major, k-step of 8 tf32 = 32 bytes inside the row.
+            const uint64_t da = smem_desc(a + j * 32, 16, S::A_SBO, S::A_LAYOUT);
+            const uint64_t das = smem_desc(as + j * 32, 16, S::A_SBO, S::A_LAYOUT);
+            // B: MN-major, 128-byte rows of 32 columns in 4-row (512 B) swizzle
+            // atoms; a k-step of 8 rows advances 1 KiB; 32-column groups are
+            // B_GROUP bytes apart.
+            const uint64_t dbb = smem_desc(bb + j * 1024, S::B_GROUP, 512, 1);
+            const uint64_t dbs = smem_desc(bs + j * 1024, S::B_GROUP, 512, 1);
+            mma_tf32(d, das, dbb, idesc, (it | j) != 0);
+            mma_tf32(d, da, dbs, idesc, 1);
+            mma_tf32(d, da, dbb, idesc, 1);
+          }
+          mma_commit(&empty_bar[s]);  // stage s may be refilled once these MMAs finish
         }
-        mma_commit(&empty_bar[s]);  // stage s may be refilled once these MMAs finish
+        mma_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
       }
-      mma_commit(&accum_bar);
     }
-  } else {  // ---------------- converter + epilogue (warps 2..5)
+  } else if (warp < 2 + kConvThreads / 32) {  // ---------------- converter (warps 2..5)
     const int t = threadIdx.x - 64;
-    for (int it = 0; it < ktiles && !abort_sh; ++it) {
-      const int s = it % STAGES, r = it / STAGES;
-      if (!mbar_wait(&full_bar[s], r & 1)) {
+    int g = 0;
+    for (int tile = blockIdx.x; tile < total && !abort_sh; tile += gridDim.x) {
+      for (int it = 0; it < ktiles && !abort_sh; ++it, ++g) {
+        const int s = g % STAGES, r = g / STAGES;
+        if (!mbar_wait(&full_bar[s], r & 1)) {
+          fail();
+          break;
+        }
+        float4* a4 = reinterpret_cast<float4*>(stage_a(s));
+        float4* as4 = reinterpret_cast<float4*>(stage_as(s));
+#pragma unroll 4
+        for (int i = t; i < (int)(S::A_BYTES / 16); i += kConvThreads) {
+          const float4 v = a4[i];
+          float4 b;
+          b.x = tf32_round(v.x); b.y = tf32_round(v.y); b.z = tf32_round(v.z); b.w = tf32_round(v.w);
+          a4[i] = b;
+          as4[i] = make_float4(v.x - b.x, v.y - b.y, v.z - b.z, v.w - b.w);
+        }
+        fence_proxy_async();  // generic-proxy writes -> visible to the tensor core
+        mbar_arrive(&conv_bar[s]);
+      }
+    }
+  } else {  // ---------------- epilogue (warps 6..13)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2 - kConvThreads / 32) >> 2;  // which half of the columns
+    const bool vec_ok = (ldc & 3) == 0 && aligned16(C) &&
+                        (EPI != EPI_BIAS_RESID || ((ep.ldr & 3) == 0 && aligned16(ep.resid))) &&
+                        (EPI == EPI_GENERIC || aligned16(ep.bias));
+    int tl = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tl) {
+      const int acc = tl & 1;
+      const bool ok = !abort_sh && mbar_wait(&tfull_bar[acc], (tl >> 1) & 1);
+      if (!ok) {
         fail();
         break;
       }
-      float4* a4 = reinterpret_cast<float4*>(stage_a(s));
-      float4* as4 = reinterpret_cast<float4*>(stage_as(s));
-#pragma unroll 4
-      for (int i = t; i < (int)(S::A_BYTES / 16); i += 128) {
-        const float4 v = a4[i];
-        float4 b;
-        b.x = tf32_round(v.x); b.y = tf32_round(v.y); b.z = tf32_round(v.z); b.w = tf32_round(v.w);
-        a4[i] = b;
-        as4[i] = make_float4(v.x - b.x, v.y - b.y, v.z - b.z, v.w - b.w);
-      }
-      fence_proxy_async();  // generic-proxy writes -> visible to the tensor core
-      mbar_arrive(&conv_bar[s]);
-    }
-    const bool ok = !abort_sh && mbar_wait(&accum_bar, 0);
-    if (!ok) fail();
-    tc_fence_after();
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int64_t row = m0 + 32 * q + lane;
+      tc_fence_after();
+      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+      const int64_t row = m0 + 32 * q + lane;
+      const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-      if (!ok || row >= M) continue;
-      const int64_t col0 = (int64_t)n0 + c0;
-      float o[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        o[i] = (col0 + i < N) ? epilogue_apply(ep, v[i], row, col0 + i) : 0.f;
-      float* dst = C + row * ldc + col0;
-      if (col0 + 16 <= N && (ldc & 3) == 0) {
-#pragma unroll
-        for (int i = 0; i < 16; i += 4)
-          *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-      } else {
-        for (int i = 0; i < 16; ++i)
-          if (col0 + i < N) dst[i] = o[i];
+      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
+        float v[16];
+        tmem_ld16(base + (uint32_t)c0, v);
+        if (row >= M) continue;
+        const int64_t col0 = (int64_t)n0 + c0;
+        epilogue16<EPI>(ep, v, row, col0, N, C + row * ldc + col0, vec_ok);
       }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);  // accumulator may be overwritten
     }
   }
   tc_fence_before();
@@ -322,7 +393,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"((uint32_t)BN));
+                 "r"((uint32_t)(2 * BN)));
   }
 }
 
@@ -374,19 +445,28 @@ CUtensorMap make_map(const float* base, int64_t rows, int64_t cols, int64_t ld, 
   return m;
 }
 
-template <int BN, int STAGES>
+int sm_count_tc() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+template <int BN, int BK, int STAGES, int EPI>
 void launch_tc(const float* A, int64_t lda, const float* Bb, const float* Bs, int64_t ldb,
                float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
                cudaStream_t st) {
-  using S = TcShape<BN, STAGES>;
-  const CUtensorMap ta = make_map(A, M, K, lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  using S = TcShape<BN, BK, STAGES>;
+  const CUtensorMap ta = make_map(A, M, K, lda, BK, BM,
+                                  BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   const CUtensorMap tbb = make_map(Bb, K, N, ldb, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   const CUtensorMap tbs = make_map(Bs, K, N, ldb, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-  IDEV_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, STAGES>,
+  IDEV_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, STAGES, EPI>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::SMEM_BYTES));
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-  gemm_tf32x3_kernel<BN, STAGES><<<grid, kThreadsTc, S::SMEM_BYTES, st>>>(
+  const int64_t tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM);
+  dim3 grid((unsigned)std::min<int64_t>(tiles, sm_count_tc()));
+  gemm_tf32x3_kernel<BN, BK, STAGES, EPI><<<grid, kThreadsTc, S::SMEM_BYTES, st>>>(
       ta, tbb, tbs, C, ldc, (int)M, (int)N, (int)K, ep);
   IDEV_LAUNCHED();
 }
@@ -405,7 +485,22 @@ void launch_gemm_tc(const float* A, int64_t lda, const float* Bb, const float* B
                     cudaStream_t st) {
   IDEV_CHECK_ARG(gemm_tc_supported(A, lda, Bb, Bs, ldb, M, N, K),
                  "tensor-core GEMM: unsupported shape or alignment");
-  launch_tc<256, 2>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);
+  // Compile-time epilogue for the plan's three shapes; anything else (scalar
+  // or full-matrix C, other activations) uses the generic one.
+  int epi = EPI_GENERIC;
+  if (ep.bias_mode == 1 && ep.act == ACT_NONE && ep.resid == nullptr) epi = EPI_BIAS;
+  if (ep.bias_mode == 1 && ep.act == ACT_GELU_ERF && ep.resid == nullptr) epi = EPI_BIAS_GELU;
+  if (ep.bias_mode == 1 && ep.act == ACT_NONE && ep.resid != nullptr) epi = EPI_BIAS_RESID;
+  switch (epi) {
+    case EPI_BIAS: launch_tc<256, 32, 2, EPI_BIAS>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st); break;
+    case EPI_BIAS_GELU:
+      launch_tc<256, 32, 2, EPI_BIAS_GELU>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);
+      break;
+    case EPI_BIAS_RESID:
+      launch_tc<256, 32, 2, EPI_BIAS_RESID>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);
+      break;
+    default: launch_tc<256, 32, 2, EPI_GENERIC>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);
+  }
 }
 
 void launch_split_tf32(const float* x, float* big, float* small, int64_t n, cudaStream_t st) {
