@@ -280,6 +280,99 @@ __global__ void __launch_bounds__(kDecThreads)
   }
 }
 
+// Vectorised decode attention (head_dim % 4 == 0, head_dim <= 128): scores
+// with one thread per key (a whole K row of independent 128-bit loads), then
+// out = sum_j p_j v_j with threads split into (float4 of head dims) x (key
+// groups) and a fixed-order reduction over the groups.
+__global__ void __launch_bounds__(kDecThreads)
+    decode_attention_vec_kernel(const float* __restrict__ q, const float* __restrict__ k_new,
+                                const float* __restrict__ v_new, float* kc, float* vc,
+                                float* __restrict__ out, int64_t hd, int64_t max_len,
+                                const int64_t* len_dev, int64_t len_host) {
+  extern __shared__ __align__(16) float dsm[];  // [max_len] scores | [kDecThreads*4] partials
+  __shared__ __align__(16) float qs[128];
+  __shared__ float red[kDecThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t h = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t L = len_dev ? *len_dev : len_host;
+  if (L <= 0 || L > max_len) return;
+  float* kh = kc + h * max_len * hd;
+  float* vh = vc + h * max_len * hd;
+  float* sc = dsm;
+  if (tid < hd) {
+    qs[tid] = q[h * hd + tid];
+    if (k_new) {
+      kh[(L - 1) * hd + tid] = k_new[h * hd + tid];
+      vh[(L - 1) * hd + tid] = v_new[h * hd + tid];
+    }
+  }
+  __syncthreads();
+  const int hd4 = (int)(hd / 4);
+  const float sq = sqrtf((float)hd);
+  const float4* q4 = reinterpret_cast<const float4*>(qs);
+  for (int64_t j = tid; j < L; j += kDecThreads) {
+    const float4* kr = reinterpret_cast<const float4*>(kh + j * hd);
+    float dot = 0.f;
+#pragma unroll 8
+    for (int d = 0; d < hd4; ++d) {
+      const float4 kv = kr[d], qv = q4[d];
+      dot = fmaf(qv.x, kv.x, dot);
+      dot = fmaf(qv.y, kv.y, dot);
+      dot = fmaf(qv.z, kv.z, dot);
+      dot = fmaf(qv.w, kv.w, dot);
+    }
+    sc[j] = dot / sq;
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int64_t j = tid; j < L; j += kDecThreads) mx = fmaxf(mx, sc[j]);
+  mx = warp_max(mx);
+  if (lane == 0) red[wid] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < kDecThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int64_t j = tid; j < L; j += kDecThreads) {
+    const float e = expf(sc[j] - mx);
+    sc[j] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[wid] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int w = 0; w < kDecThreads / 32; ++w) sum += red[w];
+  const float inv = 1.0f / sum;
+  const int groups = kDecThreads / hd4;  // key groups
+  const int d4 = tid % hd4, g = tid / hd4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (g < groups) {
+#pragma unroll 4
+    for (int64_t j = g; j < L; j += groups) {
+      const float p = sc[j] * inv;
+      const float4 vv = reinterpret_cast<const float4*>(vh + j * hd)[d4];
+      acc.x = fmaf(p, vv.x, acc.x);
+      acc.y = fmaf(p, vv.y, acc.y);
+      acc.z = fmaf(p, vv.z, acc.z);
+      acc.w = fmaf(p, vv.w, acc.w);
+    }
+  }
+  float4* part = reinterpret_cast<float4*>(dsm + max_len + ((max_len & 3) ? 4 - (max_len & 3) : 0));
+  part[tid] = acc;
+  __syncthreads();
+  if (tid < hd4) {
+    float4 r = part[tid];
+    for (int gg = 1; gg < groups; ++gg) {
+      const float4 t = part[gg * hd4 + tid];
+      r.x += t.x; r.y += t.y; r.z += t.z; r.w += t.w;
+    }
+    reinterpret_cast<float4*>(out + h * hd)[tid] = r;
+  }
+}
+
 __global__ void kv_append_kernel(const float* __restrict__ k_new, const float* __restrict__ v_new,
                                  int64_t ld_new, float* kc, float* vc, int64_t heads, int64_t hd,
                                  int64_t max_len, const int64_t* pos_dev, int64_t pos_host,
@@ -336,6 +429,14 @@ void launch_decode_attention(const float* q, const float* k_new, const float* v_
                              const int64_t* len_dev, int64_t len_host, cudaStream_t st) {
   IDEV_CHECK_ARG(hd > 0 && hd <= 128, "decode attention: head_dim must be in [1, 128]");
   IDEV_CHECK_ARG(max_len > 0 && max_len <= 8192, "decode attention: max_len must be <= 8192");
+  const bool vec = hd % 4 == 0 && aligned16(q) && aligned16(kc) && aligned16(vc) &&
+                   aligned16(out) && (k_new == nullptr || (aligned16(k_new) && aligned16(v_new)));
+  if (vec) {
+    const size_t smem = (size_t)(max_len + 4 + 4 * kDecThreads) * sizeof(float);
+    launch_pdl(decode_attention_vec_kernel, dim3((unsigned)heads), dim3(kDecThreads), smem, st, q,
+               k_new, v_new, kc, vc, out, hd, max_len, len_dev, len_host);
+    return;
+  }
   const size_t smem = (size_t)(max_len + kDecThreads) * sizeof(float);
   decode_attention_kernel<<<(unsigned)heads, kDecThreads, smem, st>>>(
       q, k_new, v_new, kc, vc, out, hd, max_len, len_dev, len_host);

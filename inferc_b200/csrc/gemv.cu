@@ -105,31 +105,33 @@ __global__ void __launch_bounds__(kThreads)
   const int split = blockIdx.y;
   const int64_t k0 = split * k_per_split;
   const int64_t k1 = min(a.K, k0 + k_per_split);
+  // Weights do not depend on the previous kernel: fetch this warp's first
+  // kPrefetch rows into registers before waiting on it.
+  constexpr int kPrefetch = 8;
+  const int64_t col = n0 + lane * 4;
+  const bool colok = col < a.N;
+  const float* wp = a.w + col;
+  float4 wr[kPrefetch];
+#pragma unroll
+  for (int r = 0; r < kPrefetch; ++r) {
+    const int64_t k = k0 + wid + r * kWarps;
+    wr[r] = (colok && k < k1) ? __ldg(reinterpret_cast<const float4*>(wp + k * a.N))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
   stage_x(a.x, a.ln_gamma, a.ln_beta, a.ln_eps, a.K, k0, k1, xs, red);
 
-  const int64_t col = n0 + lane * 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (col < a.N) {
-    const float* wp = a.w + col;
-    int64_t k = k0 + wid;
-    // 4 independent 128-bit loads in flight per lane.
-    for (; k + 3 * kWarps < k1; k += 4 * kWarps) {
-      float4 w0 = __ldg(reinterpret_cast<const float4*>(wp + (k)*a.N));
-      float4 w1 = __ldg(reinterpret_cast<const float4*>(wp + (k + kWarps) * a.N));
-      float4 w2 = __ldg(reinterpret_cast<const float4*>(wp + (k + 2 * kWarps) * a.N));
-      float4 w3 = __ldg(reinterpret_cast<const float4*>(wp + (k + 3 * kWarps) * a.N));
-      const float x0 = xs[k - k0], x1 = xs[k + kWarps - k0], x2 = xs[k + 2 * kWarps - k0],
-                  x3 = xs[k + 3 * kWarps - k0];
-      acc.x = fmaf(x0, w0.x, acc.x); acc.y = fmaf(x0, w0.y, acc.y);
-      acc.z = fmaf(x0, w0.z, acc.z); acc.w = fmaf(x0, w0.w, acc.w);
-      acc.x = fmaf(x1, w1.x, acc.x); acc.y = fmaf(x1, w1.y, acc.y);
-      acc.z = fmaf(x1, w1.z, acc.z); acc.w = fmaf(x1, w1.w, acc.w);
-      acc.x = fmaf(x2, w2.x, acc.x); acc.y = fmaf(x2, w2.y, acc.y);
-      acc.z = fmaf(x2, w2.z, acc.z); acc.w = fmaf(x2, w2.w, acc.w);
-      acc.x = fmaf(x3, w3.x, acc.x); acc.y = fmaf(x3, w3.y, acc.y);
-      acc.z = fmaf(x3, w3.z, acc.z); acc.w = fmaf(x3, w3.w, acc.w);
-    }
-    for (; k < k1; k += kWarps) {
+#pragma unroll
+  for (int r = 0; r < kPrefetch; ++r) {
+    const int64_t k = k0 + wid + r * kWarps;
+    const float x0 = k < k1 ? xs[k - k0] : 0.f;
+    acc.x = fmaf(x0, wr[r].x, acc.x); acc.y = fmaf(x0, wr[r].y, acc.y);
+    acc.z = fmaf(x0, wr[r].z, acc.z); acc.w = fmaf(x0, wr[r].w, acc.w);
+  }
+  if (colok) {
+    for (int64_t k = k0 + wid + kPrefetch * kWarps; k < k1; k += kWarps) {
       const float4 w0 = __ldg(reinterpret_cast<const float4*>(wp + k * a.N));
       const float x0 = xs[k - k0];
       acc.x = fmaf(x0, w0.x, acc.x); acc.y = fmaf(x0, w0.y, acc.y);
@@ -220,25 +222,44 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ int64_t si[kWarps];
   __shared__ bool last;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  pdl_launch_dependents();
+  pdl_wait();
   stage_x(a.x, a.ln_gamma, a.ln_beta, a.ln_eps, a.K, 0, a.K, xs, red);
   const int64_t K4 = a.K / 4;
   const float4* x4 = reinterpret_cast<const float4*>(xs);
   float bv = -INFINITY;
   int64_t bi = INT64_MAX;
   const int64_t stride = (int64_t)gridDim.x * kWarps;
-  for (int64_t r = (int64_t)blockIdx.x * kWarps + wid; r < a.N; r += stride) {
-    const float4* w4 = reinterpret_cast<const float4*>(a.w + r * a.K);
-    float acc = 0.f;
+  // Four rows per warp per iteration: 4 x K4/32 independent 128-bit loads in
+  // flight per lane.
+  for (int64_t r0 = (int64_t)blockIdx.x * kWarps + wid; r0 < a.N; r0 += 4 * stride) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int64_t k = lane; k < K4; k += 32) {
-      const float4 w = __ldg(w4 + k), xv = x4[k];
-      acc = fmaf(xv.x, w.x, acc);
-      acc = fmaf(xv.y, w.y, acc);
-      acc = fmaf(xv.z, w.z, acc);
-      acc = fmaf(xv.w, w.w, acc);
+      const float4 xv = x4[k];
+      float4 w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t r = r0 + u * stride;
+        w[u] = r < a.N ? __ldg(reinterpret_cast<const float4*>(a.w + r * a.K) + k)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc[u] = fmaf(xv.x, w[u].x, acc[u]);
+        acc[u] = fmaf(xv.y, w[u].y, acc[u]);
+        acc[u] = fmaf(xv.z, w[u].z, acc[u]);
+        acc[u] = fmaf(xv.w, w[u].w, acc[u]);
+      }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) a.y[r] = acc;
-    if (better(acc, r, bv, bi)) { bv = acc; bi = r; }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t r = r0 + u * stride;
+      const float v = warp_sum(acc[u]);
+      if (r < a.N) {
+        if (lane == 0) a.y[r] = v;
+        if (better(v, r, bv, bi)) { bv = v; bi = r; }
+      }
+    }
   }
   if (a.argmax_out == nullptr) return;
   // bv/bi are identical across the lanes of a warp (warp_sum broadcasts).
@@ -322,6 +343,8 @@ __global__ void argmax_kernel(const float* __restrict__ x, int64_t n, int64_t* o
 __global__ void decode_embed_kernel(const int64_t* tok, const int64_t* pos, const float* wte,
                                     const float* wpe, float* x, int64_t H, int64_t vocab,
                                     int64_t max_pos, int* err) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t t = *tok, p = *pos - 1;
   if (t < 0 || t >= vocab || p < 0 || p >= max_pos) {
     if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(err, 1);
@@ -370,15 +393,18 @@ void launch_gemv(const GemvArgs& g, cudaStream_t st) {
   }
   const int64_t tiles = (g.N + kColsPerCta - 1) / kColsPerCta;
   const int64_t target = 2 * (int64_t)sm_count();
+  // Enough CTAs to cover the SMs, and at most 64 rows per CTA so that each
+  // warp's rows fit the register prefetch.
   int64_t splits = std::max<int64_t>(1, target / tiles);
-  splits = std::min<int64_t>(splits, std::max<int64_t>(1, g.K / (2 * kWarps)));
+  splits = std::max<int64_t>(splits, (g.K + 63) / 64);
+  splits = std::min<int64_t>(splits, std::max<int64_t>(1, g.K / kWarps));
   while (splits > 1 && (size_t)(splits * g.N) > ws.partial_floats) --splits;
   if ((size_t)tiles + 2 > ws.n_counters) splits = 1;  // last two slots: argmax
   int64_t kps = (g.K + splits - 1) / splits;
   splits = (g.K + kps - 1) / kps;
   dim3 grid((unsigned)tiles, (unsigned)splits);
-  gemv_kn_kernel<<<grid, kThreads, 0, st>>>(g, kps, (int)splits, ws.partials, ws.counters);
-  IDEV_LAUNCHED();
+  launch_pdl(gemv_kn_kernel, grid, dim3(kThreads), 0, st, g, kps, (int)splits, ws.partials,
+             ws.counters);
 }
 
 void launch_row_gemv(const RowGemvArgs& g, cudaStream_t st) {
@@ -394,9 +420,8 @@ void launch_row_gemv(const RowGemvArgs& g, cudaStream_t st) {
   // [blocks] int64 (8-byte aligned offset).
   float* best_v = ws.partials;
   int64_t* best_i = reinterpret_cast<int64_t*>(ws.partials + ((blocks + 1) & ~1));
-  row_gemv_kernel<<<blocks, kThreads, 0, st>>>(g, best_v, best_i,
-                                               ws.counters + ws.n_counters - 1);
-  IDEV_LAUNCHED();
+  launch_pdl(row_gemv_kernel, dim3(blocks), dim3(kThreads), 0, st, g, best_v, best_i,
+             ws.counters + ws.n_counters - 1);
 }
 
 void launch_argmax(const float* x, int64_t n, int64_t* out, cudaStream_t st) {
@@ -413,9 +438,8 @@ void launch_argmax(const float* x, int64_t n, int64_t* out, cudaStream_t st) {
 void launch_decode_embed(const int64_t* tok, const int64_t* pos, const float* wte,
                          const float* wpe, float* x, int64_t H, int64_t vocab, int64_t max_pos,
                          int* err, cudaStream_t st) {
-  decode_embed_kernel<<<(unsigned)((H + 255) / 256), 256, 0, st>>>(tok, pos, wte, wpe, x, H,
-                                                                    vocab, max_pos, err);
-  IDEV_LAUNCHED();
+  launch_pdl(decode_embed_kernel, dim3((unsigned)((H + 255) / 256)), dim3(256), 0, st, tok, pos,
+             wte, wpe, x, H, vocab, max_pos, err);
 }
 
 void launch_rows_embed(const int64_t* ids, int64_t n, int64_t pos0, const float* wte,
