@@ -129,13 +129,26 @@ int inferc_dev_tf32_split(const float* w, float* big, float* small, int64_t n,
  * Y[M,N] = act(A[M,K] (B_big + B_small)[K,N] + bias[N] + resid[M,N]) with A
  * and Y row strides lda / ldy and resid row stride ldr; bias / resid may be
  * NULL; act as for inferc_dev_gemv. Runs the tcgen05 3xTF32 kernel when
- * M >= 256 and operands are 16-byte aligned, else the CUDA-core kernel on
+ * M >= 64 and operands are 16-byte aligned, else the CUDA-core kernel on
  * B_big + B_small. */
 int inferc_dev_gemm_tf32x3(const float* a, int64_t lda, const float* b_big,
                            const float* b_small, int64_t ldb, const float* bias,
                            const float* resid, int64_t ldr, float* y,
                            int64_t ldy, int64_t M, int64_t N, int64_t K,
                            int act, void* stream);
+
+/* FusedQKV + FusedAttention as one call on prepared weights (the encoder
+ * plan's attention block): qkv = X Wqkv + bqkv with Wqkv = [Wq | Wk | Wv]
+ * ([H, 3H], split by inferc_dev_tf32_split into w_big / w_small) and bqkv
+ * [3H]; then attention over the q/k/v column blocks of qkv read in place
+ * (row stride 3H). key_mask: optional bool [B,S], true = key masked (the
+ * [B,1,1,S] padding mask of the reference graph); scratch_qkv: caller buffer
+ * of B*S*3H floats; out: [B,S,H]. */
+int inferc_dev_qkv_attention(const float* x, const float* w_big,
+                             const float* w_small, const float* bqkv,
+                             const uint8_t* key_mask, int64_t B, int64_t S,
+                             int64_t H, int64_t head_dim, float fill,
+                             float* scratch_qkv, float* out, void* stream);
 
 /* ------------------------------------------------------------ decode ops */
 

@@ -249,6 +249,35 @@ int inferc_dev_gemm_tf32x3(const float* a, int64_t lda, const float* b_big, cons
   });
 }
 
+int inferc_dev_qkv_attention(const float* x, const float* w_big, const float* w_small,
+                             const float* bqkv, const uint8_t* key_mask, int64_t B, int64_t S,
+                             int64_t H, int64_t head_dim, float fill, float* scratch_qkv,
+                             float* out, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(B >= 0 && S >= 0 && H > 0, "qkv_attention: bad shape");
+    IDEV_CHECK_ARG(head_dim > 0 && H % head_dim == 0,
+                   "qkv_attention: H not divisible by head_dim");
+    if (B == 0 || S == 0) return;
+    cudaStream_t st = as_stream(stream);
+    const int64_t M = B * S;
+    IDEV_CHECK_ARG(inferc_dev_gemm_tf32x3(x, H, w_big, w_small, 3 * H, bqkv, nullptr, 0,
+                                          scratch_qkv, 3 * H, M, 3 * H, H, 0, stream) == 0,
+                   std::string("qkv_attention: ") + g_last_error);
+    AttnArgs a{};
+    a.q = scratch_qkv; a.k = scratch_qkv + H; a.v = scratch_qkv + 2 * H; a.out = out;
+    a.ldq = a.ldk = a.ldv = 3 * H;
+    a.ldo = H;
+    a.bstride_q = a.bstride_k = a.bstride_v = S * 3 * H;
+    a.bstride_o = S * H;
+    a.mask = key_mask;
+    a.ms[0] = S; a.ms[1] = 0; a.ms[2] = 0; a.ms[3] = 1;
+    a.B = B; a.S = S; a.nH = H / head_dim; a.hd = head_dim;
+    a.scale = 1.0f / std::sqrt((float)head_dim);
+    a.fill = fill;
+    launch_attention(a, st);
+  });
+}
+
 int inferc_dev_gemv(const float* x, const float* w, const float* b, const float* resid, float* y,
                     int64_t K, int64_t N, int act, void* stream) {
   return guard([&] {

@@ -491,16 +491,24 @@ void launch_gemm_tc(const float* A, int64_t lda, const float* Bb, const float* B
   if (ep.bias_mode == 1 && ep.act == ACT_NONE && ep.resid == nullptr) epi = EPI_BIAS;
   if (ep.bias_mode == 1 && ep.act == ACT_GELU_ERF && ep.resid == nullptr) epi = EPI_BIAS_GELU;
   if (ep.bias_mode == 1 && ep.act == ACT_NONE && ep.resid != nullptr) epi = EPI_BIAS_RESID;
+  // BN = 256 when there are enough output tiles to fill the SMs, else BN =
+  // 128 (twice the CTAs; three stages fit in shared memory).
+  const int64_t tiles256 = ((N + 255) / 256) * ((M + BM - 1) / BM);
+  const bool wide = tiles256 >= sm_count_tc() / 2;
+#define IDEV_TC(EPIK)                                                                 \
+  do {                                                                                \
+    if (wide)                                                                         \
+      launch_tc<256, 32, 2, EPIK>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);     \
+    else                                                                              \
+      launch_tc<128, 32, 3, EPIK>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);     \
+  } while (0)
   switch (epi) {
-    case EPI_BIAS: launch_tc<256, 32, 2, EPI_BIAS>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st); break;
-    case EPI_BIAS_GELU:
-      launch_tc<256, 32, 2, EPI_BIAS_GELU>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);
-      break;
-    case EPI_BIAS_RESID:
-      launch_tc<256, 32, 2, EPI_BIAS_RESID>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);
-      break;
-    default: launch_tc<256, 32, 2, EPI_GENERIC>(A, lda, Bb, Bs, ldb, C, ldc, M, N, K, ep, st);
+    case EPI_BIAS: IDEV_TC(EPI_BIAS); break;
+    case EPI_BIAS_GELU: IDEV_TC(EPI_BIAS_GELU); break;
+    case EPI_BIAS_RESID: IDEV_TC(EPI_BIAS_RESID); break;
+    default: IDEV_TC(EPI_GENERIC); break;
   }
+#undef IDEV_TC
 }
 
 void launch_split_tf32(const float* x, float* big, float* small, int64_t n, cudaStream_t st) {

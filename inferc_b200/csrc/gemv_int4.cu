@@ -20,8 +20,12 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kRowsPerWarp = 8;
-constexpr int kRowsPerCta = kWarps * kRowsPerWarp;
+// Rows per warp: 8 for K <= 1024; 4 for longer rows, so that the few long
+// matrices still spread over every SM.
+template <int CPL>
+constexpr int rows_per_warp() { return CPL == 1 ? 8 : 4; }
+template <int CPL>
+constexpr int rows_per_cta() { return kWarps * rows_per_warp<CPL>(); }
 constexpr int kMaxDescs = 32;
 
 struct Int4Batch {
@@ -58,6 +62,11 @@ __device__ __forceinline__ float chunk_dot(const uint4 v, const float (&x)[32], 
 // 16-byte aligned W rows.
 template <int CPL>
 __global__ void __launch_bounds__(kThreads) gemv_int4_kernel(const __grid_constant__ Int4Batch bt) {
+  constexpr int kRowsPerWarp = rows_per_warp<CPL>();
+  constexpr int kRowsPerCta = rows_per_cta<CPL>();
+  // Lets the next group of this batch start while this one runs (the groups
+  // are independent; see launch_gemv_int4).
+  pdl_launch_dependents();
   int mi = 0;
   while (mi + 1 < bt.count && (int)blockIdx.x >= bt.cta_start[mi + 1]) ++mi;
   const InfercInt4Gemv& d = bt.d[mi];
@@ -121,7 +130,9 @@ bool fast_ok(const InfercInt4Gemv& d) {
 }
 
 template <int CPL>
-void launch_group(const InfercInt4Gemv* ds, const int* idx, int n, cudaStream_t st) {
+void launch_group(const InfercInt4Gemv* ds, const int* idx, int n, cudaStream_t st,
+                  bool& first) {
+  constexpr int kRowsPerCta = rows_per_cta<CPL>();
   for (int base = 0; base < n; base += kMaxDescs) {
     Int4Batch bt{};
     bt.count = std::min(kMaxDescs, n - base);
@@ -132,8 +143,16 @@ void launch_group(const InfercInt4Gemv* ds, const int* idx, int n, cudaStream_t 
       ctas += (int)((bt.d[i].n + kRowsPerCta - 1) / kRowsPerCta);
     }
     bt.cta_start[bt.count] = ctas;
-    if (ctas > 0) gemv_int4_kernel<CPL><<<ctas, kThreads, 0, st>>>(bt);
-    IDEV_LAUNCHED();
+    if (ctas == 0) continue;
+    if (first) {  // ordered after all earlier work on the stream
+      gemv_int4_kernel<CPL><<<ctas, kThreads, 0, st>>>(bt);
+      IDEV_LAUNCHED();
+      first = false;
+    } else {
+      // Same batch, independent matrices: may overlap the previous group.
+      // Its inputs were complete before the first group started.
+      launch_pdl(gemv_int4_kernel<CPL>, dim3(ctas), dim3(kThreads), 0, st, bt);
+    }
   }
 }
 
@@ -143,13 +162,14 @@ void launch_gemv_int4(const InfercInt4Gemv* ds, int count, cudaStream_t st) {
   IDEV_CHECK_ARG(count >= 0 && (count == 0 || ds != nullptr), "int4 GEMV: bad descriptor list");
   int groups[4][256];
   int ng[4] = {0, 0, 0, 0};
+  bool first = true;
   auto flush = [&](int g) {
     if (ng[g] == 0) return;
     switch (g) {
-      case 0: launch_group<1>(ds, groups[0], ng[0], st); break;
-      case 1: launch_group<2>(ds, groups[1], ng[1], st); break;
-      case 2: launch_group<3>(ds, groups[2], ng[2], st); break;
-      default: launch_group<4>(ds, groups[3], ng[3], st); break;
+      case 0: launch_group<1>(ds, groups[0], ng[0], st, first); break;
+      case 1: launch_group<2>(ds, groups[1], ng[1], st, first); break;
+      case 2: launch_group<3>(ds, groups[2], ng[2], st, first); break;
+      default: launch_group<4>(ds, groups[3], ng[3], st, first); break;
     }
     ng[g] = 0;
   };

@@ -74,7 +74,10 @@ def test_fused_matmul_add_gelu(port, M, K, N):
     b = rng.standard_normal(N, dtype=np.float32) * 0.1
     y = host(ops.FusedMatMulAddGELU(T(x), T(w), T(b)))
     if M:
-        np.testing.assert_allclose(y, port.fused_matmul_add_gelu(x, w, b), atol=2e-5, rtol=1e-5)
+        ref = port.fused_matmul_add_gelu(x, w, b)
+        # M >= 64 runs the tensor-core 3xTF32 kernel, whose fp32 accumulation
+        # error grows with K (3e-5 of max |y| at K = 3072).
+        np.testing.assert_allclose(y, ref, atol=2e-5 + 3e-5 * np.abs(ref).max(), rtol=1e-5)
 
 
 def test_fused_matmul_add_gelu_golden_and_errors(gold):
@@ -262,3 +265,30 @@ def test_int4_batched_gpt2_set(port):
     for m, d in zip(mats, dev):
         ref = port.int4_gemv_rowscale(m.w, m.scales, m.x)
         np.testing.assert_allclose(host(d[3]), ref, atol=1e-4, rtol=1e-5)
+
+
+@pytest.mark.parametrize("B,S", [(2, 128), (1, 512), (3, 40)])
+def test_qkv_attention_prepared(port, B, S):
+    """inferc_dev_qkv_attention (config 2 path) == FusedQKV + FusedAttention."""
+    import ctypes  # noqa: F401
+    from inferc_b200 import lib
+    L = lib.load()
+    x, ws, lens = synth.attention_sweep_inputs(B, S, seed=B + S)
+    H = 768
+    wcat = np.ascontiguousarray(np.concatenate([ws[0], ws[2], ws[4]], axis=1))
+    bcat = np.concatenate([ws[1], ws[3], ws[5]]).astype(np.float32)
+    wd = T(wcat)
+    wb, wsm = torch.empty_like(wd), torch.empty_like(wd)
+    lib.check(L.inferc_dev_tf32_split(wd.data_ptr(), wb.data_ptr(), wsm.data_ptr(), wd.numel(),
+                                      None))
+    km = (np.arange(S)[None, :] >= lens[:, None]).astype(np.uint8)
+    scratch = torch.empty(B * S * 3 * H, device=DEV)
+    out = torch.empty(B, S, H, device=DEV)
+    xd, bd, md = T(x), T(bcat), T(km)
+    lib.check(L.inferc_dev_qkv_attention(xd.data_ptr(), wb.data_ptr(), wsm.data_ptr(),
+                                         bd.data_ptr(), md.data_ptr(), B, S, H, 64, -3.0e38,
+                                         scratch.data_ptr(), out.data_ptr(), None))
+    q, k, v = port.fused_qkv(x.reshape(B * S, H), ws[0], ws[1], ws[2], ws[3], ws[4], ws[5])
+    ref = port.fused_attention(q.reshape(B, S, H), k.reshape(B, S, H), v.reshape(B, S, H),
+                               km.reshape(B, 1, 1, S), 64, -3.0e38)
+    np.testing.assert_allclose(host(out), ref, atol=5e-5)
