@@ -129,8 +129,7 @@ int inferc_dev_tf32_split(const float* w, float* big, float* small, int64_t n,
  * Y[M,N] = act(A[M,K] (B_big + B_small)[K,N] + bias[N] + resid[M,N]) with A
  * and Y row strides lda / ldy and resid row stride ldr; bias / resid may be
  * NULL; act as for inferc_dev_gemv. Runs the tcgen05 3xTF32 kernel when
- * M >= 64 and operands are 16-byte aligned, else the CUDA-core kernel on
- * B_big + B_small. */
+ * operands are 16-byte aligned, else the CUDA-core kernel on B_big + B_small. */
 int inferc_dev_gemm_tf32x3(const float* a, int64_t lda, const float* b_big,
                            const float* b_small, int64_t ldb, const float* bias,
                            const float* resid, int64_t ldr, float* y,

@@ -18,7 +18,7 @@ void launch_split_tf32(const float* x, float* big, float* small, int64_t n, cuda
 
 namespace {
 
-constexpr int64_t kTcMinRows = 64;
+constexpr int64_t kTcMinRows = 1;
 
 // Per-device buffer for the tf32 split of a raw B operand (op-level calls;
 // prepared plans split their weights once at creation).
