@@ -1,0 +1,781 @@
+// Persistent decode kernel: every single-token step of GPT-2 greedy decode
+// (the with-past graph of `inferc decode`, src/cli/main.cpp:854-889) for any
+// number of steps in ONE cooperative launch.
+//
+// One CTA per SM. A step is a sequence of phases separated by grid barriers:
+//   per layer:  QKV   y = LN1(x) W_attn + b            (144 column panels)
+//               ATTN  per head: KV append at pos, softmax(q.K/8) V   (12 CTAs)
+//               PROJ  x += ctx W_proj + b              (192 panels)
+//               FC    f = tanhGELU(LN2(x) W_fc + b)    (192 panels)
+//               FP    x += f W_fcproj + b              (192 panels)
+//   then        LM    logits = LNf(x) wte^T, per-CTA best (first max wins)
+// and the next step's embedding is computed by every CTA from the argmax of
+// the 148 per-CTA bests, so no extra phase is needed.
+//
+// Weights are pre-tiled at plan creation into column panels [K][P]
+// (contiguous), so a CTA fetches a panel with one bulk copy into shared
+// memory. Four 48 KiB slots form two pairs; while a phase computes from one
+// pair, the next weight phase is already streaming into the other, so HBM
+// keeps streaming across barriers. Each output column is produced by exactly
+// one CTA with a fixed summation order (deterministic).
+//
+// Data produced inside the kernel (x, qkv, ctx, f, the per-CTA bests) is read
+// with L2-coherent loads (__ldcg), never through L1. Grid barriers and
+// mbarrier waits are bounded: on a timeout the kernel sets an error flag,
+// every CTA leaves at its next barrier, and the host reports the failure.
+#include <cuda.h>
+
+#include <cfloat>
+#include <vector>
+
+#include "decode_mega.cuh"
+#include "kernels.cuh"
+
+namespace inferc_dev {
+
+namespace {
+
+constexpr int kMegaThreads = 256;
+constexpr int kSlotBytes = 48 * 1024;
+constexpr int kSlots = 4;
+constexpr uint32_t kMegaSpin = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mb_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mb_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mb_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_addr(bar);
+  for (uint32_t i = 0; i < kMegaSpin; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes and
+// addresses multiples of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+
+struct Smem {
+  uint64_t bar[kSlots];
+  uint32_t uses[kSlots];    // completed waits per slot (parity tracking)
+  uint32_t issued[kSlots];  // issued fills per slot (thread 0 only)
+  float xs[3072];         // staged GEMV input (normalised when LN applies)
+  float red[2 * kMegaThreads];
+  float stat[2];
+  float bv[kMegaThreads / 32];
+  int64_t bi[kMegaThreads / 32];
+  int abort_flag;
+  unsigned nbar;  // barriers passed (thread 0)
+};
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Grid-wide barrier (all CTAs co-resident: cooperative launch). Returns
+// false when the kernel must stop (timeout here or elsewhere).
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid-wide barrier over a monotonic arrival counter (zeroed by the host
+// before each launch): barrier number b completes when the counter reaches
+// (b + 1) * gridDim.x. Arrival is a fire-and-forget release add, so CTAs do
+// not serialise on returning atomics. Returns false when the kernel must
+// stop (timeout here or an error flagged elsewhere).
+__device__ bool grid_sync(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
+  if (a.prof && step == 1 && blockIdx.x == 0 && threadIdx.x == 0 && tag >= 0)
+    a.prof[2 * tag] = gtimer();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned target = (++sm.nbar) * gridDim.x;
+    red_release_add(a.bar_count, 1u);
+    uint32_t i = 0;
+    while ((int)(ld_acquire(a.bar_count) - target) < 0) {
+      if (++i > kMegaSpin || (i % 1024 == 0 && *(volatile int*)a.err)) {
+        atomicExch(a.err, 1);
+        break;
+      }
+    }
+    sm.abort_flag = *(volatile int*)a.err;
+    if (a.prof && step == 1 && blockIdx.x == 0 && tag >= 0) a.prof[2 * tag + 1] = gtimer();
+  }
+  __syncthreads();
+  return sm.abort_flag == 0;
+}
+
+// Issue this CTA's panels of a GEMV phase into slot pair `pair`.
+__device__ void prefetch_panels(const MegaPanels& m, int pair, uint8_t* slots, Smem& sm) {
+  if (threadIdx.x != 0) return;
+  for (int j = 0; j < 2; ++j) {
+    const int p = blockIdx.x + j * gridDim.x;
+    if (p >= m.npanels) break;
+    const int s = 2 * pair + j;
+    const uint32_t bytes = (uint32_t)m.K * m.P * 4;
+    sm.issued[s]++;
+    mb_expect_tx(&sm.bar[s], bytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(m.data + (size_t)p * m.K * m.P);
+    for (uint32_t off = 0; off < bytes; off += 16384)
+      bulk_load(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
+                &sm.bar[s]);
+  }
+}
+
+// Waits for slot s; all threads; false on timeout.
+__device__ bool wait_slot(int s, Smem& sm, const MegaArgs& a) {
+  const bool ok = __syncthreads_and(mb_wait(&sm.bar[s], sm.uses[s] & 1)) != 0;
+  if (threadIdx.x == 0) {
+    sm.uses[s]++;
+    if (!ok) atomicExch(a.err, 1);
+  }
+  __syncthreads();
+  return ok;
+}
+
+// Before leaving early: wait (bounded) for this CTA's bulk copies still in
+// flight, so none lands in shared memory after the CTA has exited.
+__device__ void drain(Smem& sm) {
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int s = 0; s < kSlots; ++s)
+      while (sm.issued[s] > sm.uses[s]) {
+        mb_wait(&sm.bar[s], sm.uses[s] & 1);
+        sm.uses[s]++;
+      }
+  __syncthreads();
+}
+
+// Stages x (global, written in this kernel) into sm.xs, normalised with
+// (g, b) when g != null (two-pass mean / biased variance, as rt::LayerNorm).
+__device__ void stage_input(const float* x, int K, const float* g, const float* b, float eps,
+                            Smem& sm) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  // K <= 3072: at most 12 elements per thread; x, gamma and beta loads are
+  // all issued before any is used.
+  float v[12], gv[12], bv[12];
+#pragma unroll
+  for (int i = 0; i < 12; ++i) {
+    const int k = tid + i * kMegaThreads;
+    v[i] = k < K ? __ldcg(x + k) : 0.f;
+    if (g != nullptr) {
+      gv[i] = k < K ? __ldg(g + k) : 0.f;
+      bv[i] = k < K ? __ldg(b + k) : 0.f;
+    }
+  }
+  if (g == nullptr) {
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+      const int k = tid + i * kMegaThreads;
+      if (k < K) sm.xs[k] = v[i];
+    }
+    __syncthreads();
+    return;
+  }
+  constexpr int nw = kMegaThreads / 32;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 12; ++i) s += v[i];
+  s = warp_sum(s);
+  if (lane == 0) sm.red[wid] = s;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < nw; ++w) tot += sm.red[w];
+  const float mean = tot / (float)K;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 12; ++i) {
+    const int k = tid + i * kMegaThreads;
+    const float d = k < K ? v[i] - mean : 0.f;
+    q += d * d;
+  }
+  q = warp_sum(q);
+  if (lane == 0) sm.red[nw + wid] = q;
+  __syncthreads();
+  float tq = 0.f;
+#pragma unroll
+  for (int w = 0; w < nw; ++w) tq += sm.red[nw + w];
+  const float inv = 1.0f / sqrtf(tq / (float)K + eps);
+#pragma unroll
+  for (int i = 0; i < 12; ++i) {
+    const int k = tid + i * kMegaThreads;
+    if (k < K) sm.xs[k] = ((v[i] - mean) * inv) * gv[i] + bv[i];
+  }
+  __syncthreads();
+}
+
+// LayerNorm of sm.xs[0:K) in place (the values are already staged).
+__device__ void stage_smem_ln(int K, const float* g, const float* b, float eps, Smem& sm) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  constexpr int nw = kMegaThreads / 32;
+  float s = 0.f;
+  for (int k = tid; k < K; k += kMegaThreads) s += sm.xs[k];
+  s = warp_sum(s);
+  if (lane == 0) sm.red[wid] = s;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < nw; ++w) tot += sm.red[w];
+  const float mean = tot / (float)K;
+  float q = 0.f;
+  for (int k = tid; k < K; k += kMegaThreads) {
+    const float d = sm.xs[k] - mean;
+    q += d * d;
+  }
+  q = warp_sum(q);
+  if (lane == 0) sm.red[nw + wid] = q;
+  __syncthreads();
+  float tq = 0.f;
+#pragma unroll
+  for (int w = 0; w < nw; ++w) tq += sm.red[nw + w];
+  const float inv = 1.0f / sqrtf(tq / (float)K + eps);
+  __syncthreads();
+  for (int k = tid; k < K; k += kMegaThreads) sm.xs[k] = ((sm.xs[k] - mean) * inv) * g[k] + b[k];
+  __syncthreads();
+}
+
+// Epilogue inputs of this thread's output columns (threads tid < P own
+// column p*P + tid of each of the CTA's two panels), loaded before the input
+// staging so their latency overlaps it.
+struct EpiIn {
+  float add[2];
+};
+
+__device__ __forceinline__ EpiIn gemv_preload(const MegaPanels& m, const float* bias,
+                                              const float* resid) {
+  EpiIn e{{0.f, 0.f}};
+  const int tid = threadIdx.x;
+  if (tid < m.P) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int p = blockIdx.x + j * gridDim.x;
+      const int col = p * m.P + tid;
+      if (p < m.npanels && col < m.N) {
+        float v = __ldg(bias + col);
+        if (resid) v += __ldcg(resid + col);
+        e.add[j] = v;
+      }
+    }
+  }
+  return e;
+}
+
+// y[col] = act(xs . panel[:, c] + bias[col] (+ resid[col])) for this CTA's
+// panels (slots 2*pair, 2*pair+1), both panels in one pass. resid may alias
+// y (each column is read and written by one thread).
+__device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, const EpiIn& e,
+                           float* y, int act, Smem& sm, const MegaArgs& a, int ptag = -1) {
+  const int tid = threadIdx.x;
+  auto mark = [&](int i) {
+    if (a.prof && ptag >= 0 && blockIdx.x == 0 && tid == 0) a.prof[512 + 8 * ptag + i] = gtimer();
+  };
+  mark(0);
+  const int P = m.P, K = m.K;
+  const int P4 = P / 4;                  // float4 columns per row
+  const int slices = kMegaThreads / P4;  // rows processed in parallel
+  const int c4 = tid % P4, sl = tid / P4;
+  const int np = (int)(blockIdx.x < (unsigned)m.npanels) + (int)(blockIdx.x + gridDim.x < (unsigned)m.npanels);
+  for (int j = 0; j < np; ++j)
+    if (!wait_slot(2 * pair + j, sm, a)) return false;
+  mark(1);
+  const float* w0 = reinterpret_cast<const float*>(slots + (size_t)(2 * pair) * kSlotBytes);
+  const float* w1 = reinterpret_cast<const float*>(slots + (size_t)(2 * pair + 1) * kSlotBytes);
+  float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+  const float4* w04 = reinterpret_cast<const float4*>(w0);
+  const float4* w14 = reinterpret_cast<const float4*>(w1);
+  if (np == 2) {
+#pragma unroll 4
+    for (int k = sl; k < K; k += slices) {
+      const float xv = sm.xs[k];
+      const float4 u = w04[k * P4 + c4], t = w14[k * P4 + c4];
+      a0.x = fmaf(xv, u.x, a0.x); a0.y = fmaf(xv, u.y, a0.y);
+      a0.z = fmaf(xv, u.z, a0.z); a0.w = fmaf(xv, u.w, a0.w);
+      a1.x = fmaf(xv, t.x, a1.x); a1.y = fmaf(xv, t.y, a1.y);
+      a1.z = fmaf(xv, t.z, a1.z); a1.w = fmaf(xv, t.w, a1.w);
+    }
+  } else if (np == 1) {
+#pragma unroll 4
+    for (int k = sl; k < K; k += slices) {
+      const float xv = sm.xs[k];
+      const float4 u = w04[k * P4 + c4];
+      a0.x = fmaf(xv, u.x, a0.x); a0.y = fmaf(xv, u.y, a0.y);
+      a0.z = fmaf(xv, u.z, a0.z); a0.w = fmaf(xv, u.w, a0.w);
+    }
+  }
+  // lanes with the same float4 column (lane % P4) hold successive row
+  // slices: fold them with shuffles, then add the 8 warps' results in order.
+  float r[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  for (int o = P4; o < 32; o <<= 1)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] += __shfl_xor_sync(0xffffffffu, r[i], o);
+  constexpr int nw = kMegaThreads / 32;
+  if ((tid & 31) < P4) {
+    const int wq = tid >> 5, cc = (tid & 31) * 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sm.red[wq * P + cc + i] = r[i];
+      sm.red[(nw + wq) * P + cc + i] = r[4 + i];
+    }
+  }
+  __syncthreads();
+  if (tid < P) {
+    for (int j = 0; j < np; ++j) {
+      float t = 0.f;
+      for (int q = 0; q < nw; ++q) t += sm.red[(j * nw + q) * P + tid];
+      const int col = (blockIdx.x + j * gridDim.x) * P + tid;
+      if (col < m.N) y[col] = apply_act(t + e.add[j], act);
+    }
+  }
+  __syncthreads();
+  mark(2);
+  return true;
+}
+
+// Attention for head h = blockIdx.x (< heads): append k, v of the current
+// token at position pos, then out = softmax(q.k_j / sqrt(hd)) v over j <= pos.
+// Loads are issued in independent batches (the cache is read from L2).
+__device__ void attention_head(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
+                               Smem& sm, int h, bool append, float* ctx_out) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, hd = a.hd, H = a.H;
+  float* qs = scr;             // [hd]
+  float* kn = scr + 128;       // [hd] new key
+  float* vn = scr + 256;       // [hd] new value
+  float* sc = scr + 384;       // [max_len] scores
+  float* part = sc + a.max_len + 4;  // [8 warps][hd], hd <= 128 (reserved 8 x 128)
+  float* kh = L.kc + (size_t)h * a.max_len * hd;
+  float* vh = L.vc + (size_t)h * a.max_len * hd;
+  if (tid < hd) {
+    qs[tid] = __ldcg(a.qkv + h * hd + tid);
+    kn[tid] = __ldcg(a.qkv + H + h * hd + tid);
+    vn[tid] = __ldcg(a.qkv + 2 * H + h * hd + tid);
+    if (append) {
+      kh[pos * hd + tid] = kn[tid];
+      vh[pos * hd + tid] = vn[tid];
+    }
+  }
+  __syncthreads();
+  const int64_t Lk = pos + 1;
+  const float sq = sqrtf((float)hd);
+  const int hd4 = hd / 4;
+  // scores: one thread per key, the key row's hd/4 128-bit loads in flight
+  for (int64_t j = tid; j < Lk; j += kMegaThreads) {
+    float4 kv[32];
+    if (j == pos) {  // the new key, from shared memory
+      const float4* kr = reinterpret_cast<const float4*>(kn);
+#pragma unroll
+      for (int d = 0; d < 32; ++d)
+        if (d < hd4) kv[d] = kr[d];
+    } else {
+      const float4* kr = reinterpret_cast<const float4*>(kh + j * hd);
+#pragma unroll
+      for (int d = 0; d < 32; ++d)
+        if (d < hd4) kv[d] = __ldcg(kr + d);
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int d = 0; d < 32; ++d)
+      if (d < hd4) {
+        dot = fmaf(qs[4 * d], kv[d].x, dot);
+        dot = fmaf(qs[4 * d + 1], kv[d].y, dot);
+        dot = fmaf(qs[4 * d + 2], kv[d].z, dot);
+        dot = fmaf(qs[4 * d + 3], kv[d].w, dot);
+      }
+    sc[j] = dot / sq;
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int64_t j = tid; j < Lk; j += kMegaThreads) mx = fmaxf(mx, sc[j]);
+  mx = warp_max(mx);
+  if (lane == 0) sm.red[wid] = mx;
+  __syncthreads();
+  mx = sm.red[0];
+  for (int w = 1; w < kMegaThreads / 32; ++w) mx = fmaxf(mx, sm.red[w]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int64_t j = tid; j < Lk; j += kMegaThreads) {
+    const float e = expf(sc[j] - mx);
+    sc[j] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) sm.red[wid] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int w = 0; w < kMegaThreads / 32; ++w) sum += sm.red[w];
+  const float inv = 1.0f / sum;
+  // out: warp w takes keys w, w+8, ...; lane covers dims lane, lane+32, ...
+  // (hd <= 128 -> up to 4 dims per lane); 4 keys per batch of loads.
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int nw = kMegaThreads / 32;
+  for (int64_t j0 = wid; j0 < Lk; j0 += 4 * nw) {
+    float vv[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t j = j0 + u * nw;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = lane + 32 * e;
+        float t = 0.f;
+        if (j < Lk && d < hd) {
+          if (j == pos) t = vn[d];
+          else t = __ldcg(vh + j * hd + d);
+        }
+        vv[u][e] = t;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t j = j0 + u * nw;
+      const float pj = j < Lk ? sc[j] * inv : 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, vv[u][e], acc[e]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int d = lane + 32 * e;
+    if (d < hd) part[wid * hd + d] = acc[e];
+  }
+  __syncthreads();
+  if (tid < hd) {
+    float r = 0.f;
+    for (int w = 0; w < nw; ++w) r += part[w * hd + tid];
+    ctx_out[tid] = r;
+  }
+  __syncthreads();
+}
+
+// FC-phase input: xm = xa + b_proj + sum_h part[h] (heads in order); CTA 0
+// publishes xm (the FP residual); then LN2 in place.
+__device__ void stage_attn_residual(const MegaArgs& a, const MegaLayer& L, const float* xa,
+                                    float* xm, Smem& sm) {
+  const int tid = threadIdx.x, H = a.H;
+  for (int k = tid; k < H; k += kMegaThreads) {
+    float p[16];
+#pragma unroll
+    for (int h = 0; h < 16; ++h) p[h] = h < a.heads ? __ldcg(a.part + (size_t)h * H + k) : 0.f;
+    float v = __ldcg(xa + k);
+    const float bp = __ldg(L.proj_b + k);
+    float t = 0.f;
+#pragma unroll
+    for (int h = 0; h < 16; ++h) t += p[h];
+    v = v + (t + bp);
+    sm.xs[k] = v;
+    if (blockIdx.x == 0) xm[k] = v;
+  }
+  __syncthreads();
+  stage_smem_ln(H, L.ln2_g, L.ln2_b, a.eps, sm);
+}
+
+// Attention + output projection for one (head, column chunk): CTA c < heads
+// * chunks computes head h = c / chunks (redundantly with the other chunks
+// of that head; chunk 0 also appends the new K/V to the cache), then
+// part[h][cols] = ctx_h . W_proj[h*hd:(h+1)*hd, cols] from its prefetched
+// [hd][Wc] panel in slot `slot`. The partials are summed (fixed order) by
+// the next phase.
+__device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
+                                const uint8_t* slots, int slot, Smem& sm) {
+  const int chunks = a.proj_chunks;
+  const int c = blockIdx.x;
+  if (c >= a.heads * chunks) return true;
+  const int h = c / chunks, cc = c % chunks;
+  float* ctx = scr + 384 + a.max_len + 4 + (kMegaThreads / 32) * 128;  // [hd]
+  attention_head(a, L, pos, scr, sm, h, cc == 0, ctx);
+  if (!wait_slot(slot, sm, a)) return false;
+  const MegaPanels& m = L.proj;  // K = hd, P = chunk width
+  const float* w = reinterpret_cast<const float*>(slots + (size_t)slot * kSlotBytes);
+  const int tid = threadIdx.x;
+  const int Wc = m.P, hd = a.hd;
+  // threads: (column, row-slice); Wc <= 256
+  const int slices = kMegaThreads / Wc;
+  const int col = tid % Wc, sl = tid / Wc;
+  float acc = 0.f;
+  if (sl < slices)
+    for (int k = sl; k < hd; k += slices) acc = fmaf(ctx[k], w[k * Wc + col], acc);
+  sm.red[tid] = acc;
+  __syncthreads();
+  if (tid < Wc) {
+    float t = 0.f;
+    for (int q = 0; q < slices; ++q) t += sm.red[q * Wc + tid];
+    const int gcol = cc * Wc + tid;
+    if (gcol < a.H) a.part[(size_t)h * a.H + gcol] = t;
+  }
+  __syncthreads();
+  return true;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __grid_constant__ MegaArgs a) {
+  extern __shared__ __align__(128) uint8_t mega_smem[];
+  uint8_t* slots = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mega_smem) + 127) &
+                                              ~uintptr_t(127));
+  __shared__ Smem sm;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (tid == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mb_init(&sm.bar[s], 1);
+      sm.uses[s] = 0;
+      sm.issued[s] = 0;
+    }
+    sm.abort_flag = 0;
+    sm.nbar = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int H = a.H;
+  float* scr = reinterpret_cast<float*>(slots + (size_t)kSlots * kSlotBytes);
+  // Residual stream: xa = layer input / FP output, xm = after the attention
+  // block (written by CTA 0 in the FC phase).
+  float* xa = a.x;
+  float* xm = a.x + H;
+
+  int64_t tok = *a.tok;
+  prefetch_panels(a.layer[0].attn, 0, slots, sm);
+  for (int step = 0; step < a.nsteps; ++step) {
+    const int64_t pos = a.pos0 + step;
+    if (tok < 0 || tok >= a.V || pos < 0 || pos >= a.max_pos || pos >= a.max_len) {
+      if (tid == 0) atomicExch(a.err, 2);
+      drain(sm);
+      return;
+    }
+    for (int l = 0; l < a.layers; ++l) {
+      const MegaLayer L = a.layer[l];
+      // ---- QKV (pair 0); the attention block's W_proj panel streams into slot 2.
+      if (tid == 0 && blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) {
+        const uint32_t bytes = (uint32_t)L.proj.K * L.proj.P * 4;
+        sm.issued[2]++;
+        mb_expect_tx(&sm.bar[2], bytes);
+        bulk_load(slots + 2 * (size_t)kSlotBytes,
+                  L.proj.data + (size_t)blockIdx.x * L.proj.K * L.proj.P, bytes, &sm.bar[2]);
+      }
+      const EpiIn e_qkv = gemv_preload(L.attn, L.attn_b, nullptr);
+      if (l == 0) {
+        // Embedding of the current token, built by every CTA; CTA 0 also
+        // publishes it as the residual stream.
+        for (int k = tid; k < H; k += kMegaThreads) {
+          const float v = __ldg(a.wte + tok * H + k) + __ldg(a.wpe + pos * H + k);
+          sm.xs[k] = v;
+          if (blockIdx.x == 0) xa[k] = v;
+        }
+        __syncthreads();
+        stage_smem_ln(H, L.ln1_g, L.ln1_b, a.eps, sm);
+      } else {
+        stage_input(xa, H, L.ln1_g, L.ln1_b, a.eps, sm);
+      }
+      if (!gemv_phase(L.attn, 0, slots, e_qkv, a.qkv, ACT_NONE, sm, a)) { drain(sm); return; }
+      if (!grid_sync(a, sm, 4 * l + 0, step)) { drain(sm); return; }
+      // ---- attention + output projection partials; FC streams into pair 0.
+      prefetch_panels(L.fc, 0, slots, sm);
+      if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm)) { drain(sm); return; }
+      if (!grid_sync(a, sm, 4 * l + 1, step)) { drain(sm); return; }
+      // ---- FC (pair 0): xm = xa + b_proj + sum_h part[h]; f = gelu(LN2(xm) W + b).
+      //      FP streams into pair 1.
+      prefetch_panels(L.fp, 1, slots, sm);
+      const EpiIn e_fc = gemv_preload(L.fc, L.fc_b, nullptr);
+      stage_attn_residual(a, L, xa, xm, sm);
+      if (!gemv_phase(L.fc, 0, slots, e_fc, a.f, ACT_GELU_TANH, sm, a)) { drain(sm); return; }
+      if (!grid_sync(a, sm, 4 * l + 2, step)) { drain(sm); return; }
+      // ---- FP (pair 1): xa = xm + f W + b; the next layer's QKV streams into pair 0.
+      if (l + 1 < a.layers) prefetch_panels(a.layer[l + 1].attn, 0, slots, sm);
+      const EpiIn e_fp = gemv_preload(L.fp, L.fp_b, xm);
+      stage_input(a.f, a.F, nullptr, nullptr, 0.f, sm);
+      if (!gemv_phase(L.fp, 1, slots, e_fp, xa, ACT_NONE, sm, a)) { drain(sm); return; }
+      if (!grid_sync(a, sm, 4 * l + 3, step)) { drain(sm); return; }
+    }
+    // LM head: logits = LNf(x) . wte[r] for this CTA's row range, streamed
+    // through all four slots (16 rows = 48 KiB per chunk).
+    stage_input(xa, H, a.lnf_g, a.lnf_b, a.eps, sm);
+    {
+      const int rows_per = (a.V + gridDim.x - 1) / gridDim.x;
+      const int r0 = blockIdx.x * rows_per;
+      const int r1 = min(a.V, r0 + rows_per);
+      const int crow = kSlotBytes / (H * 4);  // rows per chunk
+      const int nchunks = r1 > r0 ? (r1 - r0 + crow - 1) / crow : 0;
+      auto issue = [&](int ch) {
+        if (tid != 0 || ch >= nchunks) return;
+        const int s = ch % kSlots;
+        const int ra = r0 + ch * crow, rb = min(r1, ra + crow);
+        const uint32_t bytes = (uint32_t)(rb - ra) * H * 4;
+        sm.issued[s]++;
+        mb_expect_tx(&sm.bar[s], bytes);
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wte + (size_t)ra * H);
+        for (uint32_t off = 0; off < bytes; off += 16384)
+          bulk_load(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
+                    &sm.bar[s]);
+      };
+      for (int ch = 0; ch < kSlots; ++ch) issue(ch);
+      float bv = -INFINITY;
+      int64_t bi = INT64_MAX;
+      for (int ch = 0; ch < nchunks; ++ch) {
+        const int s = ch % kSlots;
+        if (!wait_slot(s, sm, a)) { drain(sm); return; }
+        const float* w = reinterpret_cast<const float*>(slots + (size_t)s * kSlotBytes);
+        const int ra = r0 + ch * crow, rb = min(r1, ra + crow);
+        for (int r = ra + wid; r < rb; r += kMegaThreads / 32) {
+          const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(r - ra) * H);
+          const float4* x4 = reinterpret_cast<const float4*>(sm.xs);
+          float acc = 0.f;
+          for (int k = lane; k < H / 4; k += 32) {
+            const float4 wv = wr[k], xv = x4[k];
+            acc = fmaf(xv.x, wv.x, acc);
+            acc = fmaf(xv.y, wv.y, acc);
+            acc = fmaf(xv.z, wv.z, acc);
+            acc = fmaf(xv.w, wv.w, acc);
+          }
+          acc = warp_sum(acc);
+          if (lane == 0) a.logits[r] = acc;
+          if (acc > bv || (acc == bv && r < bi)) { bv = acc; bi = r; }
+        }
+        __syncthreads();  // slot s fully consumed
+        issue(ch + kSlots);
+      }
+      if (lane == 0) { sm.bv[wid] = bv; sm.bi[wid] = bi; }
+      __syncthreads();
+      if (tid == 0) {
+        float v = sm.bv[0];
+        int64_t i = sm.bi[0];
+        for (int w = 1; w < kMegaThreads / 32; ++w)
+          if (sm.bv[w] > v || (sm.bv[w] == v && sm.bi[w] < i)) { v = sm.bv[w]; i = sm.bi[w]; }
+        a.best_v[blockIdx.x] = v;
+        a.best_i[blockIdx.x] = i;
+      }
+    }
+    // Next step's first weights stream while the argmax is finalised.
+    if (step + 1 < a.nsteps) prefetch_panels(a.layer[0].attn, 0, slots, sm);
+    if (!grid_sync(a, sm, 4 * a.layers, step)) { drain(sm); return; }
+    // Every CTA reduces the per-CTA bests in the same order (first max wins).
+    if (wid == 0) {
+      float v = -INFINITY;
+      int64_t i = INT64_MAX;
+      for (int b = lane; b < (int)gridDim.x; b += 32) {
+        const float ov = __ldcg(a.best_v + b);
+        const int64_t oi = __ldcg(a.best_i + b);
+        if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int64_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+      }
+      if (lane == 0) sm.bi[0] = (i == INT64_MAX) ? 0 : i;
+    }
+    __syncthreads();
+    tok = sm.bi[0];
+    if (blockIdx.x == 0 && tid == 0) {
+      a.token_log[a.log_offset + step] = tok;
+      *a.tok = tok;
+    }
+  }
+}
+
+// ------------------------------------------------------------ host side
+size_t mega_smem_bytes(int max_len) {
+  // attention scratch: q, k_new, v_new (3 x 128), scores [max_len] (+4 pad),
+  // per-warp partial outputs [8][128], the head's context [128]
+  return (size_t)kSlots * kSlotBytes + 128 +
+         (size_t)(384 + max_len + 4 + (kMegaThreads / 32) * 128 + 128) * sizeof(float);
+}
+
+void launch_decode_mega(const MegaArgs& a, int grid, cudaStream_t st) {
+  const size_t smem = mega_smem_bytes(a.max_len);
+  IDEV_CUDA(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+  void* args[] = {const_cast<MegaArgs*>(&a)};
+  IDEV_CUDA(cudaLaunchCooperativeKernel((const void*)decode_mega_kernel, dim3(grid),
+                                        dim3(kMegaThreads), args, smem, st));
+}
+
+int mega_max_grid(int max_len) {
+  const size_t smem = mega_smem_bytes(max_len);
+  IDEV_CUDA(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+  int per_sm = 0, dev = 0, sms = 0;
+  IDEV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mega_kernel,
+                                                          kMegaThreads, smem));
+  IDEV_CUDA(cudaGetDevice(&dev));
+  IDEV_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  return std::min(per_sm, 1) * sms;
+}
+
+// Re-tiles W [K,N] (device, row-major) into panels [npanels][K][P] (zero
+// padded past N).
+__global__ void panelize_kernel(const float* __restrict__ w, float* __restrict__ out, int K, int N,
+                                int P, int npanels) {
+  const int64_t total = (int64_t)npanels * K * P;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(e % P);
+    const int k = (int)((e / P) % K);
+    const int p = (int)(e / ((int64_t)P * K));
+    const int col = p * P + c;
+    out[e] = col < N ? w[(int64_t)k * N + col] : 0.f;
+  }
+}
+
+// W_proj [H, H] -> panels [heads][chunks][hd][Wc]: rows of head h, columns
+// of chunk cc (zero padded past H).
+__global__ void panelize_proj_kernel(const float* __restrict__ w, float* __restrict__ out, int H,
+                                     int hd, int heads, int chunks, int Wc) {
+  const int64_t total = (int64_t)heads * chunks * hd * Wc;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(e % Wc);
+    const int k = (int)((e / Wc) % hd);
+    const int cc = (int)((e / ((int64_t)Wc * hd)) % chunks);
+    const int h = (int)(e / ((int64_t)Wc * hd * chunks));
+    const int col = cc * Wc + c;
+    out[e] = col < H ? w[(int64_t)(h * hd + k) * H + col] : 0.f;
+  }
+}
+
+void launch_panelize_proj(const float* w, float* out, int H, int hd, int heads, int chunks, int Wc,
+                          cudaStream_t st) {
+  panelize_proj_kernel<<<148 * 8, 256, 0, st>>>(w, out, H, hd, heads, chunks, Wc);
+  IDEV_LAUNCHED();
+}
+
+void launch_panelize(const float* w, float* out, int K, int N, int P, int npanels,
+                     cudaStream_t st) {
+  const int64_t total = (int64_t)npanels * K * P;
+  panelize_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16), 256, 0, st>>>(
+      w, out, K, N, P, npanels);
+  IDEV_LAUNCHED();
+}
+
+}  // namespace inferc_dev

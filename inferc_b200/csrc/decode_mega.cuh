@@ -1,0 +1,54 @@
+// Parameters of the persistent decode kernel (decode_mega.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace inferc_dev {
+
+// ------------------------------------------------------------ parameters
+struct MegaPanels {
+  const float* data;  // [npanels][K][P]
+  int K, N, P, npanels;
+};
+
+struct MegaLayer {
+  MegaPanels attn, proj, fc, fp;
+  const float *attn_b, *proj_b, *fc_b, *fp_b;
+  const float *ln1_g, *ln1_b, *ln2_g, *ln2_b;
+  float *kc, *vc;  // [heads][max_len][hd]
+};
+
+struct MegaArgs {
+  const MegaLayer* layer;  // [layers], device memory
+  int layers, H, heads, hd, F, V, max_len, max_pos;
+  float eps;
+  const float *wte, *wpe, *lnf_g, *lnf_b;
+  // state / scratch (device)
+  float *x, *qkv, *ctx, *f, *logits;  // x: [2][H] residual buffers
+  float* part;      // [heads][H] output-projection partials
+  int proj_chunks;  // column chunks per head in the attention block
+  float* best_v;
+  int64_t* best_i;
+  unsigned int* bar_count;
+  unsigned int* bar_gen;
+  int* err;
+  int64_t* tok;        // in: current token; out: last generated token
+  int64_t* token_log;  // token_log[log_offset + s] = token generated at step s
+  int64_t log_offset;
+  int64_t pos0;        // position of the current token at the first step
+  int nsteps;
+  unsigned long long* prof;  // optional: phase timestamps of CTA 0, step 1
+};
+
+
+// Dynamic shared memory the kernel needs for a cache of max_len positions.
+size_t mega_smem_bytes(int max_len);
+// CTAs that can be co-resident (0 when the kernel does not fit).
+int mega_max_grid(int max_len);
+void launch_decode_mega(const MegaArgs& a, int grid, cudaStream_t st);
+void launch_panelize(const float* w, float* out, int K, int N, int P, int npanels,
+                     cudaStream_t st);
+void launch_panelize_proj(const float* w, float* out, int H, int hd, int heads, int chunks, int Wc,
+                          cudaStream_t st);
+
+}  // namespace inferc_dev

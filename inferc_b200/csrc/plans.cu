@@ -20,12 +20,15 @@
 // advances them itself, so successive replays need no host work.
 #include <cfloat>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
 #include <utility>
 #include <vector>
 
+#include "decode_mega.cuh"
 #include "kernels.cuh"
 
 namespace inferc_dev {
@@ -312,6 +315,16 @@ struct InfercDecoderPlan {
   int64_t *len, *tok, *token_log;
   int* err;
   std::unique_ptr<Graph> step_graph;
+  // persistent-kernel state
+  bool use_mega = false;
+  int mega_grid = 0;
+  MegaLayer* mega_layers = nullptr;  // device array [L]
+  float* best_v = nullptr;
+  int64_t* best_i = nullptr;
+  unsigned int* bar = nullptr;  // [count, generation]
+  float* mega_x = nullptr;      // [2][H] residual buffers
+  float* mega_part = nullptr;   // [heads][H]
+  int mega_chunks = 0;
 
   ~InfercDecoderPlan() {
     step_graph.reset();
@@ -425,7 +438,47 @@ struct InfercDecoderPlan {
     IDEV_CUDA(cudaMemcpyAsync(ids, prompt, n * sizeof(int64_t), cudaMemcpyHostToDevice, st));
     n_host_scratch = n;
     prefill(n, st);
-    if (max_tokens > 1) {
+    if (max_tokens > 1 && use_mega) {
+      // All max_tokens-1 single-token steps in one persistent launch.
+      MegaArgs a{};
+      a.layer = mega_layers;
+      a.layers = (int)L; a.H = (int)H; a.heads = (int)nH; a.hd = (int)hd; a.F = (int)F;
+      a.V = (int)V; a.max_len = (int)max_len; a.max_pos = (int)P; a.eps = eps;
+      a.wte = wte; a.wpe = wpe; a.lnf_g = lnf_g; a.lnf_b = lnf_b;
+      a.x = mega_x; a.qkv = qkv; a.ctx = ctx; a.f = f; a.logits = logits;
+      a.part = mega_part; a.proj_chunks = mega_chunks;
+      a.best_v = best_v; a.best_i = best_i; a.bar_count = bar; a.bar_gen = bar + 1;
+      a.err = err; a.tok = tok; a.token_log = token_log; a.log_offset = 1;
+      a.pos0 = n; a.nsteps = (int)(max_tokens - 1);
+      static unsigned long long* prof = nullptr;
+      const bool want_prof = std::getenv("INFERC_DECODE_PROF") != nullptr;
+      if (want_prof && !prof) IDEV_CUDA(cudaMalloc(&prof, 2 * 1024 * sizeof(unsigned long long)));
+      a.prof = want_prof ? prof : nullptr;
+      IDEV_CUDA(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned int), st));
+      IDEV_CUDA(cudaEventRecord(ev0, st));
+      launch_decode_mega(a, mega_grid, st);
+      IDEV_CUDA(cudaEventRecord(ev1, st));
+      if (want_prof) {
+        std::vector<unsigned long long> h(2 * (4 * L + 2));
+        IDEV_CUDA(cudaMemcpyAsync(h.data(), prof, h.size() * 8, cudaMemcpyDeviceToHost, st));
+        IDEV_CUDA(cudaStreamSynchronize(st));
+        std::vector<unsigned long long> d(100);
+        IDEV_CUDA(cudaMemcpy(d.data(), prof + 512, 100 * 8, cudaMemcpyDeviceToHost));
+        fprintf(stderr, "QKV l1: stage %.2f | wait %.2f compute %.2f\n", (d[0] - d[88]) / 1e3,
+                (d[1] - d[0]) / 1e3, (d[2] - d[1]) / 1e3);
+        fprintf(stderr, "FC l1: wait %.2f compute %.2f\n", (d[9] - d[8]) / 1e3,
+                (d[10] - d[9]) / 1e3);
+        std::vector<unsigned long long> c(32);
+        IDEV_CUDA(cudaMemcpy(c.data(), prof + 1024, 32 * 8, cudaMemcpyDeviceToHost));
+        for (int q = 0; q < 2; ++q)
+          fprintf(stderr, "FC cta%d cycles: prefetch %llu stage %llu gemv %llu barrier %llu\n",
+                  q ? 100 : 0, c[16 * q + 1] - c[16 * q], c[16 * q + 2] - c[16 * q + 1],
+                  c[16 * q + 3] - c[16 * q + 2], c[16 * q + 4] - c[16 * q + 3]);
+        for (size_t t = 0; t + 1 < h.size() / 2; ++t)
+          fprintf(stderr, "phase %zu: work %.2f us, barrier %.2f us\n", t,
+                  (h[2 * (t + 1)] - h[2 * t + 1]) / 1e3, (h[2 * t + 1] - h[2 * t]) / 1e3);
+      }
+    } else if (max_tokens > 1) {
       if (!step_graph || log_base != n) {
         // The graph bakes log_base; (re)capture when the prompt length
         // changes. The first capture is preceded by nothing eager: every
@@ -455,6 +508,73 @@ struct InfercDecoderPlan {
     }
   }
 };
+
+// Prepares the persistent decode kernel when the model fits its layout:
+// column panels of 48 KiB at most, at most two panels per CTA, hidden and
+// FFN widths the shared staging buffer holds. Otherwise (or with
+// INFERC_DECODE_GRAPH=1) decode runs the per-kernel CUDA-graph step.
+static void setup_mega(InfercDecoderPlan* p) {
+  const char* force = std::getenv("INFERC_DECODE_GRAPH");
+  if (force && std::strcmp(force, "1") == 0) return;
+  const int H = (int)p->H, F = (int)p->F;
+  int dev = 0, optin = 0;
+  IDEV_CUDA(cudaGetDevice(&dev));
+  IDEV_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (mega_smem_bytes((int)p->max_len) + 16 * 1024 > (size_t)optin) return;
+  if (H > 3072 || F > 3072 || H % 16 || F % 16 || p->hd % 4 || 256 % p->hd || p->hd > 128 ||
+      (H * 4) > 48 * 1024 || p->L < 1 || p->nH > 16)
+    return;
+  const int grid = mega_max_grid((int)p->max_len);
+  if (grid < 1) return;
+  // attention block: heads x chunks CTAs, chunk width Wc (multiple of 4)
+  const int chunks = std::min<int>(grid / (int)p->nH, H / 4);
+  if (chunks < 1) return;
+  const int Wc = ((H + chunks - 1) / chunks + 3) / 4 * 4;
+  if (Wc > 256 || (size_t)p->hd * Wc * 4 > 48 * 1024) return;
+  auto panels = [&](const float* w, int K, int N) -> MegaPanels {
+    // narrowest P (4, 8 or 16; the most panels, so the most CTAs streaming)
+    // with a panel <= 48 KiB and at most two panels per CTA
+    for (int P : {4, 8, 16}) {
+      const int np = (N + P - 1) / P;
+      if ((size_t)K * P * 4 <= 48 * 1024 && np <= 2 * grid && P <= 256) {
+        float* d = p->mem.alloc<float>((size_t)np * K * P);
+        launch_panelize(w, d, K, N, P, np, nullptr);
+        return MegaPanels{d, K, N, P, np};
+      }
+    }
+    return MegaPanels{nullptr, K, N, 0, 0};
+  };
+  std::vector<MegaLayer> layers((size_t)p->L);
+  for (int64_t l = 0; l < p->L; ++l) {
+    MegaLayer& m = layers[(size_t)l];
+    m.attn = panels(p->attn_w[l], H, 3 * H);
+    {
+      const int np = (int)p->nH * chunks;
+      float* d = p->mem.alloc<float>((size_t)np * p->hd * Wc);
+      launch_panelize_proj(p->proj_w[l], d, H, (int)p->hd, (int)p->nH, chunks, Wc, nullptr);
+      m.proj = MegaPanels{d, (int)p->hd, H, Wc, np};
+    }
+    m.fc = panels(p->fc_w[l], H, F);
+    m.fp = panels(p->fp_w[l], F, H);
+    if (!m.attn.data || !m.proj.data || !m.fc.data || !m.fp.data) return;
+    m.attn_b = p->attn_b[l]; m.proj_b = p->proj_b[l]; m.fc_b = p->fc_b[l]; m.fp_b = p->fp_b[l];
+    m.ln1_g = p->ln1g[l]; m.ln1_b = p->ln1b[l]; m.ln2_g = p->ln2g[l]; m.ln2_b = p->ln2b[l];
+    m.kc = p->kc[l]; m.vc = p->vc[l];
+  }
+  p->mega_layers = p->mem.alloc<MegaLayer>(layers.size());
+  IDEV_CUDA(cudaMemcpy(p->mega_layers, layers.data(), layers.size() * sizeof(MegaLayer),
+                       cudaMemcpyHostToDevice));
+  p->best_v = p->mem.alloc<float>(grid);
+  p->best_i = p->mem.alloc<int64_t>(grid);
+  p->bar = p->mem.alloc<unsigned int>(2);
+  p->mega_x = p->mem.alloc<float>(2 * (size_t)H);
+  p->mega_part = p->mem.alloc<float>((size_t)p->nH * H);
+  p->mega_chunks = chunks;
+  IDEV_CUDA(cudaMemset(p->bar, 0, 2 * sizeof(unsigned int)));
+  IDEV_CUDA(cudaDeviceSynchronize());
+  p->mega_grid = grid;
+  p->use_mega = true;
+}
 
 static void decoder_create(const InfercGpt2Weights* w, int64_t max_len, InfercDecoderPlan* p) {
   IDEV_CHECK_ARG(w != nullptr, "decoder_create: null weights");
@@ -504,6 +624,7 @@ static void decoder_create(const InfercGpt2Weights* w, int64_t max_len, InfercDe
   IDEV_CUDA(cudaMemset(p->err, 0, sizeof(int)));
   p->ws.allocate(size_t(1) << 20, 1024);
   IDEV_CUDA(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
+  setup_mega(p);
   IDEV_CUDA(cudaEventCreate(&p->ev0));
   IDEV_CUDA(cudaEventCreate(&p->ev1));
 }
