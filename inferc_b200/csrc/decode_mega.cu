@@ -38,7 +38,7 @@ namespace {
 constexpr int kMegaThreads = 256;
 constexpr int kSlotBytes = 48 * 1024;
 constexpr int kSlots = 4;
-constexpr uint32_t kMegaSpin = 1u << 24;
+constexpr unsigned long long kMegaWaitNs = 50ull * 1000 * 1000;  // 50 ms per wait
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -54,9 +54,17 @@ __device__ __forceinline__ void mb_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+__device__ __forceinline__ unsigned long long gclock() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait (at most kMegaWaitNs) for the phase with the given parity.
 __device__ __forceinline__ bool mb_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_addr(bar);
-  for (uint32_t i = 0; i < kMegaSpin; ++i) {
+  const unsigned long long t0 = gclock();
+  for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -66,8 +74,8 @@ __device__ __forceinline__ bool mb_wait(uint64_t* bar, uint32_t parity) {
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 255) == 255 && gclock() - t0 > kMegaWaitNs) return false;
   }
-  return false;
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes and
@@ -126,8 +134,9 @@ __device__ bool grid_sync(const MegaArgs& a, Smem& sm, int tag = -1, int step = 
     const unsigned target = (++sm.nbar) * gridDim.x;
     red_release_add(a.bar_count, 1u);
     uint32_t i = 0;
+    const unsigned long long t0 = gclock();
     while ((int)(ld_acquire(a.bar_count) - target) < 0) {
-      if (++i > kMegaSpin || (i % 1024 == 0 && *(volatile int*)a.err)) {
+      if ((++i & 63) == 0 && (gclock() - t0 > kMegaWaitNs || *(volatile int*)a.err)) {
         atomicExch(a.err, 1);
         break;
       }
@@ -301,10 +310,6 @@ __device__ __forceinline__ EpiIn gemv_preload(const MegaPanels& m, const float* 
 __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, const EpiIn& e,
                            float* y, int act, Smem& sm, const MegaArgs& a, int ptag = -1) {
   const int tid = threadIdx.x;
-  auto mark = [&](int i) {
-    if (a.prof && ptag >= 0 && blockIdx.x == 0 && tid == 0) a.prof[512 + 8 * ptag + i] = gtimer();
-  };
-  mark(0);
   const int P = m.P, K = m.K;
   const int P4 = P / 4;                  // float4 columns per row
   const int slices = kMegaThreads / P4;  // rows processed in parallel
@@ -312,7 +317,6 @@ __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, 
   const int np = (int)(blockIdx.x < (unsigned)m.npanels) + (int)(blockIdx.x + gridDim.x < (unsigned)m.npanels);
   for (int j = 0; j < np; ++j)
     if (!wait_slot(2 * pair + j, sm, a)) return false;
-  mark(1);
   const float* w0 = reinterpret_cast<const float*>(slots + (size_t)(2 * pair) * kSlotBytes);
   const float* w1 = reinterpret_cast<const float*>(slots + (size_t)(2 * pair + 1) * kSlotBytes);
   float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
@@ -362,7 +366,6 @@ __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, 
     }
   }
   __syncthreads();
-  mark(2);
   return true;
 }
 
@@ -371,6 +374,7 @@ __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, 
 // Loads are issued in independent batches (the cache is read from L2).
 __device__ void attention_head(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
                                Smem& sm, int h, bool append, float* ctx_out) {
+
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, hd = a.hd, H = a.H;
   float* qs = scr;             // [hd]
   float* kn = scr + 128;       // [hd] new key
@@ -480,6 +484,124 @@ __device__ void attention_head(const MegaArgs& a, const MegaLayer& L, int64_t po
   __syncthreads();
 }
 
+// head_dim == 64: one pass over the keys. Each thread takes keys tid,
+// tid + 256, ...; loads the K and V rows together (one L2 round trip per
+// key batch), keeps an online-softmax partial (m, l, o[64]); partials are
+// merged with a block max and shuffle sums.
+__device__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
+                                 Smem& sm, int h, bool append, float* ctx_out) {
+  constexpr int HD = 64;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, H = a.H;
+  constexpr int nw = kMegaThreads / 32;
+  float* qs = scr;        // [64]
+  float* kn = scr + 128;  // [64]
+  float* vn = scr + 256;  // [64]
+  float* part = scr + 384 + a.max_len + 4;  // [8][65]
+  float* kh = L.kc + (size_t)h * a.max_len * HD;
+  float* vh = L.vc + (size_t)h * a.max_len * HD;
+  if (tid < HD) {
+    qs[tid] = __ldcg(a.qkv + h * HD + tid);
+    kn[tid] = __ldcg(a.qkv + H + h * HD + tid);
+    vn[tid] = __ldcg(a.qkv + 2 * H + h * HD + tid);
+    if (append) {
+      kh[pos * HD + tid] = kn[tid];
+      vh[pos * HD + tid] = vn[tid];
+    }
+  }
+  __syncthreads();
+  const int64_t Lk = pos + 1;
+  const float sq = sqrtf((float)HD);
+  // thread pair (2i, 2i+1) shares key i: each lane holds half the dims.
+  const int half = tid & 1;
+  float m = -INFINITY, l = 0.f, o[32];
+#pragma unroll
+  for (int d = 0; d < 32; ++d) o[d] = 0.f;
+  const float4* q4 = reinterpret_cast<const float4*>(qs + 32 * half);
+  // The loop bound is warp-uniform (every lane runs every iteration) because
+  // the pair shuffle below needs all 32 lanes.
+#pragma unroll 1
+  for (int64_t base = 0; base < Lk; base += kMegaThreads / 2) {
+    const int64_t j = base + (tid >> 1);
+    const bool valid = j < Lk;
+    float4 kr[8], vr[8];
+    if (j == pos) {
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        kr[d] = reinterpret_cast<const float4*>(kn + 32 * half)[d];
+        vr[d] = reinterpret_cast<const float4*>(vn + 32 * half)[d];
+      }
+    } else if (valid) {
+      const float4* kg = reinterpret_cast<const float4*>(kh + j * HD + 32 * half);
+      const float4* vg = reinterpret_cast<const float4*>(vh + j * HD + 32 * half);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        kr[d] = __ldcg(kg + d);
+        vr[d] = __ldcg(vg + d);
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < 8; ++d) kr[d] = vr[d] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+      const float4 qv = q4[d];
+      dot = fmaf(qv.x, kr[d].x, dot);
+      dot = fmaf(qv.y, kr[d].y, dot);
+      dot = fmaf(qv.z, kr[d].z, dot);
+      dot = fmaf(qv.w, kr[d].w, dot);
+    }
+    // dims 0..31 partial + dims 32..63 partial (same sum order in both lanes)
+    const float other = __shfl_xor_sync(0xffffffffu, dot, 1);
+    if (!valid) continue;
+    const float sc = (half == 0 ? dot + other : other + dot) / sq;
+    const float mn = fmaxf(m, sc);
+    const float c = expf(m - mn);  // 0 on the first key (m = -inf)
+    const float p = expf(sc - mn);
+    l = l * c + p;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+      o[4 * d] = fmaf(p, vr[d].x, o[4 * d] * c);
+      o[4 * d + 1] = fmaf(p, vr[d].y, o[4 * d + 1] * c);
+      o[4 * d + 2] = fmaf(p, vr[d].z, o[4 * d + 2] * c);
+      o[4 * d + 3] = fmaf(p, vr[d].w, o[4 * d + 3] * c);
+    }
+    m = mn;
+  }
+  // block max of m
+  float mx = warp_max(m);
+  if (lane == 0) sm.red[wid] = mx;
+  __syncthreads();
+  float M = sm.red[0];
+#pragma unroll
+  for (int w = 1; w < nw; ++w) M = fmaxf(M, sm.red[w]);
+  const float scale = (m == -INFINITY) ? 0.f : expf(m - M);
+  l = half == 0 ? l * scale : 0.f;  // count each key once
+#pragma unroll
+  for (int d = 0; d < 32; ++d) o[d] *= scale;
+  l = warp_sum(l);
+#pragma unroll
+  for (int off = 2; off < 32; off <<= 1)
+#pragma unroll
+    for (int d = 0; d < 32; ++d) o[d] += __shfl_xor_sync(0xffffffffu, o[d], off);
+  if (lane < 2) {
+#pragma unroll
+    for (int d = 0; d < 32; ++d) part[wid * 65 + 32 * lane + d] = o[d];
+    if (lane == 0) part[wid * 65 + 64] = l;
+  }
+  __syncthreads();
+  if (tid < HD) {
+    float r = 0.f, t = 0.f;
+#pragma unroll
+    for (int w = 0; w < nw; ++w) {
+      r += part[w * 65 + tid];
+      t += part[w * 65 + 64];
+    }
+    ctx_out[tid] = r / t;
+  }
+  __syncthreads();
+}
+
 // FC-phase input: xm = xa + b_proj + sum_h part[h] (heads in order); CTA 0
 // publishes xm (the FP residual); then LN2 in place.
 __device__ void stage_attn_residual(const MegaArgs& a, const MegaLayer& L, const float* xa,
@@ -515,7 +637,10 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
   if (c >= a.heads * chunks) return true;
   const int h = c / chunks, cc = c % chunks;
   float* ctx = scr + 384 + a.max_len + 4 + (kMegaThreads / 32) * 128;  // [hd]
-  attention_head(a, L, pos, scr, sm, h, cc == 0, ctx);
+  if (a.hd == 64)
+    attention_head64(a, L, pos, scr, sm, h, cc == 0, ctx);
+  else
+    attention_head(a, L, pos, scr, sm, h, cc == 0, ctx);
   if (!wait_slot(slot, sm, a)) return false;
   const MegaPanels& m = L.proj;  // K = hd, P = chunk width
   const float* w = reinterpret_cast<const float*>(slots + (size_t)slot * kSlotBytes);
@@ -575,7 +700,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       return;
     }
     for (int l = 0; l < a.layers; ++l) {
-      const MegaLayer L = a.layer[l];
+      const MegaLayer& L = a.layer[l];  // read on use (keeps registers free)
       // ---- QKV (pair 0); the attention block's W_proj panel streams into slot 2.
       if (tid == 0 && blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) {
         const uint32_t bytes = (uint32_t)L.proj.K * L.proj.P * 4;

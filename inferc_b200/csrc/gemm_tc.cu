@@ -42,7 +42,7 @@ constexpr int BM = 128;
 constexpr int kConvThreads = 128;  // warps 2..5
 constexpr int kEpiThreads = 256;   // warps 6..13 (two per TMEM lane quarter)
 constexpr int kThreadsTc = 64 + kConvThreads + kEpiThreads;
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;  // 200 ms per wait
 
 // ------------------------------------------------------------ PTX helpers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -64,9 +64,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 // Bounded wait for the phase with the given parity; false on timeout.
+__device__ __forceinline__ unsigned long long gclock_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  const unsigned long long t0 = gclock_ns();
+  for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -76,8 +83,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 255) == 255 && gclock_ns() - t0 > kWaitLimitNs) return false;
   }
-  return false;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,

@@ -450,34 +450,11 @@ struct InfercDecoderPlan {
       a.best_v = best_v; a.best_i = best_i; a.bar_count = bar; a.bar_gen = bar + 1;
       a.err = err; a.tok = tok; a.token_log = token_log; a.log_offset = 1;
       a.pos0 = n; a.nsteps = (int)(max_tokens - 1);
-      static unsigned long long* prof = nullptr;
-      const bool want_prof = std::getenv("INFERC_DECODE_PROF") != nullptr;
-      if (want_prof && !prof) IDEV_CUDA(cudaMalloc(&prof, 2 * 1024 * sizeof(unsigned long long)));
-      a.prof = want_prof ? prof : nullptr;
+      a.prof = nullptr;
       IDEV_CUDA(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned int), st));
       IDEV_CUDA(cudaEventRecord(ev0, st));
       launch_decode_mega(a, mega_grid, st);
       IDEV_CUDA(cudaEventRecord(ev1, st));
-      if (want_prof) {
-        std::vector<unsigned long long> h(2 * (4 * L + 2));
-        IDEV_CUDA(cudaMemcpyAsync(h.data(), prof, h.size() * 8, cudaMemcpyDeviceToHost, st));
-        IDEV_CUDA(cudaStreamSynchronize(st));
-        std::vector<unsigned long long> d(100);
-        IDEV_CUDA(cudaMemcpy(d.data(), prof + 512, 100 * 8, cudaMemcpyDeviceToHost));
-        fprintf(stderr, "QKV l1: stage %.2f | wait %.2f compute %.2f\n", (d[0] - d[88]) / 1e3,
-                (d[1] - d[0]) / 1e3, (d[2] - d[1]) / 1e3);
-        fprintf(stderr, "FC l1: wait %.2f compute %.2f\n", (d[9] - d[8]) / 1e3,
-                (d[10] - d[9]) / 1e3);
-        std::vector<unsigned long long> c(32);
-        IDEV_CUDA(cudaMemcpy(c.data(), prof + 1024, 32 * 8, cudaMemcpyDeviceToHost));
-        for (int q = 0; q < 2; ++q)
-          fprintf(stderr, "FC cta%d cycles: prefetch %llu stage %llu gemv %llu barrier %llu\n",
-                  q ? 100 : 0, c[16 * q + 1] - c[16 * q], c[16 * q + 2] - c[16 * q + 1],
-                  c[16 * q + 3] - c[16 * q + 2], c[16 * q + 4] - c[16 * q + 3]);
-        for (size_t t = 0; t + 1 < h.size() / 2; ++t)
-          fprintf(stderr, "phase %zu: work %.2f us, barrier %.2f us\n", t,
-                  (h[2 * (t + 1)] - h[2 * t + 1]) / 1e3, (h[2 * t + 1] - h[2 * t]) / 1e3);
-      }
     } else if (max_tokens > 1) {
       if (!step_graph || log_base != n) {
         // The graph bakes log_base; (re)capture when the prompt length
