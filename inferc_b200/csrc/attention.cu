@@ -6,7 +6,7 @@
 // where a masked score is REPLACED by `fill` (not added to), scale =
 // 1/sqrt(head_dim), and head h lives in columns [h*hd, (h+1)*hd) of the
 // [B, S, H] tensors. The kernel never materialises the S x S scores: each CTA
-// owns 64 query rows of one (b, h), streams 64-key tiles of K and V through
+// owns 128 query rows of one (b, h), streams 64-key tiles of K and V through
 // shared memory and keeps a running (max, sum) per row (online softmax), so
 // the HBM traffic is one read of Q, K, V and one write of O.
 #include <cfloat>
@@ -16,10 +16,10 @@
 namespace inferc_dev {
 namespace {
 
-constexpr int TQ = 64;   // query rows per CTA
+constexpr int TQ = 128;  // query rows per CTA
 constexpr int TKEYS = 64;  // keys per tile
 constexpr int HD = 64;   // head dim of the fast kernel
-constexpr int PAD = 68;  // padded row length of the transposed tiles
+constexpr int PAD = 68;  // padded row length of the Q, K and P tiles
 
 __device__ __forceinline__ bool is_masked(const AttnArgs& a, int64_t b, int64_t h, int64_t i,
                                           int64_t j) {
@@ -28,12 +28,19 @@ __device__ __forceinline__ bool is_masked(const AttnArgs& a, int64_t b, int64_t 
   return false;
 }
 
-__global__ void __launch_bounds__(256) attention_hd64_kernel(AttnArgs a) {
+// head_dim 64: a CTA owns TQ = 128 query rows of one (b, h) and streams
+// 64-key tiles of K and V. 256 threads = 16 x 16 (tx, ty); thread (tx, ty)
+// owns score rows i = ty + 16 r (r < 8) and key columns j = tx + 16 c (c < 4)
+// of a tile, and output rows i with head dims [4 tx, 4 tx + 4). Q, K, V, P
+// live in shared memory in natural row-major layout with rows padded to 68
+// floats; the interleaved row ownership makes every 128-bit shared load
+// either a broadcast or conflict free.
+__global__ void __launch_bounds__(256, 2) attention_hd64_kernel(AttnArgs a) {
   extern __shared__ __align__(16) float smem[];
-  float* Qt = smem;                  // [HD][PAD]   Q^T of this query tile
-  float* Kt = Qt + HD * PAD;         // [HD][PAD]   K^T of the key tile
-  float* Vs = Kt + HD * PAD;         // [TKEYS][HD] V of the key tile
-  float* Ps = Vs + TKEYS * HD;       // [TKEYS][PAD] P^T of the tile
+  float* Qs = smem;               // [TQ][PAD]
+  float* Ks = Qs + TQ * PAD;      // [TKEYS][PAD]
+  float* Vs = Ks + TKEYS * PAD;   // [TKEYS][HD]
+  float* Ps = Vs + TKEYS * HD;    // [TQ][PAD]
 
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int64_t b = blockIdx.z, h = blockIdx.y, i0 = (int64_t)blockIdx.x * TQ;
@@ -41,20 +48,16 @@ __global__ void __launch_bounds__(256) attention_hd64_kernel(AttnArgs a) {
   const float* K = a.k + b * a.bstride_k + h * HD;
   const float* V = a.v + b * a.bstride_v + h * HD;
 
-  // Load Q^T: 64 rows x 64 dims, float4 along d.
   for (int f = tid; f < TQ * HD / 4; f += 256) {
-    const int r = f / (HD / 4), d = (f % (HD / 4)) * 4;
+    const int r = f >> 4, d = (f & 15) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (i0 + r < a.S) v = *reinterpret_cast<const float4*>(Q + (i0 + r) * a.ldq + d);
-    Qt[(d + 0) * PAD + r] = v.x;
-    Qt[(d + 1) * PAD + r] = v.y;
-    Qt[(d + 2) * PAD + r] = v.z;
-    Qt[(d + 3) * PAD + r] = v.w;
+    *reinterpret_cast<float4*>(Qs + r * PAD + d) = v;
   }
 
-  float m[4], l[4], o[4][4];
+  float m[8], l[8], o[8][4];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < 8; ++r) {
     m[r] = -INFINITY;
     l[r] = 0.f;
 #pragma unroll
@@ -64,66 +67,66 @@ __global__ void __launch_bounds__(256) attention_hd64_kernel(AttnArgs a) {
   const int64_t ntiles = (a.S + TKEYS - 1) / TKEYS;
   for (int64_t t = 0; t < ntiles; ++t) {
     const int64_t j0 = t * TKEYS;
-    __syncthreads();  // previous tile's Kt/Vs/Ps no longer in use
+    __syncthreads();  // previous tile's Ks / Vs / Ps no longer in use
     for (int f = tid; f < TKEYS * HD / 4; f += 256) {
-      const int r = f / (HD / 4), d = (f % (HD / 4)) * 4;
+      const int r = f >> 4, d = (f & 15) * 4;
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
       if (j0 + r < a.S) {
         kv = *reinterpret_cast<const float4*>(K + (j0 + r) * a.ldk + d);
         vv = *reinterpret_cast<const float4*>(V + (j0 + r) * a.ldv + d);
       }
-      Kt[(d + 0) * PAD + r] = kv.x;
-      Kt[(d + 1) * PAD + r] = kv.y;
-      Kt[(d + 2) * PAD + r] = kv.z;
-      Kt[(d + 3) * PAD + r] = kv.w;
+      *reinterpret_cast<float4*>(Ks + r * PAD + d) = kv;
       *reinterpret_cast<float4*>(Vs + r * HD + d) = vv;
     }
     __syncthreads();
 
-    float s[4][4];
+    float s[8][4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < 8; ++r)
 #pragma unroll
       for (int c = 0; c < 4; ++c) s[r][c] = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < HD; ++d) {
-      const float4 qv = *reinterpret_cast<const float4*>(Qt + d * PAD + ty * 4);
-      const float4 kv = *reinterpret_cast<const float4*>(Kt + d * PAD + tx * 4);
-      const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll 4
+    for (int d = 0; d < HD; d += 4) {
+      float4 kv[4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
+      for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(Ks + (tx + 16 * c) * PAD + d);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) s[r][c] = fmaf(qa[r], ka[c], s[r][c]);
+      for (int r = 0; r < 8; ++r) {
+        const float4 qv = *reinterpret_cast<const float4*>(Qs + (ty + 16 * r) * PAD + d);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          s[r][c] = fmaf(qv.x, kv[c].x, s[r][c]);
+          s[r][c] = fmaf(qv.y, kv[c].y, s[r][c]);
+          s[r][c] = fmaf(qv.z, kv[c].z, s[r][c]);
+          s[r][c] = fmaf(qv.w, kv[c].w, s[r][c]);
+        }
+      }
     }
 
-    float tmax[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int64_t i = i0 + ty * 4 + r;
-      tmax[r] = -INFINITY;
+    for (int r = 0; r < 8; ++r) {
+      const int64_t i = i0 + ty + 16 * r;
+      float tmax = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const int64_t j = j0 + tx * 4 + c;
+        const int64_t j = j0 + tx + 16 * c;
         float v;
         if (j >= a.S) v = -INFINITY;  // beyond the sequence: no weight at all
         else if (i < a.S && is_masked(a, b, h, i, j)) v = a.fill;
         else v = a.scale * s[r][c];
         s[r][c] = v;
-        tmax[r] = fmaxf(tmax[r], v);
+        tmax = fmaxf(tmax, v);
       }
 #pragma unroll
       for (int off = 8; off > 0; off >>= 1)
-        tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], off));
-    }
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float mn = fmaxf(m[r], tmax[r]);
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+      const float mn = fmaxf(m[r], tmax);
       const float corr = expf(m[r] - mn);  // m = -inf on the first tile -> 0
       float ps = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const float p = expf(s[r][c] - mn);
-        s[r][c] = p;
+        Ps[(ty + 16 * r) * PAD + tx + 16 * c] = p;
         ps += p;
       }
 #pragma unroll
@@ -133,27 +136,32 @@ __global__ void __launch_bounds__(256) attention_hd64_kernel(AttnArgs a) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) o[r][c] *= corr;
     }
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) Ps[(tx * 4 + c) * PAD + ty * 4 + r] = s[r][c];
     __syncthreads();
-    const int64_t jn = (a.S - j0) < TKEYS ? (a.S - j0) : TKEYS;
-    for (int j = 0; j < jn; ++j) {
-      const float4 pv = *reinterpret_cast<const float4*>(Ps + j * PAD + ty * 4);
-      const float4 vv = *reinterpret_cast<const float4*>(Vs + j * HD + tx * 4);
-      const float pa[4] = {pv.x, pv.y, pv.z, pv.w}, va[4] = {vv.x, vv.y, vv.z, vv.w};
+    const int jn = (int)((a.S - j0) < TKEYS ? (a.S - j0) : TKEYS);
+#pragma unroll 2
+    for (int j = 0; j < jn; j += 4) {
+      float4 vv[4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
+      for (int q = 0; q < 4; ++q) vv[q] = *reinterpret_cast<const float4*>(Vs + (j + q) * HD + tx * 4);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) o[r][c] = fmaf(pa[r], va[c], o[r][c]);
+      for (int r = 0; r < 8; ++r) {
+        const float4 pv = *reinterpret_cast<const float4*>(Ps + (ty + 16 * r) * PAD + j);
+        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          o[r][0] = fmaf(pa[q], vv[q].x, o[r][0]);
+          o[r][1] = fmaf(pa[q], vv[q].y, o[r][1]);
+          o[r][2] = fmaf(pa[q], vv[q].z, o[r][2]);
+          o[r][3] = fmaf(pa[q], vv[q].w, o[r][3]);
+        }
+      }
     }
   }
 
   float* O = a.out + b * a.bstride_o + h * HD;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int64_t i = i0 + ty * 4 + r;
+  for (int r = 0; r < 8; ++r) {
+    const int64_t i = i0 + ty + 16 * r;
     if (i >= a.S) continue;
     const float inv = 1.0f / l[r];
     *reinterpret_cast<float4*>(O + i * a.ldo + tx * 4) =
@@ -399,7 +407,7 @@ void launch_attention(const AttnArgs& a, cudaStream_t st) {
                     a.ldo % 4 == 0 && a.bstride_q % 4 == 0 && a.bstride_k % 4 == 0 &&
                     a.bstride_v % 4 == 0 && a.bstride_o % 4 == 0;
   if (fast) {
-    const size_t smem = (size_t)(3 * HD * PAD + TKEYS * HD) * sizeof(float);
+    const size_t smem = (size_t)(TQ * PAD + TKEYS * PAD + TKEYS * HD + TQ * PAD) * sizeof(float);
     // Per device and cheap; set on every call so that every device in the
     // process is configured.
     IDEV_CUDA(cudaFuncSetAttribute(attention_hd64_kernel,
