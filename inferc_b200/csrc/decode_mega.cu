@@ -488,7 +488,7 @@ __device__ void attention_head(const MegaArgs& a, const MegaLayer& L, int64_t po
 // tid + 256, ...; loads the K and V rows together (one L2 round trip per
 // key batch), keeps an online-softmax partial (m, l, o[64]); partials are
 // merged with a block max and shuffle sums.
-__device__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
+__device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
                                  Smem& sm, int h, bool append, float* ctx_out) {
   constexpr int HD = 64;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, H = a.H;
@@ -499,6 +499,10 @@ __device__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t 
   float* part = scr + 384 + a.max_len + 4;  // [8][65]
   float* kh = L.kc + (size_t)h * a.max_len * HD;
   float* vh = L.vc + (size_t)h * a.max_len * HD;
+  auto mk = [&](int i) {
+    if (a.prof && blockIdx.x == 0 && threadIdx.x == 0) a.prof[1100 + i] = clock64();
+  };
+  mk(0);
   if (tid < HD) {
     qs[tid] = __ldcg(a.qkv + h * HD + tid);
     kn[tid] = __ldcg(a.qkv + H + h * HD + tid);
@@ -509,6 +513,7 @@ __device__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t 
     }
   }
   __syncthreads();
+  mk(1);
   const int64_t Lk = pos + 1;
   const float sq = sqrtf((float)HD);
   // thread pair (2i, 2i+1) shares key i: each lane holds half the dims.
@@ -568,6 +573,7 @@ __device__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t 
     }
     m = mn;
   }
+  mk(2);
   // block max of m
   float mx = warp_max(m);
   if (lane == 0) sm.red[wid] = mx;
@@ -600,6 +606,7 @@ __device__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t 
     ctx_out[tid] = r / t;
   }
   __syncthreads();
+  mk(3);
 }
 
 // FC-phase input: xm = xa + b_proj + sum_h part[h] (heads in order); CTA 0
@@ -642,6 +649,7 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
   else
     attention_head(a, L, pos, scr, sm, h, cc == 0, ctx);
   if (!wait_slot(slot, sm, a)) return false;
+  if (a.prof && blockIdx.x == 0 && threadIdx.x == 0) a.prof[1104] = clock64();
   const MegaPanels& m = L.proj;  // K = hd, P = chunk width
   const float* w = reinterpret_cast<const float*>(slots + (size_t)slot * kSlotBytes);
   const int tid = threadIdx.x;
@@ -661,6 +669,7 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
     if (gcol < a.H) a.part[(size_t)h * a.H + gcol] = t;
   }
   __syncthreads();
+  if (a.prof && blockIdx.x == 0 && threadIdx.x == 0) a.prof[1105] = clock64();
   return true;
 }
 
@@ -726,6 +735,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       if (!gemv_phase(L.attn, 0, slots, e_qkv, a.qkv, ACT_NONE, sm, a)) { drain(sm); return; }
       if (!grid_sync(a, sm, 4 * l + 0, step)) { drain(sm); return; }
       // ---- attention + output projection partials; FC streams into pair 0.
+      if (a.prof && blockIdx.x == 0 && tid == 0) a.prof[1099] = clock64();
       prefetch_panels(L.fc, 0, slots, sm);
       if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm)) { drain(sm); return; }
       if (!grid_sync(a, sm, 4 * l + 1, step)) { drain(sm); return; }

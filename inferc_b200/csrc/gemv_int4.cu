@@ -39,21 +39,50 @@ __device__ __forceinline__ float nib_minus8(uint32_t w, uint32_t sel) {
   return __int_as_float(__byte_perm(w, 0x4B000000u, sel)) - 8388616.0f;
 }
 
-// Accumulates one 16-byte chunk (32 weights, k = 32c .. 32c+31).
-__device__ __forceinline__ float chunk_dot(const uint4 v, const float (&x)[32], float acc) {
+// Packed fp32x2 arithmetic (sm_100): two lanes of fp32 per instruction.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return make_float2(a, b);
+}
+
+// (2^23 + lo_nibble(byte), 2^23 + hi_nibble(byte)) of byte `sel` of the
+// nibble-split words, as a packed pair.
+__device__ __forceinline__ uint64_t nib_pair(uint32_t lo, uint32_t hi, uint32_t sel) {
+  return pack2(__int_as_float(__byte_perm(lo, 0x4B000000u, sel)),
+               __int_as_float(__byte_perm(hi, 0x4B000000u, sel)));
+}
+
+// Accumulates one 16-byte chunk (32 weights, k = 32c .. 32c+31) into the
+// packed (even k, odd k) accumulator. Byte b of word m holds k = 8m + 2b
+// (low nibble) and k = 8m + 2b + 1 (high nibble), so each byte gives one
+// (x[k], x[k+1]) pair.
+__device__ __forceinline__ uint64_t chunk_dot(const uint4 v, const uint64_t (&x2)[16], uint64_t acc) {
+  const uint64_t bias = pack2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
   const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     const uint32_t lo = ws[m] & 0x0F0F0F0Fu, hi = (ws[m] >> 4) & 0x0F0F0F0Fu;
-    // byte b of word m is k = 8m + 2b (lo) and 8m + 2b + 1 (hi)
-    acc = fmaf(nib_minus8(lo, 0x7540u), x[8 * m + 0], acc);
-    acc = fmaf(nib_minus8(hi, 0x7540u), x[8 * m + 1], acc);
-    acc = fmaf(nib_minus8(lo, 0x7541u), x[8 * m + 2], acc);
-    acc = fmaf(nib_minus8(hi, 0x7541u), x[8 * m + 3], acc);
-    acc = fmaf(nib_minus8(lo, 0x7542u), x[8 * m + 4], acc);
-    acc = fmaf(nib_minus8(hi, 0x7542u), x[8 * m + 5], acc);
-    acc = fmaf(nib_minus8(lo, 0x7543u), x[8 * m + 6], acc);
-    acc = fmaf(nib_minus8(hi, 0x7543u), x[8 * m + 7], acc);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint64_t q = add2(nib_pair(lo, hi, 0x7540u + b), bias);  // (q_k - 8, q_k+1 - 8)
+      acc = fma2(q, x2[4 * m + b], acc);
+    }
   }
   return acc;
 }
@@ -67,46 +96,56 @@ __global__ void __launch_bounds__(kThreads) gemv_int4_kernel(const __grid_consta
   // Lets the next group of this batch start while this one runs (the groups
   // are independent; see launch_gemv_int4).
   pdl_launch_dependents();
-  int mi = 0;
-  while (mi + 1 < bt.count && (int)blockIdx.x >= bt.cta_start[mi + 1]) ++mi;
-  const InfercInt4Gemv& d = bt.d[mi];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int64_t chunks = d.k / 32;
-  float xr[CPL][32];
-#pragma unroll
-  for (int c = 0; c < CPL; ++c) {
-    const int64_t ch = lane + 32 * c;
-#pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (ch < chunks) v = *reinterpret_cast<const float4*>(d.x + ch * 32 + j);
-      xr[c][j] = v.x; xr[c][j + 1] = v.y; xr[c][j + 2] = v.z; xr[c][j + 3] = v.w;
-    }
-  }
-  const int64_t row0 = (int64_t)(blockIdx.x - bt.cta_start[mi]) * kRowsPerCta + wid * kRowsPerWarp;
-  const int64_t row_bytes = d.k / 2;
-#pragma unroll 1
-  for (int rr = 0; rr < kRowsPerWarp; rr += 4) {
-    uint4 v[4][CPL];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t r = row0 + rr + u;
+  const int total = bt.cta_start[bt.count];
+  int loaded = -1;  // matrix whose x is in registers
+  uint64_t xr[CPL][16];  // (x[k], x[k+1]) pairs of this lane's chunks
+  // Persistent: each CTA walks row blocks blockIdx.x, + gridDim.x, ...
+  for (int cta = blockIdx.x; cta < total; cta += gridDim.x) {
+    int mi = 0;
+    while (mi + 1 < bt.count && cta >= bt.cta_start[mi + 1]) ++mi;
+    const InfercInt4Gemv& d = bt.d[mi];
+    const int64_t chunks = d.k / 32;
+    if (mi != loaded) {
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {
         const int64_t ch = lane + 32 * c;
-        v[u][c] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 0
-        if (r < d.n && ch < chunks)
-          v[u][c] = __ldg(reinterpret_cast<const uint4*>(d.w + r * row_bytes) + ch);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (ch < chunks) v = *reinterpret_cast<const float4*>(d.x + ch * 32 + j);
+          xr[c][j / 2] = pack2(v.x, v.y);
+          xr[c][j / 2 + 1] = pack2(v.z, v.w);
+        }
       }
+      loaded = mi;
     }
+    const int64_t row0 = (int64_t)(cta - bt.cta_start[mi]) * kRowsPerCta + wid * kRowsPerWarp;
+    const int64_t row_bytes = d.k / 2;
+#pragma unroll 1
+    for (int rr = 0; rr < kRowsPerWarp; rr += 4) {
+      uint4 v[4][CPL];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t r = row0 + rr + u;
-      float acc = 0.f;
+      for (int u = 0; u < 4; ++u) {
+        const int64_t r = row0 + rr + u;
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) acc = chunk_dot(v[u][c], xr[c], acc);
-      acc = warp_sum(acc);
-      if (lane == 0 && r < d.n) d.y[r] = d.scales[r] * acc;
+        for (int c = 0; c < CPL; ++c) {
+          const int64_t ch = lane + 32 * c;
+          v[u][c] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 0
+          if (r < d.n && ch < chunks)
+            v[u][c] = __ldg(reinterpret_cast<const uint4*>(d.w + r * row_bytes) + ch);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t r = row0 + rr + u;
+        uint64_t acc2 = pack2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) acc2 = chunk_dot(v[u][c], xr[c], acc2);
+        const float2 a2 = unpack2(acc2);
+        const float acc = warp_sum(a2.x + a2.y);
+        if (lane == 0 && r < d.n) d.y[r] = d.scales[r] * acc;
+      }
     }
   }
 }
@@ -144,14 +183,23 @@ void launch_group(const InfercInt4Gemv* ds, const int* idx, int n, cudaStream_t 
     }
     bt.cta_start[bt.count] = ctas;
     if (ctas == 0) continue;
+    // Persistent grid: as many CTAs as fit at once, each walking row blocks.
+    static int resident = [] {
+      int per_sm = 1, dev = 0, sms = 148;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_int4_kernel<CPL>, kThreads, 0);
+      if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      return std::max(1, per_sm) * sms;
+    }();
+    const int grid = std::min(ctas, resident);
     if (first) {  // ordered after all earlier work on the stream
-      gemv_int4_kernel<CPL><<<ctas, kThreads, 0, st>>>(bt);
+      gemv_int4_kernel<CPL><<<grid, kThreads, 0, st>>>(bt);
       IDEV_LAUNCHED();
       first = false;
     } else {
       // Same batch, independent matrices: may overlap the previous group.
       // Its inputs were complete before the first group started.
-      launch_pdl(gemv_int4_kernel<CPL>, dim3(ctas), dim3(kThreads), 0, st, bt);
+      launch_pdl(gemv_int4_kernel<CPL>, dim3(grid), dim3(kThreads), 0, st, bt);
     }
   }
 }

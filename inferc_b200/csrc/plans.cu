@@ -450,11 +450,21 @@ struct InfercDecoderPlan {
       a.best_v = best_v; a.best_i = best_i; a.bar_count = bar; a.bar_gen = bar + 1;
       a.err = err; a.tok = tok; a.token_log = token_log; a.log_offset = 1;
       a.pos0 = n; a.nsteps = (int)(max_tokens - 1);
-      a.prof = nullptr;
+      static unsigned long long* prof = nullptr;
+      const bool want_prof = std::getenv("INFERC_DECODE_PROF") != nullptr;
+      if (want_prof && !prof) IDEV_CUDA(cudaMalloc(&prof, 2048 * sizeof(unsigned long long)));
+      a.prof = want_prof ? prof : nullptr;
       IDEV_CUDA(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned int), st));
       IDEV_CUDA(cudaEventRecord(ev0, st));
       launch_decode_mega(a, mega_grid, st);
       IDEV_CUDA(cudaEventRecord(ev1, st));
+      if (want_prof) {  // development instrumentation (INFERC_DECODE_PROF=1)
+        std::vector<unsigned long long> c(8);
+        IDEV_CUDA(cudaMemcpyAsync(c.data(), prof + 1099, 8 * 8, cudaMemcpyDeviceToHost, st));
+        IDEV_CUDA(cudaStreamSynchronize(st));
+        fprintf(stderr, "attn phase cycles: prefetch %llu qkv-load %llu pass %llu reduce %llu wait %llu proj %llu\n",
+                c[1] - c[0], c[2] - c[1], c[3] - c[2], c[4] - c[3], c[5] - c[4], c[6] - c[5]);
+      }
     } else if (max_tokens > 1) {
       if (!step_graph || log_base != n) {
         // The graph bakes log_base; (re)capture when the prompt length
@@ -504,7 +514,8 @@ static void setup_mega(InfercDecoderPlan* p) {
   const int grid = mega_max_grid((int)p->max_len);
   if (grid < 1) return;
   // attention block: heads x chunks CTAs, chunk width Wc (multiple of 4)
-  const int chunks = std::min<int>(grid / (int)p->nH, H / 4);
+  int chunks = std::min<int>(grid / (int)p->nH, H / 4);
+  if (const char* e = std::getenv("INFERC_DECODE_CHUNKS")) chunks = std::max(1, std::min(chunks, std::atoi(e)));
   if (chunks < 1) return;
   const int Wc = ((H + chunks - 1) / chunks + 3) / 4 * 4;
   if (Wc > 256 || (size_t)p->hd * Wc * 4 > 48 * 1024) return;
