@@ -15,6 +15,7 @@ void launch_gemm_tc(const float* A, int64_t lda, const float* Bb, const float* B
                     float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
                     cudaStream_t st);
 void launch_split_tf32(const float* x, float* big, float* small, int64_t n, cudaStream_t st);
+void launch_split_small(const float* x, float* small, int64_t n, cudaStream_t st);
 
 namespace {
 
@@ -54,10 +55,9 @@ void launch_gemm(const float* A, int64_t lda, bool ta, const float* B, int64_t l
                  cudaStream_t st) {
   if (!ta && !tb && gemm_use_tc(M, N, K) && ldb == N &&
       gemm_tc_supported(A, lda, B, B, ldb, M, N, K)) {
-    float* big = split_buffer((size_t)2 * K * N);
-    float* small = big + (size_t)K * N;
-    launch_split_tf32(B, big, small, K * N, st);
-    launch_gemm_tc(A, lda, big, small, N, C, ldc, M, N, K, ep, st);
+    float* small = split_buffer((size_t)K * N);
+    launch_split_small(B, small, K * N, st);
+    launch_gemm_tc(A, lda, B, small, N, C, ldc, M, N, K, ep, st);
     return;
   }
   launch_gemm_simt(A, lda, ta, B, ldb, tb, C, ldc, M, N, K, ep, st);

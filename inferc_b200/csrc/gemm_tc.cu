@@ -8,9 +8,12 @@
 // tf32 (low 13 mantissa bits zero) and small = x - big (exact in fp32). The
 // product is accumulated in fp32 TMEM as a_s*b_b + a_b*b_s + a_b*b_b, which
 // keeps ~22 mantissa bits per product, i.e. fp32-level error, at three
-// tf32 MMAs per product. B (the weight) is split once into two [K,N] arrays
-// in HBM (split_tf32_kernel); A (the activation) is split in shared memory by
-// the converter warps as each tile arrives.
+// tf32 MMAs per product. The tensor core reads only the top 19 bits of a
+// 32-bit tf32 operand (it truncates), so a raw fp32 array already serves as
+// its own "big" half and only small = x - trunc13(x) has to be formed: for B
+// (the weight) once, in HBM; for A (the activation) in shared memory by the
+// converter warps as each tile arrives. (Verified: errors are identical to
+// an explicit round-to-nearest big half.)
 //
 // Persistent kernel (one CTA per SM striding over 128 x BN output tiles),
 // STAGES-deep TMA ring, two TMEM accumulators so the epilogue of one tile
@@ -31,6 +34,10 @@
 #include <cuda.h>
 
 #include <cstdlib>
+
+#ifndef INFERC_TC_RAW_A
+#define INFERC_TC_RAW_A 1
+#endif
 #include <mutex>
 
 #include "kernels.cuh"
@@ -356,9 +363,19 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 #pragma unroll 4
         for (int i = t; i < (int)(S::A_BYTES / 16); i += kConvThreads) {
           const float4 v = a4[i];
+#if INFERC_TC_RAW_A
+          // The tensor core reads only the top 19 bits of a tf32 operand, so
+          // raw A is its own "big" half; small = A - trunc13(A) (exact).
+          float4 b;
+          b.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+          b.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+          b.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+          b.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+#else
           float4 b;
           b.x = tf32_round(v.x); b.y = tf32_round(v.y); b.z = tf32_round(v.z); b.w = tf32_round(v.w);
           a4[i] = b;
+#endif
           as4[i] = make_float4(v.x - b.x, v.y - b.y, v.z - b.z, v.w - b.w);
         }
         fence_proxy_async();  // generic-proxy writes -> visible to the tensor core
@@ -401,6 +418,17 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"((uint32_t)(2 * BN)));
+  }
+}
+
+// small = x - trunc13(x): with raw x used as the big operand (the tensor core
+// reads only its top 19 bits), x itself need not be copied.
+__global__ void split_small_kernel(const float* __restrict__ x, float* __restrict__ small,
+                                   int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    small[i] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
   }
 }
 
@@ -516,6 +544,13 @@ void launch_gemm_tc(const float* A, int64_t lda, const float* Bb, const float* B
     default: IDEV_TC(EPI_GENERIC); break;
   }
 #undef IDEV_TC
+}
+
+void launch_split_small(const float* x, float* small, int64_t n, cudaStream_t st) {
+  if (n <= 0) return;
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8);
+  split_small_kernel<<<blocks, 256, 0, st>>>(x, small, n);
+  IDEV_LAUNCHED();
 }
 
 void launch_split_tf32(const float* x, float* big, float* small, int64_t n, cudaStream_t st) {

@@ -33,6 +33,7 @@
 
 namespace inferc_dev {
 void launch_split_tf32(const float* x, float* big, float* small, int64_t n, cudaStream_t st);
+void launch_split_small(const float* x, float* small, int64_t n, cudaStream_t st);
 void launch_gemm_presplit(const float* A, int64_t lda, const float* W, const float* Wb,
                           const float* Ws, int64_t ldb, float* C, int64_t ldc, int64_t M,
                           int64_t N, int64_t K, const Epilogue& ep, cudaStream_t st);
@@ -73,8 +74,9 @@ struct DevArena {
   }
 };
 
-// A GEMM weight held three ways: fp32 (CUDA-core path) and its tf32
-// big/small split (tensor-core 3xTF32 path), all [K,N] row-major.
+// A GEMM weight for both GEMM paths: fp32 w (the CUDA-core path, and the
+// tensor core's "big" half, which reads only w's top 19 bits) and
+// small = w - trunc13(w), both [K,N] row-major.
 struct SplitWeight {
   float* w = nullptr;
   float* big = nullptr;
@@ -84,9 +86,9 @@ struct SplitWeight {
 SplitWeight split_weight(DevArena& m, float* w, size_t n) {
   SplitWeight s;
   s.w = w;
-  s.big = m.alloc<float>(n);
+  s.big = w;
   s.small = m.alloc<float>(n);
-  launch_split_tf32(w, s.big, s.small, (int64_t)n, nullptr);
+  launch_split_small(w, s.small, (int64_t)n, nullptr);
   IDEV_CUDA(cudaDeviceSynchronize());
   return s;
 }
