@@ -402,6 +402,10 @@ __global__ void kv_append_kernel(const float* __restrict__ k_new, const float* _
 void launch_attention(const AttnArgs& a, cudaStream_t st) {
   if (a.B <= 0 || a.S <= 0 || a.nH <= 0) return;
   IDEV_CHECK_ARG(a.hd > 0 && a.hd <= 128, "FusedAttention: head_dim must be in [1, 128]");
+  if (attention_tc_supported(a) && attention_tc_enabled()) {
+    launch_attention_tc(a, st);
+    return;
+  }
   const bool fast = a.hd == HD && aligned16(a.q) && aligned16(a.k) && aligned16(a.v) &&
                     aligned16(a.out) && a.ldq % 4 == 0 && a.ldk % 4 == 0 && a.ldv % 4 == 0 &&
                     a.ldo % 4 == 0 && a.bstride_q % 4 == 0 && a.bstride_k % 4 == 0 &&

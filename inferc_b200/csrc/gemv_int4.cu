@@ -34,10 +34,6 @@ struct Int4Batch {
   int count;
 };
 
-__device__ __forceinline__ float nib_minus8(uint32_t w, uint32_t sel) {
-  // Byte `sel` of w placed in the low mantissa byte of 2^23.
-  return __int_as_float(__byte_perm(w, 0x4B000000u, sel)) - 8388616.0f;
-}
 
 // Packed fp32x2 arithmetic (sm_100): two lanes of fp32 per instruction.
 __device__ __forceinline__ uint64_t pack2(float a, float b) {

@@ -42,6 +42,10 @@ struct AttnArgs {
   int causal;                  // 1: additionally mask j > i (prefill)
 };
 void launch_attention(const AttnArgs& a, cudaStream_t st);
+// Tensor-core path (head_dim 64, S <= 128, 16-byte aligned operands).
+bool attention_tc_supported(const AttnArgs& a);
+void launch_attention_tc(const AttnArgs& a, cudaStream_t st);
+bool attention_tc_enabled();
 
 void launch_kv_append(const float* k_new, const float* v_new, int64_t ld_new, float* kc,
                       float* vc, int64_t heads, int64_t hd, int64_t max_len,
