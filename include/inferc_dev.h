@@ -40,7 +40,7 @@ enum {
   INFERC_ERR_CUDA = 2,    /* CUDA runtime or launch failure */
   INFERC_ERR_OOM = 3,     /* device or host allocation failed */
   INFERC_ERR_TIMEOUT = 4, /* a bounded device wait gave up */
-  INFERC_ERR_RANGE = 5    /* index out of range found on the device */
+  INFERC_ERR_RANGE = 5    /* index or value out of range found on the device */
 };
 
 /* ---------------------------------------------------------------- runtime */
@@ -135,6 +135,27 @@ int inferc_dev_gemm_tf32x3(const float* a, int64_t lda, const float* b_big,
                            const float* resid, int64_t ldr, float* y,
                            int64_t ldy, int64_t M, int64_t N, int64_t K,
                            int act, void* stream);
+
+/* Split-fp16 prepared weights: w [K,N] fp32 (row stride ldw) becomes two
+ * fp16 planes hi, lo of shape [N, Kp] (K-major, Kp = inferc_dev_f16_kp(K);
+ * uint16 storage of IEEE half) holding w * 2^s = hi + lo, with the power of
+ * two 2^s chosen on the device so that max|w| 2^s < 2^14; scale2 is a device
+ * array of 2 floats (scale2[1] = 2^-s). Done once per initializer. */
+int64_t inferc_dev_f16_kp(int64_t K);
+int inferc_dev_f16_split(const float* w, int64_t K, int64_t N, int64_t ldw,
+                         uint16_t* hi, uint16_t* lo, float* scale2, void* stream);
+
+/* Prepared-weight GEMM on the fp16 tensor cores with fp32-level accuracy
+ * (three fp16 MMAs per product: lo_a hi_b + hi_a lo_b + hi_a hi_b, A split
+ * on the fly), same epilogue as inferc_dev_gemm_tf32x3. A must be 16-byte
+ * aligned with lda % 4 == 0. A value of A that fp16 cannot carry (|a| >=
+ * 65520, inf, NaN) makes the next inferc_dev_stream_synchronize return
+ * INFERC_ERR_RANGE: the result is invalid and the caller reruns the GEMM
+ * with inferc_dev_gemm_tf32x3. */
+int inferc_dev_gemm_f16s(const float* a, int64_t lda, const uint16_t* hi,
+                         const uint16_t* lo, const float* scale2, const float* bias,
+                         const float* resid, int64_t ldr, float* y, int64_t ldy,
+                         int64_t M, int64_t N, int64_t K, int act, void* stream);
 
 /* FusedQKV + FusedAttention as one call on prepared weights (the encoder
  * plan's attention block): qkv = X Wqkv + bqkv with Wqkv = [Wq | Wk | Wv]

@@ -77,6 +77,9 @@ int inferc_dev_stream_synchronize(void* stream) {
     IDEV_CUDA(cudaStreamSynchronize(as_stream(stream)));
     if (read_and_clear_tc_error())
       throw Error(INFERC_ERR_TIMEOUT, "a tensor-core GEMM wait timed out (results invalid)");
+    if (read_and_clear_f16_range())
+      throw Error(INFERC_ERR_RANGE,
+                  "split-fp16 GEMM: an activation does not fit fp16 (results invalid)");
   });
 }
 
@@ -246,6 +249,38 @@ int inferc_dev_gemm_tf32x3(const float* a, int64_t lda, const float* b_big, cons
     second.resid = y;
     second.ldr = ldy;
     launch_gemm_simt(a, lda, false, b_small, ldb, false, y, ldy, M, N, K, second, st);
+  });
+}
+
+int64_t inferc_dev_f16_kp(int64_t K) { return f16_weight_kp(K); }
+
+int inferc_dev_f16_split(const float* w, int64_t K, int64_t N, int64_t ldw, uint16_t* hi,
+                         uint16_t* lo, float* scale2, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(K > 0 && N > 0 && ldw >= N && w && hi && lo && scale2,
+                   "f16_split: bad arguments");
+    prepare_weight_f16(w, K, N, ldw, hi, lo, scale2, as_stream(stream));
+  });
+}
+
+int inferc_dev_gemm_f16s(const float* a, int64_t lda, const uint16_t* hi, const uint16_t* lo,
+                         const float* scale2, const float* bias, const float* resid, int64_t ldr,
+                         float* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
+                         void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(M >= 0 && N >= 0 && K > 0 && lda >= K && ldy >= N,
+                   "gemm_f16s: bad shape / leading dimensions");
+    IDEV_CHECK_ARG(act >= 0 && act <= 3, "gemm_f16s: unknown activation");
+    IDEV_CHECK_ARG(hi && lo && scale2, "gemm_f16s: null weight");
+    if (M == 0 || N == 0) return;
+    Epilogue ep;
+    ep.bias = bias;
+    ep.bias_mode = bias ? 1 : 0;
+    ep.resid = resid;
+    ep.ldr = ldr;
+    ep.act = act;
+    launch_gemm_f16s(a, lda, hi, lo, f16_weight_kp(K), scale2, nullptr, y, ldy, M, N, K, ep,
+                     as_stream(stream));
   });
 }
 

@@ -1,6 +1,7 @@
 // Shared device helpers and host-side error plumbing for libinferc_b200.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -147,6 +148,28 @@ __device__ __forceinline__ float epilogue_apply(const Epilogue& e, float acc, in
   else if (e.bias_mode == 3) v += e.beta * e.bias[row * e.ldbias + col];
   if (e.resid) v += e.resid[row * e.ldr + col];
   return apply_act(v, e.act);
+}
+
+// fp32 -> fp16 hi / lo planes for the split-fp16 GEMM (gemm_f16s.cu):
+// x = hi + lo with hi = fp16_rn(x), lo = fp16_rn(x - hi). A destination
+// that is null writes nothing. `range` is set to 1 by any value fp16 cannot
+// carry (|x| >= 65520, inf, NaN), which invalidates the split.
+struct SplitOut {
+  uint16_t* hi = nullptr;
+  uint16_t* lo = nullptr;
+  int64_t ld = 0;     // row stride of both planes (elements)
+  int* range = nullptr;
+};
+
+__device__ __forceinline__ uint32_t split_pair(float a, float b, uint32_t& lo_bits, bool& bad) {
+  bad |= !(fabsf(a) < 65520.f) || !(fabsf(b) < 65520.f);
+  uint32_t h, l;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  const float ha = __half2float(__ushort_as_half((unsigned short)(h & 0xFFFFu)));
+  const float hb = __half2float(__ushort_as_half((unsigned short)(h >> 16)));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(l) : "f"(b - hb), "f"(a - ha));
+  lo_bits = l;
+  return h;
 }
 
 }  // namespace inferc_dev

@@ -6,15 +6,18 @@
 namespace inferc_dev {
 
 // ---- layernorm.cu
+// sp: optional fp16 hi / lo split of y for the split-fp16 GEMM.
 void launch_layernorm(const float* x, const float* gamma, const float* beta, float* y,
-                      int64_t rows, int64_t feat, float eps, cudaStream_t st);
+                      int64_t rows, int64_t feat, float eps, cudaStream_t st,
+                      const SplitOut& sp = SplitOut());
 // Encoder embedding: y[b,s,:] = LN(word[ids[b,s]] + pos[s]); cond[b,s] =
 // (mask[b,s] == 0). Out-of-range ids set *err_flag (device int) to 1 and
 // produce a zero row.
 void launch_embed_layernorm(const int64_t* ids, const int64_t* mask, const float* word,
                             const float* pos, int64_t vocab, const float* gamma,
                             const float* beta, float* y, uint8_t* cond, int64_t B,
-                            int64_t S, int64_t H, float eps, int* err_flag, cudaStream_t st);
+                            int64_t S, int64_t H, float eps, int* err_flag, cudaStream_t st,
+                            const SplitOut& sp = SplitOut());
 
 // ---- gemm_simt.cu : C[M,N] = epilogue(op(A) op(B)) on CUDA cores (fp32 FMA).
 void launch_gemm_simt(const float* A, int64_t lda, bool trans_a, const float* B, int64_t ldb,
@@ -42,6 +45,33 @@ struct AttnArgs {
   int causal;                  // 1: additionally mask j > i (prefill)
 };
 void launch_attention(const AttnArgs& a, cudaStream_t st);
+
+// Split-fp16 tensor-core GEMM (gemm_f16s.cu). Weights: fp16 hi / lo planes
+// [N, Kp] (Kp = f16_weight_kp(K)) of W * 2^s and scale2 = {scratch, 2^-s}.
+// range_flag: set to 1 when A holds a value fp16 cannot carry (the result is
+// then invalid; rerun on the 3xTF32 kernel); null = the module-wide flag.
+int64_t f16_weight_kp(int64_t K);
+void prepare_weight_f16(const float* W, int64_t K, int64_t N, int64_t ldw, uint16_t* hi,
+                        uint16_t* lo, float* scale2, cudaStream_t st);
+bool gemm_f16s_supported(const float* A, int64_t lda, int64_t M, int64_t N, int64_t K);
+void launch_gemm_f16s(const float* A, int64_t lda, const uint16_t* Bh, const uint16_t* Bl,
+                      int64_t kp, const float* scale2, int* range_flag, float* C, int64_t ldc,
+                      int64_t M, int64_t N, int64_t K, const Epilogue& ep, cudaStream_t st);
+// A operand of the split-fp16 GEMM: fp32 (a32, split by the kernel) or
+// already split into fp16 hi / lo planes (a32 null).
+struct F16GemmA {
+  const float* a32 = nullptr;
+  const uint16_t* hi = nullptr;
+  const uint16_t* lo = nullptr;
+  int64_t ld = 0;
+};
+// General form: so.hi set = write the result's fp16 split instead of C
+// (pre-split A, bias or bias+GELU epilogue only).
+void launch_gemm_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,
+                      const float* scale2, int* range_flag, float* C, int64_t ldc,
+                      const SplitOut& so, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
+                      cudaStream_t st);
+int read_and_clear_f16_range();
 // Tensor-core path (head_dim 64, S <= 128, 16-byte aligned operands).
 bool attention_tc_supported(const AttnArgs& a);
 void launch_attention_tc(const AttnArgs& a, cudaStream_t st);

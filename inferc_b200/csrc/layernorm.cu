@@ -10,11 +10,13 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 
-// Normalises one row held as VPT float4 per lane; writes y.
+// Normalises one row held as VPT float4 per lane; writes y and, when
+// sp.hi is set, the row's fp16 hi / lo split for the split-fp16 GEMM.
 template <int VPT>
 __device__ __forceinline__ void ln_row_regs(float4 (&v)[VPT], const float* __restrict__ gamma,
                                             const float* __restrict__ beta, float* __restrict__ y,
-                                            int64_t feat, float eps, int lane) {
+                                            int64_t feat, float eps, int lane,
+                                            const SplitOut& sp, int64_t row) {
   float s = 0.0f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
@@ -31,6 +33,9 @@ __device__ __forceinline__ void ln_row_regs(float4 (&v)[VPT], const float* __res
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   const float4* b4 = reinterpret_cast<const float4*>(beta);
   float4* y4 = reinterpret_cast<float4*>(y);
+  bool bad = false;
+  uint2* h2 = sp.hi ? reinterpret_cast<uint2*>(sp.hi + row * sp.ld) : nullptr;
+  uint2* l2 = sp.hi ? reinterpret_cast<uint2*>(sp.lo + row * sp.ld) : nullptr;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = lane + 32 * i;
@@ -41,13 +46,22 @@ __device__ __forceinline__ void ln_row_regs(float4 (&v)[VPT], const float* __res
     o.z = (v[i].z * inv) * g.z + b.z;
     o.w = (v[i].w * inv) * g.w + b.w;
     y4[c] = o;
+    if (h2) {
+      uint2 h, l;
+      h.x = split_pair(o.x, o.y, l.x, bad);
+      h.y = split_pair(o.z, o.w, l.y, bad);
+      h2[c] = h;
+      l2[c] = l;
+    }
   }
+  if (bad) atomicExch(sp.range, 1);
 }
 
 template <int VPT>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     layernorm_warp_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
-                          const float* __restrict__ beta, float* y, int64_t rows, float eps) {
+                          const float* __restrict__ beta, float* y, int64_t rows, float eps,
+                          SplitOut sp) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -56,7 +70,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   float4 v[VPT];
 #pragma unroll
   for (int i = 0; i < VPT; ++i) v[i] = x4[lane + 32 * i];
-  ln_row_regs<VPT>(v, gamma, beta, y + row * feat, feat, eps, lane);
+  ln_row_regs<VPT>(v, gamma, beta, y + row * feat, feat, eps, lane, sp, row);
 }
 
 // Generic path (any feat): one block per row, three sweeps through L1/L2.
@@ -99,10 +113,10 @@ __global__ void layernorm_block_kernel(const float* __restrict__ x, const float*
 
 template <int VPT>
 void launch_warp(const float* x, const float* g, const float* b, float* y, int64_t rows,
-                 float eps, cudaStream_t st) {
+                 float eps, const SplitOut& sp, cudaStream_t st) {
   const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   layernorm_warp_kernel<VPT><<<(unsigned)blocks, kWarpsPerBlock * 32, 0, st>>>(x, g, b, y, rows,
-                                                                                  eps);
+                                                                                  eps, sp);
 }
 
 // Encoder embedding + LayerNorm: one warp per token.
@@ -112,7 +126,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
                     const float* __restrict__ word, const float* __restrict__ pos, int64_t vocab,
                     const float* __restrict__ gamma, const float* __restrict__ beta,
                     float* __restrict__ y, uint8_t* __restrict__ cond, int64_t BS, int64_t S,
-                    float eps, int* err_flag) {
+                    float eps, int* err_flag, SplitOut sp) {
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   if (t >= BS) return;
@@ -124,7 +138,13 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   if (id < 0 || id >= vocab) {
     if (lane == 0) atomicExch(err_flag, 1);
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) y4[lane + 32 * i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < VPT; ++i) {
+      y4[lane + 32 * i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (sp.hi) {
+        reinterpret_cast<uint2*>(sp.hi + t * sp.ld)[lane + 32 * i] = make_uint2(0, 0);
+        reinterpret_cast<uint2*>(sp.lo + t * sp.ld)[lane + 32 * i] = make_uint2(0, 0);
+      }
+    }
     return;
   }
   const float4* w4 = reinterpret_cast<const float4*>(word + id * feat);
@@ -135,25 +155,28 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     const float4 a = __ldg(w4 + lane + 32 * i), b = __ldg(p4 + lane + 32 * i);
     v[i] = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
   }
-  ln_row_regs<VPT>(v, gamma, beta, y + t * feat, feat, eps, lane);
+  ln_row_regs<VPT>(v, gamma, beta, y + t * feat, feat, eps, lane, sp, t);
 }
 
 }  // namespace
 
 void launch_layernorm(const float* x, const float* g, const float* b, float* y, int64_t rows,
-                      int64_t feat, float eps, cudaStream_t st) {
+                      int64_t feat, float eps, cudaStream_t st, const SplitOut& sp) {
   if (rows <= 0) return;
   const bool vec = aligned16(x) && aligned16(y) && aligned16(g) && aligned16(b);
+  IDEV_CHECK_ARG(!sp.hi || (vec && feat % 128 == 0 && feat <= 1024 && sp.lo && sp.range &&
+                            aligned16(sp.hi) && aligned16(sp.lo) && sp.ld % 8 == 0),
+                 "LayerNorm: fp16 split output needs feat % 128 == 0, <= 1024, aligned planes");
   if (vec && feat % 128 == 0 && feat <= 1024) {
     switch (feat / 128) {
-      case 1: launch_warp<1>(x, g, b, y, rows, eps, st); break;
-      case 2: launch_warp<2>(x, g, b, y, rows, eps, st); break;
-      case 3: launch_warp<3>(x, g, b, y, rows, eps, st); break;
-      case 4: launch_warp<4>(x, g, b, y, rows, eps, st); break;
-      case 5: launch_warp<5>(x, g, b, y, rows, eps, st); break;
-      case 6: launch_warp<6>(x, g, b, y, rows, eps, st); break;
-      case 7: launch_warp<7>(x, g, b, y, rows, eps, st); break;
-      default: launch_warp<8>(x, g, b, y, rows, eps, st); break;
+      case 1: launch_warp<1>(x, g, b, y, rows, eps, sp, st); break;
+      case 2: launch_warp<2>(x, g, b, y, rows, eps, sp, st); break;
+      case 3: launch_warp<3>(x, g, b, y, rows, eps, sp, st); break;
+      case 4: launch_warp<4>(x, g, b, y, rows, eps, sp, st); break;
+      case 5: launch_warp<5>(x, g, b, y, rows, eps, sp, st); break;
+      case 6: launch_warp<6>(x, g, b, y, rows, eps, sp, st); break;
+      case 7: launch_warp<7>(x, g, b, y, rows, eps, sp, st); break;
+      default: launch_warp<8>(x, g, b, y, rows, eps, sp, st); break;
     }
   } else {
     layernorm_block_kernel<<<(unsigned)rows, 256, 0, st>>>(x, g, b, y, feat, eps);
@@ -164,13 +187,13 @@ void launch_layernorm(const float* x, const float* g, const float* b, float* y, 
 void launch_embed_layernorm(const int64_t* ids, const int64_t* mask, const float* word,
                             const float* pos, int64_t vocab, const float* g, const float* b,
                             float* y, uint8_t* cond, int64_t B, int64_t S, int64_t H, float eps,
-                            int* err_flag, cudaStream_t st) {
+                            int* err_flag, cudaStream_t st, const SplitOut& sp) {
   IDEV_CHECK_ARG(H % 128 == 0 && H <= 1024, "encoder hidden size must be a multiple of 128, <= 1024");
   const int64_t BS = B * S;
   const unsigned blocks = (unsigned)((BS + kWarpsPerBlock - 1) / kWarpsPerBlock);
 #define IDEV_EMB(V)                                                                         \
   embed_ln_kernel<V><<<blocks, kWarpsPerBlock * 32, 0, st>>>(ids, mask, word, pos, vocab, g, \
-                                                             b, y, cond, BS, S, eps, err_flag)
+                                                             b, y, cond, BS, S, eps, err_flag, sp)
   switch (H / 128) {
     case 1: IDEV_EMB(1); break;
     case 2: IDEV_EMB(2); break;

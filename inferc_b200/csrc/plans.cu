@@ -24,6 +24,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <tuple>
 #include <memory>
 #include <utility>
 #include <vector>
@@ -74,21 +75,31 @@ struct DevArena {
   }
 };
 
-// A GEMM weight for both GEMM paths: fp32 w (the CUDA-core path, and the
-// tensor core's "big" half, which reads only w's top 19 bits) and
-// small = w - trunc13(w), both [K,N] row-major.
+// A GEMM weight for every GEMM path: fp32 w (the CUDA-core path, and the
+// 3xTF32 kernel's "big" half, which reads only w's top 19 bits), small =
+// w - trunc13(w), both [K,N] row-major; and, for the split-fp16 kernel,
+// the fp16 hi / lo planes [N, kp] of w * 2^s with scale2 = {scratch, 2^-s}.
 struct SplitWeight {
   float* w = nullptr;
   float* big = nullptr;
   float* small = nullptr;
+  uint16_t* hi = nullptr;
+  uint16_t* lo = nullptr;
+  float* scale2 = nullptr;
+  int64_t kp = 0;
 };
 
-SplitWeight split_weight(DevArena& m, float* w, size_t n) {
+SplitWeight split_weight(DevArena& m, float* w, int64_t K, int64_t N) {
   SplitWeight s;
   s.w = w;
   s.big = w;
-  s.small = m.alloc<float>(n);
-  launch_split_small(w, s.small, (int64_t)n, nullptr);
+  s.small = m.alloc<float>((size_t)(K * N));
+  launch_split_small(w, s.small, K * N, nullptr);
+  s.kp = f16_weight_kp(K);
+  s.hi = m.alloc<uint16_t>((size_t)(N * s.kp));
+  s.lo = m.alloc<uint16_t>((size_t)(N * s.kp));
+  s.scale2 = m.alloc<float>(2);
+  prepare_weight_f16(w, K, N, N, s.hi, s.lo, s.scale2, nullptr);
   IDEV_CUDA(cudaDeviceSynchronize());
   return s;
 }
@@ -142,11 +153,20 @@ struct InfercEncoderPlan {
   uint8_t* cond;
   float *x, *qkv, *ctx, *t, *hf, *pre, *logits;
   int* err;
-  std::map<std::pair<int64_t, int64_t>, std::unique_ptr<Graph>> graphs;
+  // Split-fp16 GEMM path (default): fp16 hi / lo planes of the GEMM inputs
+  // written by their producers (LayerNorm, the FFN1 epilogue), and the flag
+  // they raise when a value does not fit fp16; the batch is then rerun on
+  // the 3xTF32 path.
+  bool f16 = false;
+  uint16_t *xs_hi = nullptr, *xs_lo = nullptr, *hf_hi = nullptr, *hf_lo = nullptr;
+  int* f16_range = nullptr;
+  int* range_host = nullptr;  // pinned
+  std::map<std::tuple<int64_t, int64_t, bool>, std::unique_ptr<Graph>> graphs;
 
   ~InfercEncoderPlan() {
     graphs.clear();
     if (stream) cudaStreamDestroy(stream);
+    if (range_host) cudaFreeHost(range_host);
   }
 
   static void gemm(const float* A, int64_t lda, const SplitWeight& w, int64_t ldb, float* C,
@@ -155,14 +175,46 @@ struct InfercEncoderPlan {
     launch_gemm_presplit(A, lda, w.w, w.big, w.small, ldb, C, ldc, M, N, K, ep, st);
   }
 
-  void forward(int64_t B, int64_t S, cudaStream_t st) {
+  // fp16 split of a [M, cols] activation (row stride cols) for the split-fp16 GEMM.
+  F16GemmA split_a(const uint16_t* hi, const uint16_t* lo, int64_t cols) const {
+    F16GemmA a;
+    a.hi = hi;
+    a.lo = lo;
+    a.ld = cols;
+    return a;
+  }
+  SplitOut split_out(uint16_t* hi, uint16_t* lo, int64_t cols) const {
+    SplitOut so;
+    so.hi = hi;
+    so.lo = lo;
+    so.ld = cols;
+    so.range = f16_range;
+    return so;
+  }
+  static F16GemmA fp32_a(const float* a, int64_t lda) {
+    F16GemmA r;
+    r.a32 = a;
+    r.ld = lda;
+    return r;
+  }
+  void gemm16(const F16GemmA& A, const SplitWeight& w, float* C, int64_t ldc, const SplitOut& so,
+              int64_t M, int64_t N, int64_t K, const Epilogue& ep, cudaStream_t st) {
+    launch_gemm_f16s(A, w.hi, w.lo, w.kp, w.scale2, f16_range, C, ldc, so, M, N, K, ep, st);
+  }
+
+  void forward(int64_t B, int64_t S, cudaStream_t st, bool use_f16) {
     const int64_t M = B * S;
-    launch_embed_layernorm(ids, mask, word, pos, V, eln_g, eln_b, x, cond, B, S, H, eps, err, st);
+    const SplitOut xs = use_f16 ? split_out(xs_hi, xs_lo, H) : SplitOut();
+    launch_embed_layernorm(ids, mask, word, pos, V, eln_g, eln_b, x, cond, B, S, H, eps, err, st,
+                           xs);
     for (int64_t l = 0; l < L; ++l) {
       Epilogue e_qkv;
       e_qkv.bias = bqkv[l];
       e_qkv.bias_mode = 1;
-      gemm(x, H, wqkv[l], 3 * H, qkv, 3 * H, M, 3 * H, H, e_qkv, st);
+      if (use_f16)
+        gemm16(split_a(xs_hi, xs_lo, H), wqkv[l], qkv, 3 * H, SplitOut(), M, 3 * H, H, e_qkv, st);
+      else
+        gemm(x, H, wqkv[l], 3 * H, qkv, 3 * H, M, 3 * H, H, e_qkv, st);
       AttnArgs a{};
       a.q = qkv; a.k = qkv + H; a.v = qkv + 2 * H; a.out = ctx;
       a.ldq = a.ldk = a.ldv = 3 * H;
@@ -180,20 +232,30 @@ struct InfercEncoderPlan {
       e_o.bias_mode = 1;
       e_o.resid = x;
       e_o.ldr = H;
-      gemm(ctx, H, wo[l], H, t, H, M, H, H, e_o, st);
-      launch_layernorm(t, ln1g[l], ln1b[l], x, M, H, eps, st);
+      if (use_f16)
+        gemm16(fp32_a(ctx, H), wo[l], t, H, SplitOut(), M, H, H, e_o, st);
+      else
+        gemm(ctx, H, wo[l], H, t, H, M, H, H, e_o, st);
+      launch_layernorm(t, ln1g[l], ln1b[l], x, M, H, eps, st, xs);
       Epilogue e_1;
       e_1.bias = b1[l];
       e_1.bias_mode = 1;
       e_1.act = ACT_GELU_ERF;
-      gemm(x, H, w1[l], F, hf, F, M, F, H, e_1, st);
+      if (use_f16)  // FFN1's output only feeds FFN2: store its fp16 split only
+        gemm16(split_a(xs_hi, xs_lo, H), w1[l], hf, F, split_out(hf_hi, hf_lo, F), M, F, H, e_1,
+               st);
+      else
+        gemm(x, H, w1[l], F, hf, F, M, F, H, e_1, st);
       Epilogue e_2;
       e_2.bias = b2[l];
       e_2.bias_mode = 1;
       e_2.resid = x;
       e_2.ldr = H;
-      gemm(hf, F, w2[l], H, t, H, M, H, F, e_2, st);
-      launch_layernorm(t, ln2g[l], ln2b[l], x, M, H, eps, st);
+      if (use_f16)
+        gemm16(split_a(hf_hi, hf_lo, F), w2[l], t, H, SplitOut(), M, H, F, e_2, st);
+      else
+        gemm(hf, F, w2[l], H, t, H, M, H, F, e_2, st);
+      launch_layernorm(t, ln2g[l], ln2b[l], x, M, H, eps, st, xs);
     }
     // Gather(CLS) -> Gemm(transB=1) + Relu -> Gemm(transB=1): the CLS rows
     // are rows b*S of x, read through lda = S*H.
@@ -208,15 +270,15 @@ struct InfercEncoderPlan {
     launch_gemm_simt(pre, H, false, cls_w, H, true, logits, C, B, C, H, e_c, st);
   }
 
-  Graph& graph_for(int64_t B, int64_t S) {
-    auto key = std::make_pair(B, S);
+  Graph& graph_for(int64_t B, int64_t S, bool use_f16) {
+    auto key = std::make_tuple(B, S, use_f16);
     auto it = graphs.find(key);
     if (it != graphs.end()) return *it->second;
     // Eager run first: configures kernel attributes outside the capture and
     // surfaces launch errors with a clear message.
-    forward(B, S, stream);
+    forward(B, S, stream, use_f16);
     IDEV_CUDA(cudaStreamSynchronize(stream));
-    auto g = capture(stream, [&] { forward(B, S, stream); });
+    auto g = capture(stream, [&] { forward(B, S, stream, use_f16); });
     Graph& ref = *g;
     graphs[key] = std::move(g);
     return ref;
@@ -230,9 +292,22 @@ struct InfercEncoderPlan {
 
   // Inputs already in plan buffers `ids`, `mask`; runs on `st` after the plan
   // stream's previous work.
+  // With the split-fp16 path this waits for the batch on `st`, to check the
+  // range flag (and rerun the batch on the 3xTF32 path when it is set).
   void run_graph(int64_t B, int64_t S, cudaStream_t st) {
-    Graph& g = graph_for(B, S);
+    if (!f16) {
+      IDEV_CUDA(cudaGraphLaunch(graph_for(B, S, false).exec, st));
+      return;
+    }
+    Graph& g = graph_for(B, S, true);
+    IDEV_CUDA(cudaMemsetAsync(f16_range, 0, sizeof(int), st));
     IDEV_CUDA(cudaGraphLaunch(g.exec, st));
+    IDEV_CUDA(cudaMemcpyAsync(range_host, f16_range, sizeof(int), cudaMemcpyDeviceToHost, st));
+    IDEV_CUDA(cudaStreamSynchronize(st));
+    if (*range_host) IDEV_CUDA(cudaGraphLaunch(graph_for(B, S, false).exec, st));
+  }
+  void prepare(int64_t B, int64_t S) {
+    graph_for(B, S, f16);
   }
 };
 
@@ -263,15 +338,15 @@ static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t 
         std::memcpy(&cat[(size_t)(k * 3 * H + i * H)], parts[i] + k * H, H * sizeof(float));
       std::memcpy(&bcat[(size_t)(i * H)], bparts[i], H * sizeof(float));
     }
-    p->wqkv.push_back(split_weight(m, m.upload(cat.data(), cat.size(), "wqkv"), cat.size()));
+    p->wqkv.push_back(split_weight(m, m.upload(cat.data(), cat.size(), "wqkv"), H, 3 * H));
     p->bqkv.push_back(m.upload(bcat.data(), bcat.size(), "bqkv"));
-    p->wo.push_back(split_weight(m, m.upload(w->wo[l], (size_t)H * H, "wo"), (size_t)H * H));
+    p->wo.push_back(split_weight(m, m.upload(w->wo[l], (size_t)H * H, "wo"), H, H));
     p->bo.push_back(m.upload(w->bo[l], H, "bo"));
     p->ln1g.push_back(m.upload(w->ln1_g[l], H, "ln1_g"));
     p->ln1b.push_back(m.upload(w->ln1_b[l], H, "ln1_b"));
-    p->w1.push_back(split_weight(m, m.upload(w->w1[l], (size_t)H * F, "w1"), (size_t)H * F));
+    p->w1.push_back(split_weight(m, m.upload(w->w1[l], (size_t)H * F, "w1"), H, F));
     p->b1.push_back(m.upload(w->b1[l], F, "b1"));
-    p->w2.push_back(split_weight(m, m.upload(w->w2[l], (size_t)F * H, "w2"), (size_t)F * H));
+    p->w2.push_back(split_weight(m, m.upload(w->w2[l], (size_t)F * H, "w2"), F, H));
     p->b2.push_back(m.upload(w->b2[l], H, "b2"));
     p->ln2g.push_back(m.upload(w->ln2_g[l], H, "ln2_g"));
     p->ln2b.push_back(m.upload(w->ln2_b[l], H, "ln2_b"));
@@ -292,6 +367,19 @@ static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t 
   p->logits = m.alloc<float>((size_t)maxB * p->C);
   p->err = m.alloc<int>(1);
   IDEV_CUDA(cudaMemset(p->err, 0, sizeof(int)));
+  // Split-fp16 GEMMs unless INFERC_ENCODER_GEMM=tf32x3 (or the shapes do not
+  // fit the fp16 producers: LayerNorm rows of 128k <= 1024 floats).
+  const char* mode = std::getenv("INFERC_ENCODER_GEMM");
+  p->f16 = !(mode && std::string(mode) == "tf32x3") && H % 128 == 0 && H <= 1024 && F % 16 == 0;
+  if (p->f16) {
+    p->xs_hi = m.alloc<uint16_t>((size_t)M * H);
+    p->xs_lo = m.alloc<uint16_t>((size_t)M * H);
+    p->hf_hi = m.alloc<uint16_t>((size_t)M * F);
+    p->hf_lo = m.alloc<uint16_t>((size_t)M * F);
+    p->f16_range = m.alloc<int>(1);
+    IDEV_CUDA(cudaMemset(p->f16_range, 0, sizeof(int)));
+    IDEV_CUDA(cudaMallocHost(&p->range_host, sizeof(int)));
+  }
   IDEV_CUDA(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
 }
 
@@ -645,7 +733,7 @@ int inferc_dev_encoder_run(inferc_encoder_t p, const int64_t* ids, const int64_t
     IDEV_CHECK_ARG(p != nullptr, "encoder_run: null plan");
     p->check_shape(B, S);
     cudaStream_t st = as_stream(stream);
-    p->graph_for(B, S);
+    p->prepare(B, S);
     IDEV_CUDA(cudaMemcpyAsync(p->ids, ids, B * S * sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
     IDEV_CUDA(cudaMemcpyAsync(p->mask, mask, B * S * sizeof(int64_t), cudaMemcpyDeviceToDevice,
                               st));
@@ -661,7 +749,7 @@ int inferc_dev_encoder_run_host(inferc_encoder_t p, const int64_t* ids, const in
     IDEV_CHECK_ARG(p != nullptr, "encoder_run_host: null plan");
     p->check_shape(B, S);
     cudaStream_t st = p->stream;
-    p->graph_for(B, S);
+    p->prepare(B, S);
     IDEV_CUDA(cudaMemcpyAsync(p->ids, ids, B * S * sizeof(int64_t), cudaMemcpyHostToDevice, st));
     IDEV_CUDA(cudaMemcpyAsync(p->mask, mask, B * S * sizeof(int64_t), cudaMemcpyHostToDevice, st));
     p->run_graph(B, S, st);

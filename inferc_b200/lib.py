@@ -47,6 +47,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "inferc_dev_tf32_split": ([_p, _p, _p, _i64, _p], _i),
     "inferc_dev_gemm_tf32x3": ([_p, _i64, _p, _p, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64,
                                 _i, _p], _i),
+    "inferc_dev_f16_kp": ([_i64], _i64),
+    "inferc_dev_f16_split": ([_p, _i64, _i64, _i64, _p, _p, _p, _p], _i),
+    "inferc_dev_gemm_f16s": ([_p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i,
+                              _p], _i),
     "inferc_dev_qkv_attention": ([_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _p, _p, _p],
                                  _i),
     "inferc_dev_gemv": ([_p, _p, _p, _p, _p, _i64, _i64, _i, _p], _i),

@@ -1,0 +1,110 @@
+"""Split-fp16 tensor-core GEMM (tcgen05 kind::f16, three MMAs per product):
+fp32-level accuracy against a float64 reference on tile-aligned and ragged
+shapes, each epilogue, weights of very different scales, and the range flag
+raised by an activation that fp16 cannot carry."""
+import numpy as np
+import pytest
+import torch
+
+from inferc_b200 import lib
+
+pytestmark = pytest.mark.gpu
+
+# Same bar as the 3xTF32 kernel: max error relative to max |C| (the tensor
+# core's fp32 accumulation dominates, ~2e-5 at K=3072).
+TC_REL_TOL = 3e-5
+
+
+def _prep(L, w):
+    K, N = w.shape
+    kp = L.inferc_dev_f16_kp(K)
+    hi = torch.empty((N, kp), dtype=torch.int16, device="cuda")
+    lo = torch.empty((N, kp), dtype=torch.int16, device="cuda")
+    sc = torch.empty(2, dtype=torch.float32, device="cuda")
+    lib.check(L.inferc_dev_f16_split(w.data_ptr(), K, N, N, hi.data_ptr(), lo.data_ptr(),
+                                     sc.data_ptr(), None))
+    return hi, lo, sc
+
+
+def _gemm(L, a, prep, N, bias=None, resid=None, act=0):
+    hi, lo, sc = prep
+    M, K = a.shape
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    lib.check(L.inferc_dev_gemm_f16s(a.data_ptr(), K, hi.data_ptr(), lo.data_ptr(), sc.data_ptr(),
+                                     bias.data_ptr() if bias is not None else None,
+                                     resid.data_ptr() if resid is not None else None, N,
+                                     y.data_ptr(), N, M, N, K, act, None))
+    return y
+
+
+def _rel_err(got, ref):
+    return float(np.abs(got - ref).max() / (np.abs(ref).max() + 1e-30))
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 64, 256), (256, 768, 3072), (512, 3072, 768),
+                                   (300, 100, 200), (4096, 768, 2304), (257, 36, 33),
+                                   (1, 768, 768), (32768, 768, 768)])
+def test_f16s_fp32_accuracy(M, K, N):
+    L = lib.load()
+    rng = np.random.default_rng(M + K + N)
+    a = rng.standard_normal((M, K), dtype=np.float32)
+    w = (rng.standard_normal((K, N), dtype=np.float32) * 0.02).astype(np.float32)
+    ta, tw = torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda()
+    y = _gemm(L, ta, _prep(L, tw), N)
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    ref = (ta.double() @ tw.double()).cpu().numpy()
+    assert _rel_err(y.cpu().numpy(), ref) < TC_REL_TOL
+
+
+@pytest.mark.parametrize("wscale,ascale", [(1e-4, 1.0), (30.0, 1e-3), (0.02, 100.0)])
+def test_f16s_operand_scales(wscale, ascale):
+    """Small and large weights (the power-of-two prescale) and activations far
+    from 1 (small ones lean on fp16 subnormals for lo)."""
+    L = lib.load()
+    rng = np.random.default_rng(7)
+    M, K, N = 512, 768, 512
+    a = (rng.standard_normal((M, K)) * ascale).astype(np.float32)
+    w = (rng.standard_normal((K, N)) * wscale).astype(np.float32)
+    ta, tw = torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda()
+    y = _gemm(L, ta, _prep(L, tw), N)
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    ref = (ta.double() @ tw.double()).cpu().numpy()
+    assert _rel_err(y.cpu().numpy(), ref) < TC_REL_TOL
+
+
+def test_f16s_epilogues():
+    L = lib.load()
+    rng = np.random.default_rng(3)
+    M, K, N = 1024, 768, 3072
+    a = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+    w = torch.from_numpy(rng.standard_normal((K, N), dtype=np.float32) * 0.02).cuda()
+    b = torch.from_numpy(rng.standard_normal(N, dtype=np.float32) * 0.1).cuda()
+    r = torch.from_numpy(rng.standard_normal((M, N), dtype=np.float32)).cuda()
+    prep = _prep(L, w)
+    v = a.double() @ w.double() + b.double()
+    y = _gemm(L, a, prep, N, bias=b, act=1)
+    ref = v * 0.5 * (1 + torch.erf(v / 2 ** 0.5))
+    assert (y.double() - ref).abs().max().item() < 3e-5
+    y = _gemm(L, a, prep, N, bias=b, resid=r)
+    assert (y.double() - (v + r.double())).abs().max().item() < 3e-5
+    lib.check(L.inferc_dev_stream_synchronize(None))
+
+
+def test_f16s_range_flag():
+    """An activation beyond fp16's range is reported at the next synchronize
+    (INFERC_ERR_RANGE) and the flag is cleared; a following in-range call is
+    clean again."""
+    L = lib.load()
+    rng = np.random.default_rng(5)
+    M, K, N = 256, 128, 256
+    a = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+    w = torch.from_numpy(rng.standard_normal((K, N), dtype=np.float32)).cuda()
+    prep = _prep(L, w)
+    bad = a.clone()
+    bad[17, 5] = 1.0e6
+    _gemm(L, bad, prep, N)
+    assert L.inferc_dev_stream_synchronize(None) == 5
+    y = _gemm(L, a, prep, N)
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    ref = (a.double() @ w.double()).cpu().numpy()
+    assert _rel_err(y.cpu().numpy(), ref) < TC_REL_TOL

@@ -76,6 +76,36 @@ def test_encoder_sub_batch_shapes(full_encoder, enc_gold):
     np.testing.assert_allclose(full_encoder.run_host(ids, mask), ref, atol=LOGIT_TOL)
 
 
+def test_encoder_tf32x3_gemm_mode(enc_gold, monkeypatch):
+    """INFERC_ENCODER_GEMM=tf32x3 selects the 3xTF32 GEMMs (the split-fp16
+    path's fallback) at plan creation; same logits bar."""
+    monkeypatch.setenv("INFERC_ENCODER_GEMM", "tf32x3")
+    cfg = synth.EncoderConfig()
+    p = plans.EncoderPlan(cfg, synth.encoder_weights(cfg, seed=0), max_batch=8, max_seq=128)
+    got = p.run_host(enc_gold["c4_ids"], enc_gold["c4_mask"])
+    np.testing.assert_allclose(got, enc_gold["c4_logits"], atol=LOGIT_TOL, rtol=0)
+
+
+def test_encoder_fp16_range_fallback():
+    """Activations beyond fp16's range (embedding LayerNorm gamma = 1e5) raise
+    the split-fp16 range flag; the plan reruns the batch on the 3xTF32 GEMMs
+    and the logits still match the reference."""
+    cfg = synth.EncoderConfig(**make_golden.SMALL_ENC)
+    w = synth.encoder_weights(cfg, seed=9)
+    w["emb_ln_g"] = np.full_like(w["emb_ln_g"], 1e5)
+    rng = np.random.default_rng(9)
+    B, S = 3, 32
+    ids = rng.integers(0, cfg.vocab, size=(B, S)).astype(np.int64)
+    mask = np.ones((B, S), np.int64)
+    mask[1, 20:] = 0
+    from inferc_b200 import structs
+    ref = oracle.port().encoder_forward(structs.encoder_struct(cfg, w), ids, mask, 2)
+    p = plans.EncoderPlan(cfg, w, max_batch=4, max_seq=64)
+    for _ in range(2):
+        got = p.run_host(ids, mask)
+        np.testing.assert_allclose(got, ref, atol=LOGIT_TOL, rtol=1e-4)
+
+
 def test_encoder_errors(full_encoder, enc_gold):
     ids = enc_gold["c0_ids"].copy()
     ids[0, 5] = 10 ** 6  # Gather index out of range (embedding.cc:63-65)
