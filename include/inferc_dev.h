@@ -157,6 +157,23 @@ int inferc_dev_gemm_f16s(const float* a, int64_t lda, const uint16_t* hi,
                          const float* resid, int64_t ldr, float* y, int64_t ldy,
                          int64_t M, int64_t N, int64_t K, int act, void* stream);
 
+/* Activation split for chains of split-fp16 GEMMs: x [rows, cols] fp32
+ * (row stride ldx) -> hi, lo fp16 planes (row stride ld); cols, ldx, ld
+ * even. Out-of-range values are reported like inferc_dev_gemm_f16s's. */
+int inferc_dev_f16_split_rows(const float* x, int64_t rows, int64_t cols, int64_t ldx,
+                              uint16_t* hi, uint16_t* lo, int64_t ld, void* stream);
+
+/* inferc_dev_gemm_f16s with A given as its fp16 planes (a_hi, a_lo, row
+ * stride lda, a multiple of 8, 16-byte aligned) — the form the encoder plan
+ * runs, A split by its producer. When y_hi / y_lo are non-NULL the result is
+ * stored as its fp16 split (row stride ldy) instead of y, for the next GEMM
+ * of a chain; that form takes a bias (act 0 or 1), no resid, N % 16 == 0. */
+int inferc_dev_gemm_f16s_planes(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda,
+                                const uint16_t* hi, const uint16_t* lo, const float* scale2,
+                                const float* bias, const float* resid, int64_t ldr, float* y,
+                                uint16_t* y_hi, uint16_t* y_lo, int64_t ldy, int64_t M,
+                                int64_t N, int64_t K, int act, void* stream);
+
 /* FusedQKV + FusedAttention as one call on prepared weights (the encoder
  * plan's attention block): qkv = X Wqkv + bqkv with Wqkv = [Wq | Wk | Wv]
  * ([H, 3H], split by inferc_dev_tf32_split into w_big / w_small) and bqkv

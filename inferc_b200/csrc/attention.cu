@@ -406,6 +406,7 @@ void launch_attention(const AttnArgs& a, cudaStream_t st) {
     launch_attention_tc(a, st);
     return;
   }
+  IDEV_CHECK_ARG(a.so.hi == nullptr, "FusedAttention: fp16 split output needs the tensor-core path");
   const bool fast = a.hd == HD && aligned16(a.q) && aligned16(a.k) && aligned16(a.v) &&
                     aligned16(a.out) && a.ldq % 4 == 0 && a.ldk % 4 == 0 && a.ldv % 4 == 0 &&
                     a.ldo % 4 == 0 && a.bstride_q % 4 == 0 && a.bstride_k % 4 == 0 &&

@@ -17,7 +17,8 @@
 //      written into shared memory in the K-major UMMA layout, over the Q/K
 //      tiles that step 3 has finished reading.
 //   5. O = P V: 16 k-steps x 3 tcgen05.mma (M=128, N=64) into TMEM.
-//   6. O is loaded from TMEM and stored to the [B, S, H] output.
+//   6. O is loaded from TMEM and stored to the [B, S, H] output (or, for a
+//      following split-fp16 GEMM, as its fp16 hi / lo planes).
 // Waits are bounded; on a timeout the CTA flags g_attn_tc_error, frees its TMEM
 // and exits.
 #include <cstdlib>
@@ -54,6 +55,7 @@ struct AttnTcArgs {
   float scale, fill;
   float* out;
   int64_t ldo, bstride_o;
+  SplitOut so;
 };
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -242,17 +244,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (ok) {
     tc_fence_after();
     // O columns [32 * half, 32 * half + 32) of row `row`
-    float* dst = a.out + (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + h * kHd + 32 * half;
+    const int64_t col = h * kHd + 32 * half;
+    float* dst = a.out + (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + col;
+    bool bad = false;
 #pragma unroll
     for (int c0 = 0; c0 < 32; c0 += 16) {
       float v[16];
       tmem_ld16(tmem + lane_base + kRows + (uint32_t)(32 * half + c0), v);
-      if (row < a.S) {
+      if (row >= a.S) continue;
+      if (a.so.hi) {  // fp16 hi / lo planes with the layout of out
+        uint32_t hw[8], lw[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) hw[q] = split_pair(v[2 * q], v[2 * q + 1], lw[q], bad);
+        const int64_t o = (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + col + c0;
+        uint4* hp = reinterpret_cast<uint4*>(a.so.hi + o);
+        uint4* lp = reinterpret_cast<uint4*>(a.so.lo + o);
+        hp[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        hp[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        lp[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        lp[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+      } else {
 #pragma unroll
         for (int q = 0; q < 16; q += 4)
           *reinterpret_cast<float4*>(dst + c0 + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
       }
     }
+    if (bad) atomicExch(a.so.range, 1);
   } else if (tid == 0) {
     atomicExch(&g_attn_tc_error, 1);
   }
@@ -331,6 +348,9 @@ void launch_attention_tc(const AttnArgs& a, cudaStream_t st) {
   t.out = a.out;
   t.ldo = a.ldo;
   t.bstride_o = a.bstride_o;
+  t.so = a.so;
+  IDEV_CHECK_ARG(!a.so.hi || (a.so.lo && a.so.range && aligned16(a.so.hi) && aligned16(a.so.lo)),
+                 "FusedAttention: fp16 split output needs aligned planes and a range flag");
   IDEV_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kSmemBytes));
   dim3 grid(1, (unsigned)a.nH, (unsigned)a.B);

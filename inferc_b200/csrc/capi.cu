@@ -284,6 +284,49 @@ int inferc_dev_gemm_f16s(const float* a, int64_t lda, const uint16_t* hi, const 
   });
 }
 
+int inferc_dev_f16_split_rows(const float* x, int64_t rows, int64_t cols, int64_t ldx,
+                              uint16_t* hi, uint16_t* lo, int64_t ld, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(rows == 0 || (x && hi && lo), "f16_split_rows: null pointer");
+    launch_split_rows_f16(x, rows, cols, ldx, hi, lo, ld, nullptr, as_stream(stream));
+  });
+}
+
+int inferc_dev_gemm_f16s_planes(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda,
+                                const uint16_t* hi, const uint16_t* lo, const float* scale2,
+                                const float* bias, const float* resid, int64_t ldr, float* y,
+                                uint16_t* y_hi, uint16_t* y_lo, int64_t ldy, int64_t M,
+                                int64_t N, int64_t K, int act, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(M >= 0 && N >= 0 && K > 0 && lda >= K && ldy >= N,
+                   "gemm_f16s_planes: bad shape / leading dimensions");
+    IDEV_CHECK_ARG(act >= 0 && act <= 3, "gemm_f16s_planes: unknown activation");
+    IDEV_CHECK_ARG(hi && lo && scale2 && a_hi && a_lo, "gemm_f16s_planes: null operand");
+    IDEV_CHECK_ARG((y_hi == nullptr) == (y_lo == nullptr) && (y_hi || y),
+                   "gemm_f16s_planes: give y, or both y_hi and y_lo");
+    if (M == 0 || N == 0) return;
+    Epilogue ep;
+    ep.bias = bias;
+    ep.bias_mode = bias ? 1 : 0;
+    ep.resid = resid;
+    ep.ldr = ldr;
+    ep.act = act;
+    F16GemmA a;
+    a.hi = a_hi;
+    a.lo = a_lo;
+    a.ld = lda;
+    SplitOut so;
+    if (y_hi) {
+      so.hi = y_hi;
+      so.lo = y_lo;
+      so.ld = ldy;
+      so.range = f16_range_flag_ptr();
+    }
+    launch_gemm_f16s(a, hi, lo, f16_weight_kp(K), scale2, nullptr, y, ldy, so, M, N, K, ep,
+                     as_stream(stream));
+  });
+}
+
 int inferc_dev_qkv_attention(const float* x, const float* w_big, const float* w_small,
                              const float* bqkv, const uint8_t* key_mask, int64_t B, int64_t S,
                              int64_t H, int64_t head_dim, float fill, float* scratch_qkv,

@@ -386,10 +386,11 @@ __global__ void absmax_kernel(const float* __restrict__ w, int64_t rows, int64_t
   if ((threadIdx.x & 31) == 0) atomicMax(out_bits, __float_as_uint(m));  // m >= 0
 }
 
-// W [K, N] fp32 (row stride ldw) -> hi, lo [N, Kp] fp16 of W * 2^s, with
-// columns K..Kp-1 zero; writes 2^-s to *inv_scale.
+// W [K, N] fp32 (row stride ldw; trans: W is [N, K]) -> hi, lo [N, Kp]
+// fp16 of W * 2^s, with columns K..Kp-1 zero; writes 2^-s to *inv_scale.
 __global__ void split_weight_f16_kernel(const float* __restrict__ w, int64_t K, int64_t N,
-                                        int64_t ldw, int64_t kp, const unsigned int* amax_bits,
+                                        int64_t ldw, bool trans, int64_t kp,
+                                        const unsigned int* amax_bits,
                                         __half* __restrict__ hi, __half* __restrict__ lo,
                                         float* __restrict__ inv_scale) {
   __shared__ float tile[32][33];
@@ -403,7 +404,11 @@ __global__ void split_weight_f16_kernel(const float* __restrict__ w, int64_t K, 
   const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int64_t k = k0 + i, n = n0 + threadIdx.x;
-    tile[i][threadIdx.x] = (k < K && n < N) ? w[k * ldw + n] * scale : 0.f;
+    const int64_t kt = k0 + threadIdx.x, nt = n0 + i;  // transposed source: coalesced in k
+    if (trans)
+      tile[threadIdx.x][i] = (kt < K && nt < N) ? w[nt * ldw + kt] * scale : 0.f;
+    else
+      tile[i][threadIdx.x] = (k < K && n < N) ? w[k * ldw + n] * scale : 0.f;
   }
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -415,6 +420,23 @@ __global__ void split_weight_f16_kernel(const float* __restrict__ w, int64_t K, 
       lo[n * kp + k] = __float2half_rn(v - __half2float(h));
     }
   }
+}
+
+// x [rows, cols] fp32 (row stride ldx) -> fp16 hi / lo planes (row stride ld).
+__global__ void split_rows_f16_kernel(const float* __restrict__ x, int64_t rows, int64_t cols,
+                                      int64_t ldx, uint16_t* __restrict__ hi,
+                                      uint16_t* __restrict__ lo, int64_t ld, int* range) {
+  bool bad = false;
+  const int64_t pairs = cols / 2, n = rows * pairs;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / pairs, c = 2 * (i % pairs);
+    uint32_t l;
+    const uint32_t h = split_pair(x[r * ldx + c], x[r * ldx + c + 1], l, bad);
+    *reinterpret_cast<uint32_t*>(hi + r * ld + c) = h;
+    *reinterpret_cast<uint32_t*>(lo + r * ld + c) = l;
+  }
+  if (bad) atomicExch(range, 1);
 }
 
 // ------------------------------------------------------------ host side
@@ -501,19 +523,19 @@ int read_and_clear(const void* sym) {
 int64_t f16_weight_kp(int64_t K) { return (K + 7) / 8 * 8; }
 
 void prepare_weight_f16(const float* W, int64_t K, int64_t N, int64_t ldw, uint16_t* hi_u,
-                        uint16_t* lo_u, float* scale2, cudaStream_t st) {
+                        uint16_t* lo_u, float* scale2, cudaStream_t st, bool trans) {
   __half* hi = reinterpret_cast<__half*>(hi_u);
   __half* lo = reinterpret_cast<__half*>(lo_u);
-  IDEV_CHECK_ARG(K >= 1 && N >= 1 && ldw >= N, "split fp16 weight: bad shape");
+  IDEV_CHECK_ARG(K >= 1 && N >= 1 && ldw >= (trans ? K : N), "split fp16 weight: bad shape");
   IDEV_CUDA(cudaMemsetAsync(scale2, 0, sizeof(float), st));
   unsigned int* amax = reinterpret_cast<unsigned int*>(scale2);
   const int64_t n = K * N;
-  absmax_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, st>>>(W, K, N,
-                                                                                         ldw, amax);
+  absmax_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, st>>>(
+      W, trans ? N : K, trans ? K : N, ldw, amax);
   IDEV_LAUNCHED();
   const int64_t kp = f16_weight_kp(K);
   dim3 grid((unsigned)((N + 31) / 32), (unsigned)((kp + 31) / 32));
-  split_weight_f16_kernel<<<grid, dim3(32, 8), 0, st>>>(W, K, N, ldw, kp, amax, hi, lo,
+  split_weight_f16_kernel<<<grid, dim3(32, 8), 0, st>>>(W, K, N, ldw, trans, kp, amax, hi, lo,
                                                         scale2 + 1);
   IDEV_LAUNCHED();
 }
@@ -584,6 +606,25 @@ void launch_gemm_f16s(const float* A, int64_t lda, const uint16_t* Bh, const uin
   a.a32 = A;
   a.ld = lda;
   launch_gemm_f16s(a, Bh, Bl, kp, scale2, range_flag, C, ldc, SplitOut(), M, N, K, ep, st);
+}
+
+void launch_split_rows_f16(const float* x, int64_t rows, int64_t cols, int64_t ldx, uint16_t* hi,
+                           uint16_t* lo, int64_t ld, int* range, cudaStream_t st) {
+  IDEV_CHECK_ARG(rows >= 0 && cols > 0 && cols % 2 == 0 && ldx >= cols && ld >= cols &&
+                     ldx % 2 == 0 && ld % 2 == 0,
+                 "f16 split of rows: cols, ldx and ld must be even");
+  if (rows == 0) return;
+  if (!range) IDEV_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&range), g_f16_range));
+  const int64_t n = rows * (cols / 2);
+  split_rows_f16_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(
+      x, rows, cols, ldx, hi, lo, ld, range);
+  IDEV_LAUNCHED();
+}
+
+int* f16_range_flag_ptr() {
+  int* p = nullptr;
+  IDEV_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_f16_range));
+  return p;
 }
 
 int read_and_clear_f16_error() { return read_and_clear(&g_f16_error); }

@@ -43,6 +43,7 @@ struct AttnArgs {
   int64_t B, S, nH, hd;
   float scale, fill;
   int causal;                  // 1: additionally mask j > i (prefill)
+  SplitOut so;                 // tensor-core path only: write out's fp16 split instead
 };
 void launch_attention(const AttnArgs& a, cudaStream_t st);
 
@@ -51,8 +52,9 @@ void launch_attention(const AttnArgs& a, cudaStream_t st);
 // range_flag: set to 1 when A holds a value fp16 cannot carry (the result is
 // then invalid; rerun on the 3xTF32 kernel); null = the module-wide flag.
 int64_t f16_weight_kp(int64_t K);
+// trans: W is stored [N, K] (the transB operand of a Gemm).
 void prepare_weight_f16(const float* W, int64_t K, int64_t N, int64_t ldw, uint16_t* hi,
-                        uint16_t* lo, float* scale2, cudaStream_t st);
+                        uint16_t* lo, float* scale2, cudaStream_t st, bool trans = false);
 bool gemm_f16s_supported(const float* A, int64_t lda, int64_t M, int64_t N, int64_t K);
 void launch_gemm_f16s(const float* A, int64_t lda, const uint16_t* Bh, const uint16_t* Bl,
                       int64_t kp, const float* scale2, int* range_flag, float* C, int64_t ldc,
@@ -72,10 +74,17 @@ void launch_gemm_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl,
                       const SplitOut& so, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
                       cudaStream_t st);
 int read_and_clear_f16_range();
+int* f16_range_flag_ptr();  // the current device's module-wide range flag
+// x [rows, cols] -> fp16 hi / lo planes; range null = the module-wide flag.
+void launch_split_rows_f16(const float* x, int64_t rows, int64_t cols, int64_t ldx, uint16_t* hi,
+                           uint16_t* lo, int64_t ld, int* range, cudaStream_t st);
 // Tensor-core path (head_dim 64, S <= 128, 16-byte aligned operands).
 bool attention_tc_supported(const AttnArgs& a);
 void launch_attention_tc(const AttnArgs& a, cudaStream_t st);
 bool attention_tc_enabled();
+inline bool attention_tc_usable(const AttnArgs& a) {
+  return attention_tc_supported(a) && attention_tc_enabled();
+}
 
 void launch_kv_append(const float* k_new, const float* v_new, int64_t ld_new, float* kc,
                       float* vc, int64_t heads, int64_t hd, int64_t max_len,

@@ -89,6 +89,20 @@ struct SplitWeight {
   int64_t kp = 0;
 };
 
+// The transB weight of a Gemm (w stored [N, K]): fp32 w for the CUDA-core
+// path and the split-fp16 planes, no tf32 small half.
+SplitWeight split_weight_t(DevArena& m, float* w, int64_t K, int64_t N) {
+  SplitWeight s;
+  s.w = w;
+  s.kp = f16_weight_kp(K);
+  s.hi = m.alloc<uint16_t>((size_t)(N * s.kp));
+  s.lo = m.alloc<uint16_t>((size_t)(N * s.kp));
+  s.scale2 = m.alloc<float>(2);
+  prepare_weight_f16(w, K, N, K, s.hi, s.lo, s.scale2, nullptr, /*trans=*/true);
+  IDEV_CUDA(cudaDeviceSynchronize());
+  return s;
+}
+
 SplitWeight split_weight(DevArena& m, float* w, int64_t K, int64_t N) {
   SplitWeight s;
   s.w = w;
@@ -159,6 +173,8 @@ struct InfercEncoderPlan {
   // the 3xTF32 path.
   bool f16 = false;
   uint16_t *xs_hi = nullptr, *xs_lo = nullptr, *hf_hi = nullptr, *hf_lo = nullptr;
+  uint16_t *ctx_hi = nullptr, *ctx_lo = nullptr;
+  SplitWeight pre16, cls16;
   int* f16_range = nullptr;
   int* range_host = nullptr;  // pinned
   std::map<std::tuple<int64_t, int64_t, bool>, std::unique_ptr<Graph>> graphs;
@@ -226,6 +242,10 @@ struct InfercEncoderPlan {
       a.B = B; a.S = S; a.nH = nH; a.hd = H / nH;
       a.scale = 1.0f / std::sqrt((float)(H / nH));
       a.fill = fill;
+      // With the split-fp16 path the tensor-core attention writes ctx as
+      // fp16 planes for the output projection.
+      const bool ctx_split = use_f16 && attention_tc_usable(a);
+      if (ctx_split) a.so = split_out(ctx_hi, ctx_lo, H);
       launch_attention(a, st);
       Epilogue e_o;
       e_o.bias = bo[l];
@@ -233,7 +253,8 @@ struct InfercEncoderPlan {
       e_o.resid = x;
       e_o.ldr = H;
       if (use_f16)
-        gemm16(fp32_a(ctx, H), wo[l], t, H, SplitOut(), M, H, H, e_o, st);
+        gemm16(ctx_split ? split_a(ctx_hi, ctx_lo, H) : fp32_a(ctx, H), wo[l], t, H, SplitOut(),
+               M, H, H, e_o, st);
       else
         gemm(ctx, H, wo[l], H, t, H, M, H, H, e_o, st);
       launch_layernorm(t, ln1g[l], ln1b[l], x, M, H, eps, st, xs);
@@ -263,11 +284,16 @@ struct InfercEncoderPlan {
     e_p.bias = pre_b;
     e_p.bias_mode = 1;
     e_p.act = ACT_RELU;
-    launch_gemm_simt(x, S * H, false, pre_w, H, true, pre, H, B, H, H, e_p, st);
     Epilogue e_c;
     e_c.bias = cls_b;
     e_c.bias_mode = 1;
-    launch_gemm_simt(pre, H, false, cls_w, H, true, logits, C, B, C, H, e_c, st);
+    if (use_f16) {
+      gemm16(fp32_a(x, S * H), pre16, pre, H, SplitOut(), B, H, H, e_p, st);
+      gemm16(fp32_a(pre, H), cls16, logits, C, SplitOut(), B, C, H, e_c, st);
+    } else {
+      launch_gemm_simt(x, S * H, false, pre_w, H, true, pre, H, B, H, H, e_p, st);
+      launch_gemm_simt(pre, H, false, cls_w, H, true, logits, C, B, C, H, e_c, st);
+    }
   }
 
   Graph& graph_for(int64_t B, int64_t S, bool use_f16) {
@@ -376,6 +402,10 @@ static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t 
     p->xs_lo = m.alloc<uint16_t>((size_t)M * H);
     p->hf_hi = m.alloc<uint16_t>((size_t)M * F);
     p->hf_lo = m.alloc<uint16_t>((size_t)M * F);
+    p->ctx_hi = m.alloc<uint16_t>((size_t)M * H);
+    p->ctx_lo = m.alloc<uint16_t>((size_t)M * H);
+    p->pre16 = split_weight_t(m, p->pre_w, H, H);
+    p->cls16 = split_weight_t(m, p->cls_w, H, p->C);
     p->f16_range = m.alloc<int>(1);
     IDEV_CUDA(cudaMemset(p->f16_range, 0, sizeof(int)));
     IDEV_CUDA(cudaMallocHost(&p->range_host, sizeof(int)));

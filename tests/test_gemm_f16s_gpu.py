@@ -108,3 +108,39 @@ def test_f16s_range_flag():
     lib.check(L.inferc_dev_stream_synchronize(None))
     ref = (a.double() @ w.double()).cpu().numpy()
     assert _rel_err(y.cpu().numpy(), ref) < TC_REL_TOL
+
+
+def test_f16s_planes_chain():
+    """The encoder plan's FFN chain through the plane entry points: x split by
+    inferc_dev_f16_split_rows, FFN1 (bias + GELU) storing its fp16 split, FFN2
+    reading that split with bias + residual; against float64."""
+    L = lib.load()
+    rng = np.random.default_rng(11)
+    M, H, F = 1000, 768, 3072
+    x = torch.from_numpy(rng.standard_normal((M, H), dtype=np.float32)).cuda()
+    w1 = torch.from_numpy(rng.standard_normal((H, F), dtype=np.float32) * 0.02).cuda()
+    b1 = torch.from_numpy(rng.standard_normal(F, dtype=np.float32) * 0.02).cuda()
+    w2 = torch.from_numpy(rng.standard_normal((F, H), dtype=np.float32) * 0.02).cuda()
+    b2 = torch.from_numpy(rng.standard_normal(H, dtype=np.float32) * 0.02).cuda()
+    p1, p2 = _prep(L, w1), _prep(L, w2)
+    xh, xl = (torch.empty((M, H), dtype=torch.int16, device="cuda") for _ in range(2))
+    hh, hl = (torch.empty((M, F), dtype=torch.int16, device="cuda") for _ in range(2))
+    lib.check(L.inferc_dev_f16_split_rows(x.data_ptr(), M, H, H, xh.data_ptr(), xl.data_ptr(), H,
+                                          None))
+    lib.check(L.inferc_dev_gemm_f16s_planes(xh.data_ptr(), xl.data_ptr(), H, p1[0].data_ptr(),
+                                            p1[1].data_ptr(), p1[2].data_ptr(), b1.data_ptr(),
+                                            None, 0, None, hh.data_ptr(), hl.data_ptr(), F, M, F,
+                                            H, 1, None))
+    y = torch.empty((M, H), device="cuda")
+    lib.check(L.inferc_dev_gemm_f16s_planes(hh.data_ptr(), hl.data_ptr(), F, p2[0].data_ptr(),
+                                            p2[1].data_ptr(), p2[2].data_ptr(), b2.data_ptr(),
+                                            x.data_ptr(), H, y.data_ptr(), None, None, H, M, H, F,
+                                            0, None))
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    v = x.double() @ w1.double() + b1.double()
+    h = v * 0.5 * (1 + torch.erf(v / 2 ** 0.5))
+    # the hidden activations reconstructed from their planes
+    hf = hh.view(torch.float16).double() + hl.view(torch.float16).double()
+    assert (hf - h).abs().max().item() < 3e-5
+    ref = h @ w2.double() + b2.double() + x.double()
+    assert (y.double() - ref).abs().max().item() < 5e-5
