@@ -419,30 +419,37 @@ def _flush_l2(buf):
 def int4_bench(dev):
     """int4 per-row-scale GEMV over the GPT-2-small weight
     volume (12 x {768x2304, 768x768, 768x3072, 3072x768} + 768x50257), all 49
-    matrices in one batched call. The set (62.9 MB) fits in L2, so L2 is
-    flushed before every timed call; each call is timed alone."""
+    matrices in one batched call. One set (62.9 MB) fits in L2, so the timed
+    calls rotate over four device copies of the set (252 MB > L2): each call
+    reads weights that the three calls before it evicted. Each call is timed
+    alone with CUDA events."""
     import torch
 
-    from inferc_b200 import ops, synth
+    from inferc_b200 import synth
     mats = synth.gpt2_int4_set(seed=3)
-    d = [(torch.from_numpy(m.w).to(dev), torch.from_numpy(m.scales).to(dev),
-          torch.from_numpy(m.x).to(dev), torch.empty(m.n, device=dev)) for m in mats]
     from inferc_b200 import lib as _lib
-    arr = (_lib.Int4Gemv * len(d))()
-    for i, (w, sc, x, y) in enumerate(d):
-        arr[i] = _lib.Int4Gemv(w.data_ptr(), sc.data_ptr(), x.data_ptr(), y.data_ptr(),
-                               w.shape[0], x.shape[0])
+    copies = []
+    for _ in range(4):
+        d = [(torch.from_numpy(m.w).to(dev), torch.from_numpy(m.scales).to(dev),
+              torch.from_numpy(m.x).to(dev), torch.empty(m.n, device=dev)) for m in mats]
+        arr = (_lib.Int4Gemv * len(d))()
+        for i, (w, sc, x, y) in enumerate(d):
+            arr[i] = _lib.Int4Gemv(w.data_ptr(), sc.data_ptr(), x.data_ptr(), y.data_ptr(),
+                                   w.shape[0], x.shape[0])
+        copies.append((d, arr))
     fn = _lib.load().inferc_dev_gemv_int4_batched
     sptr = torch.cuda.current_stream().cuda_stream
-    flush = torch.zeros(64 << 20, device=dev)
-    for _ in range(3):
-        _lib.check(fn(arr, len(d), sptr))
+    for c in range(8):
+        _lib.check(fn(copies[c % 4][1], len(mats), sptr))
+    torch.cuda.synchronize()
     times = []
-    for _ in range(20):
+    for c in range(40):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        _flush_l2(flush)  # ~80 us on the device: the launch below is queued before it ends
+        # ~50 us of device spin with no memory traffic, so that the call below
+        # is queued before the timed region starts (no host time inside it)
+        torch.cuda._sleep(100000)
         e0.record()
-        fn(arr, len(d), sptr)
+        fn(copies[c % 4][1], len(mats), sptr)
         e1.record()
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1))
@@ -453,7 +460,7 @@ def int4_bench(dev):
     return {"metric": "int4 GEMV ms per GPT-2-small weight set", "value": ms, "unit": "ms",
             "higher_is_better": False, "matrices": len(mats), "bytes": nbytes,
             "achieved_gbs": gbs, "hbm_peak_gbs": pk["hbm_gbs"], "frac": gbs / pk["hbm_gbs"],
-            "peak_basis": basis, "l2": "flushed before each timed call",
+            "peak_basis": basis, "l2": "4 rotating copies of the set (252 MB > L2)",
             "published_m1_ms_123M_weights": 7.73}
 
 

@@ -1,0 +1,584 @@
+// int4 per-row-scale GEMV on the tensor cores (tcgen05 kind::i8), batched
+// over many matrices in one launch.
+//
+// Restates scalar_int4_gemv_perRow (bench/amx/int4_gemv_amx.cc:258-271):
+//   y[r] = sum_k (s_r * (q[r,k] - 8)) * x[k]
+// with W [N, K/2] bytes, byte j of a row holding k = 2j in the low nibble
+// and k = 2j + 1 in the high nibble.
+//
+// Integer formulation. x is quantised once per matrix to 22-bit integers,
+// x_k ~= xs * a_k with xs = max|x| / (2^22 - 1), and each a_k is written as
+// three signed byte digits a_k = d0 2^16 + d1 2^8 + d2. Then
+//   sum_k (q_k - 8) a_k = sum_i 2^(16 - 8 i) sum_k q_k d_ik - 8 sum_k a_k
+// where every inner sum is an exact int32 dot product of unsigned weight
+// bytes with signed digit bytes: a tcgen05 kind::i8 MMA with M = 128 rows,
+// N = 8 (digit planes 0..2, the rest zero) and int32 accumulators in TMEM.
+// The weight bytes are used without de-interleaving:
+//   lo tile = byte & 0x0F          (q of even k)  x  digits of x[2j]
+//   hi tile = byte & 0xF0 = 16 q   (odd k)        x  digits of x[2j+1]
+// both at the byte's own position; the hi sums are divided by 16 (exact).
+// Each row's result is one integer, rounded once to fp32 and scaled by
+// s_r * xs; the quantisation of x adds at most 2^-23 max|x| per element,
+// which keeps the row sums within fp32 accumulation error.
+//
+// Two launches per batch:
+//   int4_digits_kernel  one CTA per matrix: max|x|, the digit planes, already
+//                       in the shared-memory tile layout the MMA reads, and
+//                       sum a_k, into a per-device scratch buffer;
+//   gemv_int4_tc_kernel persistent, one CTA per SM over a contiguous range of
+//                       128-row blocks of the batch's matrices (ranges of
+//                       equal numbers of 16 KB slabs), started with
+//                       programmatic dependent launch so the weight stream
+//                       begins while the digits are being made.
+// GEMV warp roles (320 threads):
+//   warp 0      TMA producer: [128 rows x 128 bytes] slabs of W (2-D maps,
+//               128-byte swizzle, rows past N zero-filled) into a 9-stage
+//               ring (144 KB in flight per SM: loaded HBM latency is ~4 us)
+//   warp 1      TMEM allocation + MMA issuer
+//   warps 2..5  unpack: hi tile in place, lo tile into one of two buffers
+//               (same swizzled offsets, so one mask pair per 16 bytes)
+//   warps 6..9  on every matrix switch a bulk copy of its digit planes, and
+//               the epilogue (tcgen05.ld of both accumulators, a row per
+//               thread)
+// Every mbarrier wait is bounded; a timeout sets g_int4_tc_error.
+#include <cuda.h>
+
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "kernels.cuh"
+#include "tc_ptx.cuh"
+
+namespace inferc_dev {
+
+__device__ int g_int4_tc_error;
+
+namespace {
+
+using namespace tc;
+
+constexpr int kStages = 9;
+constexpr uint32_t kSlab = 128 * 128;          // packed bytes of one slab (hi in place)
+constexpr int kMaxAtoms = 16;                  // K/2 <= 2048 bytes
+constexpr uint32_t kAtomB = 8 * 128;           // one 128-byte K atom of an 8-row B tile
+constexpr uint32_t kBTile = kMaxAtoms * kAtomB;
+constexpr uint32_t kSmem = kStages * kSlab + 2 * kSlab + 2 * kBTile + 1024;
+constexpr int kThreads = 320;
+constexpr int kEpi = 128;  // warps 6..9
+constexpr int kMaxMats = 64;  // ~11.5 KB of kernel parameters
+
+struct Int4TcMat {
+  const float* scales;
+  float* y;
+  const uint8_t* planes;   // [ev tile | od tile], kslabs KB each
+  const float* xs;         // activation scale
+  const long long* asum;   // sum of a_k
+  int64_t n, k;
+  int kslabs;
+};
+
+struct Int4DigitJob {
+  const float* x;
+  int64_t k;
+  int kslabs;
+  uint8_t* planes;
+  float* xs;
+  long long* asum;
+};
+
+struct Int4DigitBatch {
+  Int4DigitJob j[kMaxMats];
+  int count;
+};
+
+struct Int4TcBatch {
+  CUtensorMap maps[kMaxMats];
+  Int4TcMat m[kMaxMats];
+  int blk_start[kMaxMats + 1];   // prefix sums of 128-row blocks
+  int slab_start[kMaxMats + 1];  // prefix sums of slabs (blocks x kslabs)
+  int count;
+};
+
+// The batch's per-matrix data, copied to shared memory at kernel start: the
+// kernel parameters are larger than the constant cache, and every lookup
+// into them with a run-time index would be an L2 round trip.
+struct Int4TcMeta {
+  int count;
+  int blk_start[kMaxMats + 1];
+  int slab_start[kMaxMats + 1];
+  Int4TcMat m[kMaxMats];
+};
+
+// First block of CTA c when the batch's slabs are split evenly over G CTAs:
+// block j (slab offset o_j) belongs to the CTA c with o_j G in [c S, (c+1) S).
+__device__ __forceinline__ int first_block(const Int4TcMeta& bt, int c, int G) {
+  const long long target = (long long)c * bt.slab_start[bt.count];  // compare o_j * G >= target
+  for (int mi = 0; mi < bt.count; ++mi) {
+    // the first block at or past the target lies in matrix mi when the
+    // target is below the end of its slab range (one division, here only)
+    if (target > (long long)bt.slab_start[mi + 1] * G - bt.m[mi].kslabs * (long long)G) {
+      if (mi + 1 < bt.count) continue;
+    }
+    const long long ks = bt.m[mi].kslabs;
+    const long long base = (long long)bt.slab_start[mi] * G;
+    const int nb = bt.blk_start[mi + 1] - bt.blk_start[mi];
+    long long t = 0;
+    if (target > base) t = (target - base + ks * G - 1) / (ks * G);
+    if (t < nb) return bt.blk_start[mi] + (int)t;
+  }
+  return bt.blk_start[bt.count];
+}
+
+// kind::i8: D s32, A unsigned 8-bit, B signed 8-bit, both K-major.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// AND of `v` over the 128 epilogue threads (named barrier 2), so that they
+// leave their loop together and none is left waiting at a barrier.
+__device__ __forceinline__ bool epi_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 2, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(kEpi)
+      : "memory");
+  return r != 0;
+}
+
+// One 16-byte group of digit-plane bytes: (atom a, digit row i, physical
+// chunk pc) holds K bytes j = 128 a + 16 (pc ^ i) + b, b < 16 (SWIZZLE_128B).
+__device__ __forceinline__ uint32_t b_off(int i, int j) {
+  return (uint32_t)(j >> 7) * kAtomB + (uint32_t)i * 128 +
+         ((uint32_t)(((j & 127) >> 4) ^ i) << 4) + (uint32_t)(j & 15);
+}
+
+// One CTA (256 threads) per matrix: the digit planes of its x. The planes
+// were zeroed before the launch; only digit rows 0..2 are written.
+__global__ void __launch_bounds__(256) int4_digits_kernel(const __grid_constant__ Int4DigitBatch db) {
+  pdl_launch_dependents();  // the GEMV may start streaming weights
+  const Int4DigitJob& jb = db.j[blockIdx.x];
+  __shared__ float red_f[8];
+  __shared__ long long red_i[8];
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  // x in registers: K <= 4096 is at most 4 float4 per thread
+  float4 v[4];
+  float mx = 0.f;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t q = t + 256 * u;  // float4 index
+    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (4 * q < jb.k) v[u] = __ldg(reinterpret_cast<const float4*>(jb.x) + q);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+  }
+  mx = warp_max(mx);
+  if (lane == 0) red_f[wid] = mx;
+  __syncthreads();
+  mx = red_f[0];
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red_f[w]);
+  const float inv = mx > 0.f ? 4194303.0f / mx : 0.f;
+  uint8_t* ev = jb.planes;
+  uint8_t* od = jb.planes + (size_t)jb.kslabs * kAtomB;
+  long long part = 0;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t q = t + 256 * u;
+    if (4 * q >= jb.k) continue;
+    const float xv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {  // k = 4q + h -> packed byte j = 2q + h/2
+      int a = __float2int_rn(xv[h] * inv);
+      a = max(-4194303, min(4194303, a));
+      part += a;
+      const int d2 = ((a + 128) & 255) - 128;
+      const int a1 = (a - d2) >> 8;
+      const int d1 = ((a1 + 128) & 255) - 128;
+      const int d0 = (a1 - d1) >> 8;
+      const int jj = (int)(2 * q + h / 2);
+      uint8_t* tile = (h & 1) ? od : ev;
+      tile[b_off(0, jj)] = (uint8_t)d0;
+      tile[b_off(1, jj)] = (uint8_t)d1;
+      tile[b_off(2, jj)] = (uint8_t)d2;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (lane == 0) red_i[wid] = part;
+  __syncthreads();
+  if (t == 0) {
+    long long s = 0;
+    for (int w = 0; w < 8; ++w) s += red_i[w];
+    *jb.asum = s;
+    *jb.xs = mx > 0.f ? mx / 4194303.0f : 0.f;
+  }
+}
+
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_int4_tc_kernel(const __grid_constant__ Int4TcBatch prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* lobuf = smem + kStages * kSlab;  // two lo tiles
+  uint8_t* bplanes = lobuf + 2 * kSlab;     // [ev | od] of the current matrix
+  __shared__ __align__(8) uint64_t full_bar[kStages], conv_bar[kStages], empty_bar[kStages];
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], b_ready, b_free;
+  __shared__ uint32_t tmem_sh;
+  __shared__ volatile int abort_sh;
+
+  __shared__ Int4TcMeta bt;
+  {
+    const int nm = prm.count;
+    if (threadIdx.x == 0) bt.count = nm;
+    for (int i = threadIdx.x; i <= nm; i += blockDim.x) {
+      bt.blk_start[i] = prm.blk_start[i];
+      bt.slab_start[i] = prm.slab_start[i];
+      if (i < nm) bt.m[i] = prm.m[i];
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto fail = [&]() {
+    abort_sh = 1;
+    atomicExch(&g_int4_tc_error, 1);
+  };
+  auto mat_of = [&](int j, int& mi) {
+    while (j >= bt.blk_start[mi + 1]) ++mi;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&conv_bar[s], 128);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], kEpi);
+    }
+    mbar_init(&b_ready, 1);
+    mbar_init(&b_free, 1);
+    abort_sh = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // accumulators: [lo 8 | hi 8] x 2 buffers
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;" ::"r"(
+        smem_u32(&tmem_sh)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
+  const int j0 = first_block(bt, blockIdx.x, gridDim.x);
+  const int j1 = first_block(bt, blockIdx.x + 1, gridDim.x);
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- TMA producer
+      int g = 0, mi = 0;
+      for (int j = j0; j < j1 && !abort_sh; ++j) {
+        mat_of(j, mi);
+        const int row0 = (j - bt.blk_start[mi]) * 128;
+        for (int sl = 0; sl < bt.m[mi].kslabs; ++sl, ++g) {
+          const int s = g % kStages, r = g / kStages;
+          if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1)) {
+            fail();
+            break;
+          }
+          mbar_expect_tx(&full_bar[s], kSlab);
+          tma_load_2d(smem + s * kSlab, &prm.maps[mi], &full_bar[s], sl * 128, row0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---------------- MMA issuer
+      constexpr uint32_t idesc = idesc_i8(128, 8);
+      int g = 0, tl = 0, mi = 0, cur = -1, nsw = 0;
+      for (int j = j0; j < j1 && !abort_sh; ++j, ++tl) {
+        mat_of(j, mi);
+        if (mi != cur) {
+          if (cur >= 0) mma_commit(&b_free);  // the old digit planes are free once these finish
+          if (!mbar_wait(&b_ready, nsw & 1)) {
+            fail();
+            break;
+          }
+          ++nsw;
+          cur = mi;
+        }
+        const int acc = tl & 1;
+        if (tl >= 2 && !mbar_wait(&tempty_bar[acc], ((tl >> 1) - 1) & 1)) {
+          fail();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_lo = tmem + (uint32_t)(acc * 16), d_hi = d_lo + 8;
+        const uint32_t ev = smem_u32(bplanes), od = ev + bt.m[mi].kslabs * kAtomB;
+        for (int sl = 0; sl < bt.m[mi].kslabs && !abort_sh; ++sl, ++g) {
+          const int s = g % kStages, r = g / kStages;
+          if (!mbar_wait(&conv_bar[s], r & 1)) {
+            fail();
+            break;
+          }
+          tc_fence_after();
+          const uint32_t hi = smem_u32(smem + s * kSlab);
+          const uint32_t lo = smem_u32(lobuf + (g & 1) * kSlab);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {  // 32-byte K steps inside the 128-byte atom
+            const uint32_t acc_in = (sl | ks) != 0;
+            mma_i8(d_lo, smem_desc(lo + ks * 32, 16, 1024, 2),
+                   smem_desc(ev + sl * kAtomB + ks * 32, 16, 1024, 2), idesc, acc_in);
+            mma_i8(d_hi, smem_desc(hi + ks * 32, 16, 1024, 2),
+                   smem_desc(od + sl * kAtomB + ks * 32, 16, 1024, 2), idesc, acc_in);
+          }
+          mma_commit(&empty_bar[s]);
+        }
+        mma_commit(&tfull_bar[acc]);
+      }
+    }
+  } else if (warp < 6) {  // ---------------- unpack (warps 2..5)
+    const int t = threadIdx.x - 64;
+    int g = 0, mi = 0;
+    for (int j = j0; j < j1 && !abort_sh; ++j) {
+      mat_of(j, mi);
+      for (int sl = 0; sl < bt.m[mi].kslabs; ++sl, ++g) {
+        const int s = g % kStages, r = g / kStages;
+        if (!mbar_wait(&full_bar[s], r & 1)) {
+          fail();
+          break;
+        }
+        // lo buffer g & 1 was last read by the MMAs of slab g - 2
+        if (g >= 2 && !mbar_wait(&empty_bar[(g - 2) % kStages], ((g - 2) / kStages) & 1)) {
+          fail();
+          break;
+        }
+        uint4* p = reinterpret_cast<uint4*>(smem + s * kSlab);
+        uint4* q = reinterpret_cast<uint4*>(lobuf + (g & 1) * kSlab);
+#pragma unroll 4
+        for (int c = t; c < (int)(kSlab / 16); c += 128) {
+          const uint4 v = p[c];
+          p[c] = make_uint4(v.x & 0xF0F0F0F0u, v.y & 0xF0F0F0F0u, v.z & 0xF0F0F0F0u,
+                            v.w & 0xF0F0F0F0u);
+          q[c] = make_uint4(v.x & 0x0F0F0F0Fu, v.y & 0x0F0F0F0Fu, v.z & 0x0F0F0F0Fu,
+                            v.w & 0x0F0F0F0Fu);
+        }
+        fence_proxy_async();
+        mbar_arrive(&conv_bar[s]);
+      }
+    }
+  } else {  // ---------------- digit planes + epilogue (warps 6..9)
+    const int e = threadIdx.x - 192;
+    const int quad = warp & 3;
+    int tl = 0, mi = 0, cur = -1, nsw = 0;
+    float xs = 0.f;
+    long long asum = 0;
+    pdl_wait();  // the digit planes, xs and sum a_k come from the previous launch
+    for (int j = j0; j < j1; ++j, ++tl) {
+      mat_of(j, mi);
+      const Int4TcMat& m = bt.m[mi];
+      if (mi != cur) {
+        if (!epi_all(cur < 0 || mbar_wait(&b_free, (nsw - 1) & 1))) {
+          fail();
+          break;
+        }
+        if (e == 0) {
+          const uint32_t bytes = 2u * (uint32_t)m.kslabs * kAtomB;
+          mbar_expect_tx(&b_ready, bytes);
+          bulk_copy(bplanes, m.planes, bytes, &b_ready);
+        }
+        xs = *m.xs;
+        asum = *m.asum;
+        ++nsw;
+        cur = mi;
+      }
+      const int acc = tl & 1;
+      if (!epi_all(!abort_sh && mbar_wait(&tfull_bar[acc], (tl >> 1) & 1))) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      float v[16];
+      tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(acc * 16), v);
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      const int64_t row = (int64_t)(j - bt.blk_start[mi]) * 128 + 32 * quad + lane;
+      if (row < m.n) {
+        long long tsum = -8LL * asum;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          const long long lo = (long long)__float_as_int(v[i]);
+          const long long hi = (long long)(__float_as_int(v[8 + i]) >> 4);
+          tsum += (lo + hi) << (16 - 8 * i);
+        }
+        m.y[row] = __ldg(m.scales + row) * xs * (float)tsum;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" ::"r"(tmem));
+  }
+}
+
+CUtensorMap weight_map(const uint8_t* w, int64_t n, int64_t k) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n};
+  const cuuint64_t strides[1] = {(cuuint64_t)(k / 2)};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w),
+                                 dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw Error(INFERC_ERR_CUDA,
+                "cuTensorMapEncodeTiled (int4 GEMV) failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
+}  // namespace
+
+bool gemv_int4_tc_ok(const InfercInt4Gemv& d) {
+  return d.k % 32 == 0 && d.k / 2 <= kMaxAtoms * 128 && d.n >= 1 &&
+         (reinterpret_cast<uintptr_t>(d.w) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(d.x) & 15) == 0;
+}
+
+namespace {
+
+// Encoded weight maps by (device, pointer, rows, K): a decode loop calls the
+// GEMV with the same weights every step, and encoding a map costs host time
+// comparable to the whole kernel.
+struct MapKey {
+  int dev;
+  const void* w;
+  int64_t n, k;
+  bool operator==(const MapKey& o) const {
+    return dev == o.dev && w == o.w && n == o.n && k == o.k;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.w) ^ (std::hash<int64_t>()(k.n) * 31) ^
+           (std::hash<int64_t>()(k.k) * 131) ^ (size_t)k.dev;
+  }
+};
+
+CUtensorMap cached_weight_map(const uint8_t* w, int64_t n, int64_t k) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  int dev = 0;
+  IDEV_CUDA(cudaGetDevice(&dev));
+  const MapKey key{dev, w, n, k};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cache.size() >= 4096) cache.clear();
+  const CUtensorMap m = weight_map(w, n, k);
+  cache.emplace(key, m);
+  return m;
+}
+
+// Per-device scratch for the digit planes and per-matrix scalars.
+struct DigitScratch {
+  uint8_t* p = nullptr;
+  size_t bytes = 0;
+};
+
+uint8_t* digit_scratch(size_t bytes) {
+  static std::mutex mu;
+  static std::vector<DigitScratch> per_dev;
+  int dev = 0;
+  IDEV_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
+  DigitScratch& s = per_dev[dev];
+  if (s.bytes < bytes) {
+    if (s.p) IDEV_CUDA(cudaFree(s.p));
+    s.p = nullptr;
+    s.bytes = 0;
+    IDEV_CUDA(cudaMalloc(&s.p, bytes));
+    s.bytes = bytes;
+  }
+  return s.p;
+}
+
+}  // namespace
+
+// Matrices that pass gemv_int4_tc_ok, any count (launch pairs of up to 64).
+void launch_gemv_int4_tc(const InfercInt4Gemv* const* ds, int n, cudaStream_t st) {
+  static int sms = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  IDEV_CUDA(cudaFuncSetAttribute(gemv_int4_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmem));
+  for (int base = 0; base < n; base += kMaxMats) {
+    static thread_local Int4TcBatch bt;  // built in place, passed by value
+    static thread_local Int4DigitBatch db;
+    bt.count = db.count = std::min(kMaxMats, n - base);
+    // scratch: per matrix 2 * kslabs KB of planes, then xs and asum
+    size_t plane_bytes = 0;
+    for (int i = 0; i < bt.count; ++i)
+      plane_bytes += 2 * (size_t)((ds[base + i]->k / 2 + 127) / 128) * kAtomB;
+    uint8_t* scratch = digit_scratch(plane_bytes + (size_t)bt.count * 16);
+    long long* asums = reinterpret_cast<long long*>(scratch + plane_bytes);
+    float* xss = reinterpret_cast<float*>(asums + bt.count);
+    size_t off = 0;
+    int blks = 0, slabs = 0;
+    for (int i = 0; i < bt.count; ++i) {
+      const InfercInt4Gemv& d = *ds[base + i];
+      const int kslabs = (int)((d.k / 2 + 127) / 128);
+      bt.maps[i] = cached_weight_map(d.w, d.n, d.k);
+      bt.m[i] = Int4TcMat{d.scales, d.y, scratch + off, xss + i, asums + i, d.n, d.k, kslabs};
+      db.j[i] = Int4DigitJob{d.x, d.k, kslabs, scratch + off, xss + i, asums + i};
+      off += 2 * (size_t)kslabs * kAtomB;
+      bt.blk_start[i] = blks;
+      bt.slab_start[i] = slabs;
+      blks += (int)((d.n + 127) / 128);
+      slabs += (int)((d.n + 127) / 128) * kslabs;
+    }
+    bt.blk_start[bt.count] = blks;
+    bt.slab_start[bt.count] = slabs;
+    IDEV_CUDA(cudaMemsetAsync(scratch, 0, plane_bytes, st));
+    int4_digits_kernel<<<bt.count, 256, 0, st>>>(db);
+    IDEV_LAUNCHED();
+    launch_pdl(gemv_int4_tc_kernel, dim3(std::min(blks, sms)), dim3(kThreads), kSmem, st, bt);
+  }
+}
+
+int read_and_clear_int4_tc_error() {
+  int v = 0;
+  IDEV_CUDA(cudaMemcpyFromSymbol(&v, g_int4_tc_error, sizeof(int)));
+  if (v) {
+    const int z = 0;
+    IDEV_CUDA(cudaMemcpyToSymbol(g_int4_tc_error, &z, sizeof(int)));
+  }
+  return v;
+}
+
+}  // namespace inferc_dev

@@ -267,6 +267,27 @@ def test_int4_batched_gpt2_set(port):
         np.testing.assert_allclose(host(d[3]), ref, atol=1e-4, rtol=1e-5)
 
 
+def test_int4_batched_many_small_and_mixed(port):
+    """70 matrices of mixed shapes in one call: more than one launch pair,
+    many matrix switches inside each CTA, tails of K below one 256-weight
+    slab, a K that is not a multiple of 32 (the per-row kernel), and x of very
+    different magnitudes per matrix (each has its own activation scale)."""
+    rng = np.random.default_rng(17)
+    shapes = [(int(rng.integers(1, 300)), int(rng.choice([32, 64, 96, 768, 1024, 4096])))
+              for _ in range(68)] + [(129, 130), (3, 4096)]
+    mats = []
+    for i, (n, k) in enumerate(shapes):
+        m = synth.int4_matrix(n, k, rng)
+        m = synth.Int4Matrix(m.w, m.scales, (m.x * 10.0 ** ((i % 7) - 3)).astype(np.float32))
+        mats.append(m)
+    dev = [(T(m.w), T(m.scales), T(m.x), torch.empty(m.n, device=DEV)) for m in mats]
+    ops.Int4GemvBatched(dev)
+    for m, d in zip(mats, dev):
+        ref = port.int4_gemv_rowscale(m.w, m.scales, m.x)
+        tol = 1e-6 * np.abs(m.scales).max() * np.abs(m.x).sum() * 8 + 1e-30
+        np.testing.assert_allclose(host(d[3]), ref, atol=tol, rtol=1e-5)
+
+
 @pytest.mark.parametrize("B,S", [(2, 128), (1, 512), (3, 40)])
 def test_qkv_attention_prepared(port, B, S):
     """inferc_dev_qkv_attention (config 2 path) == FusedQKV + FusedAttention."""
