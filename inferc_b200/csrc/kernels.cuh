@@ -74,6 +74,13 @@ void launch_gemm_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl,
                       const SplitOut& so, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
                       cudaStream_t st);
 int read_and_clear_f16_range();
+// Two-SM (cta_group::2, 256-row) form of the split-fp16 GEMM for pre-split A
+// (gemm_f16s_2cta.cu); opt-in with INFERC_GEMM_2CTA=1.
+bool gemm_f16s_2cta_usable(const F16GemmA& A, int64_t M, int64_t N);
+void launch_gemm_f16s_2cta(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,
+                           const float* scale2, float* C, int64_t ldc, const SplitOut& so,
+                           int64_t M, int64_t N, int64_t K, int epi, const Epilogue& ep,
+                           cudaStream_t st);
 int* f16_range_flag_ptr();  // the current device's module-wide range flag
 // x [rows, cols] -> fp16 hi / lo planes; range null = the module-wide flag.
 void launch_split_rows_f16(const float* x, int64_t rows, int64_t cols, int64_t ldx, uint16_t* hi,

@@ -172,5 +172,25 @@ inline EncodeTiledFn encode_fn() {
 }
 
 
+// 2-D map over a row-major [rows, cols] matrix of esize-byte elements with
+// row stride ld (elements); box = box_cols x box_rows.
+inline CUtensorMap make_map_2d(CUtensorMapDataType dt, uint32_t esize, const void* base, int64_t rows,
+                        int64_t cols, int64_t ld, uint32_t box_cols, uint32_t box_rows,
+                        CUtensorMapSwizzle swz) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * esize};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode_fn()(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw Error(INFERC_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
 }  // namespace tc
 }  // namespace inferc_dev

@@ -144,3 +144,48 @@ def test_f16s_planes_chain():
     assert (hf - h).abs().max().item() < 3e-5
     ref = h @ w2.double() + b2.double() + x.double()
     assert (y.double() - ref).abs().max().item() < 5e-5
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 768, 256), (1000, 768, 2304), (4096, 3072, 768),
+                                   (777, 96, 300), (32768, 768, 3072)])
+def test_f16s_planes_shapes(M, K, N):
+    """A as fp16 planes (the plan's form; M >= 512 runs the two-SM 256-row
+    kernel) with the bias + residual epilogue, ragged M / N / K included."""
+    L = lib.load()
+    rng = np.random.default_rng(M + N)
+    a = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+    w = torch.from_numpy(rng.standard_normal((K, N), dtype=np.float32) * 0.02).cuda()
+    b = torch.from_numpy(rng.standard_normal(N, dtype=np.float32)).cuda()
+    r = torch.from_numpy(rng.standard_normal((M, N), dtype=np.float32)).cuda()
+    hi, lo, sc = _prep(L, w)
+    kp = L.inferc_dev_f16_kp(K)
+    ah, al = (torch.empty((M, kp), dtype=torch.int16, device="cuda") for _ in range(2))
+    lib.check(L.inferc_dev_f16_split_rows(a.data_ptr(), M, K, K, ah.data_ptr(), al.data_ptr(), kp,
+                                          None))
+    y = torch.empty((M, N), device="cuda")
+    lib.check(L.inferc_dev_gemm_f16s_planes(ah.data_ptr(), al.data_ptr(), kp, hi.data_ptr(),
+                                            lo.data_ptr(), sc.data_ptr(), b.data_ptr(),
+                                            r.data_ptr(), N, y.data_ptr(), None, None, N, M, N, K,
+                                            0, None))
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    ref = a.double() @ w.double() + b.double() + r.double()
+    err = (y.double() - ref).abs().max().item() / (ref.abs().max().item())
+    assert err < TC_REL_TOL
+
+
+def test_f16s_two_sm_kernel_opt_in():
+    """The two-SM (cta_group::2, 256-row) form, opt-in by INFERC_GEMM_2CTA=1 at
+    process start: run the plane GEMM check in a child process with it on."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys; sys.path.insert(0, '.');"
+        "from tests import test_gemm_f16s_gpu as t;"
+        "t.test_f16s_planes_shapes(1000, 768, 2304); t.test_f16s_planes_shapes(512, 3072, 768);"
+        "t.test_f16s_planes_chain(); print('ok')")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, INFERC_GEMM_2CTA="1")
+    out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True,
+                         text=True, timeout=300)
+    assert out.returncode == 0 and "ok" in out.stdout, out.stderr[-2000:]
