@@ -244,6 +244,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["decode", "int4", "sweep"],
+                    help="run one sub-benchmark alone and print its object (small cases for ncu)")
     ap.add_argument("--roofline-only", action="store_true",
                     help="time only the dominant kernel (FFN1 split-fp16 GEMM, B=256 S=128) "
                          "and print its roofline; the small case for ncu captures")
@@ -260,6 +262,10 @@ def main():
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.only:
+        fn = {"decode": decode_bench, "int4": int4_bench, "sweep": sweep_bench}[args.only]
+        print(json.dumps(fn(dev)), flush=True)
+        return
     if args.roofline_only:
         cfg = synth.EncoderConfig()
         pk, basis = peaks()
