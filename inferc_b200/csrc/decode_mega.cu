@@ -96,10 +96,16 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 }
 
 
+constexpr int kLnMax = 800;  // LayerNorm width whose gamma / beta (+ a bias) are prefetched
+
 struct Smem {
   uint64_t bar[kSlots];
   uint32_t uses[kSlots];    // completed waits per slot (parity tracking)
   uint32_t issued[kSlots];  // issued fills per slot (thread 0 only)
+  uint64_t ln_bar;          // gamma / beta of the next LayerNorm phase
+  uint32_t ln_uses, ln_issued;
+  unsigned target;          // arrival count that ends the current grid barrier
+  __align__(16) float lnp[3 * kLnMax];  // [gamma | beta | extra vector]
   float xs[3072];         // staged GEMV input (normalised when LN applies)
   float red[2 * kMegaThreads];
   float stat[2];
@@ -126,13 +132,21 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 // (b + 1) * gridDim.x. Arrival is a fire-and-forget release add, so CTAs do
 // not serialise on returning atomics. Returns false when the kernel must
 // stop (timeout here or an error flagged elsewhere).
-__device__ bool grid_sync(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
+// Split in two so that thread 0 can issue the next copies between its
+// arrival and its wait: grid_sync = grid_arrive + grid_wait.
+__device__ void grid_arrive(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
   if (a.prof && step == 1 && blockIdx.x == 0 && threadIdx.x == 0 && tag >= 0)
     a.prof[2 * tag] = gtimer();
-  __syncthreads();
+  __syncthreads();  // the CTA's outputs of the phase precede the release below
   if (threadIdx.x == 0) {
-    const unsigned target = (++sm.nbar) * gridDim.x;
+    sm.target = (++sm.nbar) * gridDim.x;
     red_release_add(a.bar_count, 1u);
+  }
+}
+
+__device__ bool grid_wait(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
+  if (threadIdx.x == 0) {
+    const unsigned target = sm.target;
     uint32_t i = 0;
     const unsigned long long t0 = gclock();
     while ((int)(ld_acquire(a.bar_count) - target) < 0) {
@@ -146,6 +160,58 @@ __device__ bool grid_sync(const MegaArgs& a, Smem& sm, int tag = -1, int step = 
   }
   __syncthreads();
   return sm.abort_flag == 0;
+}
+
+__device__ bool grid_sync(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
+  grid_arrive(a, sm, tag, step);
+  return grid_wait(a, sm, tag, step);
+}
+
+// Thread 0: bulk copy of a LayerNorm's gamma and beta (K floats each), and
+// optionally one more K-vector of the phase, into sm.lnp, completing on
+// sm.ln_bar; a no-op when K exceeds kLnMax (the phase then reads them from
+// global memory).
+// Whether a LayerNorm's vectors go through sm.lnp: bulk copies need 16-byte
+// aligned sources and sizes.
+__device__ __forceinline__ bool ln_prefetchable(const float* g, const float* b,
+                                                const float* extra, int K) {
+  auto al = [](const float* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return K <= kLnMax && K % 4 == 0 && al(g) && al(b) && (extra == nullptr || al(extra));
+}
+
+__device__ void prefetch_ln(const float* g, const float* b, const float* extra, int K,
+                            Smem& sm) {
+  if (threadIdx.x != 0 || !ln_prefetchable(g, b, extra, K)) return;
+  const uint32_t bytes = (uint32_t)K * 4;
+  sm.ln_issued++;
+  mb_expect_tx(&sm.ln_bar, (extra ? 3 : 2) * bytes);
+  bulk_load(sm.lnp, g, bytes, &sm.ln_bar);
+  bulk_load(sm.lnp + kLnMax, b, bytes, &sm.ln_bar);
+  if (extra) bulk_load(sm.lnp + 2 * kLnMax, extra, bytes, &sm.ln_bar);
+}
+
+// Gamma / beta (and the extra vector) of a phase with a LayerNorm of width
+// K: the prefetched copy (all threads wait for it, bounded) or, past
+// kLnMax, the global arrays.
+__device__ bool ln_params(const float* g, const float* b, const float* extra, int K, Smem& sm,
+                          const MegaArgs& a, const float** gs, const float** bs,
+                          const float** es) {
+  if (!ln_prefetchable(g, b, extra, K)) {
+    *gs = g;
+    *bs = b;
+    *es = extra;
+    return true;
+  }
+  const bool ok = __syncthreads_and(mb_wait(&sm.ln_bar, sm.ln_uses & 1)) != 0;
+  if (threadIdx.x == 0) {
+    sm.ln_uses++;
+    if (!ok) atomicExch(a.err, 1);
+  }
+  __syncthreads();
+  *gs = sm.lnp;
+  *bs = sm.lnp + kLnMax;
+  *es = sm.lnp + 2 * kLnMax;
+  return ok;
 }
 
 // Issue this CTA's panels of a GEMV phase into slot pair `pair`.
@@ -180,12 +246,17 @@ __device__ bool wait_slot(int s, Smem& sm, const MegaArgs& a) {
 // flight, so none lands in shared memory after the CTA has exited.
 __device__ void drain(Smem& sm) {
   __syncthreads();
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s)
       while (sm.issued[s] > sm.uses[s]) {
         mb_wait(&sm.bar[s], sm.uses[s] & 1);
         sm.uses[s]++;
       }
+    while (sm.ln_issued > sm.ln_uses) {
+      mb_wait(&sm.ln_bar, sm.ln_uses & 1);
+      sm.ln_uses++;
+    }
+  }
   __syncthreads();
 }
 
@@ -201,9 +272,9 @@ __device__ void stage_input(const float* x, int K, const float* g, const float* 
   for (int i = 0; i < 12; ++i) {
     const int k = tid + i * kMegaThreads;
     v[i] = k < K ? __ldcg(x + k) : 0.f;
-    if (g != nullptr) {
-      gv[i] = k < K ? __ldg(g + k) : 0.f;
-      bv[i] = k < K ? __ldg(b + k) : 0.f;
+    if (g != nullptr) {  // shared (prefetched) or global
+      gv[i] = k < K ? g[k] : 0.f;
+      bv[i] = k < K ? b[k] : 0.f;
     }
   }
   if (g == nullptr) {
@@ -611,15 +682,15 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
 
 // FC-phase input: xm = xa + b_proj + sum_h part[h] (heads in order); CTA 0
 // publishes xm (the FP residual); then LN2 in place.
-__device__ void stage_attn_residual(const MegaArgs& a, const MegaLayer& L, const float* xa,
-                                    float* xm, Smem& sm) {
+__device__ void stage_attn_residual(const MegaArgs& a, const float* proj_b, const float* g,
+                                    const float* b, const float* xa, float* xm, Smem& sm) {
   const int tid = threadIdx.x, H = a.H;
   for (int k = tid; k < H; k += kMegaThreads) {
     float p[16];
 #pragma unroll
     for (int h = 0; h < 16; ++h) p[h] = h < a.heads ? __ldcg(a.part + (size_t)h * H + k) : 0.f;
     float v = __ldcg(xa + k);
-    const float bp = __ldg(L.proj_b + k);
+    const float bp = proj_b[k];
     float t = 0.f;
 #pragma unroll
     for (int h = 0; h < 16; ++h) t += p[h];
@@ -628,7 +699,7 @@ __device__ void stage_attn_residual(const MegaArgs& a, const MegaLayer& L, const
     if (blockIdx.x == 0) xm[k] = v;
   }
   __syncthreads();
-  stage_smem_ln(H, L.ln2_g, L.ln2_b, a.eps, sm);
+  stage_smem_ln(H, g, b, a.eps, sm);
 }
 
 // Attention + output projection for one (head, column chunk): CTA c < heads
@@ -687,6 +758,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       sm.uses[s] = 0;
       sm.issued[s] = 0;
     }
+    mb_init(&sm.ln_bar, 1);
+    sm.ln_uses = 0;
+    sm.ln_issued = 0;
     sm.abort_flag = 0;
     sm.nbar = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -700,7 +774,39 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
   float* xm = a.x + H;
 
   int64_t tok = *a.tok;
+  // Copies are issued one phase ahead, by thread 0 between its arrival at a
+  // grid barrier and its wait there: a slot pair is refilled as soon as this
+  // CTA has consumed it, off the critical path of the next phase.
+  auto issue_proj = [&](const MegaLayer& Lx) {  // W_proj panel -> slot 2
+    if (tid == 0 && blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) {
+      const uint32_t bytes = (uint32_t)Lx.proj.K * Lx.proj.P * 4;
+      sm.issued[2]++;
+      mb_expect_tx(&sm.bar[2], bytes);
+      bulk_load(slots + 2 * (size_t)kSlotBytes,
+                Lx.proj.data + (size_t)blockIdx.x * Lx.proj.K * Lx.proj.P, bytes, &sm.bar[2]);
+    }
+  };
+  // LM head chunks: 16 rows of wte (48 KiB) per chunk, this CTA's row range.
+  const int lm_rows = (a.V + gridDim.x - 1) / gridDim.x;
+  const int lm_r0 = blockIdx.x * lm_rows;
+  const int lm_r1 = min(a.V, lm_r0 + lm_rows);
+  const int lm_crow = kSlotBytes / (H * 4);
+  const int lm_nchunks = lm_r1 > lm_r0 ? (lm_r1 - lm_r0 + lm_crow - 1) / lm_crow : 0;
+  auto issue_lm = [&](int ch) {
+    if (tid != 0 || ch >= lm_nchunks) return;
+    const int s = ch % kSlots;
+    const int ra = lm_r0 + ch * lm_crow, rb = min(lm_r1, ra + lm_crow);
+    const uint32_t bytes = (uint32_t)(rb - ra) * H * 4;
+    sm.issued[s]++;
+    mb_expect_tx(&sm.bar[s], bytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wte + (size_t)ra * H);
+    for (uint32_t off = 0; off < bytes; off += 16384)
+      bulk_load(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
+                &sm.bar[s]);
+  };
   prefetch_panels(a.layer[0].attn, 0, slots, sm);
+  issue_proj(a.layer[0]);
+  prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
   for (int step = 0; step < a.nsteps; ++step) {
     const int64_t pos = a.pos0 + step;
     if (tok < 0 || tok >= a.V || pos < 0 || pos >= a.max_pos || pos >= a.max_len) {
@@ -710,15 +816,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
     }
     for (int l = 0; l < a.layers; ++l) {
       const MegaLayer& L = a.layer[l];  // read on use (keeps registers free)
-      // ---- QKV (pair 0); the attention block's W_proj panel streams into slot 2.
-      if (tid == 0 && blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) {
-        const uint32_t bytes = (uint32_t)L.proj.K * L.proj.P * 4;
-        sm.issued[2]++;
-        mb_expect_tx(&sm.bar[2], bytes);
-        bulk_load(slots + 2 * (size_t)kSlotBytes,
-                  L.proj.data + (size_t)blockIdx.x * L.proj.K * L.proj.P, bytes, &sm.bar[2]);
-      }
+      const bool last = l + 1 == a.layers;
+      // ---- QKV (pair 0; W_proj is in slot 2, LN1's gamma / beta in sm.lnp)
       const EpiIn e_qkv = gemv_preload(L.attn, L.attn_b, nullptr);
+      const float *g1, *b1, *unused;
+      if (!ln_params(L.ln1_g, L.ln1_b, nullptr, H, sm, a, &g1, &b1, &unused)) { drain(sm); return; }
       if (l == 0) {
         // Embedding of the current token, built by every CTA; CTA 0 also
         // publishes it as the residual stream.
@@ -728,53 +830,54 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
           if (blockIdx.x == 0) xa[k] = v;
         }
         __syncthreads();
-        stage_smem_ln(H, L.ln1_g, L.ln1_b, a.eps, sm);
+        stage_smem_ln(H, g1, b1, a.eps, sm);
       } else {
-        stage_input(xa, H, L.ln1_g, L.ln1_b, a.eps, sm);
+        stage_input(xa, H, g1, b1, a.eps, sm);
       }
       if (!gemv_phase(L.attn, 0, slots, e_qkv, a.qkv, ACT_NONE, sm, a)) { drain(sm); return; }
-      if (!grid_sync(a, sm, 4 * l + 0, step)) { drain(sm); return; }
-      // ---- attention + output projection partials; FC streams into pair 0.
+      grid_arrive(a, sm, 4 * l + 0, step);
+      prefetch_panels(L.fc, 0, slots, sm);  // pair 0 consumed
+      if (!grid_wait(a, sm, 4 * l + 0, step)) { drain(sm); return; }
+      // ---- attention + output projection partials (slot 2)
       if (a.prof && blockIdx.x == 0 && tid == 0) a.prof[1099] = clock64();
-      prefetch_panels(L.fc, 0, slots, sm);
       if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm)) { drain(sm); return; }
-      if (!grid_sync(a, sm, 4 * l + 1, step)) { drain(sm); return; }
+      grid_arrive(a, sm, 4 * l + 1, step);
+      prefetch_panels(L.fp, 1, slots, sm);  // slot 2 consumed, slot 3 free
+      prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);
+      if (!grid_wait(a, sm, 4 * l + 1, step)) { drain(sm); return; }
       // ---- FC (pair 0): xm = xa + b_proj + sum_h part[h]; f = gelu(LN2(xm) W + b).
-      //      FP streams into pair 1.
-      prefetch_panels(L.fp, 1, slots, sm);
       const EpiIn e_fc = gemv_preload(L.fc, L.fc_b, nullptr);
-      stage_attn_residual(a, L, xa, xm, sm);
+      const float *g2, *b2, *pb;
+      if (!ln_params(L.ln2_g, L.ln2_b, L.proj_b, H, sm, a, &g2, &b2, &pb)) { drain(sm); return; }
+      stage_attn_residual(a, pb, g2, b2, xa, xm, sm);
       if (!gemv_phase(L.fc, 0, slots, e_fc, a.f, ACT_GELU_TANH, sm, a)) { drain(sm); return; }
-      if (!grid_sync(a, sm, 4 * l + 2, step)) { drain(sm); return; }
-      // ---- FP (pair 1): xa = xm + f W + b; the next layer's QKV streams into pair 0.
-      if (l + 1 < a.layers) prefetch_panels(a.layer[l + 1].attn, 0, slots, sm);
+      grid_arrive(a, sm, 4 * l + 2, step);
+      if (!last) prefetch_panels(a.layer[l + 1].attn, 0, slots, sm);  // pair 0 consumed
+      if (!grid_wait(a, sm, 4 * l + 2, step)) { drain(sm); return; }
+      // ---- FP (pair 1): xa = xm + f W + b
       const EpiIn e_fp = gemv_preload(L.fp, L.fp_b, xm);
       stage_input(a.f, a.F, nullptr, nullptr, 0.f, sm);
       if (!gemv_phase(L.fp, 1, slots, e_fp, xa, ACT_NONE, sm, a)) { drain(sm); return; }
-      if (!grid_sync(a, sm, 4 * l + 3, step)) { drain(sm); return; }
+      grid_arrive(a, sm, 4 * l + 3, step);
+      if (!last) {
+        issue_proj(a.layer[l + 1]);  // slot 2 consumed
+        prefetch_ln(a.layer[l + 1].ln1_g, a.layer[l + 1].ln1_b, nullptr, H, sm);
+      } else {
+        for (int ch = 0; ch < kSlots; ++ch) issue_lm(ch);  // every slot consumed
+        prefetch_ln(a.lnf_g, a.lnf_b, nullptr, H, sm);
+      }
+      if (!grid_wait(a, sm, 4 * l + 3, step)) { drain(sm); return; }
     }
     // LM head: logits = LNf(x) . wte[r] for this CTA's row range, streamed
-    // through all four slots (16 rows = 48 KiB per chunk).
-    stage_input(xa, H, a.lnf_g, a.lnf_b, a.eps, sm);
+    // through all four slots (the first four chunks are already in flight).
     {
-      const int rows_per = (a.V + gridDim.x - 1) / gridDim.x;
-      const int r0 = blockIdx.x * rows_per;
-      const int r1 = min(a.V, r0 + rows_per);
-      const int crow = kSlotBytes / (H * 4);  // rows per chunk
-      const int nchunks = r1 > r0 ? (r1 - r0 + crow - 1) / crow : 0;
-      auto issue = [&](int ch) {
-        if (tid != 0 || ch >= nchunks) return;
-        const int s = ch % kSlots;
-        const int ra = r0 + ch * crow, rb = min(r1, ra + crow);
-        const uint32_t bytes = (uint32_t)(rb - ra) * H * 4;
-        sm.issued[s]++;
-        mb_expect_tx(&sm.bar[s], bytes);
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wte + (size_t)ra * H);
-        for (uint32_t off = 0; off < bytes; off += 16384)
-          bulk_load(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
-                    &sm.bar[s]);
-      };
-      for (int ch = 0; ch < kSlots; ++ch) issue(ch);
+      const float *gf, *bf, *unused;
+      if (!ln_params(a.lnf_g, a.lnf_b, nullptr, H, sm, a, &gf, &bf, &unused)) { drain(sm); return; }
+      stage_input(xa, H, gf, bf, a.eps, sm);
+    }
+    {
+      const int r0 = lm_r0, r1 = lm_r1, crow = lm_crow, nchunks = lm_nchunks;
+      auto issue = [&](int ch) { issue_lm(ch); };
       float bv = -INFINITY;
       int64_t bi = INT64_MAX;
       for (int ch = 0; ch < nchunks; ++ch) {
@@ -812,8 +915,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       }
     }
     // Next step's first weights stream while the argmax is finalised.
-    if (step + 1 < a.nsteps) prefetch_panels(a.layer[0].attn, 0, slots, sm);
-    if (!grid_sync(a, sm, 4 * a.layers, step)) { drain(sm); return; }
+    grid_arrive(a, sm, 4 * a.layers, step);
+    if (step + 1 < a.nsteps) {
+      prefetch_panels(a.layer[0].attn, 0, slots, sm);
+      issue_proj(a.layer[0]);
+      prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
+    }
+    if (!grid_wait(a, sm, 4 * a.layers, step)) { drain(sm); return; }
     // Every CTA reduces the per-CTA bests in the same order (first max wins).
     if (wid == 0) {
       float v = -INFINITY;
