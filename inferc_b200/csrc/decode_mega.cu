@@ -685,16 +685,36 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
 __device__ void stage_attn_residual(const MegaArgs& a, const float* proj_b, const float* g,
                                     const float* b, const float* xa, float* xm, Smem& sm) {
   const int tid = threadIdx.x, H = a.H;
-  for (int k = tid; k < H; k += kMegaThreads) {
-    float p[16];
+  // All loads of the thread (up to 3 k's x 12 heads + x) are issued before
+  // any is used: one L2 round trip, not one per k.
+  constexpr int kK = 3, kHeads = 16;
+  float p[kK][kHeads], xv[kK], bp[kK];
 #pragma unroll
-    for (int h = 0; h < 16; ++h) p[h] = h < a.heads ? __ldcg(a.part + (size_t)h * H + k) : 0.f;
-    float v = __ldcg(xa + k);
-    const float bp = proj_b[k];
+  for (int i = 0; i < kK; ++i) {
+    const int k = tid + i * kMegaThreads;
+    const bool in = k < H;
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h)
+      p[i][h] = (in && h < a.heads) ? __ldcg(a.part + (size_t)h * H + k) : 0.f;
+    xv[i] = in ? __ldcg(xa + k) : 0.f;
+    bp[i] = in ? proj_b[k] : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < kK; ++i) {
+    const int k = tid + i * kMegaThreads;
+    if (k >= H) continue;
     float t = 0.f;
 #pragma unroll
-    for (int h = 0; h < 16; ++h) t += p[h];
-    v = v + (t + bp);
+    for (int h = 0; h < kHeads; ++h) t += p[i][h];
+    const float v = xv[i] + (t + bp[i]);
+    sm.xs[k] = v;
+    if (blockIdx.x == 0) xm[k] = v;
+  }
+  // wider rows than kK * kMegaThreads (not GPT-2-small): the remainder
+  for (int k = tid + kK * kMegaThreads; k < H; k += kMegaThreads) {
+    float t = 0.f;
+    for (int h = 0; h < a.heads; ++h) t += __ldcg(a.part + (size_t)h * H + k);
+    const float v = __ldcg(xa + k) + (t + proj_b[k]);
     sm.xs[k] = v;
     if (blockIdx.x == 0) xm[k] = v;
   }
@@ -804,9 +824,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       bulk_load(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
                 &sm.bar[s]);
   };
+  prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
   prefetch_panels(a.layer[0].attn, 0, slots, sm);
   issue_proj(a.layer[0]);
-  prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
   for (int step = 0; step < a.nsteps; ++step) {
     const int64_t pos = a.pos0 + step;
     if (tok < 0 || tok >= a.V || pos < 0 || pos >= a.max_pos || pos >= a.max_len) {
@@ -842,8 +862,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       if (a.prof && blockIdx.x == 0 && tid == 0) a.prof[1099] = clock64();
       if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm)) { drain(sm); return; }
       grid_arrive(a, sm, 4 * l + 1, step);
-      prefetch_panels(L.fp, 1, slots, sm);  // slot 2 consumed, slot 3 free
+      // LayerNorm vectors first: the copies are served in issue order and
+      // these are needed at the start of the next phase.
       prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);
+      prefetch_panels(L.fp, 1, slots, sm);  // slot 2 consumed, slot 3 free
       if (!grid_wait(a, sm, 4 * l + 1, step)) { drain(sm); return; }
       // ---- FC (pair 0): xm = xa + b_proj + sum_h part[h]; f = gelu(LN2(xm) W + b).
       const EpiIn e_fc = gemv_preload(L.fc, L.fc_b, nullptr);
@@ -860,11 +882,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       if (!gemv_phase(L.fp, 1, slots, e_fp, xa, ACT_NONE, sm, a)) { drain(sm); return; }
       grid_arrive(a, sm, 4 * l + 3, step);
       if (!last) {
-        issue_proj(a.layer[l + 1]);  // slot 2 consumed
         prefetch_ln(a.layer[l + 1].ln1_g, a.layer[l + 1].ln1_b, nullptr, H, sm);
+        issue_proj(a.layer[l + 1]);  // slot 2 consumed
       } else {
-        for (int ch = 0; ch < kSlots; ++ch) issue_lm(ch);  // every slot consumed
         prefetch_ln(a.lnf_g, a.lnf_b, nullptr, H, sm);
+        for (int ch = 0; ch < kSlots; ++ch) issue_lm(ch);  // every slot consumed
       }
       if (!grid_wait(a, sm, 4 * l + 3, step)) { drain(sm); return; }
     }
@@ -917,9 +939,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
     // Next step's first weights stream while the argmax is finalised.
     grid_arrive(a, sm, 4 * a.layers, step);
     if (step + 1 < a.nsteps) {
+      prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
       prefetch_panels(a.layer[0].attn, 0, slots, sm);
       issue_proj(a.layer[0]);
-      prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
     }
     if (!grid_wait(a, sm, 4 * a.layers, step)) { drain(sm); return; }
     // Every CTA reduces the per-CTA bests in the same order (first max wins).

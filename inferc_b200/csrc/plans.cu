@@ -584,6 +584,22 @@ struct InfercDecoderPlan {
         IDEV_CUDA(cudaStreamSynchronize(st));
         fprintf(stderr, "attn phase cycles: prefetch %llu qkv-load %llu pass %llu reduce %llu wait %llu proj %llu\n",
                 c[1] - c[0], c[2] - c[1], c[3] - c[2], c[4] - c[3], c[5] - c[4], c[6] - c[5]);
+        // grid barrier stamps of step 1, CTA 0: [2 tag] arrival, [2 tag + 1] release
+        std::vector<unsigned long long> t(2 * (4 * L + 1));
+        IDEV_CUDA(cudaMemcpy(t.data(), prof, t.size() * 8, cudaMemcpyDeviceToHost));
+        const char* names[4] = {"qkv", "attn+proj", "fc", "fp"};
+        for (int q = 4; q <= 8 && q <= 4 * L; ++q) {
+          const unsigned long long work = t[2 * q] - t[2 * q - 1], wait = t[2 * q + 1] - t[2 * q];
+          fprintf(stderr, "phase %-9s work %6.2f us  barrier %5.2f us\n",
+                  q == 4 * L ? "lm" : names[q % 4], work / 1e3, wait / 1e3);
+        }
+        std::vector<unsigned long long> u(32);  // optional sub-phase stamps [1200, 1232)
+        IDEV_CUDA(cudaMemcpy(u.data(), prof + 1200, 32 * 8, cudaMemcpyDeviceToHost));
+        for (int i = 1; i < 32; ++i)
+          if (u[i] && u[i - 1]) fprintf(stderr, "stamp %d-%d %.2f us\n", i - 1, i, (u[i] - u[i - 1]) / 1e3);
+        const int q = 4 * (int)L;
+        fprintf(stderr, "phase lm        work %6.2f us  barrier %5.2f us\n",
+                (t[2 * q] - t[2 * q - 1]) / 1e3, (t[2 * q + 1] - t[2 * q]) / 1e3);
       }
     } else if (max_tokens > 1) {
       if (!step_graph || log_base != n) {
