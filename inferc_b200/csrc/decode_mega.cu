@@ -386,8 +386,17 @@ __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, 
   const int slices = kMegaThreads / P4;  // rows processed in parallel
   const int c4 = tid % P4, sl = tid / P4;
   const int np = (int)(blockIdx.x < (unsigned)m.npanels) + (int)(blockIdx.x + gridDim.x < (unsigned)m.npanels);
-  for (int j = 0; j < np; ++j)
-    if (!wait_slot(2 * pair + j, sm, a)) return false;
+  {  // both panels' copies, one CTA barrier
+    bool ok = true;
+    for (int j = 0; j < np; ++j) ok = mb_wait(&sm.bar[2 * pair + j], sm.uses[2 * pair + j] & 1) && ok;
+    ok = __syncthreads_and(ok) != 0;
+    if (threadIdx.x == 0) {
+      for (int j = 0; j < np; ++j) sm.uses[2 * pair + j]++;
+      if (!ok) atomicExch(a.err, 1);
+    }
+    __syncthreads();
+    if (!ok) return false;
+  }
   const float* w0 = reinterpret_cast<const float*>(slots + (size_t)(2 * pair) * kSlotBytes);
   const float* w1 = reinterpret_cast<const float*>(slots + (size_t)(2 * pair + 1) * kSlotBytes);
   float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
@@ -856,15 +865,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       }
       if (!gemv_phase(L.attn, 0, slots, e_qkv, a.qkv, ACT_NONE, sm, a)) { drain(sm); return; }
       grid_arrive(a, sm, 4 * l + 0, step);
+      prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);  // LN1's copy consumed
       prefetch_panels(L.fc, 0, slots, sm);  // pair 0 consumed
       if (!grid_wait(a, sm, 4 * l + 0, step)) { drain(sm); return; }
       // ---- attention + output projection partials (slot 2)
       if (a.prof && blockIdx.x == 0 && tid == 0) a.prof[1099] = clock64();
       if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm)) { drain(sm); return; }
       grid_arrive(a, sm, 4 * l + 1, step);
-      // LayerNorm vectors first: the copies are served in issue order and
-      // these are needed at the start of the next phase.
-      prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);
       prefetch_panels(L.fp, 1, slots, sm);  // slot 2 consumed, slot 3 free
       if (!grid_wait(a, sm, 4 * l + 1, step)) { drain(sm); return; }
       // ---- FC (pair 0): xm = xa + b_proj + sum_h part[h]; f = gelu(LN2(xm) W + b).
@@ -874,6 +881,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       stage_attn_residual(a, pb, g2, b2, xa, xm, sm);
       if (!gemv_phase(L.fc, 0, slots, e_fc, a.f, ACT_GELU_TANH, sm, a)) { drain(sm); return; }
       grid_arrive(a, sm, 4 * l + 2, step);
+      // LN2's copy consumed: the next LayerNorm's vectors (small, first)
+      if (!last) prefetch_ln(a.layer[l + 1].ln1_g, a.layer[l + 1].ln1_b, nullptr, H, sm);
+      else prefetch_ln(a.lnf_g, a.lnf_b, nullptr, H, sm);
       if (!last) prefetch_panels(a.layer[l + 1].attn, 0, slots, sm);  // pair 0 consumed
       if (!grid_wait(a, sm, 4 * l + 2, step)) { drain(sm); return; }
       // ---- FP (pair 1): xa = xm + f W + b
@@ -882,10 +892,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       if (!gemv_phase(L.fp, 1, slots, e_fp, xa, ACT_NONE, sm, a)) { drain(sm); return; }
       grid_arrive(a, sm, 4 * l + 3, step);
       if (!last) {
-        prefetch_ln(a.layer[l + 1].ln1_g, a.layer[l + 1].ln1_b, nullptr, H, sm);
         issue_proj(a.layer[l + 1]);  // slot 2 consumed
       } else {
-        prefetch_ln(a.lnf_g, a.lnf_b, nullptr, H, sm);
         for (int ch = 0; ch < kSlots; ++ch) issue_lm(ch);  // every slot consumed
       }
       if (!grid_wait(a, sm, 4 * l + 3, step)) { drain(sm); return; }
