@@ -174,6 +174,19 @@ int inferc_dev_gemm_f16s_planes(const uint16_t* a_hi, const uint16_t* a_lo, int6
                                 uint16_t* y_hi, uint16_t* y_lo, int64_t ldy, int64_t M,
                                 int64_t N, int64_t K, int act, void* stream);
 
+/* FusedAttention (head_dim 64, S <= 128) on the fp16 tensor cores for q, k
+ * and v given as fp16 hi / lo planes (inferc_dev_f16_split_rows or a
+ * split-output GEMM): head h of token (b, s) at columns h*64.. of row
+ * b*S + s, row stride ld (a multiple of 8; q, k, v may be column blocks of
+ * one [B*S, 3H] plane pair). key_mask: optional bool [B,S], true = key
+ * masked. out: fp32 [B, S, nH*64]. Values fp16 cannot carry are reported
+ * like inferc_dev_gemm_f16s's. */
+int inferc_dev_fused_attention_planes(const uint16_t* q_hi, const uint16_t* q_lo,
+                                      const uint16_t* k_hi, const uint16_t* k_lo,
+                                      const uint16_t* v_hi, const uint16_t* v_lo, int64_t ld,
+                                      const uint8_t* key_mask, int64_t B, int64_t S,
+                                      int64_t heads, float fill, float* out, void* stream);
+
 /* FusedQKV + FusedAttention as one call on prepared weights (the encoder
  * plan's attention block): qkv = X Wqkv + bqkv with Wqkv = [Wq | Wk | Wv]
  * ([H, 3H], split by inferc_dev_tf32_split into w_big / w_small) and bqkv

@@ -1,0 +1,341 @@
+// FusedAttention (head_dim 64, S <= 128) on the fp16 tensor cores with
+// fp32-level accuracy, for q, k and v given as the split-fp16 planes the
+// QKV GEMM writes (x = hi + lo, gemm_f16s.cu's representation).
+//
+// One CTA per (batch, head), as in attention_tc.cu, but:
+//   * no split step: TMA loads the six hi / lo head tiles (96 KB) directly;
+//   * S = Q K^T and O = P V each take three kind::f16 MMAs per product
+//     (lo hi + hi lo + hi hi), at twice the tf32 rate;
+//   * P is written as fp16 hi / lo (P in [0, 1]: elements below 2^-14 keep
+//     an absolute error under 2^-25);
+//   * the mask is staged as one row (a mask that broadcasts over query rows,
+//     the padding mask of the encoder) or read per row from global memory.
+// That is ~98 KB of shared memory and 256 TMEM columns per CTA, so two CTAs
+// share an SM and one's softmax or epilogue overlaps the other's loads and
+// MMAs.
+//
+// Steps: TMA -> S = QK^T (M=128 queries, N=128 keys, K=64) -> masked
+// softmax (two threads per row, 64 keys each in registers; masked entries
+// are REPLACED by `fill`, keys past S get no weight, as rt::FusedAttention,
+// src/kernels/attention.cc:77-91) -> P planes over the spent Q / K tiles ->
+// O = P V (V MN-major, SWIZZLE_128B) -> O as fp32 or as fp16 planes.
+// Every mbarrier wait is bounded; a timeout sets g_attn_f16_error.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <cstdlib>
+
+#include "kernels.cuh"
+#include "tc_ptx.cuh"
+
+namespace inferc_dev {
+
+__device__ int g_attn_f16_error;
+
+namespace {
+
+using namespace tc;
+
+constexpr int kRows = 128;
+constexpr int kHd = 64;
+constexpr int kThreads = 256;
+constexpr uint32_t kTile = 16384;  // [128 rows][128 B]: one fp16 plane of a head tile
+// Q hi, Q lo, K hi, K lo, V hi, V lo; P hi / lo (two 64-key atoms each)
+// reuse Q and K once S = QK^T is done.
+constexpr uint32_t OFF_QH = 0, OFF_QL = kTile, OFF_KH = 2 * kTile, OFF_KL = 3 * kTile,
+                   OFF_VH = 4 * kTile, OFF_VL = 5 * kTile;
+constexpr uint32_t OFF_PH = 0, OFF_PL = 2 * kTile;
+constexpr uint32_t OFF_MASK = 6 * kTile;  // one row of kRows bytes
+constexpr uint32_t kSmemBytes = 6 * kTile + kRows + 1024;
+
+struct AttnF16Kern {
+  const uint8_t* mask;
+  int64_t ms[4];
+  int S;
+  float scale, fill;
+  float* out;
+  int64_t ldo, bstride_o;
+  SplitOut so;
+};
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f16 descriptors: f32 D, f16 A and B; A K-major, B K- or MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool b_mn) {
+  return (1u << 4) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    attention_f16_kernel(const __grid_constant__ CUtensorMap tQh,
+                         const __grid_constant__ CUtensorMap tQl,
+                         const __grid_constant__ CUtensorMap tKh,
+                         const __grid_constant__ CUtensorMap tKl,
+                         const __grid_constant__ CUtensorMap tVh,
+                         const __grid_constant__ CUtensorMap tVl, const AttnF16Kern a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bar_load, bar_s, bar_o;
+  __shared__ uint32_t tmem_sh;
+  __shared__ float red_max[2][kRows], red_sum[2][kRows];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int quad = warp & 3, half = warp >> 2;
+  const int row = quad * 32 + (tid & 31), col0 = 64 * half;
+  const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
+
+  if (tid == 0) {
+    mbar_init(&bar_load, 1);
+    mbar_init(&bar_s, 1);
+    mbar_init(&bar_o, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // S: columns 0..127, O: 128..191
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
+        smem_u32(&tmem_sh)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
+
+  if (tid == 0) {
+    mbar_expect_tx(&bar_load, 6 * kTile);
+    tma_load_4d(sm + OFF_QH, &tQh, &bar_load, 0, h, 0, b);
+    tma_load_4d(sm + OFF_QL, &tQl, &bar_load, 0, h, 0, b);
+    tma_load_4d(sm + OFF_KH, &tKh, &bar_load, 0, h, 0, b);
+    tma_load_4d(sm + OFF_KL, &tKl, &bar_load, 0, h, 0, b);
+    tma_load_4d(sm + OFF_VH, &tVh, &bar_load, 0, h, 0, b);
+    tma_load_4d(sm + OFF_VL, &tVl, &bar_load, 0, h, 0, b);
+  }
+  // A mask that broadcasts over query rows is staged once (one row).
+  const bool mask_bcast = a.mask && a.ms[2] == 0;
+  uint8_t* mrow_s = sm + OFF_MASK;
+  if (mask_bcast) {
+    const uint8_t* mb = a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1];
+    for (int j = tid; j < kRows; j += kThreads) mrow_s[j] = j < a.S ? mb[(int64_t)j * a.ms[3]] : 0;
+  }
+  bool ok = __syncthreads_and(mbar_wait(&bar_load, 0)) != 0;
+  if (ok) {
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f16(kRows, kRows, false);
+      const uint32_t qh = smem_u32(sm + OFF_QH), ql = smem_u32(sm + OFF_QL);
+      const uint32_t kh = smem_u32(sm + OFF_KH), kl = smem_u32(sm + OFF_KL);
+#pragma unroll
+      for (int j = 0; j < kHd / 16; ++j) {  // 16 fp16 = 32 bytes per k-step
+        const uint64_t dqh = smem_desc(qh + j * 32, 16, 1024, 2), dql = smem_desc(ql + j * 32, 16, 1024, 2);
+        const uint64_t dkh = smem_desc(kh + j * 32, 16, 1024, 2), dkl = smem_desc(kl + j * 32, 16, 1024, 2);
+        mma_f16(tmem, dql, dkh, idesc, j != 0);
+        mma_f16(tmem, dqh, dkl, idesc, 1);
+        mma_f16(tmem, dqh, dkh, idesc, 1);
+      }
+      mma_commit(&bar_s);
+    }
+    ok = __syncthreads_and(mbar_wait(&bar_s, 0)) != 0;
+  }
+  if (ok) {
+    tc_fence_after();
+    float s[64];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float v[16];
+      tmem_ld16(tmem + lane_base + (uint32_t)(col0 + 16 * c), v);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) s[16 * c + q] = v[q];
+    }
+    const uint8_t* mrow_g =
+        (a.mask && !mask_bcast && row < a.S)
+            ? a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)row * a.ms[2]
+            : nullptr;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 64; ++q) {
+      const int j = col0 + q;
+      bool masked = false;
+      if (mask_bcast) masked = mrow_s[j] != 0;
+      else if (mrow_g && j < a.S) masked = mrow_g[(int64_t)j * a.ms[3]] != 0;
+      float v;
+      if (j >= a.S) v = -INFINITY;  // beyond the sequence: no weight at all
+      else if (masked) v = a.fill;
+      else v = a.scale * s[q];
+      s[q] = v;
+      mx = fmaxf(mx, v);
+    }
+    red_max[half][row] = mx;
+    __syncthreads();
+    mx = fmaxf(red_max[0][row], red_max[1][row]);
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 64; ++q) {
+      s[q] = expf(s[q] - mx);
+      sum += s[q];
+    }
+    red_sum[half][row] = sum;
+    __syncthreads();
+    const float inv = 1.0f / (red_sum[0][row] + red_sum[1][row]);
+    // P planes: keys [0, 64) and [64, 128) are two K atoms of [128 rows][128 B];
+    // this thread's 64 keys are atom `half`, 8 chunks of 8 keys.
+    uint8_t* ph = sm + OFF_PH + half * kTile;
+    uint8_t* pl = sm + OFF_PL + half * kTile;
+    bool bad = false;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+        hw[p] = split_pair(s[8 * c + 2 * p] * inv, s[8 * c + 2 * p + 1] * inv, lw[p], bad);
+      const uint32_t off = (uint32_t)row * 128 + ((uint32_t)(c ^ (row & 7)) << 4);
+      *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f16(kRows, kHd, true);
+      const uint32_t ph0 = smem_u32(sm + OFF_PH), pl0 = smem_u32(sm + OFF_PL);
+      const uint32_t vh = smem_u32(sm + OFF_VH), vl = smem_u32(sm + OFF_VL);
+#pragma unroll
+      for (int j = 0; j < kRows / 16; ++j) {  // 16 keys per k-step
+        const uint32_t aoff = (j >> 2) * kTile + (j & 3) * 32;
+        const uint64_t dph = smem_desc(ph0 + aoff, 16, 1024, 2), dpl = smem_desc(pl0 + aoff, 16, 1024, 2);
+        // V: MN-major SWIZZLE_128B, rows of 64 d (128 B), 8-key groups 1 KiB
+        // apart; a 16-key step advances 2 KiB. N = 64 is one atom wide.
+        const uint64_t dvh = smem_desc(vh + j * 2048, 8192, 1024, 2);
+        const uint64_t dvl = smem_desc(vl + j * 2048, 8192, 1024, 2);
+        mma_f16(tmem + kRows, dpl, dvh, idesc, j != 0);
+        mma_f16(tmem + kRows, dph, dvl, idesc, 1);
+        mma_f16(tmem + kRows, dph, dvh, idesc, 1);
+      }
+      mma_commit(&bar_o);
+    }
+    ok = __syncthreads_and(mbar_wait(&bar_o, 0)) != 0;
+  }
+  if (ok) {
+    tc_fence_after();
+    const int64_t col = h * kHd + 32 * half;
+    bool bad = false;
+#pragma unroll
+    for (int c0 = 0; c0 < 32; c0 += 16) {
+      float v[16];
+      tmem_ld16(tmem + lane_base + kRows + (uint32_t)(32 * half + c0), v);
+      if (row >= a.S) continue;
+      const int64_t o = (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + col + c0;
+      if (a.so.hi) {
+        uint32_t hw[8], lw[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) hw[q] = split_pair(v[2 * q], v[2 * q + 1], lw[q], bad);
+        uint4* hp = reinterpret_cast<uint4*>(a.so.hi + o);
+        uint4* lp = reinterpret_cast<uint4*>(a.so.lo + o);
+        hp[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        hp[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        lp[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        lp[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; q += 4)
+          *reinterpret_cast<float4*>(a.out + o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+      }
+    }
+    if (bad) atomicExch(a.so.range, 1);
+  } else if (tid == 0) {
+    atomicExch(&g_attn_f16_error, 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  }
+}
+
+// 4-D map over one fp16 plane of Q, K or V inside a [B, S, ld] tensor:
+// dims (d: 64, head: nH, s: S, b: B), box (64, 1, 128, 1), 128-byte swizzle.
+CUtensorMap plane_map(const uint16_t* base, int nH, int S, int B, int64_t ld, int64_t bstride) {
+  CUtensorMap m;
+  const cuuint64_t dims[4] = {(cuuint64_t)kHd, (cuuint64_t)nH, (cuuint64_t)S, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)kHd * 2, (cuuint64_t)ld * 2, (cuuint64_t)bstride * 2};
+  const cuuint32_t box[4] = {(cuuint32_t)kHd, 1, (cuuint32_t)kRows, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                                 const_cast<uint16_t*>(base), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw Error(INFERC_ERR_CUDA, "cuTensorMapEncodeTiled (fp16 attention) failed (" +
+                                     std::to_string((int)r) + ")");
+  return m;
+}
+
+}  // namespace
+
+int read_and_clear_attn_f16_error() {
+  int v = 0;
+  IDEV_CUDA(cudaMemcpyFromSymbol(&v, g_attn_f16_error, sizeof(int)));
+  if (v) {
+    const int z = 0;
+    IDEV_CUDA(cudaMemcpyToSymbol(g_attn_f16_error, &z, sizeof(int)));
+  }
+  return v;
+}
+
+bool attention_f16_supported(const AttnF16Args& a) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool planes = al(a.qh) && al(a.ql) && al(a.kh) && al(a.kl) && al(a.vh) && al(a.vl);
+  const bool out_ok = a.so.hi ? (al(a.so.hi) && al(a.so.lo) && a.so.range != nullptr)
+                              : (al(a.out) && a.ldo % 4 == 0 && a.bstride_o % 4 == 0);
+  return a.S >= 1 && a.S <= kRows && planes && out_ok && a.ld % 8 == 0 && a.bstride % 8 == 0 &&
+         a.ld >= a.nH * kHd && a.bstride >= a.S * a.ld && a.ldo % 8 == 0 && a.B < 65536 &&
+         a.nH < 65536;
+}
+
+void launch_attention_f16(const AttnF16Args& a, cudaStream_t st) {
+  IDEV_CHECK_ARG(attention_f16_supported(a), "fp16 attention: unsupported shape or alignment");
+  const int nH = (int)a.nH, S = (int)a.S, B = (int)a.B;
+  const CUtensorMap tqh = plane_map(a.qh, nH, S, B, a.ld, a.bstride);
+  const CUtensorMap tql = plane_map(a.ql, nH, S, B, a.ld, a.bstride);
+  const CUtensorMap tkh = plane_map(a.kh, nH, S, B, a.ld, a.bstride);
+  const CUtensorMap tkl = plane_map(a.kl, nH, S, B, a.ld, a.bstride);
+  const CUtensorMap tvh = plane_map(a.vh, nH, S, B, a.ld, a.bstride);
+  const CUtensorMap tvl = plane_map(a.vl, nH, S, B, a.ld, a.bstride);
+  AttnF16Kern k{};
+  k.mask = a.mask;
+  for (int i = 0; i < 4; ++i) k.ms[i] = a.ms[i];
+  k.S = S;
+  k.scale = a.scale;
+  k.fill = a.fill;
+  k.out = a.out;
+  k.ldo = a.ldo;
+  k.bstride_o = a.bstride_o;
+  k.so = a.so;
+  IDEV_CUDA(cudaFuncSetAttribute(attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmemBytes));
+  dim3 grid(1, (unsigned)nH, (unsigned)B);
+  attention_f16_kernel<<<grid, kThreads, kSmemBytes, st>>>(tqh, tql, tkh, tkl, tvh, tvl, k);
+  IDEV_LAUNCHED();
+}
+
+}  // namespace inferc_dev

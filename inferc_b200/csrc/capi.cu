@@ -327,6 +327,32 @@ int inferc_dev_gemm_f16s_planes(const uint16_t* a_hi, const uint16_t* a_lo, int6
   });
 }
 
+int inferc_dev_fused_attention_planes(const uint16_t* q_hi, const uint16_t* q_lo,
+                                      const uint16_t* k_hi, const uint16_t* k_lo,
+                                      const uint16_t* v_hi, const uint16_t* v_lo, int64_t ld,
+                                      const uint8_t* key_mask, int64_t B, int64_t S,
+                                      int64_t heads, float fill, float* out, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(B >= 0 && S >= 0 && heads > 0, "fused_attention_planes: bad shape");
+    if (B == 0 || S == 0) return;
+    AttnF16Args a{};
+    a.qh = q_hi; a.ql = q_lo; a.kh = k_hi; a.kl = k_lo; a.vh = v_hi; a.vl = v_lo;
+    a.ld = ld;
+    a.bstride = S * ld;
+    a.mask = key_mask;
+    a.ms[0] = S; a.ms[1] = 0; a.ms[2] = 0; a.ms[3] = 1;
+    a.B = B; a.S = S; a.nH = heads;
+    a.scale = 0.125f;  // 1 / sqrt(64)
+    a.fill = fill;
+    a.out = out;
+    a.ldo = heads * 64;
+    a.bstride_o = S * heads * 64;
+    IDEV_CHECK_ARG(attention_f16_supported(a),
+                   "fused_attention_planes: needs S <= 128, 16-byte aligned planes, ld % 8 == 0");
+    launch_attention_f16(a, as_stream(stream));
+  });
+}
+
 int inferc_dev_qkv_attention(const float* x, const float* w_big, const float* w_small,
                              const float* bqkv, const uint8_t* key_mask, int64_t B, int64_t S,
                              int64_t H, int64_t head_dim, float fill, float* scratch_qkv,

@@ -133,7 +133,7 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 // not serialise on returning atomics. Returns false when the kernel must
 // stop (timeout here or an error flagged elsewhere).
 // Split in two so that thread 0 can issue the next copies between its
-// arrival and its wait: grid_sync = grid_arrive + grid_wait.
+// arrival and its wait.
 __device__ void grid_arrive(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
   if (a.prof && step == 1 && blockIdx.x == 0 && threadIdx.x == 0 && tag >= 0)
     a.prof[2 * tag] = gtimer();
@@ -160,11 +160,6 @@ __device__ bool grid_wait(const MegaArgs& a, Smem& sm, int tag = -1, int step = 
   }
   __syncthreads();
   return sm.abort_flag == 0;
-}
-
-__device__ bool grid_sync(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
-  grid_arrive(a, sm, tag, step);
-  return grid_wait(a, sm, tag, step);
 }
 
 // Thread 0: bulk copy of a LayerNorm's gamma and beta (K floats each), and

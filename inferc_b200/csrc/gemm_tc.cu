@@ -387,10 +387,12 @@ int read_and_clear_attn_tc_error();
 int read_and_clear_f16_error();
 int read_and_clear_int4_tc_error();
 int read_and_clear_f16_2cta_error();
+int read_and_clear_attn_f16_error();
 
 int read_and_clear_tc_error() {
   int v = read_and_clear_attn_tc_error() | read_and_clear_f16_error() |
-          read_and_clear_int4_tc_error() | read_and_clear_f16_2cta_error();
+          read_and_clear_int4_tc_error() | read_and_clear_f16_2cta_error() |
+          read_and_clear_attn_f16_error();
   IDEV_CUDA(cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int)));
   if (v) {
     const int z = 0;

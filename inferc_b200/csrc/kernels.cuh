@@ -89,6 +89,22 @@ void launch_split_rows_f16(const float* x, int64_t rows, int64_t cols, int64_t l
 bool attention_tc_supported(const AttnArgs& a);
 void launch_attention_tc(const AttnArgs& a, cudaStream_t st);
 bool attention_tc_enabled();
+// Split-fp16 form (attention_f16.cu): q, k, v as fp16 hi / lo planes of a
+// [B, S, ld] tensor (head h at columns h*64..h*64+63), output as fp32 or as
+// fp16 planes (so.hi). Requires S <= 128, head_dim 64, 16-byte alignment.
+struct AttnF16Args {
+  const uint16_t *qh, *ql, *kh, *kl, *vh, *vl;
+  int64_t ld, bstride;  // elements
+  const uint8_t* mask;
+  int64_t ms[4];
+  int64_t B, S, nH;
+  float scale, fill;
+  float* out;
+  int64_t ldo, bstride_o;
+  SplitOut so;
+};
+bool attention_f16_supported(const AttnF16Args& a);
+void launch_attention_f16(const AttnF16Args& a, cudaStream_t st);
 inline bool attention_tc_usable(const AttnArgs& a) {
   return attention_tc_supported(a) && attention_tc_enabled();
 }

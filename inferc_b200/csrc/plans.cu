@@ -174,6 +174,7 @@ struct InfercEncoderPlan {
   bool f16 = false;
   uint16_t *xs_hi = nullptr, *xs_lo = nullptr, *hf_hi = nullptr, *hf_lo = nullptr;
   uint16_t *ctx_hi = nullptr, *ctx_lo = nullptr;
+  uint16_t *qkv_hi = nullptr, *qkv_lo = nullptr;  // fp16 planes of qkv (S <= 128)
   SplitWeight pre16, cls16;
   int* f16_range = nullptr;
   int* range_host = nullptr;  // pinned
@@ -227,7 +228,27 @@ struct InfercEncoderPlan {
       Epilogue e_qkv;
       e_qkv.bias = bqkv[l];
       e_qkv.bias_mode = 1;
-      if (use_f16)
+      // S <= 128 with the split-fp16 GEMMs: q, k, v stay as fp16 planes and
+      // attention runs on the fp16 tensor cores (attention_f16.cu).
+      AttnF16Args af{};
+      af.qh = qkv_hi; af.ql = qkv_lo;
+      af.kh = qkv_hi + H; af.kl = qkv_lo + H;
+      af.vh = qkv_hi + 2 * H; af.vl = qkv_lo + 2 * H;
+      af.ld = 3 * H;
+      af.bstride = S * 3 * H;
+      af.mask = cond;
+      af.ms[0] = S; af.ms[1] = 0; af.ms[2] = 0; af.ms[3] = 1;
+      af.B = B; af.S = S; af.nH = nH;
+      af.scale = 1.0f / std::sqrt((float)(H / nH));
+      af.fill = fill;
+      af.ldo = H;
+      af.bstride_o = S * H;
+      af.so = split_out(ctx_hi, ctx_lo, H);
+      const bool attn16 = use_f16 && qkv_hi && H / nH == 64 && attention_f16_supported(af);
+      if (attn16)
+        gemm16(split_a(xs_hi, xs_lo, H), wqkv[l], qkv, 3 * H, split_out(qkv_hi, qkv_lo, 3 * H), M,
+               3 * H, H, e_qkv, st);
+      else if (use_f16)
         gemm16(split_a(xs_hi, xs_lo, H), wqkv[l], qkv, 3 * H, SplitOut(), M, 3 * H, H, e_qkv, st);
       else
         gemm(x, H, wqkv[l], 3 * H, qkv, 3 * H, M, 3 * H, H, e_qkv, st);
@@ -244,9 +265,13 @@ struct InfercEncoderPlan {
       a.fill = fill;
       // With the split-fp16 path the tensor-core attention writes ctx as
       // fp16 planes for the output projection.
-      const bool ctx_split = use_f16 && attention_tc_usable(a);
-      if (ctx_split) a.so = split_out(ctx_hi, ctx_lo, H);
-      launch_attention(a, st);
+      const bool ctx_split = attn16 || (use_f16 && attention_tc_usable(a));
+      if (attn16) {
+        launch_attention_f16(af, st);
+      } else {
+        if (ctx_split) a.so = split_out(ctx_hi, ctx_lo, H);
+        launch_attention(a, st);
+      }
       Epilogue e_o;
       e_o.bias = bo[l];
       e_o.bias_mode = 1;
@@ -404,6 +429,10 @@ static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t 
     p->hf_lo = m.alloc<uint16_t>((size_t)M * F);
     p->ctx_hi = m.alloc<uint16_t>((size_t)M * H);
     p->ctx_lo = m.alloc<uint16_t>((size_t)M * H);
+    if (std::getenv("INFERC_ATTN_F16") == nullptr || std::getenv("INFERC_ATTN_F16")[0] != '0') {
+      p->qkv_hi = m.alloc<uint16_t>((size_t)M * 3 * H);
+      p->qkv_lo = m.alloc<uint16_t>((size_t)M * 3 * H);
+    }
     p->pre16 = split_weight_t(m, p->pre_w, H, H);
     p->cls16 = split_weight_t(m, p->cls_w, H, p->C);
     p->f16_range = m.alloc<int>(1);

@@ -313,3 +313,29 @@ def test_qkv_attention_prepared(port, B, S):
     ref = port.fused_attention(q.reshape(B, S, H), k.reshape(B, S, H), v.reshape(B, S, H),
                                km.reshape(B, 1, 1, S), 64, -3.0e38)
     np.testing.assert_allclose(host(out), ref, atol=5e-5)
+
+
+@pytest.mark.parametrize("B,S", [(1, 128), (8, 128), (3, 70), (1, 1), (2, 17), (4, 100)])
+def test_fused_attention_planes(port, B, S):
+    """Split-fp16 tensor-core attention on q, k, v planes cut from one
+    [B*S, 3H] pair (the encoder plan's layout), against the reference."""
+    from inferc_b200 import lib
+    L = lib.load()
+    H = 768
+    lens = np.random.default_rng(B * S + 1).integers(1, S + 1, size=B)
+    q, k, v, m = _attn_case(B, S, H, 64, lens, B + S + 7)
+    qkv = np.concatenate([q, k, v], axis=2).reshape(B * S, 3 * H)
+    x = T(qkv)
+    hi, lo = (torch.empty((B * S, 3 * H), dtype=torch.int16, device=DEV) for _ in range(2))
+    lib.check(L.inferc_dev_f16_split_rows(x.data_ptr(), B * S, 3 * H, 3 * H, hi.data_ptr(),
+                                          lo.data_ptr(), 3 * H, None))
+    out = torch.empty((B, S, H), device=DEV)
+    km = T(m.reshape(B, S))
+    e = 2  # bytes per int16
+    lib.check(L.inferc_dev_fused_attention_planes(
+        hi.data_ptr(), lo.data_ptr(), hi.data_ptr() + H * e, lo.data_ptr() + H * e,
+        hi.data_ptr() + 2 * H * e, lo.data_ptr() + 2 * H * e, 3 * H, km.data_ptr(), B, S, 12,
+        -3.4028234663852886e38, out.data_ptr(), None))
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    ref = port.fused_attention(q, k, v, m, 64, -3.4028234663852886e38)
+    np.testing.assert_allclose(host(out), ref, atol=2e-5)
