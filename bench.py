@@ -244,7 +244,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["decode", "int4", "sweep"],
+    ap.add_argument("--only", choices=["decode", "int4", "sweep", "c0"],
                     help="run one sub-benchmark alone and print its object (small cases for ncu)")
     ap.add_argument("--roofline-only", action="store_true",
                     help="time only the dominant kernel (FFN1 split-fp16 GEMM, B=256 S=128) "
@@ -263,7 +263,8 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if args.only:
-        fn = {"decode": decode_bench, "int4": int4_bench, "sweep": sweep_bench}[args.only]
+        fn = {"decode": decode_bench, "int4": int4_bench, "sweep": sweep_bench,
+              "c0": encoder_c0_bench}[args.only]
         print(json.dumps(fn(dev)), flush=True)
         return
     if args.roofline_only:
@@ -374,6 +375,7 @@ def main():
     torch.cuda.empty_cache()
 
     if rank == 0 and not args.no_decode:
+        result["encoder_c0"] = encoder_c0_bench(dev)
         result["decode"] = decode_bench(dev)
         result["int4_gemv"] = int4_bench(dev)
         result["qkv_attention_sweep"] = sweep_bench(dev)
@@ -386,6 +388,59 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _cpu_oracle(prefer_ref=True):
+    """The reference's own CPU kernels (oracle/_ref) when built, else the C
+    restatement: (object, kind), with every host core for the reference."""
+    os.environ.setdefault("INFERC_THREADS", str(os.cpu_count() or 1))
+    from oracle import oracle
+    if prefer_ref:
+        r = oracle.ref()
+        if r is not None:
+            return r, "reference"
+    return oracle.port(), "port"
+
+
+def encoder_c0_bench(dev):
+    """the DistilBERT-arch encoder at batch 1, seq 128
+    (ids 101 ... 102, mask all ones; tests/golden/encoder.npz c0): device ms
+    per sequence through the plan, and the reference's CPU kernels beside it."""
+    import torch
+
+    from inferc_b200 import plans, structs, synth
+    cfg = synth.EncoderConfig()
+    w = synth.encoder_weights(cfg, seed=0)
+    gold = np.load(os.path.join(ROOT, "tests", "golden", "encoder.npz"))
+    ids_h, mask_h = gold["c0_ids"], gold["c0_mask"]
+    p = plans.EncoderPlan(cfg, w, max_batch=1, max_seq=SEQ)
+    ids, mask = torch.from_numpy(ids_h).to(dev), torch.from_numpy(mask_h).to(dev)
+    out = torch.empty(1, cfg.n_classes, device=dev)
+    sptr = torch.cuda.current_stream().cuda_stream
+    for _ in range(5):
+        p.run(ids, mask, out, sptr)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(50):
+        p.run(ids, mask, out, sptr)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 50
+    diff = float(np.abs(out.cpu().numpy() - gold["c0_logits"]).max())
+    o, kind = _cpu_oracle()
+    st = structs.encoder_struct(cfg, w)
+    o.encoder_forward(st, ids_h, mask_h, cfg.n_classes)
+    t0 = time.perf_counter()
+    for _ in range(3):
+        o.encoder_forward(st, ids_h, mask_h, cfg.n_classes)
+    cpu_ms = (time.perf_counter() - t0) / 3 * 1e3
+    return {"metric": "encoder ms per sequence (DistilBERT-arch, batch 1, seq 128)", "value": ms,
+            "unit": "ms", "higher_is_better": False,
+            "config": {"workload": "BASELINE config 0: batch 1 x seq 128, mask all ones"},
+            "logits_max_abs_diff": diff,
+            "cpu_baseline": {"value": cpu_ms, "unit": "ms", "cores": os.cpu_count() or 1,
+                             "kind": kind, "sample": "the same sequence, mean of 3"}}
 
 
 def decode_bench(dev):
@@ -415,7 +470,26 @@ def decode_bench(dev):
             "weight_bytes_per_token": layer_bytes + lm_bytes,
             "achieved_gbs": gbs, "hbm_frac": gbs / pk["hbm_gbs"], "peak_basis": basis,
             "kernel": "decode_mega_kernel (one persistent cooperative launch for all steps)",
-            "published_m1_ms_per_token": 27.9}
+            "published_m1_ms_per_token": 27.9,
+            "cpu_baseline": _decode_cpu(cfg, w, prompt)}
+
+
+def _decode_cpu(cfg, w, prompt):
+    """The reference's CPU decode loop on the host: mean ms per step over 4
+    steps after the 32-token prefill (bounded sample of config 1)."""
+    from inferc_b200 import structs
+    o, kind = _cpu_oracle()
+    st = structs.gpt2_struct(cfg, w)
+    if kind == "reference":
+        _, _, ms = o.gpt2_decode(st, prompt, 5)
+    else:
+        t0 = time.perf_counter()
+        o.gpt2_decode(st, prompt, 1)
+        t1 = time.perf_counter()
+        o.gpt2_decode(st, prompt, 5)
+        ms = ((time.perf_counter() - t1) - (t1 - t0)) / 4 * 1e3
+    return {"value": ms, "unit": "ms/token", "cores": os.cpu_count() or 1, "kind": kind,
+            "sample": "prompt 32 + 5 tokens (4 timed single-token steps)"}
 
 
 def _flush_l2(buf):
@@ -467,7 +541,20 @@ def int4_bench(dev):
             "higher_is_better": False, "matrices": len(mats), "bytes": nbytes,
             "achieved_gbs": gbs, "hbm_peak_gbs": pk["hbm_gbs"], "frac": gbs / pk["hbm_gbs"],
             "peak_basis": basis, "l2": "4 rotating copies of the set (252 MB > L2)",
-            "published_m1_ms_123M_weights": 7.73}
+            "published_m1_ms_123M_weights": 7.73,
+            "cpu_baseline": _int4_cpu(mats)}
+
+
+def _int4_cpu(mats):
+    """The C restatement of scalar_int4_gemv_perRow (the reference's int4
+    GEMV exists only as AMX code) over the full set, one host thread."""
+    o, kind = _cpu_oracle(prefer_ref=False)
+    t0 = time.perf_counter()
+    for m in mats:
+        o.int4_gemv_rowscale(m.w, m.scales, m.x)
+    ms = (time.perf_counter() - t0) * 1e3
+    return {"value": ms, "unit": "ms", "cores": 1, "kind": kind,
+            "sample": "the full 49-matrix set, once (scalar, double accumulation)"}
 
 
 def sweep_bench(dev):
@@ -522,7 +609,17 @@ def sweep_bench(dev):
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / 10
             flops = 3538944.0 * B * S + 3072.0 * B * S * S
-            out.append({"seq": S, "batch": B, "ms": ms, "tflops": flops / (ms / 1e3) / 1e12})
+            row = {"seq": S, "batch": B, "ms": ms, "tflops": flops / (ms / 1e3) / 1e12}
+            if B == 8:  # bounded CPU sample: the reference's kernels on the host
+                o, kind = _cpu_oracle()
+                mask4 = mask.reshape(B, 1, 1, S)
+                t0 = time.perf_counter()
+                q, k, v = o.fused_qkv(x.reshape(B, S, H), *ws)
+                o.fused_attention(q, k, v, mask4, 64, -3.4028234663852886e38)
+                row["cpu_baseline"] = {"value": (time.perf_counter() - t0) * 1e3, "unit": "ms",
+                                       "cores": os.cpu_count() or 1, "kind": kind,
+                                       "sample": "this (seq, batch), once"}
+            out.append(row)
     return out
 
 
