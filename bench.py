@@ -558,10 +558,11 @@ def _int4_cpu(mats):
 
 
 def sweep_bench(dev):
-    """fused QKV projection (one tensor-core GEMM over the
-    prepared [768, 2304] weight) + masked FusedAttention at hidden 768, 12
-    heads, seq {128, 512} x batch {1, 8, 64}, valid lengths uniform in
-    [16, seq]. Reports ms per (QKV + attention) and padded TFLOP/s."""
+    """fused QKV projection + masked FusedAttention at
+    hidden 768, 12 heads, seq {128, 512} x batch {1, 8, 64}, valid lengths
+    uniform in [16, seq], through inferc_dev_qkv_attention_f16 (split-fp16
+    prepared weights, planes end to end). Reports ms per (QKV + attention)
+    and padded TFLOP/s."""
     import torch
 
     from inferc_b200 import lib as _lib
@@ -571,25 +572,29 @@ def sweep_bench(dev):
     sptr = torch.cuda.current_stream().cuda_stream
     for S in (128, 512):
         for B in (1, 8, 64):
+            sptr = torch.cuda.current_stream().cuda_stream  # (the graph capture rebinds it)
             x, ws, lens = synth.attention_sweep_inputs(B, S)
             H = 768
             wcat = np.concatenate([ws[0], ws[2], ws[4]], axis=1).astype(np.float32)
             bcat = np.concatenate([ws[1], ws[3], ws[5]]).astype(np.float32)
             xd = torch.from_numpy(x).to(dev)
-            wd = torch.from_numpy(wcat).to(dev)
+            wd = torch.from_numpy(np.ascontiguousarray(wcat)).to(dev)
             bd = torch.from_numpy(bcat).to(dev)
-            wb, wsm = torch.empty_like(wd), torch.empty_like(wd)
-            _lib.check(L.inferc_dev_tf32_split(wd.data_ptr(), wb.data_ptr(), wsm.data_ptr(),
-                                               wd.numel(), sptr))
+            kp = L.inferc_dev_f16_kp(H)
+            wh, wl = (torch.empty(3 * H, kp, dtype=torch.int16, device=dev) for _ in range(2))
+            sc = torch.empty(2, device=dev)
+            _lib.check(L.inferc_dev_f16_split(wd.data_ptr(), H, 3 * H, 3 * H, wh.data_ptr(),
+                                              wl.data_ptr(), sc.data_ptr(), sptr))
             mask = (np.arange(S)[None, :] >= lens[:, None]).astype(np.uint8)
             md = torch.from_numpy(mask).to(dev)
-            qkv = torch.empty(B * S, 3 * H, device=dev)
+            scratch = torch.empty(8 * B * S * H, dtype=torch.int16, device=dev)
             ctx = torch.empty(B, S, H, device=dev)
 
             def run():
-                _lib.check(L.inferc_dev_qkv_attention(
-                    xd.data_ptr(), wb.data_ptr(), wsm.data_ptr(), bd.data_ptr(), md.data_ptr(),
-                    B, S, H, 64, -3.4028234663852886e38, qkv.data_ptr(), ctx.data_ptr(), sptr))
+                _lib.check(L.inferc_dev_qkv_attention_f16(
+                    xd.data_ptr(), wh.data_ptr(), wl.data_ptr(), sc.data_ptr(), bd.data_ptr(),
+                    md.data_ptr(), B, S, H, 64, -3.4028234663852886e38, scratch.data_ptr(),
+                    ctx.data_ptr(), sptr))
             for _ in range(3):
                 run()
             torch.cuda.synchronize()

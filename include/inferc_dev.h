@@ -200,6 +200,18 @@ int inferc_dev_qkv_attention(const float* x, const float* w_big,
                              int64_t H, int64_t head_dim, float fill,
                              float* scratch_qkv, float* out, void* stream);
 
+/* inferc_dev_qkv_attention on split-fp16 prepared weights (w_hi, w_lo,
+ * w_scale2 from inferc_dev_f16_split of Wqkv [H, 3H]): x is split into fp16
+ * planes, the QKV GEMM writes q, k, v as planes, and the split-fp16
+ * tensor-core attention (head_dim 64, S <= 4096) reads them. scratch: caller
+ * buffer of 8*B*S*H uint16 (x planes, then the qkv planes). Values fp16
+ * cannot carry are reported like inferc_dev_gemm_f16s's. */
+int inferc_dev_qkv_attention_f16(const float* x, const uint16_t* w_hi, const uint16_t* w_lo,
+                                 const float* w_scale2, const float* bqkv,
+                                 const uint8_t* key_mask, int64_t B, int64_t S, int64_t H,
+                                 int64_t head_dim, float fill, uint16_t* scratch, float* out,
+                                 void* stream);
+
 /* ------------------------------------------------------------ decode ops */
 
 /* Batch-1 fp32 GEMV with the Gemm epilogue, y[N] = act(x[K] W[K,N] + b[N]

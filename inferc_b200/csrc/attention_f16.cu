@@ -1,8 +1,8 @@
-// FusedAttention (head_dim 64, S <= 128) on the fp16 tensor cores with
+// FusedAttention (head_dim 64, S <= 4096) on the fp16 tensor cores with
 // fp32-level accuracy, for q, k and v given as the split-fp16 planes the
 // QKV GEMM writes (x = hi + lo, gemm_f16s.cu's representation).
 //
-// One CTA per (batch, head), as in attention_tc.cu, but:
+// S <= 128: one CTA per (batch, head), as in attention_tc.cu, but:
 //   * no split step: TMA loads the six hi / lo head tiles (96 KB) directly;
 //   * S = Q K^T and O = P V each take three kind::f16 MMAs per product
 //     (lo hi + hi lo + hi hi), at twice the tf32 rate;
@@ -271,6 +271,228 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// ---------------------------------------------------------------- S > 128
+// Flash form: CTA (q-block, head, batch) holds its 128 query rows and loops
+// over 128-key blocks with an online softmax. Per block: S_blk = Q K_blk^T
+// (TMEM), running row max m and sum l are updated (two threads per row,
+// 64 keys each), P_blk = exp(s - m) (in (0, 1], fp16 hi / lo) and
+// O_blk = P_blk V_blk (a fresh TMEM tile) is merged into the registers:
+// O = O c + O_blk with c = exp(m_old - m). The next block's K / V load is
+// issued as soon as this block's PV MMAs are done. O / l is stored at the end.
+// Shared memory: Q 32 KB, K 32 KB, V 32 KB, P 64 KB (one CTA per SM).
+constexpr uint32_t FL_Q = 0, FL_K = 2 * kTile, FL_V = 4 * kTile, FL_P = 6 * kTile;
+constexpr uint32_t FL_MASK = 10 * kTile;  // one mask row, up to kFlashMaxS bytes
+constexpr int kFlashMaxS = 4096;
+constexpr uint32_t kFlashSmem = 10 * kTile + kFlashMaxS + 1024;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_f16_flash_kernel(const __grid_constant__ CUtensorMap tQh,
+                               const __grid_constant__ CUtensorMap tQl,
+                               const __grid_constant__ CUtensorMap tKh,
+                               const __grid_constant__ CUtensorMap tKl,
+                               const __grid_constant__ CUtensorMap tVh,
+                               const __grid_constant__ CUtensorMap tVl, const AttnF16Kern a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bar_q, bar_kv, bar_s, bar_o;
+  __shared__ uint32_t tmem_sh;
+  __shared__ float red_max[2][kRows], red_sum[2][kRows];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int quad = warp & 3, half = warp >> 2;
+  const int lrow = quad * 32 + (tid & 31), col0 = 64 * half;
+  const int row = qb * kRows + lrow;  // query row in the sequence
+  const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
+  const int nkb = (a.S + kRows - 1) / kRows;
+
+  if (tid == 0) {
+    mbar_init(&bar_q, 1);
+    mbar_init(&bar_kv, 1);
+    mbar_init(&bar_s, 1);
+    mbar_init(&bar_o, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
+        smem_u32(&tmem_sh)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
+  auto load_kv = [&](int kb) {
+    mbar_expect_tx(&bar_kv, 4 * kTile);
+    tma_load_4d(sm + FL_K, &tKh, &bar_kv, 0, h, kb * kRows, b);
+    tma_load_4d(sm + FL_K + kTile, &tKl, &bar_kv, 0, h, kb * kRows, b);
+    tma_load_4d(sm + FL_V, &tVh, &bar_kv, 0, h, kb * kRows, b);
+    tma_load_4d(sm + FL_V + kTile, &tVl, &bar_kv, 0, h, kb * kRows, b);
+  };
+  if (tid == 0) {
+    mbar_expect_tx(&bar_q, 2 * kTile);
+    tma_load_4d(sm + FL_Q, &tQh, &bar_q, 0, h, qb * kRows, b);
+    tma_load_4d(sm + FL_Q + kTile, &tQl, &bar_q, 0, h, qb * kRows, b);
+    load_kv(0);
+  }
+  const bool mask_bcast = a.mask && a.ms[2] == 0;
+  uint8_t* mrow_s = sm + FL_MASK;
+  if (mask_bcast) {
+    const uint8_t* mb = a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1];
+    for (int j = tid; j < a.S; j += kThreads) mrow_s[j] = mb[(int64_t)j * a.ms[3]];
+  }
+  const uint8_t* mrow_g =
+      (a.mask && !mask_bcast && row < a.S)
+          ? a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)row * a.ms[2]
+          : nullptr;
+  bool ok = __syncthreads_and(mbar_wait(&bar_q, 0)) != 0;
+  float m_run = -INFINITY, l_run = 0.f;
+  float o_acc[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) o_acc[i] = 0.f;
+  for (int kb = 0; kb < nkb && ok; ++kb) {
+    ok = __syncthreads_and(mbar_wait(&bar_kv, kb & 1)) != 0;
+    if (!ok) break;
+    if (tid == 0) {  // S_blk = Q K_blk^T
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f16(kRows, kRows, false);
+      const uint32_t qh = smem_u32(sm + FL_Q), ql = qh + kTile;
+      const uint32_t kh = smem_u32(sm + FL_K), kl = kh + kTile;
+#pragma unroll
+      for (int j = 0; j < kHd / 16; ++j) {
+        const uint64_t dqh = smem_desc(qh + j * 32, 16, 1024, 2), dql = smem_desc(ql + j * 32, 16, 1024, 2);
+        const uint64_t dkh = smem_desc(kh + j * 32, 16, 1024, 2), dkl = smem_desc(kl + j * 32, 16, 1024, 2);
+        mma_f16(tmem, dql, dkh, idesc, j != 0);
+        mma_f16(tmem, dqh, dkl, idesc, 1);
+        mma_f16(tmem, dqh, dkh, idesc, 1);
+      }
+      mma_commit(&bar_s);
+    }
+    ok = __syncthreads_and(mbar_wait(&bar_s, kb & 1)) != 0;
+    if (!ok) break;
+    tc_fence_after();
+    float s[64];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float v[16];
+      tmem_ld16(tmem + lane_base + (uint32_t)(col0 + 16 * c), v);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) s[16 * c + q] = v[q];
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 64; ++q) {
+      const int j = kb * kRows + col0 + q;
+      bool masked = false;
+      if (j < a.S) {
+        if (mask_bcast) masked = mrow_s[j] != 0;
+        else if (mrow_g) masked = mrow_g[(int64_t)j * a.ms[3]] != 0;
+      }
+      float v;
+      if (j >= a.S) v = -INFINITY;
+      else if (masked) v = a.fill;
+      else v = a.scale * s[q];
+      s[q] = v;
+      mx = fmaxf(mx, v);
+    }
+    red_max[half][lrow] = mx;
+    __syncthreads();
+    const float m_new = fmaxf(m_run, fmaxf(red_max[0][lrow], red_max[1][lrow]));
+    const float corr = expf(m_run - m_new);  // 0 on the first block (m_run = -inf)
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 64; ++q) {
+      s[q] = expf(s[q] - m_new);
+      sum += s[q];
+    }
+    red_sum[half][lrow] = sum;
+    uint8_t* ph = sm + FL_P + half * kTile;
+    uint8_t* pl = sm + FL_P + 2 * kTile + half * kTile;
+    bool bad = false;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) hw[p] = split_pair(s[8 * c + 2 * p], s[8 * c + 2 * p + 1], lw[p], bad);
+      const uint32_t off = (uint32_t)lrow * 128 + ((uint32_t)(c ^ (lrow & 7)) << 4);
+      *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    l_run = l_run * corr + red_sum[0][lrow] + red_sum[1][lrow];
+    m_run = m_new;
+    if (tid == 0) {  // O_blk = P_blk V_blk, then the next K / V block
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f16(kRows, kHd, true);
+      const uint32_t ph0 = smem_u32(sm + FL_P), pl0 = ph0 + 2 * kTile;
+      const uint32_t vh = smem_u32(sm + FL_V), vl = vh + kTile;
+#pragma unroll
+      for (int j = 0; j < kRows / 16; ++j) {
+        const uint32_t aoff = (j >> 2) * kTile + (j & 3) * 32;
+        const uint64_t dph = smem_desc(ph0 + aoff, 16, 1024, 2), dpl = smem_desc(pl0 + aoff, 16, 1024, 2);
+        const uint64_t dvh = smem_desc(vh + j * 2048, 8192, 1024, 2);
+        const uint64_t dvl = smem_desc(vl + j * 2048, 8192, 1024, 2);
+        mma_f16(tmem + kRows, dpl, dvh, idesc, j != 0);
+        mma_f16(tmem + kRows, dph, dvl, idesc, 1);
+        mma_f16(tmem + kRows, dph, dvh, idesc, 1);
+      }
+      mma_commit(&bar_o);
+    }
+    ok = __syncthreads_and(mbar_wait(&bar_o, kb & 1)) != 0;
+    if (!ok) break;
+    if (tid == 0 && kb + 1 < nkb) load_kv(kb + 1);  // K, V and P are free again
+    tc_fence_after();
+#pragma unroll
+    for (int c0 = 0; c0 < 32; c0 += 16) {
+      float v[16];
+      tmem_ld16(tmem + lane_base + kRows + (uint32_t)(32 * half + c0), v);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) o_acc[c0 + q] = o_acc[c0 + q] * corr + v[q];
+    }
+    tc_fence_before();
+  }
+  if (ok) {
+    const float inv = 1.0f / l_run;
+    if (row < a.S) {
+      const int64_t o = (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + h * kHd + 32 * half;
+      bool bad = false;
+#pragma unroll
+      for (int c0 = 0; c0 < 32; c0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) v[q] = o_acc[c0 + q] * inv;
+        if (a.so.hi) {
+          uint32_t hw[8], lw[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) hw[q] = split_pair(v[2 * q], v[2 * q + 1], lw[q], bad);
+          uint4* hp = reinterpret_cast<uint4*>(a.so.hi + o + c0);
+          uint4* lp = reinterpret_cast<uint4*>(a.so.lo + o + c0);
+          hp[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          hp[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+          lp[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          lp[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 16; q += 4)
+            *reinterpret_cast<float4*>(a.out + o + c0 + q) =
+                make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+        }
+      }
+      if (bad) atomicExch(a.so.range, 1);
+    }
+  } else if (tid == 0) {
+    atomicExch(&g_attn_f16_error, 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  }
+}
+
 // 4-D map over one fp16 plane of Q, K or V inside a [B, S, ld] tensor:
 // dims (d: 64, head: nH, s: S, b: B), box (64, 1, 128, 1), 128-byte swizzle.
 CUtensorMap plane_map(const uint16_t* base, int nH, int S, int B, int64_t ld, int64_t bstride) {
@@ -307,7 +529,7 @@ bool attention_f16_supported(const AttnF16Args& a) {
   const bool planes = al(a.qh) && al(a.ql) && al(a.kh) && al(a.kl) && al(a.vh) && al(a.vl);
   const bool out_ok = a.so.hi ? (al(a.so.hi) && al(a.so.lo) && a.so.range != nullptr)
                               : (al(a.out) && a.ldo % 4 == 0 && a.bstride_o % 4 == 0);
-  return a.S >= 1 && a.S <= kRows && planes && out_ok && a.ld % 8 == 0 && a.bstride % 8 == 0 &&
+  return a.S >= 1 && a.S <= kFlashMaxS && planes && out_ok && a.ld % 8 == 0 && a.bstride % 8 == 0 &&
          a.ld >= a.nH * kHd && a.bstride >= a.S * a.ld && a.ldo % 8 == 0 && a.B < 65536 &&
          a.nH < 65536;
 }
@@ -331,10 +553,18 @@ void launch_attention_f16(const AttnF16Args& a, cudaStream_t st) {
   k.ldo = a.ldo;
   k.bstride_o = a.bstride_o;
   k.so = a.so;
-  IDEV_CUDA(cudaFuncSetAttribute(attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kSmemBytes));
-  dim3 grid(1, (unsigned)nH, (unsigned)B);
-  attention_f16_kernel<<<grid, kThreads, kSmemBytes, st>>>(tqh, tql, tkh, tkl, tvh, tvl, k);
+  if (S <= kRows) {  // one key block: the two-CTAs-per-SM kernel
+    IDEV_CUDA(cudaFuncSetAttribute(attention_f16_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    dim3 grid(1, (unsigned)nH, (unsigned)B);
+    attention_f16_kernel<<<grid, kThreads, kSmemBytes, st>>>(tqh, tql, tkh, tkl, tvh, tvl, k);
+  } else {
+    IDEV_CUDA(cudaFuncSetAttribute(attention_f16_flash_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlashSmem));
+    dim3 grid((unsigned)((S + kRows - 1) / kRows), (unsigned)nH, (unsigned)B);
+    attention_f16_flash_kernel<<<grid, kThreads, kFlashSmem, st>>>(tqh, tql, tkh, tkl, tvh, tvl,
+                                                                   k);
+  }
   IDEV_LAUNCHED();
 }
 

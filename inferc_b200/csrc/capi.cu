@@ -382,6 +382,57 @@ int inferc_dev_qkv_attention(const float* x, const float* w_big, const float* w_
   });
 }
 
+int inferc_dev_qkv_attention_f16(const float* x, const uint16_t* w_hi, const uint16_t* w_lo,
+                                 const float* w_scale2, const float* bqkv,
+                                 const uint8_t* key_mask, int64_t B, int64_t S, int64_t H,
+                                 int64_t head_dim, float fill, uint16_t* scratch, float* out,
+                                 void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(B >= 0 && S >= 0 && H > 0 && head_dim == 64 && H % 64 == 0,
+                   "qkv_attention_f16: head_dim must be 64 and divide H");
+    IDEV_CHECK_ARG(x && w_hi && w_lo && w_scale2 && bqkv && scratch && out,
+                   "qkv_attention_f16: null pointer");
+    if (B == 0 || S == 0) return;
+    cudaStream_t st = as_stream(stream);
+    const int64_t M = B * S;
+    uint16_t* xh = scratch;
+    uint16_t* xl = xh + M * H;
+    uint16_t* qh = xl + M * H;
+    uint16_t* ql = qh + M * 3 * H;
+    int* range = f16_range_flag_ptr();
+    launch_split_rows_f16(x, M, H, H, xh, xl, H, range, st);
+    F16GemmA a;
+    a.hi = xh;
+    a.lo = xl;
+    a.ld = H;
+    SplitOut so;
+    so.hi = qh;
+    so.lo = ql;
+    so.ld = 3 * H;
+    so.range = range;
+    Epilogue ep;
+    ep.bias = bqkv;
+    ep.bias_mode = 1;
+    launch_gemm_f16s(a, w_hi, w_lo, f16_weight_kp(H), w_scale2, range, nullptr, 3 * H, so, M,
+                     3 * H, H, ep, st);
+    AttnF16Args at{};
+    at.qh = qh; at.ql = ql; at.kh = qh + H; at.kl = ql + H; at.vh = qh + 2 * H; at.vl = ql + 2 * H;
+    at.ld = 3 * H;
+    at.bstride = S * 3 * H;
+    at.mask = key_mask;
+    at.ms[0] = S; at.ms[1] = 0; at.ms[2] = 0; at.ms[3] = 1;
+    at.B = B; at.S = S; at.nH = H / 64;
+    at.scale = 0.125f;
+    at.fill = fill;
+    at.out = out;
+    at.ldo = H;
+    at.bstride_o = S * H;
+    IDEV_CHECK_ARG(attention_f16_supported(at),
+                   "qkv_attention_f16: needs S <= 4096 and 16-byte aligned buffers");
+    launch_attention_f16(at, st);
+  });
+}
+
 int inferc_dev_gemv(const float* x, const float* w, const float* b, const float* resid, float* y,
                     int64_t K, int64_t N, int act, void* stream) {
   return guard([&] {

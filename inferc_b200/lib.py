@@ -56,6 +56,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
                                      _i64, _i64, _i64, _i, _p], _i),
     "inferc_dev_fused_attention_planes": ([_p] * 6 + [_i64, _p, _i64, _i64, _i64, _f, _p, _p],
                                           _i),
+    "inferc_dev_qkv_attention_f16": ([_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _p, _p,
+                                      _p], _i),
     "inferc_dev_qkv_attention": ([_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _p, _p, _p],
                                  _i),
     "inferc_dev_gemv": ([_p, _p, _p, _p, _p, _i64, _i64, _i, _p], _i),

@@ -315,10 +315,12 @@ def test_qkv_attention_prepared(port, B, S):
     np.testing.assert_allclose(host(out), ref, atol=5e-5)
 
 
-@pytest.mark.parametrize("B,S", [(1, 128), (8, 128), (3, 70), (1, 1), (2, 17), (4, 100)])
+@pytest.mark.parametrize("B,S", [(1, 128), (8, 128), (3, 70), (1, 1), (2, 17), (4, 100),
+                                 (2, 512), (1, 300), (3, 257)])
 def test_fused_attention_planes(port, B, S):
     """Split-fp16 tensor-core attention on q, k, v planes cut from one
-    [B*S, 3H] pair (the encoder plan's layout), against the reference."""
+    [B*S, 3H] pair (the encoder plan's layout), against the reference; S > 128
+    runs the flash form (online softmax over 128-key blocks)."""
     from inferc_b200 import lib
     L = lib.load()
     H = 768
@@ -339,3 +341,33 @@ def test_fused_attention_planes(port, B, S):
     lib.check(L.inferc_dev_stream_synchronize(None))
     ref = port.fused_attention(q, k, v, m, 64, -3.4028234663852886e38)
     np.testing.assert_allclose(host(out), ref, atol=2e-5)
+
+
+@pytest.mark.parametrize("B,S", [(2, 128), (1, 512), (3, 40)])
+def test_qkv_attention_f16(port, B, S):
+    """inferc_dev_qkv_attention_f16 (split-fp16 weights, planes end to end) ==
+    FusedQKV + FusedAttention of the reference."""
+    from inferc_b200 import lib
+    L = lib.load()
+    x, ws, lens = synth.attention_sweep_inputs(B, S, seed=B + S + 3)
+    H = 768
+    wcat = T(np.ascontiguousarray(np.concatenate([ws[0], ws[2], ws[4]], axis=1)))
+    bcat = T(np.concatenate([ws[1], ws[3], ws[5]]).astype(np.float32))
+    kp = L.inferc_dev_f16_kp(H)
+    wh, wl = (torch.empty((3 * H, kp), dtype=torch.int16, device=DEV) for _ in range(2))
+    sc = torch.empty(2, device=DEV)
+    lib.check(L.inferc_dev_f16_split(wcat.data_ptr(), H, 3 * H, 3 * H, wh.data_ptr(),
+                                     wl.data_ptr(), sc.data_ptr(), None))
+    km = (np.arange(S)[None, :] >= lens[:, None]).astype(np.uint8)
+    scratch = torch.empty(8 * B * S * H, dtype=torch.int16, device=DEV)
+    out = torch.empty(B, S, H, device=DEV)
+    xd, md = T(x), T(km)
+    lib.check(L.inferc_dev_qkv_attention_f16(xd.data_ptr(), wh.data_ptr(), wl.data_ptr(),
+                                             sc.data_ptr(), bcat.data_ptr(), md.data_ptr(), B, S,
+                                             H, 64, -3.0e38, scratch.data_ptr(), out.data_ptr(),
+                                             None))
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    q, k, v = port.fused_qkv(x.reshape(B * S, H), ws[0], ws[1], ws[2], ws[3], ws[4], ws[5])
+    ref = port.fused_attention(q.reshape(B, S, H), k.reshape(B, S, H), v.reshape(B, S, H),
+                               km.reshape(B, 1, 1, S), 64, -3.0e38)
+    np.testing.assert_allclose(host(out), ref, atol=5e-5)
