@@ -25,9 +25,12 @@
 //   int4_digits_kernel  one CTA per matrix: max|x|, the digit planes, already
 //                       in the shared-memory tile layout the MMA reads, and
 //                       sum a_k, into a per-device scratch buffer;
-//   gemv_int4_tc_kernel persistent, one CTA per SM over a contiguous range of
-//                       128-row blocks of the batch's matrices (ranges of
-//                       equal numbers of 16 KB slabs), started with
+//   gemv_int4_tc_kernel persistent, one CTA per SM over an equal contiguous
+//                       range of the batch's 16 KB slabs (128 rows x 256 K);
+//                       a 128-row block cut by a range boundary is summed
+//                       by its CTAs in exact int64 partial sums, and the
+//                       CTA that adds the block's last slab writes it;
+//                       started with
 //                       programmatic dependent launch so the weight stream
 //                       begins while the digits are being made.
 // GEMV warp roles (320 threads):
@@ -99,6 +102,8 @@ struct Int4TcBatch {
   int blk_start[kMaxMats + 1];   // prefix sums of 128-row blocks
   int slab_start[kMaxMats + 1];  // prefix sums of slabs (blocks x kslabs)
   int count;
+  unsigned long long* part_sum;  // [blocks x 128] row partial sums of split blocks (zero at rest)
+  int* part_cnt;                 // [blocks] slabs added so far (zero at rest)
 };
 
 // The batch's per-matrix data, copied to shared memory at kernel start: the
@@ -111,24 +116,25 @@ struct Int4TcMeta {
   Int4TcMat m[kMaxMats];
 };
 
-// First block of CTA c when the batch's slabs are split evenly over G CTAs:
-// block j (slab offset o_j) belongs to the CTA c with o_j G in [c S, (c+1) S).
-__device__ __forceinline__ int first_block(const Int4TcMeta& bt, int c, int G) {
-  const long long target = (long long)c * bt.slab_start[bt.count];  // compare o_j * G >= target
-  for (int mi = 0; mi < bt.count; ++mi) {
-    // the first block at or past the target lies in matrix mi when the
-    // target is below the end of its slab range (one division, here only)
-    if (target > (long long)bt.slab_start[mi + 1] * G - bt.m[mi].kslabs * (long long)G) {
-      if (mi + 1 < bt.count) continue;
-    }
-    const long long ks = bt.m[mi].kslabs;
-    const long long base = (long long)bt.slab_start[mi] * G;
-    const int nb = bt.blk_start[mi + 1] - bt.blk_start[mi];
-    long long t = 0;
-    if (target > base) t = (target - base + ks * G - 1) / (ks * G);
-    if (t < nb) return bt.blk_start[mi] + (int)t;
-  }
-  return bt.blk_start[bt.count];
+// Position in the batch's sequence of slabs: matrix mi, 128-row block j
+// (global index), slab sl inside the block. CTA c of G owns the slabs
+// [c S / G, (c+1) S / G) of the S in the batch, so a block whose slabs are
+// split between CTAs is finished by whichever of them adds its last slab.
+struct SlabPos {
+  int mi, j, sl;
+};
+
+__device__ __forceinline__ SlabPos slab_pos(const Int4TcMeta& bt, int g) {
+  int mi = 0;
+  while (mi + 1 < bt.count && g >= bt.slab_start[mi + 1]) ++mi;
+  const int off = g - bt.slab_start[mi], ks = bt.m[mi].kslabs;
+  return SlabPos{mi, bt.blk_start[mi] + off / ks, off % ks};
+}
+
+// Step to the first slab of the next block.
+__device__ __forceinline__ void next_block(const Int4TcMeta& bt, SlabPos& p) {
+  p.sl = 0;
+  if (++p.j >= bt.blk_start[p.mi + 1] && p.mi + 1 < bt.count) ++p.mi;
 }
 
 // kind::i8: D s32, A unsigned 8-bit, B signed 8-bit, both K-major.
@@ -160,6 +166,11 @@ __device__ __forceinline__ bool epi_all(bool v) {
       : "r"((uint32_t)v), "r"(kEpi)
       : "memory");
   return r != 0;
+}
+
+// Barrier of the 128 epilogue threads (named barrier 3).
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 3, %0;" ::"r"(kEpi) : "memory");
 }
 
 // One 16-byte group of digit-plane bytes: (atom a, digit row i, physical
@@ -248,6 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], b_ready, b_free;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
+  __shared__ int last_sh;
 
   __shared__ Int4TcMeta bt;
   {
@@ -263,9 +275,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto fail = [&]() {
     abort_sh = 1;
     atomicExch(&g_int4_tc_error, 1);
-  };
-  auto mat_of = [&](int j, int& mi) {
-    while (j >= bt.blk_start[mi + 1]) ++mi;
   };
 
   if (threadIdx.x == 0) {
@@ -292,32 +301,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_sh;
-  const int j0 = first_block(bt, blockIdx.x, gridDim.x);
-  const int j1 = first_block(bt, blockIdx.x + 1, gridDim.x);
+  const int S = bt.slab_start[bt.count];
+  const int g0 = (int)((long long)blockIdx.x * S / gridDim.x);
+  const int g1 = (int)((long long)(blockIdx.x + 1) * S / gridDim.x);
 
   if (warp == 0) {
     if (lane == 0) {  // ---------------- TMA producer
-      int g = 0, mi = 0;
-      for (int j = j0; j < j1 && !abort_sh; ++j) {
-        mat_of(j, mi);
-        const int row0 = (j - bt.blk_start[mi]) * 128;
-        for (int sl = 0; sl < bt.m[mi].kslabs; ++sl, ++g) {
-          const int s = g % kStages, r = g / kStages;
-          if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1)) {
-            fail();
-            break;
-          }
-          mbar_expect_tx(&full_bar[s], kSlab);
-          tma_load_2d(smem + s * kSlab, &prm.maps[mi], &full_bar[s], sl * 128, row0);
+      SlabPos p = slab_pos(bt, g0);
+      for (int g = 0; g < g1 - g0 && !abort_sh; ++g) {
+        const int s = g % kStages, r = g / kStages;
+        if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1)) {
+          fail();
+          break;
         }
+        mbar_expect_tx(&full_bar[s], kSlab);
+        tma_load_2d(smem + s * kSlab, &prm.maps[p.mi], &full_bar[s], p.sl * 128,
+                    (p.j - bt.blk_start[p.mi]) * 128);
+        if (++p.sl == bt.m[p.mi].kslabs) next_block(bt, p);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_i8(128, 8);
-      int g = 0, tl = 0, mi = 0, cur = -1, nsw = 0;
-      for (int j = j0; j < j1 && !abort_sh; ++j, ++tl) {
-        mat_of(j, mi);
+      int g = 0, tl = 0, cur = -1, nsw = 0;
+      for (SlabPos p = slab_pos(bt, g0); g < g1 - g0 && !abort_sh; next_block(bt, p), ++tl) {
+        const int mi = p.mi;
+        const int nsl = min(bt.m[mi].kslabs - p.sl, g1 - g0 - g);  // this CTA's slabs of block p.j
         if (mi != cur) {
           if (cur >= 0) mma_commit(&b_free);  // the old digit planes are free once these finish
           if (!mbar_wait(&b_ready, nsw & 1)) {
@@ -335,7 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_lo = tmem + (uint32_t)(acc * 16), d_hi = d_lo + 8;
         const uint32_t ev = smem_u32(bplanes), od = ev + bt.m[mi].kslabs * kAtomB;
-        for (int sl = 0; sl < bt.m[mi].kslabs && !abort_sh; ++sl, ++g) {
+        for (int i = 0; i < nsl && !abort_sh; ++i, ++g) {
+          const int sl = p.sl + i;
           const int s = g % kStages, r = g / kStages;
           if (!mbar_wait(&conv_bar[s], r & 1)) {
             fail();
@@ -346,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t lo = smem_u32(lobuf + (g & 1) * kSlab);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {  // 32-byte K steps inside the 128-byte atom
-            const uint32_t acc_in = (sl | ks) != 0;
+            const uint32_t acc_in = (i | ks) != 0;
             mma_i8(d_lo, smem_desc(lo + ks * 32, 16, 1024, 2),
                    smem_desc(ev + sl * kAtomB + ks * 32, 16, 1024, 2), idesc, acc_in);
             mma_i8(d_hi, smem_desc(hi + ks * 32, 16, 1024, 2),
@@ -359,10 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 6) {  // ---------------- unpack (warps 2..5)
     const int t = threadIdx.x - 64;
-    int g = 0, mi = 0;
-    for (int j = j0; j < j1 && !abort_sh; ++j) {
-      mat_of(j, mi);
-      for (int sl = 0; sl < bt.m[mi].kslabs; ++sl, ++g) {
+    {
+      for (int g = 0; g < g1 - g0 && !abort_sh; ++g) {
         const int s = g % kStages, r = g / kStages;
         if (!mbar_wait(&full_bar[s], r & 1)) {
           fail();
@@ -401,13 +409,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {  // ---------------- digit planes + epilogue (warps 6..9)
     const int e = threadIdx.x - 192;
     const int quad = warp & 3;
-    int tl = 0, mi = 0, cur = -1, nsw = 0;
+    int g = 0, tl = 0, cur = -1, nsw = 0;
     float xs = 0.f;
     long long asum = 0;
     pdl_wait();  // the digit planes, xs and sum a_k come from the previous launch
-    for (int j = j0; j < j1; ++j, ++tl) {
-      mat_of(j, mi);
+    for (SlabPos p = slab_pos(bt, g0); g < g1 - g0; next_block(bt, p), ++tl) {
+      const int mi = p.mi, j = p.j;
       const Int4TcMat& m = bt.m[mi];
+      const int nsl = min(m.kslabs - p.sl, g1 - g0 - g);
+      g += nsl;
       if (mi != cur) {
         if (!epi_all(cur < 0 || mbar_wait(&b_free, (nsw - 1) & 1))) {
           fail();
@@ -433,17 +443,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(acc * 16), v);
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
-      const int64_t row = (int64_t)(j - bt.blk_start[mi]) * 128 + 32 * quad + lane;
-      if (row < m.n) {
-        long long tsum = -8LL * asum;
+      const int rl = 32 * quad + lane;
+      const int64_t row = (int64_t)(j - bt.blk_start[mi]) * 128 + rl;
+      long long tsum = 0;
 #pragma unroll
-        for (int i = 0; i < 3; ++i) {
-          const long long lo = (long long)__float_as_int(v[i]);
-          const long long hi = (long long)(__float_as_int(v[8 + i]) >> 4);
-          tsum += (lo + hi) << (16 - 8 * i);
-        }
-        m.y[row] = __ldg(m.scales + row) * xs * (float)tsum;
+      for (int i = 0; i < 3; ++i) {
+        const long long lo = (long long)__float_as_int(v[i]);
+        const long long hi = (long long)(__float_as_int(v[8 + i]) >> 4);
+        tsum += (lo + hi) << (16 - 8 * i);
       }
+      if (nsl < m.kslabs) {
+        // Part of a block split between CTAs: add the exact integer partial
+        // sums; the CTA whose slabs complete the block writes the rows
+        // (threadfence-reduction order: sums, fence, count; count, fence,
+        // sums) and returns the scratch to zero.
+        unsigned long long* ps = prm.part_sum + (size_t)j * 128 + rl;
+        if (row < m.n) atomicAdd(ps, (unsigned long long)tsum);
+        __threadfence();
+        epi_sync();
+        if (e == 0) {
+          const int done = atomicAdd(prm.part_cnt + j, nsl) + nsl;
+          last_sh = done == m.kslabs;
+          if (done == m.kslabs) atomicExch(prm.part_cnt + j, 0);
+          __threadfence();
+        }
+        epi_sync();
+        if (!last_sh) continue;
+        if (row < m.n) tsum = (long long)atomicExch(ps, 0ull);
+      }
+      if (row < m.n) m.y[row] = __ldg(m.scales + row) * xs * (float)(tsum - 8LL * asum);
     }
   }
   tc_fence_before();
@@ -537,6 +565,38 @@ uint8_t* digit_scratch(size_t bytes) {
   return s.p;
 }
 
+// Per-device scratch for the partial row sums of blocks split between CTAs:
+// zeroed when allocated and left zero by every launch that completes (the
+// finishing CTA clears what it read). After a reported kernel error it is
+// zeroed again before the next launch.
+struct PartialScratch {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+bool g_partials_dirty = false;
+
+void* partial_scratch(size_t bytes, cudaStream_t st) {
+  static std::mutex mu;
+  static std::vector<PartialScratch> per_dev;
+  int dev = 0;
+  IDEV_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
+  PartialScratch& s = per_dev[dev];
+  if (s.bytes < bytes) {
+    if (s.p) IDEV_CUDA(cudaFree(s.p));
+    s.p = nullptr;
+    s.bytes = 0;
+    IDEV_CUDA(cudaMalloc(&s.p, bytes));
+    s.bytes = bytes;
+    IDEV_CUDA(cudaMemsetAsync(s.p, 0, bytes, st));
+  } else if (g_partials_dirty) {
+    IDEV_CUDA(cudaMemsetAsync(s.p, 0, s.bytes, st));
+  }
+  g_partials_dirty = false;
+  return s.p;
+}
+
 }  // namespace
 
 // Matrices that pass gemv_int4_tc_ok, any count (launch pairs of up to 64).
@@ -576,10 +636,13 @@ void launch_gemv_int4_tc(const InfercInt4Gemv* const* ds, int n, cudaStream_t st
     }
     bt.blk_start[bt.count] = blks;
     bt.slab_start[bt.count] = slabs;
+    void* part = partial_scratch((size_t)blks * (128 * 8 + 4), st);
+    bt.part_sum = static_cast<unsigned long long*>(part);
+    bt.part_cnt = reinterpret_cast<int*>(bt.part_sum + (size_t)blks * 128);
     IDEV_CUDA(cudaMemsetAsync(scratch, 0, plane_bytes, st));
     int4_digits_kernel<<<bt.count, 256, 0, st>>>(db);
     IDEV_LAUNCHED();
-    launch_pdl(gemv_int4_tc_kernel, dim3(std::min(blks, sms)), dim3(kThreads), kSmem, st, bt);
+    launch_pdl(gemv_int4_tc_kernel, dim3(std::min(slabs, sms)), dim3(kThreads), kSmem, st, bt);
   }
 }
 
@@ -587,6 +650,7 @@ int read_and_clear_int4_tc_error() {
   int v = 0;
   IDEV_CUDA(cudaMemcpyFromSymbol(&v, g_int4_tc_error, sizeof(int)));
   if (v) {
+    g_partials_dirty = true;
     const int z = 0;
     IDEV_CUDA(cudaMemcpyToSymbol(g_int4_tc_error, &z, sizeof(int)));
   }

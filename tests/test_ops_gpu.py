@@ -288,6 +288,23 @@ def test_int4_batched_many_small_and_mixed(port):
         np.testing.assert_allclose(host(d[3]), ref, atol=tol, rtol=1e-5)
 
 
+@pytest.mark.parametrize("n,k", [(128, 4096), (200, 4096), (300, 2048), (5, 1024)])
+def test_int4_split_blocks_repeat(port, n, k):
+    """Few blocks with many slabs: the grid is one CTA per slab or so, so
+    every 128-row block is summed by several CTAs through the partial-sum
+    scratch. Three calls in a row must agree bit for bit (the scratch returns
+    to zero after each launch) and match the port."""
+    rng = np.random.default_rng(n * 7 + k)
+    m = synth.int4_matrix(n, k, rng)
+    ref = port.int4_gemv_rowscale(m.w, m.scales, m.x)
+    outs = []
+    for _ in range(3):
+        y = host(ops.Int4GemvRowScale(T(m.w), T(m.scales), T(m.x)))
+        np.testing.assert_allclose(y, ref, atol=1e-4, rtol=1e-5)
+        outs.append(y)
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
 @pytest.mark.parametrize("B,S", [(2, 128), (1, 512), (3, 40)])
 def test_qkv_attention_prepared(port, B, S):
     """inferc_dev_qkv_attention (config 2 path) == FusedQKV + FusedAttention."""
