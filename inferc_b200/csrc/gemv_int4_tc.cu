@@ -180,8 +180,11 @@ __device__ __forceinline__ uint32_t b_off(int i, int j) {
          ((uint32_t)(((j & 127) >> 4) ^ i) << 4) + (uint32_t)(j & 15);
 }
 
-// One CTA (256 threads) per matrix: the digit planes of its x. The planes
-// were zeroed before the launch; only digit rows 0..2 are written.
+// One CTA (256 threads) per matrix: the digit planes of its x. Only digit
+// rows 0..2 are written. Rows 3..7 of the N = 8 tile feed accumulator
+// columns 3..7, which the epilogue never reads, and K bytes past K/2 in the
+// last atom meet weight columns that TMA fills with zeros, so the rest of
+// the tile may hold anything and is not cleared.
 __global__ void __launch_bounds__(256) int4_digits_kernel(const __grid_constant__ Int4DigitBatch db) {
   pdl_launch_dependents();  // the GEMV may start streaming weights
   const Int4DigitJob& jb = db.j[blockIdx.x];
@@ -639,7 +642,6 @@ void launch_gemv_int4_tc(const InfercInt4Gemv* const* ds, int n, cudaStream_t st
     void* part = partial_scratch((size_t)blks * (128 * 8 + 4), st);
     bt.part_sum = static_cast<unsigned long long*>(part);
     bt.part_cnt = reinterpret_cast<int*>(bt.part_sum + (size_t)blks * 128);
-    IDEV_CUDA(cudaMemsetAsync(scratch, 0, plane_bytes, st));
     int4_digits_kernel<<<bt.count, 256, 0, st>>>(db);
     IDEV_LAUNCHED();
     launch_pdl(gemv_int4_tc_kernel, dim3(std::min(slabs, sms)), dim3(kThreads), kSmem, st, bt);
