@@ -12,11 +12,13 @@
 //   sum_k (q_k - 8) a_k = sum_i 2^(16 - 8 i) sum_k q_k d_ik - 8 sum_k a_k
 // where every inner sum is an exact int32 dot product of unsigned weight
 // bytes with signed digit bytes: a tcgen05 kind::i8 MMA with M = 128 rows,
-// N = 8 (digit planes 0..2, the rest zero) and int32 accumulators in TMEM.
-// The weight bytes are used without de-interleaving:
-//   lo tile = byte & 0x0F          (q of even k)  x  digits of x[2j]
-//   hi tile = byte & 0xF0 = 16 q   (odd k)        x  digits of x[2j+1]
+// N = 8 and int32 accumulators in TMEM. The weight bytes are used without
+// de-interleaving, against one digit tile per matrix whose rows 0..2 hold
+// the digits of the even elements x[2j] and rows 3..5 those of x[2j+1]:
+//   lo tile = byte & 0x0F          (q of even k)  x  tile -> columns 0..2
+//   hi tile = byte & 0xF0 = 16 q   (odd k)        x  tile -> columns 3..5
 // both at the byte's own position; the hi sums are divided by 16 (exact).
+// The other columns of each accumulator are never read.
 // Each row's result is one integer, rounded once to fp32 and scaled by
 // s_r * xs; the quantisation of x adds at most 2^-23 max|x| per element,
 // which keeps the row sums within fp32 accumulation error.
@@ -41,7 +43,8 @@
 //   warp 1      TMEM allocation + MMA issuer
 //   warps 2..5  unpack: hi tile in place, lo tile into one of two buffers,
 //               both written at the SWIZZLE_128B positions the MMA reads
-//   warps 6..9  on every matrix switch a bulk copy of its digit planes, and
+//   warps 6..9  bulk copies of the digit tiles into a double buffer (the next
+//               matrix's tile lands while the current one streams), and
 //               the epilogue (tcgen05.ld of both accumulators, a row per
 //               thread)
 // Every mbarrier wait is bounded; a timeout sets g_int4_tc_error.
@@ -76,7 +79,7 @@ constexpr int kMaxMats = 64;  // ~11.5 KB of kernel parameters
 struct Int4TcMat {
   const float* scales;
   float* y;
-  const uint8_t* planes;   // [ev tile | od tile], kslabs KB each
+  const uint8_t* planes;   // digit tile, kslabs KB: rows 0..2 even k, rows 3..5 odd k
   const float* xs;         // activation scale
   const long long* asum;   // sum of a_k
   int64_t n, k;
@@ -189,11 +192,10 @@ __device__ __forceinline__ uint32_t b_off(int i, int j) {
          ((uint32_t)(((j & 127) >> 4) ^ i) << 4) + (uint32_t)(j & 15);
 }
 
-// One CTA (256 threads) per matrix: the digit planes of its x. Only digit
-// rows 0..2 are written. Rows 3..7 of the N = 8 tile feed accumulator
-// columns 3..7, which the epilogue never reads, and K bytes past K/2 in the
-// last atom meet weight columns that TMA fills with zeros, so the rest of
-// the tile may hold anything and is not cleared.
+// One CTA (256 threads) per matrix: the digit tile of its x. Only rows 0..5
+// are written. Rows 6..7 feed accumulator columns the epilogue never reads,
+// and K bytes past K/2 in the last atom meet weight columns that TMA fills
+// with zeros, so the rest of the tile may hold anything and is not cleared.
 __global__ void __launch_bounds__(256) int4_digits_kernel(const Int4Params* __restrict__ prms) {
   pdl_launch_dependents();  // the GEMV may start streaming weights
   const Int4DigitJob& jb = prms->db.j[blockIdx.x];
@@ -216,8 +218,7 @@ __global__ void __launch_bounds__(256) int4_digits_kernel(const Int4Params* __re
   mx = red_f[0];
   for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red_f[w]);
   const float inv = mx > 0.f ? 4194303.0f / mx : 0.f;
-  uint8_t* ev = jb.planes;
-  uint8_t* od = jb.planes + (size_t)jb.kslabs * kAtomB;
+  uint8_t* tile = jb.planes;
   long long part = 0;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
@@ -234,10 +235,10 @@ __global__ void __launch_bounds__(256) int4_digits_kernel(const Int4Params* __re
       const int d1 = ((a1 + 128) & 255) - 128;
       const int d0 = (a1 - d1) >> 8;
       const int jj = (int)(2 * q + h / 2);
-      uint8_t* tile = (h & 1) ? od : ev;
-      tile[b_off(0, jj)] = (uint8_t)d0;
-      tile[b_off(1, jj)] = (uint8_t)d1;
-      tile[b_off(2, jj)] = (uint8_t)d2;
+      const int r0 = (h & 1) * 3;  // odd k: rows 3..5
+      tile[b_off(r0, jj)] = (uint8_t)d0;
+      tile[b_off(r0 + 1, jj)] = (uint8_t)d1;
+      tile[b_off(r0 + 2, jj)] = (uint8_t)d2;
     }
   }
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
@@ -267,9 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* lobuf = smem + kStages * kSlab;  // two lo tiles
-  uint8_t* bplanes = lobuf + 2 * kSlab;     // [ev | od] of the current matrix
+  uint8_t* bplanes = lobuf + 2 * kSlab;     // digit tiles of two matrices (double buffer)
   __shared__ __align__(8) uint64_t full_bar[kStages], conv_bar[kStages], empty_bar[kStages];
-  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], b_ready, b_free;
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], b_ready[2], b_free[2];
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   __shared__ int last_sh;
@@ -300,8 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], kEpi);
     }
-    mbar_init(&b_ready, 1);
-    mbar_init(&b_free, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&b_ready[b], 1);
+      mbar_init(&b_free[b], 1);
+    }
     abort_sh = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -343,17 +346,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_i8(128, 8);
-      int g = 0, tl = 0, cur = -1, nsw = 0;
+      int g = 0, tl = 0, cur = -1, q = -1;  // q: local index of the current matrix
       for (SlabPos p = slab_pos(bt, g0); g < g1 - g0 && !abort_sh; next_block(bt, p), ++tl) {
         const int mi = p.mi;
         const int nsl = min(bt.m[mi].kslabs - p.sl, g1 - g0 - g);  // this CTA's slabs of block p.j
         if (mi != cur) {
-          if (cur >= 0) mma_commit(&b_free);  // the old digit planes are free once these finish
-          if (!mbar_wait(&b_ready, nsw & 1)) {
+          if (cur >= 0) mma_commit(&b_free[q & 1]);  // the old tile is free once these finish
+          ++q;
+          if (!mbar_wait(&b_ready[q & 1], (q >> 1) & 1)) {
             fail();
             break;
           }
-          ++nsw;
           cur = mi;
         }
         const int acc = tl & 1;
@@ -363,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_lo = tmem + (uint32_t)(acc * 16), d_hi = d_lo + 8;
-        const uint32_t ev = smem_u32(bplanes), od = ev + bt.m[mi].kslabs * kAtomB;
+        const uint32_t bb = smem_u32(bplanes + (q & 1) * kBTile);
         for (int i = 0; i < nsl && !abort_sh; ++i, ++g) {
           const int sl = p.sl + i;
           const int s = g % kStages, r = g / kStages;
@@ -378,9 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < 4; ++ks) {  // 32-byte K steps inside the 128-byte atom
             const uint32_t acc_in = (i | ks) != 0;
             mma_i8(d_lo, smem_desc(lo + ks * 32, 16, 1024, 2),
-                   smem_desc(ev + sl * kAtomB + ks * 32, 16, 1024, 2), idesc, acc_in);
+                   smem_desc(bb + sl * kAtomB + ks * 32, 16, 1024, 2), idesc, acc_in);
             mma_i8(d_hi, smem_desc(hi + ks * 32, 16, 1024, 2),
-                   smem_desc(od + sl * kAtomB + ks * 32, 16, 1024, 2), idesc, acc_in);
+                   smem_desc(bb + sl * kAtomB + ks * 32, 16, 1024, 2), idesc, acc_in);
           }
           mma_commit(&empty_bar[s]);
         }
@@ -429,28 +432,47 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {  // ---------------- digit planes + epilogue (warps 6..9)
     const int e = threadIdx.x - 192;
     const int quad = warp & 3;
-    int g = 0, tl = 0, cur = -1, nsw = 0;
+    int g = 0, tl = 0, cur = -1, q = -1;
     float xs = 0.f;
     long long asum = 0;
+    // Copy the digit tile of local matrix qq (batch matrix mi) into buffer
+    // qq & 1 once the MMAs of matrix qq - 2 have released it. Uniform over
+    // the epilogue threads; false on a timeout.
+    auto load_tile = [&](int qq, int mi) -> bool {
+      const int b = qq & 1;
+      if (!epi_all(qq < 2 || mbar_wait(&b_free[b], ((qq >> 1) - 1) & 1))) return false;
+      if (e == 0) {
+        const uint32_t bytes = (uint32_t)bt.m[mi].kslabs * kAtomB;
+        mbar_expect_tx(&b_ready[b], bytes);
+        bulk_copy(bplanes + b * kBTile, bt.m[mi].planes, bytes, &b_ready[b]);
+      }
+      return true;
+    };
+    // matrix mi + 1 has slabs in this CTA's range
+    auto has_next = [&](int mi) { return mi + 1 < bt.count && bt.slab_start[mi + 1] < g1; };
     pdl_wait();  // the digit planes, xs and sum a_k come from the previous launch
+    {
+      const int mi0 = slab_pos(bt, g0).mi;  // this CTA's first two tiles, at once
+      bool ok = load_tile(0, mi0);
+      if (ok && has_next(mi0)) ok = load_tile(1, mi0 + 1);
+      if (!ok) {
+        fail();
+        g = g1 - g0;  // skip the loop
+      }
+    }
     for (SlabPos p = slab_pos(bt, g0); g < g1 - g0; next_block(bt, p), ++tl) {
       const int mi = p.mi, j = p.j;
       const Int4TcMat& m = bt.m[mi];
       const int nsl = min(m.kslabs - p.sl, g1 - g0 - g);
       g += nsl;
       if (mi != cur) {
-        if (!epi_all(cur < 0 || mbar_wait(&b_free, (nsw - 1) & 1))) {
+        ++q;  // the tile of matrix q + 1 goes into the buffer matrix q - 1 has left
+        if (q >= 1 && has_next(mi) && !load_tile(q + 1, mi + 1)) {
           fail();
           break;
         }
-        if (e == 0) {
-          const uint32_t bytes = 2u * (uint32_t)m.kslabs * kAtomB;
-          mbar_expect_tx(&b_ready, bytes);
-          bulk_copy(bplanes, m.planes, bytes, &b_ready);
-        }
         xs = *m.xs;
         asum = *m.asum;
-        ++nsw;
         cur = mi;
       }
       const int acc = tl & 1;
@@ -469,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
         const long long lo = (long long)__float_as_int(v[i]);
-        const long long hi = (long long)(__float_as_int(v[8 + i]) >> 4);
+        const long long hi = (long long)(__float_as_int(v[8 + 3 + i]) >> 4);  // odd-k rows 3..5
         tsum += (lo + hi) << (16 - 8 * i);
       }
       if (nsl < m.kslabs) {
@@ -687,10 +709,10 @@ void launch_gemv_int4_tc(const InfercInt4Gemv* const* ds, int n, cudaStream_t st
     Int4TcBatch& bt = hp.bt;
     Int4DigitBatch& db = hp.db;
     bt.count = db.count = std::min(kMaxMats, n - base);
-    // scratch: per matrix 2 * kslabs KB of planes, then xs and asum
+    // scratch: per matrix kslabs KB of digit tile, then xs and asum
     size_t plane_bytes = 0;
     for (int i = 0; i < bt.count; ++i)
-      plane_bytes += 2 * (size_t)((ds[base + i]->k / 2 + 127) / 128) * kAtomB;
+      plane_bytes += (size_t)((ds[base + i]->k / 2 + 127) / 128) * kAtomB;
     uint8_t* scratch = digit_scratch(plane_bytes + (size_t)bt.count * 16);
     long long* asums = reinterpret_cast<long long*>(scratch + plane_bytes);
     float* xss = reinterpret_cast<float*>(asums + bt.count);
@@ -702,7 +724,7 @@ void launch_gemv_int4_tc(const InfercInt4Gemv* const* ds, int n, cudaStream_t st
       bt.maps[i] = cached_weight_map(d.w, d.n, d.k);
       bt.m[i] = Int4TcMat{d.scales, d.y, scratch + off, xss + i, asums + i, d.n, d.k, kslabs};
       db.j[i] = Int4DigitJob{d.x, d.k, kslabs, scratch + off, xss + i, asums + i};
-      off += 2 * (size_t)kslabs * kAtomB;
+      off += (size_t)kslabs * kAtomB;
       bt.blk_start[i] = blks;
       bt.slab_start[i] = slabs;
       blks += (int)((d.n + 127) / 128);
