@@ -236,6 +236,22 @@ def roofline_ffn1(cfg, M, dev, stream, pk, reps):
     return kms, flops, achieved, peak_eff
 
 
+# DRAM bytes (read + write) of one FFN1 launch at M = 32768 from one ncu
+# capture on a B200:
+#   python bench.py --roofline-only --steps 2 && ncu --metrics
+#   dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
+#   --clock-control none -k regex:gemm_f16s_kernel -s 3 -c 1 --csv
+#   python bench.py --roofline-only --steps 2
+# read 111,074,048 + write 349,294,848. Other M scale the activation and
+# output part by M / 32768; the weight planes (F x Kp x 2 planes x 2 B) do not.
+FFN1_DRAM_BYTES_M32768 = 111_074_048 + 349_294_848
+
+
+def ffn1_traffic(M, cfg):
+    w = cfg.ffn * cfg.hidden * 2 * 2
+    return int(w + (FFN1_DRAM_BYTES_M32768 - w) * M / 32768)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -353,8 +369,12 @@ def main():
                          "frac": achieved / peak_eff,
                          "peak_basis": f"split fp16 (3 MMAs/product) = {basis} bf16 "
                                        f"{pk['bf16_tflops']} / 3",
+                         # the leg is ~11 ms of back-to-back launches, under the
+                         # power cap: its fraction of the sustained rate, for context
+                         "frac_of_sustained": achieved / (pk["bf16_tflops_sustained"] / 3.0),
                          "ms_per_launch": kms, "flops_per_launch": flops,
-                         "traffic": None},
+                         "traffic": ffn1_traffic(B * SEQ, cfg),
+                         "traffic_unit": "bytes per launch (ncu dram read + write)"},
             "e2e": {"value": e2e_value, "unit": "seq/s",
                     "h2d_bytes_per_step": int(ids_h.numel() * 8 * 2),
                     "d2h_bytes_per_step": int(GLOBAL_BATCH * cfg.n_classes * 4)},

@@ -388,3 +388,24 @@ def test_qkv_attention_f16(port, B, S):
     ref = port.fused_attention(q.reshape(B, S, H), k.reshape(B, S, H), v.reshape(B, S, H),
                                km.reshape(B, 1, 1, S), 64, -3.0e38)
     np.testing.assert_allclose(host(out), ref, atol=5e-5)
+
+
+def test_empty_inputs():
+    """Zero rows, batch or sequence length. The reference kernels' loops run
+    zero times and return empty tensors; every entry here returns status 0
+    without a launch, and the outputs keep their shapes."""
+    def z(*s):
+        return torch.zeros(*s, device=DEV)
+
+    assert ops.FusedMatMulAddGELU(z(0, 768), z(768, 3072), z(3072)).shape == (0, 3072)
+    outs = ops.FusedQKVProjection(z(0, 4, 768), z(768, 768), z(768), z(768, 768), z(768),
+                                  z(768, 768), z(768))
+    assert [tuple(o.shape) for o in outs] == [(0, 4, 768)] * 3
+    assert ops.LayerNorm(z(0, 768), z(768) + 1, z(768)).shape == (0, 768)
+    assert ops.Gemm(z(0, 4), z(4, 5)).shape == (0, 5)
+    assert ops.FusedAttention(z(0, 128, 768), z(0, 128, 768), z(0, 128, 768)).shape == (0, 128, 768)
+    assert ops.FusedAttention(z(2, 0, 768), z(2, 0, 768), z(2, 0, 768)).shape == (2, 0, 768)
+    w = torch.zeros(0, 384, dtype=torch.uint8, device=DEV)
+    assert ops.Int4GemvRowScale(w, z(0), z(768)).shape == (0,)
+    ops.Int4GemvBatched([])
+    torch.cuda.synchronize()
