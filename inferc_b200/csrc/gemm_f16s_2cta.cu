@@ -8,9 +8,9 @@
 // tensor rate. In the pair, each SM holds its own 128 rows of A and half of
 // B (128 of the 256 output columns); one MMA instruction computes the
 // 256 x 256 tile and each SM reads only its halves: 2/3 of the traffic.
-// Measured on the encoder's shapes it is nevertheless 6-13 % slower than the
-// one-SM kernel (three 64 KB stages fit, and every stage needs cross-SM
-// barrier hops), so it is opt-in: INFERC_GEMM_2CTA=1.
+// Measured on the encoder's FFN1 it is nevertheless ~3 % slower than the
+// one-SM kernel (0.431 vs 0.417 ms; only three 64 KB stages fit), so it is
+// opt-in: INFERC_GEMM_2CTA=1.
 //
 // A cluster of two CTAs per tile (rank 0 leads):
 //   warp 0      TMA producer in both CTAs: its A rows and its B columns, both
@@ -21,9 +21,9 @@
 //               both SMs); in the leader, the MMA issuer
 //   warps 2..9  epilogue in both CTAs: each reads its SM's 128 accumulator
 //               rows, and tells the leader when the accumulator is drained
-// The leader's tcgen05.commit arrives on its own stage-free and
-// accumulator-full barriers; the leader's producer and epilogue pass each
-// completion on to the peer CTA's barrier with a remote mbarrier arrive.
+// The leader's MMA issuer commits each stage and each accumulator twice:
+// to its own barrier and to the peer CTA's (by its cluster address), so
+// neither CTA waits for a forwarded signal.
 // Every wait is bounded; on a timeout the CTA sets g_f16_2cta_error and leaves;
 // both CTAs meet at a cluster barrier before freeing TMEM and exiting.
 #include <cuda.h>
@@ -162,10 +162,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 2);   // leader: one expect_tx arrive per CTA
-      mbar_init(&empty_bar[s], 1);  // leader: its MMA commit; peer: the leader's forward
+      mbar_init(&empty_bar[s], 1);  // the leader's MMA commit (to both CTAs)
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull_bar[b], 1);  // leader: its MMA commit; peer: the leader's forward
+      mbar_init(&tfull_bar[b], 1);  // the leader's MMA commit (to both CTAs)
       mbar_init(&tempty_bar[b], 2 * kEpiThreads);  // leader: both CTAs' epilogues
     }
     abort_sh = 0;
@@ -194,7 +194,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             fail();
             break;
           }
-          if (r > 0 && leader) mbar_arrive_cluster(map_to_rank(smem_u32(&empty_bar[s]), 1));
           const uint32_t lead_full = map_to_rank(smem_u32(&full_bar[s]), 0);
           mbar_arrive_expect_cluster(lead_full, 2 * kAPlane + 2 * S::B_PLANE);
           const uint32_t base = smem_u32(stage_base(s));
@@ -236,9 +235,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mma_f16_2sm(d, dah, dbl, idesc, 1);
             mma_f16_2sm(d, dah, dbh, idesc, 1);
           }
-          commit_2sm(smem_u32(&empty_bar[s]));  // stage s free once these MMAs finish
+          // stage s is free in both CTAs once these MMAs finish
+          commit_2sm(smem_u32(&empty_bar[s]));
+          commit_2sm(map_to_rank(smem_u32(&empty_bar[s]), 1));
         }
         commit_2sm(smem_u32(&tfull_bar[acc]));
+        commit_2sm(map_to_rank(smem_u32(&tfull_bar[acc]), 1));
       }
     }
   } else {  // ---------------- epilogue (warps 2..9, both CTAs)
@@ -258,8 +260,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         fail();
         break;
       }
-      if (leader && threadIdx.x == 64)  // pass the completion on to the peer
-        mbar_arrive_cluster(map_to_rank(smem_u32(&tfull_bar[acc]), 1));
       tc_fence_after();
       const int m0 = (tile / tiles_n) * 256 + (int)rank * 128, n0 = (tile % tiles_n) * BN;
       const int64_t row = m0 + 32 * q + lane;
@@ -349,9 +349,8 @@ int read_and_clear_f16_2cta_error() {
 }
 
 bool gemm_f16s_2cta_usable(const F16GemmA& A, int64_t M, int64_t N) {
-  // Opt-in (INFERC_GEMM_2CTA=1): on the encoder's shapes it measured 6-13 %
-  // slower than the one-SM kernel (the cross-SM barrier hops and the three
-  // 64 KB stages that fit leave the pair's TMA stream short of data).
+  // Opt-in (INFERC_GEMM_2CTA=1): on the encoder's FFN1 it measured ~3 %
+  // slower than the one-SM kernel.
   static const bool on = [] {
     const char* e = std::getenv("INFERC_GEMM_2CTA");
     return e && e[0] == '1';
