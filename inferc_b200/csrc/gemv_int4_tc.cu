@@ -614,15 +614,16 @@ uint8_t* digit_scratch(size_t bytes) {
 struct PartialScratch {
   void* p = nullptr;
   size_t bytes = 0;
+  bool dirty = false;  // a launch on this device reported an error
 };
-bool g_partials_dirty = false;
+std::mutex g_partials_mu;
+std::vector<PartialScratch> g_partials;  // per device
 
 void* partial_scratch(size_t bytes, cudaStream_t st) {
-  static std::mutex mu;
-  static std::vector<PartialScratch> per_dev;
   int dev = 0;
   IDEV_CUDA(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lock(mu);
+  std::lock_guard<std::mutex> lock(g_partials_mu);
+  std::vector<PartialScratch>& per_dev = g_partials;
   if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
   PartialScratch& s = per_dev[dev];
   if (s.bytes < bytes) {
@@ -632,10 +633,10 @@ void* partial_scratch(size_t bytes, cudaStream_t st) {
     IDEV_CUDA(cudaMalloc(&s.p, bytes));
     s.bytes = bytes;
     IDEV_CUDA(cudaMemsetAsync(s.p, 0, bytes, st));
-  } else if (g_partials_dirty) {
+  } else if (s.dirty) {
     IDEV_CUDA(cudaMemsetAsync(s.p, 0, s.bytes, st));
   }
-  g_partials_dirty = false;
+  s.dirty = false;
   return s.p;
 }
 
@@ -746,7 +747,12 @@ int read_and_clear_int4_tc_error() {
   int v = 0;
   IDEV_CUDA(cudaMemcpyFromSymbol(&v, g_int4_tc_error, sizeof(int)));
   if (v) {
-    g_partials_dirty = true;
+    int dev = 0;
+    IDEV_CUDA(cudaGetDevice(&dev));
+    {
+      std::lock_guard<std::mutex> lock(g_partials_mu);
+      if ((int)g_partials.size() > dev) g_partials[dev].dirty = true;
+    }
     const int z = 0;
     IDEV_CUDA(cudaMemcpyToSymbol(g_int4_tc_error, &z, sizeof(int)));
   }
