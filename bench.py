@@ -157,7 +157,8 @@ def run_reference(args):
     ref = oracle.ref()
     kind = "reference" if ref is not None else "port"
     o = ref if ref is not None else oracle.port()
-    s = structs.encoder_struct(cfg, synth.encoder_weights(cfg, seed=0))
+    w = synth.encoder_weights(cfg, seed=0)
+    s = structs.encoder_struct(cfg, w)
     t0 = time.perf_counter()
     o.encoder_forward(s, ids[:1], mask[:1], cfg.n_classes)
     one = time.perf_counter() - t0

@@ -52,6 +52,7 @@ def _fill(struct, cfg, tensors, layer_fields, scalars):
                 arr[l] = _addr(tensors[f"{name}.{l}"])
         else:
             setattr(s, name, _addr(tensors[name]))
+    s._keep = tensors  # the table holds raw addresses: keep the arrays alive with it
     return s
 
 
