@@ -306,10 +306,95 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
       const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
       const int64_t row = m0 + 32 * q + lane;
       const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
+      // whole-tile fast paths below (warp-uniform); split outputs have
+      // aligned planes and bias by the dispatcher's checks
+      const bool staged = (SOUT || vec_ok) && n0 + BN <= N;
 #pragma unroll 1
       for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
         float v[16];
         tmem_ld16(base + (uint32_t)c0, v);
+        if constexpr (EPI == EPI_BIAS_RESID && !SOUT) {
+          if (staged) {
+            // fp32 + residual, staged through shared memory: the warp's
+            // 32 rows x 16 columns are written row per lane (rows padded to
+            // 20 floats: conflict-free float4 stores) and read back as
+            // float4s that cover 8 rows x 64 contiguous bytes per warp
+            // instruction, so the residual loads and C stores use whole
+            // 32-byte sectors. Arithmetic as in epilogue16<EPI_BIAS_RESID>.
+            __shared__ __align__(16) float stage[kEpiThreads / 32][32 * 20];
+            float* wb = stage[warp - 2 - kConvThreads / 32];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<float4*>(wb + lane * 20)[j] =
+                  make_float4(v[4 * j] * sc, v[4 * j + 1] * sc, v[4 * j + 2] * sc,
+                              v[4 * j + 3] * sc);
+            __syncwarp();
+            const int c4 = (lane & 3) * 4;
+            const int64_t col = (int64_t)n0 + c0 + c4;
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+            float4 rr[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int64_t grow = m0 + 32 * q + (lane >> 2) + 8 * k;
+              rr[k] = grow < M ? *reinterpret_cast<const float4*>(ep.resid + grow * ep.ldr + col)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int rl = (lane >> 2) + 8 * k;
+              const int64_t grow = m0 + 32 * q + rl;
+              if (grow >= M) continue;
+              const float4 x = *reinterpret_cast<const float4*>(wb + rl * 20 + c4);
+              float4 o;
+              o.x = ep.alpha * x.x + ep.beta * bb.x; o.x += rr[k].x;
+              o.y = ep.alpha * x.y + ep.beta * bb.y; o.y += rr[k].y;
+              o.z = ep.alpha * x.z + ep.beta * bb.z; o.z += rr[k].z;
+              o.w = ep.alpha * x.w + ep.beta * bb.w; o.w += rr[k].w;
+              *reinterpret_cast<float4*>(C + grow * ldc + col) = o;
+            }
+            __syncwarp();
+            continue;
+          }
+        }
+        if constexpr (SOUT && (EPI == EPI_BIAS || EPI == EPI_BIAS_GELU)) {
+          if (staged) {
+            // fp16 hi / lo planes, staged the same way: each lane finishes 4
+            // columns of a row and writes 8 contiguous bytes to each plane
+            // (8 rows x 32 bytes per warp instruction). Arithmetic as in
+            // epilogue16_split<EPI>.
+            __shared__ __align__(16) float stage[kEpiThreads / 32][32 * 20];
+            float* wb = stage[warp - 2 - kConvThreads / 32];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<float4*>(wb + lane * 20)[j] =
+                  make_float4(v[4 * j] * sc, v[4 * j + 1] * sc, v[4 * j + 2] * sc,
+                              v[4 * j + 3] * sc);
+            __syncwarp();
+            const int c4 = (lane & 3) * 4;
+            const int64_t col = (int64_t)n0 + c0 + c4;
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int rl = (lane >> 2) + 8 * k;
+              const int64_t grow = m0 + 32 * q + rl;
+              if (grow >= M) continue;
+              const float4 x = *reinterpret_cast<const float4*>(wb + rl * 20 + c4);
+              float o[4] = {ep.alpha * x.x + ep.beta * bb.x, ep.alpha * x.y + ep.beta * bb.y,
+                            ep.alpha * x.z + ep.beta * bb.z, ep.alpha * x.w + ep.beta * bb.w};
+              if (EPI == EPI_BIAS_GELU) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = gelu_erf(o[i]);
+              }
+              uint32_t l0, l1;
+              const uint32_t h0 = split_pair(o[0], o[1], l0, bad);
+              const uint32_t h1 = split_pair(o[2], o[3], l1, bad);
+              *reinterpret_cast<uint2*>(so.hi + grow * so.ld + col) = make_uint2(h0, h1);
+              *reinterpret_cast<uint2*>(so.lo + grow * so.ld + col) = make_uint2(l0, l1);
+            }
+            __syncwarp();
+            continue;
+          }
+        }
         if (row >= M) continue;
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] *= sc;
