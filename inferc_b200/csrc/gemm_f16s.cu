@@ -400,7 +400,8 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
         for (int i = 0; i < 16; ++i) v[i] *= sc;
         const int64_t col0 = (int64_t)n0 + c0;
         if (SOUT) {
-          epilogue16_split<EPI>(ep, v, row, col0, so, bad);
+          // N % 16 == 0 for split outputs: a chunk is wholly inside or outside
+          if (col0 < N) epilogue16_split<EPI>(ep, v, row, col0, so, bad);
         } else {
           epilogue16<EPI>(ep, v, row, col0, N, C + row * ldc + col0, vec_ok);
         }
@@ -603,7 +604,7 @@ void launch_gemm_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl,
   if (ep.bias_mode == 1 && ep.act == ACT_NONE && ep.resid == nullptr) epi = EPI_BIAS;
   if (ep.bias_mode == 1 && ep.act == ACT_GELU_ERF && ep.resid == nullptr) epi = EPI_BIAS_GELU;
   if (ep.bias_mode == 1 && ep.act == ACT_NONE && ep.resid != nullptr) epi = EPI_BIAS_RESID;
-  if (as && gemm_f16s_2cta_usable(A, M, N) &&
+  if (as && gemm_f16s_2cta_usable(A, M, N, so.hi != nullptr) &&
       (!so.hi || ((epi == EPI_BIAS || epi == EPI_BIAS_GELU) && N % 16 == 0 && so.lo &&
                   so.range && aligned16(so.hi) && aligned16(so.lo) && so.ld % 8 == 0 &&
                   so.ld >= N && aligned16(ep.bias)))) {

@@ -8,9 +8,9 @@
 // tensor rate. In the pair, each SM holds its own 128 rows of A and half of
 // B (128 of the 256 output columns); one MMA instruction computes the
 // 256 x 256 tile and each SM reads only its halves: 2/3 of the traffic.
-// Measured on the encoder's FFN1 it is nevertheless ~3 % slower than the
-// one-SM kernel (0.431 vs 0.417 ms; only three 64 KB stages fit), so it is
-// opt-in: INFERC_GEMM_2CTA=1.
+// With the shared-memory-staged epilogues it is ahead of the one-SM kernel
+// for the GEMMs that write fp16 planes and slightly behind for the fp32
+// residual ones; gemm_f16s_2cta_usable picks it accordingly.
 //
 // A cluster of two CTAs per tile (rank 0 leads):
 //   warp 0      TMA producer in both CTAs: its A rows and its B columns, both
@@ -264,16 +264,69 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int m0 = (tile / tiles_n) * 256 + (int)rank * 128, n0 = (tile % tiles_n) * BN;
       const int64_t row = m0 + 32 * q + lane;
       const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
+      // whole-tile fast paths (warp-uniform), as in gemm_f16s.cu
+      const bool staged = (SOUT || vec_ok) && n0 + BN <= N;
 #pragma unroll 1
       for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
         float v[16];
         tmem_ld16(base + (uint32_t)c0, v);
+        if (staged && (SOUT ? (EPI == EPI_BIAS || EPI == EPI_BIAS_GELU) : EPI == EPI_BIAS_RESID)) {
+          // The warp's 32 rows x 16 columns go through shared memory (rows
+          // padded to 20 floats) and come back as float4s covering 8 rows x
+          // 64 contiguous bytes per warp instruction: whole-sector residual
+          // loads and stores. Arithmetic as in epilogue16 / epilogue16_split.
+          __shared__ __align__(16) float stage[kEpiThreads / 32][32 * 20];
+          float* wb = stage[warp - 2];
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            reinterpret_cast<float4*>(wb + lane * 20)[j] = make_float4(
+                v[4 * j] * sc, v[4 * j + 1] * sc, v[4 * j + 2] * sc, v[4 * j + 3] * sc);
+          __syncwarp();
+          const int c4 = (lane & 3) * 4;
+          const int64_t col = (int64_t)n0 + c0 + c4;
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+          float4 rr[4];
+          if (!SOUT) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int64_t grow = m0 + 32 * q + (lane >> 2) + 8 * k;
+              rr[k] = grow < M ? *reinterpret_cast<const float4*>(ep.resid + grow * ep.ldr + col)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int rl = (lane >> 2) + 8 * k;
+            const int64_t grow = m0 + 32 * q + rl;
+            if (grow >= M) continue;
+            const float4 x = *reinterpret_cast<const float4*>(wb + rl * 20 + c4);
+            float o[4] = {ep.alpha * x.x + ep.beta * bb.x, ep.alpha * x.y + ep.beta * bb.y,
+                          ep.alpha * x.z + ep.beta * bb.z, ep.alpha * x.w + ep.beta * bb.w};
+            if (SOUT) {
+              if (EPI == EPI_BIAS_GELU) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = gelu_erf(o[i]);
+              }
+              uint32_t l0, l1;
+              const uint32_t h0 = split_pair(o[0], o[1], l0, bad);
+              const uint32_t h1 = split_pair(o[2], o[3], l1, bad);
+              *reinterpret_cast<uint2*>(so.hi + grow * so.ld + col) = make_uint2(h0, h1);
+              *reinterpret_cast<uint2*>(so.lo + grow * so.ld + col) = make_uint2(l0, l1);
+            } else {
+              o[0] += rr[k].x; o[1] += rr[k].y; o[2] += rr[k].z; o[3] += rr[k].w;
+              *reinterpret_cast<float4*>(C + grow * ldc + col) = make_float4(o[0], o[1], o[2], o[3]);
+            }
+          }
+          __syncwarp();
+          continue;
+        }
         if (row >= M) continue;
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] *= sc;
         const int64_t col0 = (int64_t)n0 + c0;
         if (SOUT) {
-          epilogue16_split<EPI>(ep, v, row, col0, so, bad);
+          // N % 16 == 0 for split outputs: a chunk is wholly inside or outside
+          if (col0 < N) epilogue16_split<EPI>(ep, v, row, col0, so, bad);
         } else {
           epilogue16<EPI>(ep, v, row, col0, N, C + row * ldc + col0, vec_ok);
         }
@@ -348,14 +401,19 @@ int read_and_clear_f16_2cta_error() {
   return v;
 }
 
-bool gemm_f16s_2cta_usable(const F16GemmA& A, int64_t M, int64_t N) {
-  // Opt-in (INFERC_GEMM_2CTA=1): on the encoder's FFN1 it measured ~3 %
-  // slower than the one-SM kernel.
-  static const bool on = [] {
+bool gemm_f16s_2cta_usable(const F16GemmA& A, int64_t M, int64_t N, bool split_out) {
+  // Measured on the encoder's GEMMs (M = 32768), with the staged epilogues:
+  // ahead of the one-SM kernel where the result is written as fp16 planes
+  // (FFN1 358 vs 367 us, QKV 254 vs 264 us), behind it for the fp32
+  // residual epilogue (117 vs 113 us at K = 768). So by default it takes the
+  // split-output GEMMs; INFERC_GEMM_2CTA=1 uses it for every eligible GEMM,
+  // =0 for none.
+  static const int mode = [] {
     const char* e = std::getenv("INFERC_GEMM_2CTA");
-    return e && e[0] == '1';
+    return e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
   }();
-  return on && A.a32 == nullptr && M >= 512 && N >= 256;
+  if (A.a32 != nullptr || M < 512 || N < 256) return false;
+  return mode == 1 || (mode == -1 && split_out);
 }
 
 void launch_gemm_f16s_2cta(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,

@@ -149,8 +149,9 @@ def test_f16s_planes_chain():
 @pytest.mark.parametrize("M,K,N", [(512, 768, 256), (1000, 768, 2304), (4096, 3072, 768),
                                    (777, 96, 300), (32768, 768, 3072)])
 def test_f16s_planes_shapes(M, K, N):
-    """A as fp16 planes (the plan's form; M >= 512 runs the two-SM 256-row
-    kernel) with the bias + residual epilogue, ragged M / N / K included."""
+    """A as fp16 planes (the plan's form) with the bias + residual epilogue
+    (fp32 out), ragged M / N / K included: whole 256-column tiles take the
+    shared-memory-staged epilogue, a partial last tile the per-row one."""
     L = lib.load()
     rng = np.random.default_rng(M + N)
     a = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
@@ -173,9 +174,40 @@ def test_f16s_planes_shapes(M, K, N):
     assert err < TC_REL_TOL
 
 
-def test_f16s_two_sm_kernel_opt_in():
-    """The two-SM (cta_group::2, 256-row) form, opt-in by INFERC_GEMM_2CTA=1 at
-    process start: run the plane GEMM check in a child process with it on."""
+@pytest.mark.parametrize("M,K,N,act", [(777, 768, 784, 1), (1000, 768, 2304, 0),
+                                       (513, 3072, 272, 1)])
+def test_f16s_split_out_shapes(M, K, N, act):
+    """Split-plane output (bias, or bias + GELU) with ragged M and an N whose
+    last 256-column tile is partial (staged and per-row epilogues in one
+    launch); the planes' sum against float64."""
+    L = lib.load()
+    rng = np.random.default_rng(M * 3 + N)
+    a = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+    w = torch.from_numpy(rng.standard_normal((K, N), dtype=np.float32) * 0.02).cuda()
+    b = torch.from_numpy(rng.standard_normal(N, dtype=np.float32) * 0.02).cuda()
+    hi, lo, sc = _prep(L, w)
+    ah, al = (torch.empty((M, K), dtype=torch.int16, device="cuda") for _ in range(2))
+    lib.check(L.inferc_dev_f16_split_rows(a.data_ptr(), M, K, K, ah.data_ptr(), al.data_ptr(), K,
+                                          None))
+    yh, yl = (torch.empty((M, N), dtype=torch.int16, device="cuda") for _ in range(2))
+    lib.check(L.inferc_dev_gemm_f16s_planes(ah.data_ptr(), al.data_ptr(), K, hi.data_ptr(),
+                                            lo.data_ptr(), sc.data_ptr(), b.data_ptr(), None, 0,
+                                            None, yh.data_ptr(), yl.data_ptr(), N, M, N, K, act,
+                                            None))
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    v = a.double() @ w.double() + b.double()
+    ref = v * 0.5 * (1 + torch.erf(v / 2 ** 0.5)) if act else v
+    got = yh.view(torch.float16).double() + yl.view(torch.float16).double()
+    assert (got - ref).abs().max().item() < 3e-5 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("mode", ["1", "0"])
+def test_f16s_two_sm_kernel_modes(mode):
+    """INFERC_GEMM_2CTA (read at process start) picks the GEMM form: "1" puts
+    every eligible GEMM on the two-SM (cta_group::2, 256-row) kernel, "0"
+    every GEMM on the one-SM kernel (by default split-plane outputs take the
+    two-SM kernel and fp32 outputs the one-SM kernel). Run the plane and
+    residual GEMM checks in a child process for each."""
     import os
     import subprocess
     import sys
@@ -185,7 +217,7 @@ def test_f16s_two_sm_kernel_opt_in():
         "t.test_f16s_planes_shapes(1000, 768, 2304); t.test_f16s_planes_shapes(512, 3072, 768);"
         "t.test_f16s_planes_chain(); print('ok')")
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, INFERC_GEMM_2CTA="1")
+    env = dict(os.environ, INFERC_GEMM_2CTA=mode)
     out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True,
                          text=True, timeout=300)
     assert out.returncode == 0 and "ok" in out.stdout, out.stderr[-2000:]
