@@ -238,14 +238,14 @@ def roofline_ffn1(cfg, M, dev, stream, pk, reps):
 
 
 # DRAM bytes (read + write) of one FFN1 launch at M = 32768 from one ncu
-# capture on a B200:
+# capture on a B200 (the two-SM kernel the plan uses for split outputs):
 #   python bench.py --roofline-only --steps 2 && ncu --metrics
 #   dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
-#   --clock-control none -k regex:gemm_f16s_kernel -s 3 -c 1 --csv
+#   --clock-control none -k regex:gemm_f16s_2cta -s 3 -c 1 --csv
 #   python bench.py --roofline-only --steps 2
-# read 111,074,048 + write 349,294,848. Other M scale the activation and
+# read 110,978,816 + write 351,867,136. Other M scale the activation and
 # output part by M / 32768; the weight planes (F x Kp x 2 planes x 2 B) do not.
-FFN1_DRAM_BYTES_M32768 = 111_074_048 + 349_294_848
+FFN1_DRAM_BYTES_M32768 = 110_978_816 + 351_867_136
 
 
 def ffn1_traffic(M, cfg):
@@ -289,7 +289,7 @@ def main():
         pk, basis = peaks()
         kms, flops, achieved, peak_eff = roofline_ffn1(
             cfg, GLOBAL_BATCH * SEQ, dev, torch.cuda.current_stream(dev), pk, args.steps)
-        print(json.dumps({"kernel": "gemm_f16s_kernel (FFN1, planes in, split out)",
+        print(json.dumps({"kernel": "gemm_f16s_2cta_kernel (FFN1, planes in, split out)",
                           "ms_per_launch": kms, "achieved_tflops": achieved,
                           "peak_tflops": peak_eff, "frac": achieved / peak_eff,
                           "launches": args.steps + 3}), flush=True)
@@ -365,7 +365,8 @@ def main():
                        "global_batch": GLOBAL_BATCH, "seq_len": SEQ,
                        "parallelism": f"dp{world}",
                        "l2": "working set > L2 (weights 170 MB + activations)"},
-            "roofline": {"kernel": "FusedMatMulAddGELU (FFN1 GEMM)", "bound": "tensor",
+            "roofline": {"kernel": "FusedMatMulAddGELU (FFN1 GEMM, gemm_f16s_2cta_kernel)",
+                         "bound": "tensor",
                          "achieved": achieved, "peak": peak_eff, "unit": "TFLOP/s",
                          "frac": achieved / peak_eff,
                          "peak_basis": f"split fp16 (3 MMAs/product) = {basis} bf16 "
