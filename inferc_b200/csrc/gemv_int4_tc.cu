@@ -106,8 +106,8 @@ struct alignas(64) Int4TcBatch {
   int blk_start[kMaxMats + 1];   // prefix sums of 128-row blocks
   int slab_start[kMaxMats + 1];  // prefix sums of slabs (blocks x kslabs)
   int count;
-  unsigned long long* part_sum;  // [blocks x 128] row partial sums of split blocks (zero at rest)
-  int* part_cnt;                 // [blocks] slabs added so far (zero at rest)
+  unsigned long long* part_sum;  // [blocks x 128] (slab count << 48) + partial row sum of
+                                 // split blocks (zero at rest)
 };
 
 // Both launches' parameters, kept in device memory: as kernel parameters
@@ -178,11 +178,6 @@ __device__ __forceinline__ bool epi_all(bool v) {
       : "r"((uint32_t)v), "r"(kEpi)
       : "memory");
   return r != 0;
-}
-
-// Barrier of the 128 epilogue threads (named barrier 3).
-__device__ __forceinline__ void epi_sync() {
-  asm volatile("bar.sync 3, %0;" ::"r"(kEpi) : "memory");
 }
 
 // One 16-byte group of digit-plane bytes: (atom a, digit row i, physical
@@ -273,7 +268,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], b_ready[2], b_free[2];
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
-  __shared__ int last_sh;
 
   __shared__ Int4TcMeta bt;
   {
@@ -495,23 +489,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tsum += (lo + hi) << (16 - 8 * i);
       }
       if (nsl < m.kslabs) {
-        // Part of a block split between CTAs: add the exact integer partial
-        // sums; the CTA whose slabs complete the block writes the rows
-        // (threadfence-reduction order: sums, fence, count; count, fence,
-        // sums) and returns the scratch to zero.
+        // Part of a block split between CTAs. Each row's scratch word holds
+        // (slabs added so far) << 48 plus the exact partial sum (|sum| <
+        // 2^38, so the two fields never mix). One atomic add per row returns
+        // the word; the contributor whose slabs complete the count has the
+        // whole sum, writes the row and returns the word to zero.
+        if (row >= m.n) continue;
         unsigned long long* ps = prm.part_sum + (size_t)j * 128 + rl;
-        if (row < m.n) atomicAdd(ps, (unsigned long long)tsum);
-        __threadfence();
-        epi_sync();
-        if (e == 0) {
-          const int done = atomicAdd(prm.part_cnt + j, nsl) + nsl;
-          last_sh = done == m.kslabs;
-          if (done == m.kslabs) atomicExch(prm.part_cnt + j, 0);
-          __threadfence();
-        }
-        epi_sync();
-        if (!last_sh) continue;
-        if (row < m.n) tsum = (long long)atomicExch(ps, 0ull);
+        const unsigned long long add = ((unsigned long long)nsl << 48) + (unsigned long long)tsum;
+        const long long now = (long long)(atomicAdd(ps, add) + add);
+        const long long cnt = (now + (1LL << 47)) >> 48;
+        if (cnt != m.kslabs) continue;
+        tsum = now - (cnt << 48);
+        *ps = 0ull;
       }
       if (row < m.n) m.y[row] = __ldg(m.scales + row) * xs * (float)(tsum - 8LL * asum);
     }
@@ -733,9 +723,7 @@ void launch_gemv_int4_tc(const InfercInt4Gemv* const* ds, int n, cudaStream_t st
     }
     bt.blk_start[bt.count] = blks;
     bt.slab_start[bt.count] = slabs;
-    void* part = partial_scratch((size_t)blks * (128 * 8 + 4), st);
-    bt.part_sum = static_cast<unsigned long long*>(part);
-    bt.part_cnt = reinterpret_cast<int*>(bt.part_sum + (size_t)blks * 128);
+    bt.part_sum = static_cast<unsigned long long*>(partial_scratch((size_t)blks * 128 * 8, st));
     const Int4Params* dp = device_params(hp, st);
     int4_digits_kernel<<<bt.count, 256, 0, st>>>(dp);
     IDEV_LAUNCHED();
