@@ -306,22 +306,27 @@ def main():
     mask_h = torch.from_numpy(mask_all[s0:s1].copy()).pin_memory()
     ids_d, mask_d = ids_h.to(dev), mask_h.to(dev)
     logits_d = torch.empty(B, cfg.n_classes, device=dev)
-    logits_h = torch.empty(B, cfg.n_classes).pin_memory()
+    # rank 0 receives the whole batch's logits; the gather writes into a
+    # buffer reused every step
+    logits_h = torch.empty(GLOBAL_BATCH, cfg.n_classes).pin_memory()
+    biggest = dp.shard_rows(GLOBAL_BATCH, world, 0)[1]
+    gather_buf = torch.empty(world * biggest, cfg.n_classes, device=dev) if rank == 0 else None
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
 
     def step():
         plan.run(ids_d, mask_d, logits_d, sptr)
         if world > 1:
-            dp.gather_logits(logits_d, GLOBAL_BATCH)
+            dp.gather_logits(logits_d, GLOBAL_BATCH, out=gather_buf)
 
     def e2e_step():
         ids_d.copy_(ids_h, non_blocking=True)
         mask_d.copy_(mask_h, non_blocking=True)
         plan.run(ids_d, mask_d, logits_d, sptr)
-        full = dp.gather_logits(logits_d, GLOBAL_BATCH) if world > 1 else logits_d
+        full = dp.gather_logits(logits_d, GLOBAL_BATCH, out=gather_buf) if world > 1 \
+            else logits_d
         if full is not None:
-            logits_h[: full.shape[0]].copy_(full[: logits_h.shape[0]], non_blocking=True)
+            logits_h.copy_(full, non_blocking=True)
         stream.synchronize()
 
     def timed(fn, steps):
@@ -378,21 +383,35 @@ def main():
                          "traffic": ffn1_traffic(B * SEQ, cfg),
                          "traffic_unit": "bytes per launch (ncu dram read + write)"},
             "e2e": {"value": e2e_value, "unit": "seq/s",
-                    "h2d_bytes_per_step": int(ids_h.numel() * 8 * 2),
-                    "d2h_bytes_per_step": int(GLOBAL_BATCH * cfg.n_classes * 4)},
+                    "h2d_bytes_per_step": int(GLOBAL_BATCH * SEQ * 8 * 2),
+                    "d2h_bytes_per_step": int(GLOBAL_BATCH * cfg.n_classes * 4),
+                    "path": "inferc_dev_encoder_run (C ABI) per rank: pinned host ids/mask "
+                            "copied in, logits gathered to rank 0 and copied out, every step"},
             "gpu_launches": int(args.steps * (1 + cfg.layers * 7 + 2)),
             "clocks": clocks.summary(),
         }
+    from inferc_b200 import lib as _lib
+    fallbacks = int(_lib.load().inferc_dev_encoder_range_fallbacks(plan._h))
+    if world > 1:
+        fb = torch.tensor([fallbacks], device=dev)
+        dist.all_reduce(fb)
+        fallbacks = int(fb.item())
     if rank == 0:
-        # Parity on the committed reference fixture (8 variable-length
-        # sequences of this workload's model, reference kernels' logits).
-        gold = np.load(os.path.join(ROOT, "tests", "golden", "encoder.npz"))
-        g_ids, g_mask = gold["c4_ids"], gold["c4_mask"]
-        n = min(len(g_ids), B)
-        got = plan.run_host(g_ids[:n], g_mask[:n])
+        # Parity of the timed workload itself: the logits of the last e2e
+        # step (all 256 sequences, gathered to rank 0 when N > 1) against the
+        # reference kernels' logits for the same 256 sequences.
+        gold = np.load(os.path.join(ROOT, "tests", "golden", "encoder_c4_bench.npz"))
+        got = logits_h.numpy()
+        diff = np.abs(got - gold["logits"])
         result["parity"] = {
-            "encoder_logits_max_abs_diff": float(np.abs(got - gold["c4_logits"][:n]).max()),
-            "tolerance": 1e-4, "fixture": "tests/golden/encoder.npz c4 (reference kernels)"}
+            "encoder_logits_max_abs_diff": float(diff.max()),
+            "rows_compared": int(got.shape[0]), "gathered_from_ranks": world,
+            "argmax_agree": bool((got.argmax(1) == gold["logits"].argmax(1)).all()),
+            "tolerance": 1e-4,
+            "fixture": "tests/golden/encoder_c4_bench.npz (reference kernels, all 256 rows)"}
+        # batches the plan reran on its 3xTF32 graph (fp16 range flag) during
+        # the warm-up, timed and e2e steps, summed over ranks
+        result["range_fallbacks"] = fallbacks
     del plan
     torch.cuda.empty_cache()
 
@@ -424,10 +443,14 @@ def _cpu_oracle(prefer_ref=True):
     return oracle.port(), "port"
 
 
+ENCODER_GFLOP_PER_SEQ = 11.17  # per sequence of 128 tokens (QKV, out, FFN x2, attention) x 6
+
+
 def encoder_c0_bench(dev):
     """the DistilBERT-arch encoder at batch 1, seq 128
     (ids 101 ... 102, mask all ones; tests/golden/encoder.npz c0): device ms
-    per sequence through the plan, and the reference's CPU kernels beside it."""
+    per sequence through the plan, the same through the host-buffer entry
+    (e2e), and the reference's CPU kernels beside it."""
     import torch
 
     from inferc_b200 import plans, structs, synth
@@ -450,6 +473,13 @@ def encoder_c0_bench(dev):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / 50
     diff = float(np.abs(out.cpu().numpy() - gold["c0_logits"]).max())
+    # e2e: the host-buffer entry (copies in, run, copies out, synchronises)
+    for _ in range(3):
+        p.run_host(ids_h, mask_h)
+    t0 = time.perf_counter()
+    for _ in range(50):
+        got = p.run_host(ids_h, mask_h)
+    e2e_ms = (time.perf_counter() - t0) / 50 * 1e3
     o, kind = _cpu_oracle()
     st = structs.encoder_struct(cfg, w)
     o.encoder_forward(st, ids_h, mask_h, cfg.n_classes)
@@ -457,10 +487,21 @@ def encoder_c0_bench(dev):
     for _ in range(3):
         o.encoder_forward(st, ids_h, mask_h, cfg.n_classes)
     cpu_ms = (time.perf_counter() - t0) / 3 * 1e3
+    pk, basis = peaks()
+    achieved = ENCODER_GFLOP_PER_SEQ / (ms / 1e3) / 1e3
+    peak = pk["bf16_tflops"] / 3.0
     return {"metric": "encoder ms per sequence (DistilBERT-arch, batch 1, seq 128)", "value": ms,
             "unit": "ms", "higher_is_better": False,
             "config": {"workload": "BASELINE config 0: batch 1 x seq 128, mask all ones"},
             "logits_max_abs_diff": diff,
+            "e2e_logits_max_abs_diff": float(np.abs(got - gold["c0_logits"]).max()),
+            "roofline": {"bound": "tensor (launch-bound at M = 128)", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "flops_per_unit": ENCODER_GFLOP_PER_SEQ * 1e9,
+                         "peak_basis": f"split fp16 = {basis} bf16 / 3"},
+            "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": int(ids_h.nbytes * 2),
+                    "d2h_bytes_per_step": 4 * cfg.n_classes,
+                    "path": "inferc_dev_encoder_run_host (host ids/mask in, logits out)"},
             "cpu_baseline": {"value": cpu_ms, "unit": "ms", "cores": os.cpu_count() or 1,
                              "kind": kind, "sample": "the same sequence, mean of 3"}}
 
@@ -475,9 +516,15 @@ def decode_bench(dev):
     prompt = synth.gpt2_prompt(32, seed=2)
     p = plans.DecoderPlan(cfg, w, max_len=1024)
     p.decode(prompt, 128)  # warm-up: captures the step graph
-    runs = [p.decode(prompt, 128) for _ in range(3)]
+    runs = []
+    walls = []
+    for _ in range(3):  # inferc_dev_decode: host prompt in, host tokens out, synchronous
+        t0 = time.perf_counter()
+        runs.append(p.decode(prompt, 128))
+        walls.append(time.perf_counter() - t0)
     toks = runs[-1][0]
     ms = statistics.median(r[1] for r in runs)
+    e2e_ms = statistics.median(walls) * 1e3 / 128
     gold = np.load(os.path.join(ROOT, "tests", "golden", "decode.npz"))
     lm_bytes = cfg.vocab * cfg.hidden * 4
     layer_bytes = cfg.layers * 4 * (cfg.hidden * 3 * cfg.hidden + cfg.hidden * cfg.hidden +
@@ -493,6 +540,10 @@ def decode_bench(dev):
             "achieved_gbs": gbs, "hbm_frac": gbs / pk["hbm_gbs"], "peak_basis": basis,
             "kernel": "decode_mega_kernel (one persistent cooperative launch for all steps)",
             "published_m1_ms_per_token": 27.9,
+            "e2e": {"value": e2e_ms, "unit": "ms/token",
+                    "h2d_bytes_per_step": int(prompt.nbytes), "d2h_bytes_per_step": 8 * 128,
+                    "path": "inferc_dev_decode wall time (host prompt in, prefill + 127 "
+                            "steps, host token ids out) / 128 tokens; a step is one decode"},
             "cpu_baseline": _decode_cpu(cfg, w, prompt)}
 
 
@@ -556,6 +607,25 @@ def int4_bench(dev):
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1))
     ms = statistics.median(times)
+    # e2e: the activation vectors come from pinned host memory and the results
+    # go back to it every call (the weights are the resident model)
+    xs_h = [torch.from_numpy(m.x).pin_memory() for m in mats]
+    ys_h = [torch.empty(m.n).pin_memory() for m in mats]
+    d0 = copies[0][0]
+
+    def e2e_call():
+        for (w, sc, x, y), xh in zip(d0, xs_h):
+            x.copy_(xh, non_blocking=True)
+        fn(copies[0][1], len(mats), sptr)
+        for (w, sc, x, y), yh in zip(d0, ys_h):
+            yh.copy_(y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    for _ in range(3):
+        e2e_call()
+    t0 = time.perf_counter()
+    for _ in range(20):
+        e2e_call()
+    e2e_ms = (time.perf_counter() - t0) / 20 * 1e3
     nbytes = sum(m.w.nbytes + m.scales.nbytes + m.x.nbytes + 4 * m.n for m in mats)
     pk, basis = peaks()
     gbs = nbytes / (ms / 1e3) / 1e9
@@ -564,6 +634,11 @@ def int4_bench(dev):
             "achieved_gbs": gbs, "hbm_peak_gbs": pk["hbm_gbs"], "frac": gbs / pk["hbm_gbs"],
             "peak_basis": basis, "l2": "4 rotating copies of the set (252 MB > L2)",
             "published_m1_ms_123M_weights": 7.73,
+            "e2e": {"value": e2e_ms, "unit": "ms",
+                    "h2d_bytes_per_step": int(sum(m.x.nbytes for m in mats)),
+                    "d2h_bytes_per_step": int(sum(4 * m.n for m in mats)),
+                    "path": "inferc_dev_gemv_int4_batched with x copied from pinned host and "
+                            "y copied back per call (one copy each per matrix)"},
             "cpu_baseline": _int4_cpu(mats)}
 
 
@@ -583,13 +658,19 @@ def sweep_bench(dev):
     """fused QKV projection + masked FusedAttention at
     hidden 768, 12 heads, seq {128, 512} x batch {1, 8, 64}, valid lengths
     uniform in [16, seq], through inferc_dev_qkv_attention_f16 (split-fp16
-    prepared weights, planes end to end). Reports ms per (QKV + attention)
-    and padded TFLOP/s."""
+    prepared weights, planes end to end). Per point: device ms (CUDA-graph
+    replay), padded and valid TFLOP/s with their fractions of the split-fp16
+    peak, an e2e time with x from pinned host memory and the context copied
+    back, parity of four sampled sequences against the reference kernels, and
+    the reference kernels' CPU time on the whole point."""
     import torch
 
     from inferc_b200 import lib as _lib
     from inferc_b200 import synth
     L = _lib.load()
+    pk, basis = peaks()
+    peak = pk["bf16_tflops"] / 3.0
+    o, kind = _cpu_oracle()
     out = []
     sptr = torch.cuda.current_stream().cuda_stream
     for S in (128, 512):
@@ -620,6 +701,8 @@ def sweep_bench(dev):
             for _ in range(3):
                 run()
             torch.cuda.synchronize()
+            _lib.check(L.inferc_dev_stream_synchronize(None))
+            got = ctx.cpu().numpy()
             # Replay as a CUDA graph so host-side launch preparation (tensor
             # maps, ctypes) is not inside the device-timed region.
             g = torch.cuda.CUDAGraph()
@@ -635,18 +718,53 @@ def sweep_bench(dev):
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / 10
+            # e2e: x from pinned host memory in, the context back to pinned
+            # host memory, every call
+            x_h = torch.from_numpy(x).pin_memory()
+            ctx_h = torch.empty(B, S, H).pin_memory()
+            st = torch.cuda.current_stream()
+
+            def e2e_call():
+                xd.copy_(x_h, non_blocking=True)
+                g.replay()
+                ctx_h.copy_(ctx, non_blocking=True)
+                st.synchronize()
+            for _ in range(2):
+                e2e_call()
+            t0 = time.perf_counter()
+            for _ in range(10):
+                e2e_call()
+            e2e_ms = (time.perf_counter() - t0) / 10 * 1e3
             flops = 3538944.0 * B * S + 3072.0 * B * S * S
-            row = {"seq": S, "batch": B, "ms": ms, "tflops": flops / (ms / 1e3) / 1e12}
-            if B == 8:  # bounded CPU sample: the reference's kernels on the host
-                o, kind = _cpu_oracle()
-                mask4 = mask.reshape(B, 1, 1, S)
-                t0 = time.perf_counter()
-                q, k, v = o.fused_qkv(x.reshape(B, S, H), *ws)
-                o.fused_attention(q, k, v, mask4, 64, -3.4028234663852886e38)
-                row["cpu_baseline"] = {"value": (time.perf_counter() - t0) * 1e3, "unit": "ms",
-                                       "cores": os.cpu_count() or 1, "kind": kind,
-                                       "sample": "this (seq, batch), once"}
-            out.append(row)
+            valid = 3538944.0 * B * S + 3072.0 * S * float(lens.sum())
+            tf, tv = flops / (ms / 1e3) / 1e12, valid / (ms / 1e3) / 1e12
+            # parity: four sampled sequences against the reference kernels
+            worst = 0.0
+            for b in sorted({0, B - 1, B // 2, B // 3}):
+                q, k, v = o.fused_qkv(x[b].reshape(S, H), *ws)
+                want = o.fused_attention(q.reshape(1, S, H), k.reshape(1, S, H),
+                                         v.reshape(1, S, H), mask[b].reshape(1, 1, 1, S), 64,
+                                         -3.4028234663852886e38)[0]
+                worst = max(worst, float(np.abs(got[b] - want).max()))
+            t0 = time.perf_counter()
+            q, k, v = o.fused_qkv(x.reshape(B * S, H), *ws)
+            o.fused_attention(q.reshape(B, S, H), k.reshape(B, S, H), v.reshape(B, S, H),
+                              mask.reshape(B, 1, 1, S), 64, -3.4028234663852886e38)
+            cpu_ms = (time.perf_counter() - t0) * 1e3
+            out.append({
+                "seq": S, "batch": B, "ms": ms, "tflops": tf, "tflops_valid": tv,
+                "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                             "frac": tf / peak, "frac_valid": tv / peak,
+                             "flops_padded": flops, "flops_valid": valid,
+                             "peak_basis": f"split fp16 = {basis} bf16 / 3"},
+                "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": int(x.nbytes),
+                        "d2h_bytes_per_step": int(B * S * H * 4)},
+                "parity": {"max_abs_diff": worst, "tolerance": 5e-5,
+                           "sequences_compared": len({0, B - 1, B // 2, B // 3}),
+                           "against": kind},
+                "cpu_baseline": {"value": cpu_ms, "unit": "ms", "cores": os.cpu_count() or 1,
+                                 "kind": kind, "sample": "this (seq, batch) point, once"}})
+            del g
     return out
 
 

@@ -48,8 +48,6 @@ enum {
 /* Message of the last failed call on this host thread (never NULL). */
 const char* inferc_dev_last_error_string(void);
 
-/* Waits for the stream; also reports INFERC_ERR_TIMEOUT when a bounded
- * device wait of an earlier tensor-core GEMM gave up (then cleared). */
 /* Library version string, e.g. "inferc_b200 0.1 sm_100a". */
 const char* inferc_dev_version(void);
 
@@ -58,7 +56,21 @@ int inferc_dev_alloc(void** ptr, size_t bytes);
 int inferc_dev_free(void* ptr);
 int inferc_dev_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
 int inferc_dev_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+/* Waits for the stream; also reports INFERC_ERR_TIMEOUT when a bounded
+ * device wait of an earlier tensor-core kernel gave up, and INFERC_ERR_RANGE
+ * when an earlier split-fp16 call met a value fp16 cannot carry (both flags
+ * are then cleared). */
 int inferc_dev_stream_synchronize(void* stream);
+
+/* Test hook for the failure path, used by no plan and with no counterpart in
+ * the reference: runs one of the library's bounded device waits on something
+ * that is never signalled (which = 0: an mbarrier phase as in the TMA /
+ * tcgen05 pipelines; 1: a grid-barrier arrival counter as in the persistent
+ * decode kernel) with a limit of limit_us microseconds. The wait gives up,
+ * sets the device error flag and returns; the next
+ * inferc_dev_stream_synchronize reports INFERC_ERR_TIMEOUT and clears it.
+ * Nothing traps, faults or hangs; the context stays usable. */
+int inferc_dev_selftest_wait_timeout(int which, int64_t limit_us, void* stream);
 
 /* ------------------------------------------------------------- fused ops */
 
@@ -298,6 +310,9 @@ int inferc_dev_encoder_run(inferc_encoder_t plan, const int64_t* ids,
 int inferc_dev_encoder_run_host(inferc_encoder_t plan, const int64_t* ids,
                                 const int64_t* mask, int64_t B, int64_t S,
                                 float* logits);
+/* Number of batches this plan has rerun on its 3xTF32 graph because the
+ * split-fp16 graph met a value fp16 cannot carry (-1 for a NULL plan). */
+int64_t inferc_dev_encoder_range_fallbacks(inferc_encoder_t plan);
 void inferc_dev_encoder_destroy(inferc_encoder_t plan);
 
 /* A prepared GPT-2 greedy decoder (`inferc decode`, src/cli/main.cpp:700-945)

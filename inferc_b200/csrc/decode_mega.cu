@@ -115,11 +115,13 @@ struct Smem {
   unsigned nbar;  // barriers passed (thread 0)
 };
 
+#ifdef INFERC_DECODE_PROFILE
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+#endif
 
 // Grid-wide barrier (all CTAs co-resident: cooperative launch). Returns
 // false when the kernel must stop (timeout here or elsewhere).
@@ -135,8 +137,10 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 // Split in two so that thread 0 can issue the next copies between its
 // arrival and its wait.
 __device__ void grid_arrive(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
+#ifdef INFERC_DECODE_PROFILE
   if (a.prof && step == 1 && blockIdx.x == 0 && threadIdx.x == 0 && tag >= 0)
     a.prof[2 * tag] = gtimer();
+#endif
   __syncthreads();  // the CTA's outputs of the phase precede the release below
   if (threadIdx.x == 0) {
     sm.target = (++sm.nbar) * gridDim.x;
@@ -156,7 +160,9 @@ __device__ bool grid_wait(const MegaArgs& a, Smem& sm, int tag = -1, int step = 
       }
     }
     sm.abort_flag = *(volatile int*)a.err;
+#ifdef INFERC_DECODE_PROFILE
     if (a.prof && step == 1 && blockIdx.x == 0 && tag >= 0) a.prof[2 * tag + 1] = gtimer();
+#endif
   }
   __syncthreads();
   return sm.abort_flag == 0;
@@ -574,10 +580,6 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
   float* part = scr + 384 + a.max_len + 4;  // [8][65]
   float* kh = L.kc + (size_t)h * a.max_len * HD;
   float* vh = L.vc + (size_t)h * a.max_len * HD;
-  auto mk = [&](int i) {
-    if (a.prof && blockIdx.x == 0 && threadIdx.x == 0) a.prof[1100 + i] = clock64();
-  };
-  mk(0);
   if (tid < HD) {
     qs[tid] = __ldcg(a.qkv + h * HD + tid);
     kn[tid] = __ldcg(a.qkv + H + h * HD + tid);
@@ -588,7 +590,6 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
     }
   }
   __syncthreads();
-  mk(1);
   const int64_t Lk = pos + 1;
   const float sq = sqrtf((float)HD);
   // thread pair (2i, 2i+1) shares key i: each lane holds half the dims.
@@ -648,7 +649,6 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
     }
     m = mn;
   }
-  mk(2);
   // block max of m
   float mx = warp_max(m);
   if (lane == 0) sm.red[wid] = mx;
@@ -681,7 +681,6 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
     ctx_out[tid] = r / t;
   }
   __syncthreads();
-  mk(3);
 }
 
 // FC-phase input: xm = xa + b_proj + sum_h part[h] (heads in order); CTA 0
@@ -744,7 +743,6 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
   else
     attention_head(a, L, pos, scr, sm, h, cc == 0, ctx);
   if (!wait_slot(slot, sm, a)) return false;
-  if (a.prof && blockIdx.x == 0 && threadIdx.x == 0) a.prof[1104] = clock64();
   const MegaPanels& m = L.proj;  // K = hd, P = chunk width
   const float* w = reinterpret_cast<const float*>(slots + (size_t)slot * kSlotBytes);
   const int tid = threadIdx.x;
@@ -764,7 +762,6 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
     if (gcol < a.H) a.part[(size_t)h * a.H + gcol] = t;
   }
   __syncthreads();
-  if (a.prof && blockIdx.x == 0 && threadIdx.x == 0) a.prof[1105] = clock64();
   return true;
 }
 
@@ -864,7 +861,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       prefetch_panels(L.fc, 0, slots, sm);  // pair 0 consumed
       if (!grid_wait(a, sm, 4 * l + 0, step)) { drain(sm); return; }
       // ---- attention + output projection partials (slot 2)
-      if (a.prof && blockIdx.x == 0 && tid == 0) a.prof[1099] = clock64();
       if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm)) { drain(sm); return; }
       grid_arrive(a, sm, 4 * l + 1, step);
       prefetch_panels(L.fp, 1, slots, sm);  // slot 2 consumed, slot 3 free

@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES], conv_bar[STAGES], empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2];
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], kEpiThreads);
     }
+    mbar_init(&drain_bar, 1);
     abort_sh = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -194,6 +195,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
           tma_load_2d(stage_bl(s), &tmBl, &full_bar[s], it * BK, n0);
         }
       }
+      if (abort_sh) drain_tma_ring(full_bar, STAGES, g);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
@@ -230,6 +232,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
         }
         mma_commit(&tfull_bar[acc]);
       }
+      if (abort_sh) drain_mma(&drain_bar);
     }
   } else if (warp < 2 + kConvThreads / 32) {  // ---------------- converter (warps 2..5)
     if (!AS) {

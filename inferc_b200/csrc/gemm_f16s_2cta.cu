@@ -142,7 +142,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2];
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -168,6 +168,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&tfull_bar[b], 1);  // the leader's MMA commit (to both CTAs)
       mbar_init(&tempty_bar[b], 2 * kEpiThreads);  // leader: both CTAs' epilogues
     }
+    mbar_init(&drain_bar, 1);
     abort_sh = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -202,6 +203,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tma_load_2d_2sm(base + 2 * kAPlane, &tmBh, lead_full, it * kBK, n0);
           tma_load_2d_2sm(base + 2 * kAPlane + S::B_PLANE, &tmBl, lead_full, it * kBK, n0);
         }
+      }
+      // On abort the leader waits (bounded) for the ring generations it
+      // issued. Both CTAs' copies complete on the leader's barriers, so this
+      // also covers the peer's copies of those generations; the cluster
+      // barrier below keeps the peer resident until then.
+      if (abort_sh && leader) {
+        for (int j = g > STAGES ? g - STAGES : 0; j < g; ++j)
+          mbar_wait_cl(&full_bar[j % STAGES], (uint32_t)(j / STAGES) & 1);
       }
     }
   } else if (warp == 1) {
@@ -241,6 +250,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         commit_2sm(smem_u32(&tfull_bar[acc]));
         commit_2sm(map_to_rank(smem_u32(&tfull_bar[acc]), 1));
+      }
+      if (abort_sh) {  // every pair MMA issued so far finishes before TMEM is freed
+        commit_2sm(smem_u32(&drain_bar));
+        mbar_wait_cl(&drain_bar, 0);
       }
     }
   } else {  // ---------------- epilogue (warps 2..9, both CTAs)
@@ -337,7 +350,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (SOUT && bad) atomicExch(so.range, 1);
   }
   tc_fence_before();
-  cluster_sync();  // no MMA, TMA or remote arrive of either CTA is still pending
+  // No MMA, TMA or remote arrive of either CTA is still pending here: on the
+  // normal path every stage and accumulator was consumed; on abort the
+  // leader's producer and MMA thread drained theirs above.
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),

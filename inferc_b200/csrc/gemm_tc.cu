@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES], conv_bar[STAGES], empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2];
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], kEpiThreads);
     }
+    mbar_init(&drain_bar, 1);
     abort_sh = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -149,6 +150,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
           }
         }
       }
+      if (abort_sh) drain_tma_ring(full_bar, STAGES, g);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
@@ -189,6 +191,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         }
         mma_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
       }
+      if (abort_sh) drain_mma(&drain_bar);
     }
   } else if (warp < 2 + kConvThreads / 32) {  // ---------------- converter (warps 2..5)
     const int t = threadIdx.x - 64;
@@ -388,17 +391,19 @@ int read_and_clear_f16_error();
 int read_and_clear_int4_tc_error();
 int read_and_clear_f16_2cta_error();
 int read_and_clear_attn_f16_error();
+int read_and_clear_selftest_error();
 
 int read_and_clear_tc_error() {
-  int v = read_and_clear_attn_tc_error() | read_and_clear_f16_error() |
-          read_and_clear_int4_tc_error() | read_and_clear_f16_2cta_error() |
-          read_and_clear_attn_f16_error();
+  const int others = read_and_clear_attn_tc_error() | read_and_clear_f16_error() |
+                     read_and_clear_int4_tc_error() | read_and_clear_f16_2cta_error() |
+                     read_and_clear_attn_f16_error() | read_and_clear_selftest_error();
+  int v = 0;
   IDEV_CUDA(cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int)));
   if (v) {
     const int z = 0;
     IDEV_CUDA(cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int)));
   }
-  return v;
+  return v | others;
 }
 
 }  // namespace inferc_dev

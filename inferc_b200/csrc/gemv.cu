@@ -381,6 +381,25 @@ int sm_count() {
 
 }  // namespace
 
+// Split-K count of gemv_kn_kernel for a [K, N] weight: enough CTAs to cover
+// the SMs, at most 64 rows per CTA (so that each warp's rows fit the register
+// prefetch), bounded by the partial-sum floats and reduction counters of the
+// scratch the call uses. *kps receives the rows per split. Both the
+// workspace GEMV and the allocation-free one use this rule, so they sum in
+// the same order and give identical results.
+int64_t gemv_splits(int64_t K, int64_t N, size_t partial_floats, size_t counters,
+                    int64_t* kps) {
+  const int64_t tiles = (N + kColsPerCta - 1) / kColsPerCta;
+  const int64_t target = 2 * (int64_t)sm_count();
+  int64_t splits = std::max<int64_t>(1, target / tiles);
+  splits = std::max<int64_t>(splits, (K + 63) / 64);
+  splits = std::min<int64_t>(splits, std::max<int64_t>(1, K / kWarps));
+  while (splits > 1 && (size_t)(splits * N) > partial_floats) --splits;
+  if ((size_t)tiles > counters) splits = 1;
+  *kps = (K + splits - 1) / splits;
+  return (K + *kps - 1) / *kps;
+}
+
 void launch_gemv(const GemvArgs& g, cudaStream_t st) {
   if (g.N <= 0) return;
   IDEV_CHECK_ARG(g.K > 0 && g.K <= kMaxK, "GEMV: K must be in [1, 8192]");
@@ -392,16 +411,10 @@ void launch_gemv(const GemvArgs& g, cudaStream_t st) {
     return;
   }
   const int64_t tiles = (g.N + kColsPerCta - 1) / kColsPerCta;
-  const int64_t target = 2 * (int64_t)sm_count();
-  // Enough CTAs to cover the SMs, and at most 64 rows per CTA so that each
-  // warp's rows fit the register prefetch.
-  int64_t splits = std::max<int64_t>(1, target / tiles);
-  splits = std::max<int64_t>(splits, (g.K + 63) / 64);
-  splits = std::min<int64_t>(splits, std::max<int64_t>(1, g.K / kWarps));
-  while (splits > 1 && (size_t)(splits * g.N) > ws.partial_floats) --splits;
-  if ((size_t)tiles + 2 > ws.n_counters) splits = 1;  // last two slots: argmax
-  int64_t kps = (g.K + splits - 1) / splits;
-  splits = (g.K + kps - 1) / kps;
+  int64_t kps = 0;
+  // the last two counter slots belong to the argmax kernels
+  const int64_t splits = gemv_splits(g.K, g.N, ws.partial_floats,
+                                     ws.n_counters >= 2 ? ws.n_counters - 2 : 0, &kps);
   dim3 grid((unsigned)tiles, (unsigned)splits);
   launch_pdl(gemv_kn_kernel, grid, dim3(kThreads), 0, st, g, kps, (int)splits, ws.partials,
              ws.counters);
@@ -525,14 +538,10 @@ extern "C" int inferc_dev_gemv_noalloc(const float* x, const float* w, const flo
     unsigned int* counters = nullptr;
     noalloc_scratch(&partials, &counters);
     const int64_t tiles = (N + kColsPerCta - 1) / kColsPerCta;
-    int64_t splits = std::max<int64_t>(1, 2 * (int64_t)sm_count() / tiles);
-    splits = std::min<int64_t>(splits, std::max<int64_t>(1, K / (2 * kWarps)));
-    while (splits > 1 && (size_t)(splits * N) > kNoAllocPartials) --splits;
-    if ((size_t)tiles > kNoAllocCounters) splits = 1;
-    int64_t kps = (K + splits - 1) / splits;
-    splits = (K + kps - 1) / kps;
-    if (splits > 1)  // the reduction counters must start at zero
-      IDEV_CUDA(cudaMemsetAsync(counters, 0, (size_t)tiles * sizeof(unsigned int), st));
+    int64_t kps = 0;
+    const int64_t splits = gemv_splits(K, N, kNoAllocPartials, kNoAllocCounters, &kps);
+    // The counters start at zero (static storage) and the kernel's last CTA
+    // per column tile puts its counter back to zero, so no clearing is needed.
     dim3 grid((unsigned)tiles, (unsigned)splits);
     gemv_kn_kernel<<<grid, kThreads, 0, st>>>(g, kps, (int)splits, partials, counters);
     IDEV_LAUNCHED();

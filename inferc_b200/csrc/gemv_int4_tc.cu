@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* bplanes = lobuf + 2 * kSlab;     // digit tiles of two matrices (double buffer)
   __shared__ __align__(8) uint64_t full_bar[kStages], conv_bar[kStages], empty_bar[kStages];
   __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], b_ready[2], b_free[2];
+  __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
 
@@ -299,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&b_ready[b], 1);
       mbar_init(&b_free[b], 1);
     }
+    mbar_init(&drain_bar, 1);
     abort_sh = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -318,8 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {  // ---------------- TMA producer
       SlabPos p = slab_pos(bt, g0);
-      int fenced = -1;
-      for (int g = 0; g < g1 - g0 && !abort_sh; ++g) {
+      int fenced = -1, g = 0;
+      for (; g < g1 - g0 && !abort_sh; ++g) {
         const int s = g % kStages, r = g / kStages;
         if (p.mi != fenced) {  // the map was written to global memory by a copy
           asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
@@ -336,6 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     (p.j - bt.blk_start[p.mi]) * 128);
         if (++p.sl == bt.m[p.mi].kslabs) next_block(bt, p);
       }
+      if (abort_sh) drain_tma_ring(full_bar, kStages, g);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
@@ -383,6 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&tfull_bar[acc]);
       }
+      if (abort_sh) drain_mma(&drain_bar);
     }
   } else if (warp < 6) {  // ---------------- unpack (warps 2..5)
     const int t = threadIdx.x - 64;
@@ -426,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {  // ---------------- digit planes + epilogue (warps 6..9)
     const int e = threadIdx.x - 192;
     const int quad = warp & 3;
-    int g = 0, tl = 0, cur = -1, q = -1;
+    int g = 0, tl = 0, cur = -1, q = -1, tiles_issued = 0;
     float xs = 0.f;
     long long asum = 0;
     // Copy the digit tile of local matrix qq (batch matrix mi) into buffer
@@ -440,6 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(&b_ready[b], bytes);
         bulk_copy(bplanes + b * kBTile, bt.m[mi].planes, bytes, &b_ready[b]);
       }
+      tiles_issued = qq + 1;
       return true;
     };
     // matrix mi + 1 has slabs in this CTA's range
@@ -505,6 +510,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (row < m.n) m.y[row] = __ldg(m.scales + row) * xs * (float)(tsum - 8LL * asum);
     }
+    // On abort, the digit-tile copies this thread issued land before the CTA
+    // leaves (bounded waits on the last two tiles' barriers).
+    if (abort_sh && e == 0)
+      for (int qq = tiles_issued > 2 ? tiles_issued - 2 : 0; qq < tiles_issued; ++qq)
+        mbar_wait(&b_ready[qq & 1], (uint32_t)(qq >> 1) & 1);
   }
   tc_fence_before();
   __syncthreads();

@@ -179,6 +179,7 @@ struct InfercEncoderPlan {
   int* f16_range = nullptr;
   int* range_host = nullptr;  // pinned
   std::map<std::tuple<int64_t, int64_t, bool>, std::unique_ptr<Graph>> graphs;
+  int64_t range_fallbacks = 0;  // batches rerun on the 3xTF32 graph
 
   ~InfercEncoderPlan() {
     graphs.clear();
@@ -355,7 +356,10 @@ struct InfercEncoderPlan {
     IDEV_CUDA(cudaGraphLaunch(g.exec, st));
     IDEV_CUDA(cudaMemcpyAsync(range_host, f16_range, sizeof(int), cudaMemcpyDeviceToHost, st));
     IDEV_CUDA(cudaStreamSynchronize(st));
-    if (*range_host) IDEV_CUDA(cudaGraphLaunch(graph_for(B, S, false).exec, st));
+    if (*range_host) {
+      ++range_fallbacks;
+      IDEV_CUDA(cudaGraphLaunch(graph_for(B, S, false).exec, st));
+    }
   }
   void prepare(int64_t B, int64_t S) {
     graph_for(B, S, f16);
@@ -474,6 +478,7 @@ struct InfercDecoderPlan {
   float* mega_x = nullptr;      // [2][H] residual buffers
   float* mega_part = nullptr;   // [heads][H]
   int mega_chunks = 0;
+  unsigned long long* prof_buf = nullptr;  // -DINFERC_DECODE_PROFILE builds only
 
   ~InfercDecoderPlan() {
     step_graph.reset();
@@ -599,37 +604,29 @@ struct InfercDecoderPlan {
       a.best_v = best_v; a.best_i = best_i; a.bar_count = bar; a.bar_gen = bar + 1;
       a.err = err; a.tok = tok; a.token_log = token_log; a.log_offset = 1;
       a.pos0 = n; a.nsteps = (int)(max_tokens - 1);
-      static unsigned long long* prof = nullptr;
-      const bool want_prof = std::getenv("INFERC_DECODE_PROF") != nullptr;
-      if (want_prof && !prof) IDEV_CUDA(cudaMalloc(&prof, 2048 * sizeof(unsigned long long)));
-      a.prof = want_prof ? prof : nullptr;
+      a.prof = nullptr;
+#ifdef INFERC_DECODE_PROFILE
+      // Development build only (-DINFERC_DECODE_PROFILE): CTA 0 stamps the
+      // global timer at each grid barrier of step 1 into a per-plan buffer.
+      if (!prof_buf) prof_buf = mem.alloc<unsigned long long>(2048);
+      a.prof = prof_buf;
+#endif
       IDEV_CUDA(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned int), st));
       IDEV_CUDA(cudaEventRecord(ev0, st));
       launch_decode_mega(a, mega_grid, st);
       IDEV_CUDA(cudaEventRecord(ev1, st));
-      if (want_prof) {  // development instrumentation (INFERC_DECODE_PROF=1)
-        std::vector<unsigned long long> c(8);
-        IDEV_CUDA(cudaMemcpyAsync(c.data(), prof + 1099, 8 * 8, cudaMemcpyDeviceToHost, st));
-        IDEV_CUDA(cudaStreamSynchronize(st));
-        fprintf(stderr, "attn phase cycles: prefetch %llu qkv-load %llu pass %llu reduce %llu wait %llu proj %llu\n",
-                c[1] - c[0], c[2] - c[1], c[3] - c[2], c[4] - c[3], c[5] - c[4], c[6] - c[5]);
-        // grid barrier stamps of step 1, CTA 0: [2 tag] arrival, [2 tag + 1] release
+#ifdef INFERC_DECODE_PROFILE
+      {
         std::vector<unsigned long long> t(2 * (4 * L + 1));
-        IDEV_CUDA(cudaMemcpy(t.data(), prof, t.size() * 8, cudaMemcpyDeviceToHost));
+        IDEV_CUDA(cudaMemcpyAsync(t.data(), prof_buf, t.size() * 8, cudaMemcpyDeviceToHost, st));
+        IDEV_CUDA(cudaStreamSynchronize(st));
         const char* names[4] = {"qkv", "attn+proj", "fc", "fp"};
-        for (int q = 4; q <= 8 && q <= 4 * L; ++q) {
-          const unsigned long long work = t[2 * q] - t[2 * q - 1], wait = t[2 * q + 1] - t[2 * q];
+        for (int q = 1; q <= 4 * L; ++q)
           fprintf(stderr, "phase %-9s work %6.2f us  barrier %5.2f us\n",
-                  q == 4 * L ? "lm" : names[q % 4], work / 1e3, wait / 1e3);
-        }
-        std::vector<unsigned long long> u(32);  // optional sub-phase stamps [1200, 1232)
-        IDEV_CUDA(cudaMemcpy(u.data(), prof + 1200, 32 * 8, cudaMemcpyDeviceToHost));
-        for (int i = 1; i < 32; ++i)
-          if (u[i] && u[i - 1]) fprintf(stderr, "stamp %d-%d %.2f us\n", i - 1, i, (u[i] - u[i - 1]) / 1e3);
-        const int q = 4 * (int)L;
-        fprintf(stderr, "phase lm        work %6.2f us  barrier %5.2f us\n",
-                (t[2 * q] - t[2 * q - 1]) / 1e3, (t[2 * q + 1] - t[2 * q]) / 1e3);
+                  q == 4 * L ? "lm" : names[q % 4], (t[2 * q] - t[2 * q - 1]) / 1e3,
+                  (t[2 * q + 1] - t[2 * q]) / 1e3);
       }
+#endif
     } else if (max_tokens > 1) {
       if (!step_graph || log_base != n) {
         // The graph bakes log_base; (re)capture when the prompt length
@@ -838,6 +835,10 @@ int inferc_dev_encoder_run_host(inferc_encoder_t p, const int64_t* ids, const in
       throw Error(INFERC_ERR_RANGE, "encoder: Gather index out of range");
     }
   });
+}
+
+int64_t inferc_dev_encoder_range_fallbacks(inferc_encoder_t p) {
+  return p ? p->range_fallbacks : -1;
 }
 
 void inferc_dev_encoder_destroy(inferc_encoder_t p) { delete p; }

@@ -38,7 +38,8 @@ __device__ __forceinline__ unsigned long long gclock_ns() {
   return t;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   const uint32_t addr = smem_u32(bar);
   const unsigned long long t0 = gclock_ns();
   for (uint32_t i = 0;; ++i) {
@@ -51,8 +52,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
-    if ((i & 255) == 255 && gclock_ns() - t0 > kWaitLimitNs) return false;
+    if ((i & 255) == 255 && gclock_ns() - t0 > limit_ns) return false;
   }
+}
+
+// Abort path of a TMA producer thread: waits (bounded) on the full barriers
+// of the last min(issued, stages) ring generations it issued, so that no
+// copy into this CTA's shared memory is still in flight when the CTA leaves.
+// A generation that already completed returns at once (the ring cannot run
+// two phases ahead of its consumer).
+__device__ __forceinline__ void drain_tma_ring(uint64_t* full, int stages, int issued) {
+  for (int j = issued > stages ? issued - stages : 0; j < issued; ++j)
+    mbar_wait(&full[j % stages], (uint32_t)(j / stages) & 1);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -115,6 +126,14 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
       : "memory");
+}
+
+// Abort path of an MMA-issuing thread: one more commit to a private barrier
+// (initialised with count 1) and a bounded wait on it, so that every MMA this
+// thread issued has finished before TMEM is freed or the CTA leaves.
+__device__ __forceinline__ void drain_mma(uint64_t* bar) {
+  mma_commit(bar);
+  mbar_wait(bar, 0);
 }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {

@@ -34,6 +34,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "inferc_dev_memcpy_h2d": ([_p, _p, _sz, _p], _i),
     "inferc_dev_memcpy_d2h": ([_p, _p, _sz, _p], _i),
     "inferc_dev_stream_synchronize": ([_p], _i),
+    "inferc_dev_selftest_wait_timeout": ([_i, _i64, _p], _i),
     "inferc_dev_layernorm": ([_p, _p, _p, _p, _i64, _i64, _f, _p], _i),
     "inferc_dev_fused_matmul_add_gelu": ([_p, _p, _p, _p, _i64, _i64, _i64, _p], _i),
     "inferc_dev_fused_qkv": ([_p] * 10 + [_i64] * 3 + [_p], _i),
@@ -71,6 +72,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
                                    ctypes.POINTER(_p)], _i),
     "inferc_dev_encoder_run": ([_p, _p, _p, _i64, _i64, _p, _p], _i),
     "inferc_dev_encoder_run_host": ([_p, _p, _p, _i64, _i64, _p], _i),
+    "inferc_dev_encoder_range_fallbacks": ([_p], _i64),
     "inferc_dev_encoder_destroy": ([_p], None),
     "inferc_dev_decoder_create": ([ctypes.POINTER(structs.Gpt2Weights), _i64,
                                    ctypes.POINTER(_p)], _i),

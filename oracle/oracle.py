@@ -4,8 +4,8 @@ the product package.
 
   port() -> oracle/_build/liborc_port.so  (C restatement, inferc_oracle.c)
   ref()  -> oracle/_ref/libinferc_ref.so  (the reference's own kernel sources,
-            built by oracle/Makefile; present only where /root/reference was
-            available at build time, None otherwise)
+            built by oracle/Makefile; present only where the reference checkout
+            (INFERC_REF_ROOT, or the Makefile's REF) was available at build time, None otherwise)
 """
 from __future__ import annotations
 
@@ -25,11 +25,26 @@ _p = ctypes.c_void_p
 _i = ctypes.c_int
 
 
+# Root of the reference checkout whose kernel sources `make ref` compiles:
+# INFERC_REF_ROOT when set, else the Makefile's default REF.
+def _ref_root() -> str:
+    env = os.environ.get("INFERC_REF_ROOT")
+    if env:
+        return env
+    with open(os.path.join(HERE, "Makefile")) as f:
+        for line in f:
+            if line.startswith("REF ?="):
+                return line.split("=", 1)[1].strip()
+    return ""
+
+
 def build(with_ref: bool = True) -> None:
     targets = ["port"]
-    if with_ref and os.path.isdir("/root/reference/src"):
+    root = _ref_root()
+    extra = [f"REF={root}"] if root else []
+    if with_ref and root and os.path.isdir(os.path.join(root, "src")):
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+    subprocess.run(["make", "-s", "-C", HERE] + extra + targets, check=True)
 
 
 def ptr(a: np.ndarray | None):

@@ -156,6 +156,20 @@ def test_port_encoder_matches_reference_golden(port):
     np.testing.assert_allclose(logits, g["small_logits"], atol=1e-5)
 
 
+def test_port_matches_c4_bench_golden(port):
+    """The bench workload's fixture (reference logits of all 256 sequences):
+    the port agrees on a spread of sequences, so the fixture and the port pin
+    each other."""
+    g = np.load(os.path.join(GOLD, "encoder_c4_bench.npz"))
+    assert g["logits"].shape == (256, 2)
+    cfg = synth.EncoderConfig()
+    ids, mask = synth.encoder_inputs(256, 128, seed=int(g["seed"]), variable_lengths=True)
+    rows = [0, 97, 255]
+    got = port.encoder_forward(structs.encoder_struct(cfg, synth.encoder_weights(cfg, seed=0)),
+                               ids[rows], mask[rows], 2)
+    np.testing.assert_allclose(got, g["logits"][rows], atol=1e-5)
+
+
 def test_port_decode_matches_reference_golden(port):
     g = np.load(os.path.join(GOLD, "decode.npz"))
     cfg = synth.Gpt2Config(**make_golden.SMALL_GPT2)
