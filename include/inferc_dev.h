@@ -82,6 +82,26 @@ int inferc_dev_layernorm(const float* x, const float* gamma, const float* beta,
                          float* y, int64_t rows, int64_t feat, float eps,
                          void* stream);
 
+/* Op-level GEMMs and their weights. inferc_dev_fused_matmul_add_gelu,
+ * _fused_qkv, _gemm (M > 1) and _matmul treat B / W as a long-lived
+ * initializer, as the reference's executor does (it copies each initializer
+ * once per Executor, src/runtime/executor.cc:89-96): the first call that
+ * sees a weight (device pointer, K, N, layout) converts it once into
+ * split-fp16 planes kept in a per-device cache, and every later call runs
+ * the split-fp16 tensor-core GEMM on those planes (fp32-level accuracy; an
+ * activation fp16 cannot carry makes the same call recompute its result on
+ * the CUDA cores, on the device, with no host round trip). That first call
+ * synchronises its stream and cannot be stream-captured; later calls can.
+ * The cache assumes the weight's values stay fixed: before rewriting or
+ * freeing a cached weight, call inferc_dev_weight_cache_evict(w) (or _clear)
+ * with its device current. Calls on different streams may run concurrently;
+ * each stream has its own scratch flag. INFERC_OP_GEMM=tf32x3 selects the
+ * 3xTF32 kernel with a per-call weight split instead. */
+int inferc_dev_weight_cache_evict(const float* w);
+int inferc_dev_weight_cache_clear(void);
+/* Device bytes held by the cache (all devices). */
+int64_t inferc_dev_weight_cache_bytes(void);
+
 /* FusedMatMulAddGELU (src/kernels/fused_matmul_add_gelu.cc:13-80):
  * Y[M,N] = erfGELU(X[M,K] W[K,N] + b[N]). */
 int inferc_dev_fused_matmul_add_gelu(const float* x, const float* w,
@@ -235,7 +255,9 @@ int inferc_dev_gemv(const float* x, const float* w, const float* b,
                     int act, void* stream);
 
 /* Allocation-free variant of inferc_dev_gemv, with the same arguments and
- * result. No counterpart in the reference: it exists for callers that may not
+ * the same split-K rule (so the same result, bit for bit, whenever the
+ * built-in scratch does not cap the split count; otherwise equal within fp32
+ * rounding). No counterpart in the reference: it exists for callers that may not
  * allocate device memory (a host framework that owns the device heap, an
  * allocator-less runtime, a real-time loop), whereas inferc_dev_gemv
  * allocates its split-K scratch on first use. Its scratch is a fixed 1 MiB

@@ -5,6 +5,9 @@
 #include <cstring>
 #include <string>
 
+#include <mutex>
+#include <unordered_map>
+
 #include "kernels.cuh"
 
 namespace inferc_dev {
@@ -29,10 +32,25 @@ void launch_gemm_tc(const float* A, int64_t lda, const float* Bb, const float* B
 void launch_gemm(const float* A, int64_t lda, bool ta, const float* B, int64_t ldb, bool tb,
                  float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
                  cudaStream_t st);
+// The op-level form: split-fp16 on cached weight planes (gemm_dispatch.cu).
+void launch_gemm_op(const float* A, int64_t lda, bool ta, const float* B, int64_t ldb, bool tb,
+                    float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
+                    cudaStream_t st);
 
 }  // namespace inferc_dev
 
 using namespace inferc_dev;
+
+namespace inferc_dev {
+void weight_cache_evict_range(const void* base, size_t bytes);
+}  // namespace inferc_dev
+
+namespace {
+// Sizes of the buffers inferc_dev_alloc handed out, so that inferc_dev_free
+// can drop cached weight planes that lived in the freed range.
+std::mutex g_alloc_mu;
+std::unordered_map<void*, size_t> g_alloc_sizes;
+}  // namespace
 
 extern "C" {
 
@@ -51,12 +69,26 @@ int inferc_dev_alloc(void** ptr, size_t bytes) {
       throw Error(INFERC_ERR_OOM, "alloc: out of device memory (" + std::to_string(bytes) + " B)");
     }
     IDEV_CUDA(e);
+    std::lock_guard<std::mutex> lock(g_alloc_mu);
+    g_alloc_sizes[*ptr] = bytes;
   });
 }
 
 int inferc_dev_free(void* ptr) {
   return guard([&] {
-    if (ptr) IDEV_CUDA(cudaFree(ptr));
+    if (!ptr) return;
+    size_t bytes = 0;
+    {
+      std::lock_guard<std::mutex> lock(g_alloc_mu);
+      auto it = g_alloc_sizes.find(ptr);
+      if (it != g_alloc_sizes.end()) {
+        bytes = it->second;
+        g_alloc_sizes.erase(it);
+      }
+    }
+    // prepared planes of op-level GEMM weights that lived in this buffer
+    if (bytes) weight_cache_evict_range(ptr, bytes);
+    IDEV_CUDA(cudaFree(ptr));
   });
 }
 
@@ -101,7 +133,7 @@ int inferc_dev_fused_matmul_add_gelu(const float* x, const float* w, const float
     ep.bias = b;
     ep.bias_mode = 1;
     ep.act = ACT_GELU_ERF;
-    launch_gemm(x, K, false, w, N, false, y, N, M, N, K, ep, as_stream(stream));
+    launch_gemm_op(x, K, false, w, N, false, y, N, M, N, K, ep, as_stream(stream));
   });
 }
 
@@ -118,7 +150,7 @@ int inferc_dev_fused_qkv(const float* x, const float* wq, const float* bq, const
       Epilogue ep;
       ep.bias = bs[i];
       ep.bias_mode = 1;
-      launch_gemm(x, K, false, ws[i], N, false, os[i], N, M, N, K, ep, as_stream(stream));
+      launch_gemm_op(x, K, false, ws[i], N, false, os[i], N, M, N, K, ep, as_stream(stream));
     }
   });
 }
@@ -186,7 +218,7 @@ int inferc_dev_gemm(const float* a, const float* b, const float* c, int64_t c_le
       ep.bias_mode = c_len == M * N ? 3 : c_len == N ? 1 : 2;
       ep.ldbias = N;
     }
-    launch_gemm(a, trans_a ? M : K, trans_a != 0, b, trans_b ? K : N, trans_b != 0, y, N, M, N,
+    launch_gemm_op(a, trans_a ? M : K, trans_a != 0, b, trans_b ? K : N, trans_b != 0, y, N, M, N,
                 K, ep, st);
   });
 }
@@ -196,7 +228,7 @@ int inferc_dev_matmul(const float* a, const float* b, float* y, int64_t M, int64
   return guard([&] {
     IDEV_CHECK_ARG(M >= 0 && K > 0 && N >= 0, "MatMul: bad shape");
     Epilogue ep;
-    launch_gemm(a, K, false, b, N, false, y, N, M, N, K, ep, as_stream(stream));
+    launch_gemm_op(a, K, false, b, N, false, y, N, M, N, K, ep, as_stream(stream));
   });
 }
 

@@ -138,6 +138,10 @@ struct Epilogue {
   const float* resid = nullptr;
   int64_t ldr = 0;
   int act = ACT_NONE;
+  // CUDA-core GEMM only: when set, the kernel runs only if *run_if != 0 (a
+  // device flag raised by an earlier kernel), else it returns at once. The
+  // op-level split-fp16 GEMM uses it to queue its own fallback.
+  const int* run_if = nullptr;
 };
 
 __device__ __forceinline__ float epilogue_apply(const Epilogue& e, float acc, int64_t row,

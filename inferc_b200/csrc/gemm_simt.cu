@@ -25,6 +25,7 @@ __global__ void __launch_bounds__((BM / 8) * (BN / 8))
   __shared__ __align__(16) float As[2][BK][BM];
   __shared__ __align__(16) float Bs[2][BK][BN];
 
+  if (ep.run_if && *reinterpret_cast<const volatile int*>(ep.run_if) == 0) return;
   const int tid = threadIdx.x;
   const int tx = tid % TX, ty = tid / TX;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;

@@ -35,6 +35,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "inferc_dev_memcpy_d2h": ([_p, _p, _sz, _p], _i),
     "inferc_dev_stream_synchronize": ([_p], _i),
     "inferc_dev_selftest_wait_timeout": ([_i, _i64, _p], _i),
+    "inferc_dev_weight_cache_evict": ([_p], _i),
+    "inferc_dev_weight_cache_clear": ([], _i),
+    "inferc_dev_weight_cache_bytes": ([], _i64),
     "inferc_dev_layernorm": ([_p, _p, _p, _p, _i64, _i64, _f, _p], _i),
     "inferc_dev_fused_matmul_add_gelu": ([_p, _p, _p, _p, _i64, _i64, _i64, _p], _i),
     "inferc_dev_fused_qkv": ([_p] * 10 + [_i64] * 3 + [_p], _i),

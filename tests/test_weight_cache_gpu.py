@@ -1,0 +1,162 @@
+"""The op-level GEMM entry points (FusedMatMulAddGELU, FusedQKV, Gemm,
+MatMul) on cached split-fp16 weight planes: results match the reference
+restatement on the first call (which prepares the planes) and on later
+calls; activations fp16 cannot carry and weights replaced behind the cache's
+back still give exact fp32-level results (the on-device CUDA-core fallback);
+eviction (explicit, and through inferc_dev_free) releases the planes; calls on
+two streams and a captured CUDA graph work."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from inferc_b200 import lib, ops
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def T(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _tol(ref):
+    return 2e-5 + 3e-5 * np.abs(ref).max()
+
+
+def _case(M, K, N, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = (rng.standard_normal((K, N), dtype=np.float32) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(N, dtype=np.float32) * 0.1).astype(np.float32)
+    return x, w, b
+
+
+def test_first_and_later_calls_match():
+    port = oracle.port()
+    x, w, b = _case(256, 768, 3072, 1)
+    xd, wd, bd = T(x), T(w), T(b)
+    ref = port.fused_matmul_add_gelu(x, w, b)
+    before = lib.load().inferc_dev_weight_cache_bytes()
+    for _ in range(3):
+        y = ops.FusedMatMulAddGELU(xd, wd, bd)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(y.cpu().numpy(), ref, atol=_tol(ref), rtol=1e-5)
+    assert lib.load().inferc_dev_weight_cache_bytes() >= before + 2 * 2 * 768 * 3072
+    lib.check(lib.load().inferc_dev_weight_cache_evict(wd.data_ptr()))
+
+
+def test_activation_beyond_fp16_range_recomputed_on_device():
+    port = oracle.port()
+    x, w, b = _case(130, 768, 768, 2)
+    x[7, 11] = 1.0e6  # no fp16 hi exists for this activation
+    x[100, 3] = -7.0e5
+    xd, wd, bd = T(x), T(w), T(b)
+    y = ops.FusedMatMulAddGELU(xd, wd, bd)
+    torch.cuda.synchronize()
+    ref = port.fused_matmul_add_gelu(x, w, b)
+    np.testing.assert_allclose(y.cpu().numpy(), ref, atol=_tol(ref), rtol=1e-5)
+    # nothing is left for the stream-synchronize range report: the op handled it
+    assert lib.load().inferc_dev_stream_synchronize(None) == 0
+    lib.check(lib.load().inferc_dev_weight_cache_evict(wd.data_ptr()))
+
+
+def test_weight_replaced_at_the_same_address():
+    """A new weight written over a cached one (what a recycled allocation
+    looks like): the sampled check sees it, the call falls back on the device,
+    and the next call prepares the new planes."""
+    port = oracle.port()
+    x, w1, b = _case(200, 768, 768, 3)
+    _, w2, _ = _case(200, 768, 768, 4)
+    xd, wd, bd = T(x), T(w1), T(b)
+    y = ops.FusedMatMulAddGELU(xd, wd, bd)
+    torch.cuda.synchronize()
+    r1 = port.fused_matmul_add_gelu(x, w1, b)
+    np.testing.assert_allclose(y.cpu().numpy(), r1, atol=_tol(r1), rtol=1e-5)
+    wd.copy_(T(w2))
+    r2 = port.fused_matmul_add_gelu(x, w2, b)
+    for _ in range(2):  # fallback call, then the re-prepared fast path
+        y = ops.FusedMatMulAddGELU(xd, wd, bd)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(y.cpu().numpy(), r2, atol=_tol(r2), rtol=1e-5)
+    lib.check(lib.load().inferc_dev_weight_cache_evict(wd.data_ptr()))
+
+
+def test_free_through_the_library_evicts():
+    L = lib.load()
+    x, w, b = _case(64, 512, 1024, 5)
+    p = ctypes.c_void_p()
+    lib.check(L.inferc_dev_alloc(ctypes.byref(p), w.nbytes))
+    lib.check(L.inferc_dev_memcpy_h2d(p, w.ctypes.data, w.nbytes, None))
+    xd, bd = T(x), T(b)
+    y = torch.empty(64, 1024, device="cuda")
+    lib.check(L.inferc_dev_fused_matmul_add_gelu(xd.data_ptr(), p.value, bd.data_ptr(),
+                                                 y.data_ptr(), 64, 512, 1024, None))
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    held = L.inferc_dev_weight_cache_bytes()
+    lib.check(L.inferc_dev_free(p))
+    assert L.inferc_dev_weight_cache_bytes() == held - 2 * 2 * 1024 * 512
+    ref = oracle.port().fused_matmul_add_gelu(x, w, b)
+    np.testing.assert_allclose(y.cpu().numpy(), ref, atol=_tol(ref), rtol=1e-5)
+
+
+def test_two_streams_share_a_cached_weight():
+    port = oracle.port()
+    _, w, b = _case(1, 768, 2304, 6)
+    wd, bd = T(w), T(b)
+    xs = [np.random.default_rng(10 + i).standard_normal((512, 768), dtype=np.float32)
+          for i in range(2)]
+    ops.FusedMatMulAddGELU(T(xs[0][:8]), wd, bd)  # prepare
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream() for _ in range(2)]
+    outs = []
+    for s, x in zip(streams, xs):
+        with torch.cuda.stream(s):
+            xd = T(x)
+            outs.append(ops.FusedMatMulAddGELU(xd, wd, bd))
+    torch.cuda.synchronize()
+    for x, y in zip(xs, outs):
+        ref = port.fused_matmul_add_gelu(x, w, b)
+        np.testing.assert_allclose(y.cpu().numpy(), ref, atol=_tol(ref), rtol=1e-5)
+    lib.check(lib.load().inferc_dev_weight_cache_evict(wd.data_ptr()))
+
+
+def test_capture_after_the_first_call():
+    port = oracle.port()
+    x, w, b = _case(384, 768, 768, 7)
+    xd, wd, bd = T(x), T(w), T(b)
+    y = torch.empty(384, 768, device="cuda")
+    L = lib.load()
+
+    def call(stream):
+        lib.check(L.inferc_dev_fused_matmul_add_gelu(xd.data_ptr(), wd.data_ptr(), bd.data_ptr(),
+                                                     y.data_ptr(), 384, 768, 768, stream))
+    call(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        call(torch.cuda.current_stream().cuda_stream)
+    y.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    ref = port.fused_matmul_add_gelu(x, w, b)
+    np.testing.assert_allclose(y.cpu().numpy(), ref, atol=_tol(ref), rtol=1e-5)
+    lib.check(L.inferc_dev_weight_cache_evict(wd.data_ptr()))
+
+
+def test_first_call_inside_a_capture_is_rejected():
+    x, w, b = _case(64, 256, 256, 8)
+    xd, wd, bd = T(x), T(w), T(b)
+    y = torch.empty(64, 256, device="cuda")
+    L = lib.load()
+    g = torch.cuda.CUDAGraph()
+    rc = None
+    try:
+        with torch.cuda.graph(g):
+            rc = L.inferc_dev_fused_matmul_add_gelu(
+                xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), y.data_ptr(), 64, 256, 256,
+                torch.cuda.current_stream().cuda_stream)
+    except RuntimeError:
+        pass
+    assert rc == 1 and b"captured" in L.inferc_dev_last_error_string()

@@ -26,7 +26,7 @@ def _call(name, x, w, b, r, y, act):
 
 
 @pytest.mark.parametrize("K,N,act", [(768, 2304, 0), (3072, 768, 0), (768, 3072, 2),
-                                     (768, 50, 3), (8192, 1024, 0), (8192, 4096, 1)])
+                                     (768, 50, 3), (8192, 1024, 0), (8192, 2048, 3), (8192, 4096, 1)])
 def test_noalloc_matches_gemv_twice(K, N, act):
     rng = np.random.default_rng(K * 7 + N)
     x = torch.from_numpy(rng.standard_normal(K, dtype=np.float32)).cuda()
@@ -40,8 +40,15 @@ def test_noalloc_matches_gemv_twice(K, N, act):
         _call("inferc_dev_gemv_noalloc", x, w, b, r, got, act)
         torch.cuda.synchronize()
         # Both entry points pick the split-K count by one rule, so they sum in
-        # the same order: the results are identical, not only close.
-        np.testing.assert_array_equal(got.cpu().numpy(), want.cpu().numpy())
+        # the same order and agree bit for bit, unless the built-in 1 MiB
+        # scratch caps the split count (splits x N partial sums must fit):
+        # then the order differs and they agree within fp32 rounding.
+        splits = max(-(-K // 64), 1)
+        if splits * N <= (1 << 18):
+            np.testing.assert_array_equal(got.cpu().numpy(), want.cpu().numpy())
+        else:
+            np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), atol=1e-5,
+                                       rtol=1e-5)
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
