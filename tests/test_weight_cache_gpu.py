@@ -38,6 +38,9 @@ def test_first_and_later_calls_match():
     x, w, b = _case(256, 768, 3072, 1)
     xd, wd, bd = T(x), T(w), T(b)
     ref = port.fused_matmul_add_gelu(x, w, b)
+    # an earlier test's weight may have lived at this address (torch reuses
+    # freed blocks): start from no entry for it
+    lib.check(lib.load().inferc_dev_weight_cache_evict(wd.data_ptr()))
     before = lib.load().inferc_dev_weight_cache_bytes()
     for _ in range(3):
         y = ops.FusedMatMulAddGELU(xd, wd, bd)
