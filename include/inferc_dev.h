@@ -315,6 +315,45 @@ int inferc_dev_decode_attention(const float* q, const float* k_cache,
                                 int64_t heads, int64_t head_dim,
                                 int64_t max_len, int64_t L, void* stream);
 
+/* ------------------------------------------------------- graph executor */
+
+/* A device executor for an optimized inferc plan: the ONNX model `inferc
+ * optimize` writes (src/cli/main.cpp:200-227), run node by node on the GPU in
+ * place of Executor::Run (src/runtime/executor.cc:98-366) with the same op
+ * names (the ONNX ops the reference executor takes and the inferc-domain
+ * fused ops), attributes, defaults and error messages. Initializers are
+ * uploaded once at load (executor.cc:89-96); activations come from the
+ * device's stream-ordered pool and are released after their last reader.
+ * Shape metadata (Shape / Constant / small int64 arithmetic) is evaluated on
+ * the host when all of an op's inputs are known there; every tensor that
+ * depends on an input's values is computed on the device. An op the reference
+ * executor does not take makes load fail with its "unsupported op" message. */
+typedef struct InfercGraph* inferc_graph_t;
+
+/* Parses `model` (serialized ONNX ModelProto, HOST bytes) without touching a
+ * device and writes a JSON summary (node count, op histogram, opsets, inputs,
+ * outputs) into buf (NUL-terminated; *needed receives the size it takes;
+ * buf may be NULL to query it). */
+int inferc_dev_graph_describe(const void* model, size_t len, char* buf, size_t cap,
+                              size_t* needed);
+/* Parses the model and uploads its initializers to the current device. */
+int inferc_dev_graph_load(const void* model, size_t len, inferc_graph_t* out);
+/* Binds graph input `name`: dtype is an ONNX TensorProto code (1 float, 6
+ * int32, 7 int64, 9 bool, 2 uint8), shape a HOST array of rank dims; data is
+ * copied (from HOST memory, or DEVICE memory when data_on_device) on stream
+ * into a buffer the graph owns, so it may be reused after the call. */
+int inferc_dev_graph_set_input(inferc_graph_t g, const char* name, int dtype,
+                               const int64_t* shape, int rank, const void* data,
+                               int data_on_device, void* stream);
+/* Runs every node on stream and waits for it (the reference's Run is
+ * synchronous); a Gather index out of range returns INFERC_ERR_RANGE. */
+int inferc_dev_graph_run(inferc_graph_t g, void* stream);
+/* Graph output `name` of the last run: dtype, shape (HOST array of at least 8),
+ * rank and its DEVICE address, valid until the next run or destroy. */
+int inferc_dev_graph_output(inferc_graph_t g, const char* name, int* dtype, int64_t* shape,
+                            int* rank, const void** data);
+void inferc_dev_graph_destroy(inferc_graph_t g);
+
 /* ------------------------------------------------------------------ plans */
 
 /* A prepared DistilBERT-architecture encoder (the `inferc optimize` plan run

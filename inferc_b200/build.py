@@ -50,7 +50,7 @@ def _compile(src: str, force: bool, verbose_ptxas: bool) -> str:
 
 def build(force: bool = False, verbose_ptxas: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
-    sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cc")))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, force, verbose_ptxas), sources))
     if force or _stale(LIB, objs):

@@ -71,6 +71,13 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "inferc_dev_argmax": ([_p, _i64, _p, _p], _i),
     "inferc_dev_kv_append": ([_p, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _p], _i),
     "inferc_dev_decode_attention": ([_p, _p, _p, _p, _i64, _i64, _i64, _i64, _p], _i),
+    "inferc_dev_graph_describe": ([_p, _sz, _p, _sz, ctypes.POINTER(_sz)], _i),
+    "inferc_dev_graph_load": ([_p, _sz, ctypes.POINTER(_p)], _i),
+    "inferc_dev_graph_set_input": ([_p, ctypes.c_char_p, _i, _p, _i, _p, _i, _p], _i),
+    "inferc_dev_graph_run": ([_p, _p], _i),
+    "inferc_dev_graph_output": ([_p, ctypes.c_char_p, ctypes.POINTER(_i), _p, ctypes.POINTER(_i),
+                                 ctypes.POINTER(_p)], _i),
+    "inferc_dev_graph_destroy": ([_p], None),
     "inferc_dev_encoder_create": ([ctypes.POINTER(structs.EncoderWeights), _i64, _i64,
                                    ctypes.POINTER(_p)], _i),
     "inferc_dev_encoder_run": ([_p, _p, _p, _i64, _i64, _p, _p], _i),
