@@ -261,7 +261,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["decode", "int4", "sweep", "c0"],
+    ap.add_argument("--only", choices=["decode", "int4", "sweep", "c0", "executor"],
                     help="run one sub-benchmark alone and print its object (small cases for ncu)")
     ap.add_argument("--roofline-only", action="store_true",
                     help="time only the dominant kernel (FFN1 split-fp16 GEMM, B=256 S=128) "
@@ -281,7 +281,7 @@ def main():
     dev = torch.device("cuda", local)
     if args.only:
         fn = {"decode": decode_bench, "int4": int4_bench, "sweep": sweep_bench,
-              "c0": encoder_c0_bench}[args.only]
+              "c0": encoder_c0_bench, "executor": executor_bench}[args.only]
         print(json.dumps(fn(dev)), flush=True)
         return
     if args.roofline_only:
@@ -420,6 +420,7 @@ def main():
         result["decode"] = decode_bench(dev)
         result["int4_gemv"] = int4_bench(dev)
         result["qkv_attention_sweep"] = sweep_bench(dev)
+        result["plan_executor"] = executor_bench(dev, plan_seq_s=e2e_value)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, kind, cores, sample = cpu_reference_encoder(cfg, ids_all, mask_all, budget_s=15.0)
         result["cpu_baseline"] = {"value": v, "unit": "seq/s", "cores": cores, "kind": kind,
@@ -659,6 +660,77 @@ def _int4_cpu(mats):
     ms = (time.perf_counter() - t0) * 1e3
     return {"value": ms, "unit": "ms", "cores": 1, "kind": kind,
             "sample": "the full 49-matrix set, once (scalar, double accumulation)"}
+
+
+def executor_bench(dev, plan_seq_s=None):
+    """The drop-in path: the optimized DistilBERT plan (ONNX bytes, the form
+    `inferc optimize` writes) run node by node by the device executor
+    (inferc_dev_graph_*), the way the reference's `inferc run` walks it
+    (Executor::Run). Per step: host ids / mask set as graph inputs, every node
+    run, logits copied back (e2e through the public C ABI), on the batch-256
+    bench workload and on config 0; plus GPT-2-small greedy decode through the
+    prefill + with-past plans (`inferc decode`'s loop). Parity against the
+    same reference fixtures as the plans."""
+    import torch
+
+    from inferc_b200 import executor, plan_synth, synth
+    cfg = synth.EncoderConfig()
+    w = synth.encoder_weights(cfg, seed=0)
+    g = executor.Graph(plan_synth.distilbert_plan(cfg, w))
+    gold = np.load(os.path.join(ROOT, "tests", "golden", "encoder_c4_bench.npz"))
+    ids, mask = synth.encoder_inputs(GLOBAL_BATCH, SEQ, seed=int(gold["seed"]),
+                                     variable_lengths=True)
+
+    def step():
+        return g.run_host({"input_ids": ids, "attention_mask": mask}, ["logits"])["logits"]
+    for _ in range(3):
+        got = step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    reps = 10
+    for _ in range(reps):
+        got = step()
+    ms = (time.perf_counter() - t0) / reps * 1e3
+    e0 = np.load(os.path.join(ROOT, "tests", "golden", "encoder.npz"))
+    for _ in range(3):
+        c0 = g.run_host({"input_ids": e0["c0_ids"], "attention_mask": e0["c0_mask"]},
+                        ["logits"])["logits"]
+    t0 = time.perf_counter()
+    for _ in range(20):
+        c0 = g.run_host({"input_ids": e0["c0_ids"], "attention_mask": e0["c0_mask"]},
+                        ["logits"])["logits"]
+    c0_ms = (time.perf_counter() - t0) / 20 * 1e3
+    g.close()
+    del g
+    gcfg = synth.Gpt2Config()
+    a, b = plan_synth.gpt2_plans(gcfg, synth.gpt2_weights(gcfg, seed=0))
+    pre, stp = executor.Graph(a), executor.Graph(b)
+    dgold = np.load(os.path.join(ROOT, "tests", "golden", "decode.npz"))
+    toks, dec_ms = executor.greedy_decode(pre, stp, gcfg.layers, dgold["c1_prompt"], 128)
+    pre.close()
+    stp.close()
+    seq_s = GLOBAL_BATCH / (ms / 1e3)
+    return {
+        "metric": "encoder seqs/s through the device executor on the optimized ONNX plan",
+        "value": seq_s, "unit": "seq/s",
+        "config": {"workload": "BASELINE config 4 (batch 256 x seq 128, variable lengths), "
+                               "plan = synthetic optimized DistilBERT ONNX (fused ops as "
+                               "`inferc optimize` emits them)"},
+        "e2e": {"value": seq_s, "unit": "seq/s",
+                "h2d_bytes_per_step": int(ids.nbytes + mask.nbytes),
+                "d2h_bytes_per_step": int(GLOBAL_BATCH * cfg.n_classes * 4),
+                "path": "inferc_dev_graph_set_input (host) + inferc_dev_graph_run + output "
+                        "copy, every step"},
+        "vs_prepared_plan": (plan_seq_s / seq_s) if plan_seq_s else None,
+        "parity": {"encoder_logits_max_abs_diff": float(np.abs(got - gold["logits"]).max()),
+                   "c0_logits_max_abs_diff": float(np.abs(c0 - e0["c0_logits"]).max()),
+                   "tolerance": 1e-4},
+        "c0_ms": c0_ms,
+        "decode": {"ms_per_token": dec_ms,
+                   "tokens_match_reference": bool((toks == dgold["c1_tokens"]).all()),
+                   "path": "prefill + with-past plans, present.* fed back as "
+                           "past_key_values.* each step (Concat-growing cache, as the "
+                           "reference's graphs do)"}}
 
 
 def sweep_bench(dev):
