@@ -388,6 +388,23 @@ int inferc_dev_decoder_create(const InfercGpt2Weights* w, int64_t max_len,
 int inferc_dev_decode(inferc_decoder_t plan, const int64_t* prompt,
                       int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
                       double* step_ms_out);
+/* Weight-only int4 variant of inferc_dev_decoder_create (no counterpart in
+ * the reference's runtime, which benchmarks its int4 GEMV only,
+ * bench/amx/int4_gemv_amx.cc:258-271): the four matrices of every layer and
+ * the tied LM head are quantised on the device, per output row, to the int4
+ * per-row-scale layout of inferc_dev_gemv_int4_rowscale (scale = max|w|/7,
+ * q = clamp(rint(w/scale), -8, 7)); inferc_dev_decode then runs every
+ * position (prompt included) as one single-token step of int4 row GEMVs with
+ * fused LayerNorm prologues, bias / GELU / residual epilogues and the greedy
+ * argmax, replayed as a CUDA graph. The result is greedy decode of the model
+ * whose weights are the dequantised scale * (q - 8). */
+int inferc_dev_decoder_create_int4(const InfercGpt2Weights* w, int64_t max_len,
+                                   inferc_decoder_t* out);
+/* The packer itself: w [K, N] fp32 (row stride ldw; trans: w is [N, K]) ->
+ * out [N, K/2] int4 bytes (even k in the low nibble, stored q + 8) and
+ * scales [N], as above. K even. */
+int inferc_dev_int4_pack_rowscale(const float* w, int64_t K, int64_t N, int64_t ldw, int trans,
+                                  uint8_t* out, float* scales, void* stream);
 /* Device logits [vocab] of the most recent step (valid after decode). */
 const float* inferc_dev_decoder_logits(inferc_decoder_t plan);
 void inferc_dev_decoder_destroy(inferc_decoder_t plan);

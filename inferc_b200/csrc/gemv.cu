@@ -379,6 +379,128 @@ int sm_count() {
   return n;
 }
 
+
+// ------------------------------------------------------------ int4 rows
+// y[r] = act(s_r * sum_k (q[r,k] - 8) x_k + b[r] + resid[r]) over int4 weights
+// in the layout of bench/amx/int4_gemv_amx.cc:258-271 (row r = K/2 bytes,
+// even k in the low nibble, stored nibble = q + 8), with the optional
+// LayerNorm prologue and fused greedy argmax of row_gemv. One warp per row,
+// four rows in flight per warp; lane l reads 4-byte words l, l+32, ... of the
+// row (8 weights each) and the matching 8 staged x values (two float4 reads,
+// 32 bytes apart across lanes: at most 2-way bank conflicts). The weight is
+// formed as (q - 8) in fp32 exactly; the row sum is scaled once by s_r.
+__global__ void __launch_bounds__(kThreads)
+    int4_row_gemv_kernel(Int4RowArgs a, float* best_v, int64_t* best_i, unsigned int* counter) {
+  __shared__ __align__(16) float xs[kMaxK];
+  __shared__ float red[kWarps];
+  __shared__ float sv[kWarps];
+  __shared__ int64_t si[kWarps];
+  __shared__ bool last;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  pdl_launch_dependents();
+  pdl_wait();
+  stage_x(a.x, a.ln_gamma, a.ln_beta, a.ln_eps, a.K, 0, a.K, xs, red);
+  const int64_t words = a.K / 8;
+  const float4* x4 = reinterpret_cast<const float4*>(xs);
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  for (int64_t r0 = (int64_t)blockIdx.x * kWarps + wid; r0 < a.N; r0 += 4 * stride) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t wi = lane; wi < words; wi += 32) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t r = r0 + u * stride;
+        wv[u] = r < a.N ? __ldg(reinterpret_cast<const uint32_t*>(a.w + r * (a.K / 2)) + wi) : 0x88888888u;
+      }
+      const float4 xa = x4[2 * wi], xb = x4[2 * wi + 1];
+      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          acc[u] = fmaf((float)((int)((wv[u] >> (4 * e)) & 15u) - 8), xv[e], acc[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t r = r0 + u * stride;
+      const float dot = warp_sum(acc[u]);
+      if (r < a.N) {
+        float v = __ldg(a.scales + r) * dot;
+        if (a.bias) v += a.bias[r];
+        if (a.resid) v += a.resid[r];
+        v = apply_act(v, a.act);
+        if (lane == 0) a.y[r] = v;
+        if (better(v, r, bv, bi)) { bv = v; bi = r; }
+      }
+    }
+  }
+  if (a.argmax_out == nullptr) return;
+  if (lane == 0) { sv[wid] = bv; si[wid] = bi; }
+  __syncthreads();
+  if (tid == 0) {
+    float v = sv[0];
+    int64_t i = si[0];
+    for (int w = 1; w < kWarps; ++w)
+      if (better(sv[w], si[w], v, i)) { v = sv[w]; i = si[w]; }
+    best_v[blockIdx.x] = v;
+    best_i[blockIdx.x] = i;
+    __threadfence();
+    last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (wid == 0) {
+    float v = -INFINITY;
+    int64_t i = INT64_MAX;
+    for (int64_t b = lane; b < gridDim.x; b += 32) {
+      const float ov = __ldcg(&best_v[b]);
+      const int64_t oi = __ldcg(&best_i[b]);
+      if (better(ov, oi, v, i)) { v = ov; i = oi; }
+    }
+    warp_best(v, i);
+    if (lane == 0) {
+      *a.argmax_out = i;
+      if (a.pos_counter) {
+        const int64_t pos = *a.pos_counter;
+        if (a.token_log) a.token_log[pos - a.log_base] = i;
+        *a.pos_counter = pos + 1;
+      }
+      *counter = 0u;
+    }
+  }
+}
+
+// Per-row symmetric int4 quantisation of a weight matrix: output row r is
+// column r of a [K, N] Conv1D weight (trans = false) or row r of an [N, K]
+// weight (trans = true). s_r = max_k |w| / 7 (1 for an all-zero row),
+// q = clamp(rint(w / s_r), -8, 7), stored as q + 8 two per byte (even k low).
+__global__ void int4_pack_kernel(const float* __restrict__ w, int64_t K, int64_t N, int64_t ldw,
+                                 bool trans, uint8_t* __restrict__ out,
+                                 float* __restrict__ scales) {
+  __shared__ float red[kWarps];
+  const int64_t r = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  auto at = [&](int64_t k) { return trans ? w[r * ldw + k] : w[k * ldw + r]; };
+  float m = 0.f;
+  for (int64_t k = tid; k < K; k += kThreads) m = fmaxf(m, fabsf(at(k)));
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[wid] = m;
+  __syncthreads();
+  m = red[0];
+  for (int i = 1; i < kWarps; ++i) m = fmaxf(m, red[i]);
+  const float s = m > 0.f ? m / 7.0f : 1.0f;
+  if (tid == 0) scales[r] = s;
+  for (int64_t j = tid; j < K / 2; j += kThreads) {
+    const float q0 = fminf(fmaxf(rintf(at(2 * j) / s), -8.f), 7.f);
+    const float q1 = fminf(fmaxf(rintf(at(2 * j + 1) / s), -8.f), 7.f);
+    out[r * (K / 2) + j] = (uint8_t)(((int)q0 + 8) | (((int)q1 + 8) << 4));
+  }
+}
+
 }  // namespace
 
 // Split-K count of gemv_kn_kernel for a [K, N] weight: enough CTAs to cover
@@ -435,6 +557,30 @@ void launch_row_gemv(const RowGemvArgs& g, cudaStream_t st) {
   int64_t* best_i = reinterpret_cast<int64_t*>(ws.partials + ((blocks + 1) & ~1));
   launch_pdl(row_gemv_kernel, dim3(blocks), dim3(kThreads), 0, st, g, best_v, best_i,
              ws.counters + ws.n_counters - 1);
+}
+
+void launch_int4_row_gemv(const Int4RowArgs& g, cudaStream_t st) {
+  if (g.N <= 0) return;
+  IDEV_CHECK_ARG(g.K > 0 && g.K <= kMaxK && g.K % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(g.w) & 3) == 0 && (g.K / 2) % 4 == 0,
+                 "int4 row GEMV: K must be a multiple of 8 in [8, 8192], W 4-byte aligned");
+  Workspace& ws = g.ws ? *g.ws : workspace_for_current_device();
+  const int64_t want = std::min<int64_t>(4 * (int64_t)sm_count(), (g.N + kWarps - 1) / kWarps);
+  const int blocks = (int)std::max<int64_t>(1, want);
+  IDEV_CHECK_ARG((size_t)blocks * 3 <= ws.partial_floats && ws.n_counters >= 1,
+                 "int4 row GEMV: workspace too small");
+  float* best_v = ws.partials;
+  int64_t* best_i = reinterpret_cast<int64_t*>(ws.partials + ((blocks + 1) & ~1));
+  launch_pdl(int4_row_gemv_kernel, dim3(blocks), dim3(kThreads), 0, st, g, best_v, best_i,
+             ws.counters + ws.n_counters - 1);
+}
+
+void launch_int4_pack(const float* w, int64_t K, int64_t N, int64_t ldw, bool trans,
+                      uint8_t* out, float* scales, cudaStream_t st) {
+  IDEV_CHECK_ARG(K > 0 && K % 2 == 0 && N >= 0, "int4 pack: K must be even");
+  if (N == 0) return;
+  int4_pack_kernel<<<(unsigned)N, kThreads, 0, st>>>(w, K, N, ldw, trans, out, scales);
+  IDEV_LAUNCHED();
 }
 
 void launch_argmax(const float* x, int64_t n, int64_t* out, cudaStream_t st) {

@@ -164,6 +164,36 @@ void launch_row_gemv(const RowGemvArgs& g, cudaStream_t st);
 
 void launch_argmax(const float* x, int64_t n, int64_t* out, cudaStream_t st);
 
+// int4 per-row-scale row GEMV (gemv.cu) for weight-only int4 decode: W in the
+// reference's int4 layout [N, K/2] bytes with scales [N]; y[r] =
+// act(s_r * sum_k (q-8) x_k + bias[r] + resid[r]), optional LayerNorm
+// prologue on x and fused greedy argmax with the decode-loop bookkeeping of
+// RowGemvArgs. K % 8 == 0. (Epilogue order as GemvArgs: act(s*dot + b + resid).)
+struct Int4RowArgs {
+  Workspace* ws = nullptr;
+  const float* x;
+  const float* ln_gamma;
+  const float* ln_beta;
+  float ln_eps;
+  const uint8_t* w;
+  const float* scales;
+  const float* bias;
+  const float* resid;  // may alias y
+  float* y;
+  int64_t K, N;
+  int act;
+  int64_t* argmax_out;
+  int64_t* pos_counter;
+  int64_t* token_log;
+  int64_t log_base;
+};
+void launch_int4_row_gemv(const Int4RowArgs& g, cudaStream_t st);
+// Per-row symmetric int4 quantisation (s = max|w|/7, q = clamp(rint(w/s)))
+// of a [K, N] weight (output row = column; trans: an [N, K] weight) into
+// out [N, K/2] + scales [N].
+void launch_int4_pack(const float* w, int64_t K, int64_t N, int64_t ldw, bool trans,
+                      uint8_t* out, float* scales, cudaStream_t st);
+
 // ---- gemv_int4.cu
 void launch_gemv_int4(const InfercInt4Gemv* descs_host, int count, cudaStream_t st);
 

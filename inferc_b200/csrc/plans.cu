@@ -479,6 +479,14 @@ struct InfercDecoderPlan {
   float* mega_part = nullptr;   // [heads][H]
   int mega_chunks = 0;
   unsigned long long* prof_buf = nullptr;  // -DINFERC_DECODE_PROFILE builds only
+  // Weight-only int4 mode (inferc_dev_decoder_create_int4): the four layer
+  // matrices and the tied LM head as per-row-scale int4 [N, K/2] + scales.
+  bool int4 = false;
+  std::vector<uint8_t*> q_attn, q_proj, q_fc, q_fp;
+  std::vector<float*> s_attn, s_proj, s_fc, s_fp;
+  uint8_t* q_lm = nullptr;
+  float* s_lm = nullptr;
+  std::unique_ptr<Graph> int4_graph;
 
   ~InfercDecoderPlan() {
     step_graph.reset();
@@ -580,6 +588,77 @@ struct InfercDecoderPlan {
   }
   int64_t log_base = 0;  // n_prompt of the current decode; baked into the step graph
 
+  // One single-token step on the int4 weights (captured once): the token in
+  // `tok` at position *len - 1 goes through every layer; the LM head's argmax
+  // becomes the next `tok`, is logged at token_log[*len] and *len advances.
+  void step_int4(cudaStream_t st) {
+    launch_decode_embed(tok, len, wte, wpe, x, H, V, P, err, st);
+    auto row = [&](const float* in, const float* g, const float* b, const uint8_t* q,
+                   const float* sc, const float* bias, const float* resid, float* y, int64_t K,
+                   int64_t N, int act) {
+      Int4RowArgs a{};
+      a.ws = &ws;
+      a.x = in; a.ln_gamma = g; a.ln_beta = b; a.ln_eps = eps;
+      a.w = q; a.scales = sc; a.bias = bias; a.resid = resid; a.y = y;
+      a.K = K; a.N = N; a.act = act;
+      return a;
+    };
+    for (int64_t l = 0; l < L; ++l) {
+      launch_int4_row_gemv(row(x, ln1g[l], ln1b[l], q_attn[l], s_attn[l], attn_b[l], nullptr,
+                               qkv, H, 3 * H, ACT_NONE), st);
+      launch_decode_attention(qkv, qkv + H, qkv + 2 * H, kc[l], vc[l], ctx, nH, hd, max_len, len,
+                              0, st);
+      launch_int4_row_gemv(row(ctx, nullptr, nullptr, q_proj[l], s_proj[l], proj_b[l], x, x, H, H,
+                               ACT_NONE), st);
+      launch_int4_row_gemv(row(x, ln2g[l], ln2b[l], q_fc[l], s_fc[l], fc_b[l], nullptr, f, H, F,
+                               ACT_GELU_TANH), st);
+      launch_int4_row_gemv(row(f, nullptr, nullptr, q_fp[l], s_fp[l], fp_b[l], x, x, F, H,
+                               ACT_NONE), st);
+    }
+    Int4RowArgs lm = row(x, lnf_g, lnf_b, q_lm, s_lm, nullptr, nullptr, logits, H, V, ACT_NONE);
+    lm.argmax_out = tok;
+    lm.pos_counter = len;
+    lm.token_log = token_log;
+    lm.log_base = 0;
+    launch_int4_row_gemv(lm, st);
+  }
+
+  // Greedy decode on the int4 weights: the prompt runs through the same
+  // single-token step, one position at a time (its tokens are copied into
+  // `tok` before each step), then max_tokens-1 generated steps follow.
+  void decode_int4(const int64_t* prompt, int64_t n, int64_t max_tokens, int64_t* out,
+                   double* step_ms) {
+    cudaStream_t st = stream;
+    IDEV_CUDA(cudaMemcpyAsync(ids, prompt, n * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    n_host_scratch = 1;
+    IDEV_CUDA(cudaMemcpyAsync(len, &n_host_scratch, sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    if (!int4_graph) {
+      IDEV_CUDA(cudaStreamSynchronize(st));
+      int4_graph = capture(st, [&] { step_int4(st); });
+    }
+    for (int64_t i = 0; i < n; ++i) {
+      IDEV_CUDA(cudaMemcpyAsync(tok, ids + i, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
+      IDEV_CUDA(cudaGraphLaunch(int4_graph->exec, st));
+    }
+    IDEV_CUDA(cudaEventRecord(ev0, st));
+    for (int64_t s = 1; s < max_tokens; ++s) IDEV_CUDA(cudaGraphLaunch(int4_graph->exec, st));
+    IDEV_CUDA(cudaEventRecord(ev1, st));
+    IDEV_CUDA(cudaMemcpyAsync(out, token_log + n, max_tokens * sizeof(int64_t),
+                              cudaMemcpyDeviceToHost, st));
+    int herr = 0;
+    IDEV_CUDA(cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    IDEV_CUDA(cudaStreamSynchronize(st));
+    if (herr) {
+      IDEV_CUDA(cudaMemset(err, 0, sizeof(int)));
+      throw Error(INFERC_ERR_RANGE, "decode: token or position out of range on the device");
+    }
+    if (step_ms) {
+      float ms = 0.f;
+      if (max_tokens > 1) IDEV_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
+      *step_ms = max_tokens > 1 ? ms / double(max_tokens - 1) : 0.0;
+    }
+  }
+
   void decode(const int64_t* prompt, int64_t n, int64_t max_tokens, int64_t* out,
               double* step_ms) {
     IDEV_CHECK_ARG(prompt != nullptr && out != nullptr, "decode: null prompt or output");
@@ -588,6 +667,7 @@ struct InfercDecoderPlan {
                    "decode: prompt + new tokens exceed the context / cache length");
     for (int64_t i = 0; i < n; ++i)
       IDEV_CHECK_ARG(prompt[i] >= 0 && prompt[i] < V, "decode: prompt token id out of range");
+    if (int4) return decode_int4(prompt, n, max_tokens, out, step_ms);
     cudaStream_t st = stream;
     IDEV_CUDA(cudaMemcpyAsync(ids, prompt, n * sizeof(int64_t), cudaMemcpyHostToDevice, st));
     n_host_scratch = n;
@@ -850,6 +930,47 @@ int inferc_dev_decoder_create(const InfercGpt2Weights* w, int64_t max_len, infer
     auto p = std::make_unique<InfercDecoderPlan>();
     decoder_create(w, max_len, p.get());
     *out = p.release();
+  });
+}
+
+int inferc_dev_decoder_create_int4(const InfercGpt2Weights* w, int64_t max_len,
+                                   inferc_decoder_t* out) {
+  return guard([&] {
+    IDEV_CHECK_ARG(out != nullptr, "decoder_create_int4: null out");
+    *out = nullptr;
+    IDEV_CHECK_ARG(w != nullptr && w->hidden % 8 == 0 && w->ffn % 8 == 0 &&
+                       w->hidden <= 8192 && w->ffn <= 8192,
+                   "decoder_create_int4: hidden and ffn must be multiples of 8, at most 8192");
+    auto p = std::make_unique<InfercDecoderPlan>();
+    decoder_create(w, max_len, p.get());
+    InfercDecoderPlan& d = *p;
+    const int64_t H = d.H, F = d.F;
+    auto pack = [&](const float* src, int64_t K, int64_t N, bool trans, std::vector<uint8_t*>* qv,
+                    std::vector<float*>* sv, uint8_t** q1, float** s1) {
+      uint8_t* q = d.mem.alloc<uint8_t>((size_t)N * (K / 2));
+      float* sc = d.mem.alloc<float>((size_t)N);
+      launch_int4_pack(src, K, N, trans ? K : N, trans, q, sc, nullptr);
+      if (qv) { qv->push_back(q); sv->push_back(sc); }
+      if (q1) { *q1 = q; *s1 = sc; }
+    };
+    for (int64_t l = 0; l < d.L; ++l) {
+      pack(d.attn_w[l], H, 3 * H, false, &d.q_attn, &d.s_attn, nullptr, nullptr);
+      pack(d.proj_w[l], H, H, false, &d.q_proj, &d.s_proj, nullptr, nullptr);
+      pack(d.fc_w[l], H, F, false, &d.q_fc, &d.s_fc, nullptr, nullptr);
+      pack(d.fp_w[l], F, H, false, &d.q_fp, &d.s_fp, nullptr, nullptr);
+    }
+    pack(d.wte, H, d.V, true, nullptr, nullptr, &d.q_lm, &d.s_lm);
+    IDEV_CUDA(cudaDeviceSynchronize());
+    d.int4 = true;
+    *out = p.release();
+  });
+}
+
+int inferc_dev_int4_pack_rowscale(const float* w, int64_t K, int64_t N, int64_t ldw, int trans,
+                                  uint8_t* out, float* scales, void* stream) {
+  return guard([&] {
+    IDEV_CHECK_ARG(ldw >= (trans ? K : N), "int4_pack_rowscale: ldw too small");
+    launch_int4_pack(w, K, N, ldw, trans != 0, out, scales, as_stream(stream));
   });
 }
 

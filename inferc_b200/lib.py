@@ -86,6 +86,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "inferc_dev_encoder_destroy": ([_p], None),
     "inferc_dev_decoder_create": ([ctypes.POINTER(structs.Gpt2Weights), _i64,
                                    ctypes.POINTER(_p)], _i),
+    "inferc_dev_decoder_create_int4": ([ctypes.POINTER(structs.Gpt2Weights), _i64,
+                                        ctypes.POINTER(_p)], _i),
+    "inferc_dev_int4_pack_rowscale": ([_p, _i64, _i64, _i64, _i, _p, _p, _p], _i),
     "inferc_dev_decode": ([_p, _p, _i64, _i64, _p, ctypes.POINTER(ctypes.c_double)], _i),
     "inferc_dev_decoder_logits": ([_p], _p),
     "inferc_dev_decoder_destroy": ([_p], None),

@@ -56,12 +56,14 @@ class EncoderPlan:
 
 
 class DecoderPlan:
-    def __init__(self, cfg, weights: dict, max_len: int = 1024):
+    def __init__(self, cfg, weights: dict, max_len: int = 1024, int4: bool = False):
+        """int4: the weight-only int4 decoder (inferc_dev_decoder_create_int4)."""
         self.cfg = cfg
         self._w = structs.gpt2_struct(cfg, weights)
         h = ctypes.c_void_p()
-        _lib.check(_lib.load().inferc_dev_decoder_create(ctypes.byref(self._w), max_len,
-                                                         ctypes.byref(h)))
+        L = _lib.load()
+        create = L.inferc_dev_decoder_create_int4 if int4 else L.inferc_dev_decoder_create
+        _lib.check(create(ctypes.byref(self._w), max_len, ctypes.byref(h)))
         self._h = h
         self.max_len = max_len
 

@@ -211,3 +211,43 @@ def attention_sweep_inputs(batch: int, seq: int, hidden: int = 768, seed: int = 
         ws.append(_normal(rng, (hidden,)))
     lens = rng.integers(min(16, seq), seq + 1, size=batch)
     return x, tuple(ws), lens
+
+
+def quantize_int4_rowscale(w: np.ndarray, trans: bool = False) -> Int4Matrix:
+    """Per-output-row symmetric int4 quantisation, the packer of
+    inferc_dev_int4_pack_rowscale restated in numpy (bit-identical): output
+    row r is column r of a [K, N] Conv1D weight (row r of an [N, K] weight
+    when trans); s_r = max|w| / 7 (1 for an all-zero row), q = clip(rint(w /
+    s_r), -8, 7). Returns the packed matrix with x = zeros(K)."""
+    rows = np.ascontiguousarray(w if trans else w.T, np.float32)  # [N, K]
+    m = np.abs(rows).max(axis=1)
+    s = np.where(m > 0, m / np.float32(7), np.float32(1)).astype(np.float32)
+    q = np.clip(np.rint(rows / s[:, None]), -8, 7).astype(np.int8)
+    return Int4Matrix(pack_int4(q), s, np.zeros(rows.shape[1], np.float32))
+
+
+def dequantize_int4_rowscale(m: Int4Matrix, trans: bool = False) -> np.ndarray:
+    """The fp32 weight an int4 row GEMV applies: s_r * (q - 8) formed in fp32
+    (bench/amx/int4_gemv_amx.cc:265-267), back in the source layout."""
+    lo = (m.w & 0x0F).astype(np.int16) - 8
+    hi = (m.w >> 4).astype(np.int16) - 8
+    q = np.empty((m.w.shape[0], 2 * m.w.shape[1]), np.float32)
+    q[:, 0::2] = lo
+    q[:, 1::2] = hi
+    rows = (m.scales[:, None] * q).astype(np.float32)
+    return np.ascontiguousarray(rows if trans else rows.T)
+
+
+def gpt2_weights_int4_dequantized(cfg: Gpt2Config, w: dict) -> dict:
+    """The GPT-2 weights the int4 decoder plan computes with: the four layer
+    matrices and the tied LM head replaced by their int4 round trip. The
+    embedding lookup keeps the fp32 wte, so the LM head is returned
+    separately as "lm_head" ([vocab, hidden])."""
+    out = dict(w)
+    for l in range(cfg.layers):
+        for name in ("attn_w", "proj_w", "fc_w", "fcproj_w"):
+            k = f"{name}.{l}"
+            out[k] = dequantize_int4_rowscale(quantize_int4_rowscale(w[k]))
+    out["lm_head"] = dequantize_int4_rowscale(quantize_int4_rowscale(w["wte"], trans=True),
+                                              trans=True)
+    return out

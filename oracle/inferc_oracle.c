@@ -310,7 +310,7 @@ typedef struct {
 /* One forward over n new tokens at positions [pos0, pos0+n), appending their
  * K/V to the cache; writes the logits of the last token to `logits`. Causal
  * masking inside the new block; all cached positions visible. */
-static void gpt2_forward(const InfercGpt2Weights* w, KvCache* kv,
+static void gpt2_forward(const InfercGpt2Weights* w, const float* lm, KvCache* kv,
                          const int64_t* toks, int64_t n, int64_t pos0,
                          float* logits) {
   const int64_t H = w->hidden, F = w->ffn, nH = w->heads, hd = H / nH;
@@ -368,7 +368,7 @@ static void gpt2_forward(const InfercGpt2Weights* w, KvCache* kv,
   }
   orc_layernorm(x + (n - 1) * H, w->lnf_g, w->lnf_b, h, 1, H, w->ln_eps);
   /* LM head: MatMul(x, wte^T) */
-  orc_sgemm(0, 1, 1, w->vocab, H, 1.0f, h, H, w->wte, H, 0.0f, logits, w->vocab);
+  orc_sgemm(0, 1, 1, w->vocab, H, 1.0f, h, H, lm, H, 0.0f, logits, w->vocab);
   free(x); free(h); free(qkv); free(ctx); free(a); free(f); free(g); free(sc); free(p);
 }
 
@@ -379,9 +379,11 @@ static float top2_margin(const float* x, int64_t n, int64_t best) {
   return x[best] - second;
 }
 
-int orc_gpt2_decode(const InfercGpt2Weights* w, const int64_t* prompt,
-                    int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
-                    float* margins_out) {
+/* Greedy decode with the LM head `lm` ([vocab, hidden]; the tied wte in
+ * GPT-2, its int4 round trip for the weight-only int4 decoder). */
+int orc_gpt2_decode_lm(const InfercGpt2Weights* w, const float* lm, const int64_t* prompt,
+                       int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
+                       float* margins_out) {
   if (n_prompt <= 0 || max_tokens <= 0 || n_prompt + max_tokens - 1 > w->max_pos) return -1;
   for (int64_t i = 0; i < n_prompt; ++i)
     if (prompt[i] < 0 || prompt[i] >= w->vocab) return -1;
@@ -392,16 +394,22 @@ int orc_gpt2_decode(const InfercGpt2Weights* w, const int64_t* prompt,
   kv.k = (float*)calloc(cache, sizeof(float));
   kv.v = (float*)calloc(cache, sizeof(float));
   float* logits = (float*)malloc((size_t)w->vocab * sizeof(float));
-  gpt2_forward(w, &kv, prompt, n_prompt, 0, logits);
+  gpt2_forward(w, lm, &kv, prompt, n_prompt, 0, logits);
   int64_t tok = orc_argmax(logits, w->vocab);
   tokens_out[0] = tok;
   if (margins_out) margins_out[0] = top2_margin(logits, w->vocab, tok);
   for (int64_t step = 1; step < max_tokens; ++step) {
-    gpt2_forward(w, &kv, &tok, 1, n_prompt + step - 1, logits);
+    gpt2_forward(w, lm, &kv, &tok, 1, n_prompt + step - 1, logits);
     tok = orc_argmax(logits, w->vocab);
     tokens_out[step] = tok;
     if (margins_out) margins_out[step] = top2_margin(logits, w->vocab, tok);
   }
   free(kv.k); free(kv.v); free(logits);
   return 0;
+}
+
+int orc_gpt2_decode(const InfercGpt2Weights* w, const int64_t* prompt,
+                    int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
+                    float* margins_out) {
+  return orc_gpt2_decode_lm(w, w->wte, prompt, n_prompt, max_tokens, tokens_out, margins_out);
 }

@@ -98,6 +98,9 @@ int orc_encoder_forward(const InfercEncoderWeights* w, const int64_t* ids,
  * the prompt, then max_tokens-1 single-token steps. tokens_out receives
  * max_tokens ids; margins_out (may be NULL) the top1-top2 logit gap of each
  * generated token. Returns 0, or -1 on bad arguments. */
+int orc_gpt2_decode_lm(const InfercGpt2Weights* w, const float* lm, const int64_t* prompt,
+                       int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
+                       float* margins_out);
 int orc_gpt2_decode(const InfercGpt2Weights* w, const int64_t* prompt,
                     int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
                     float* margins_out);

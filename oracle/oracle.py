@@ -204,6 +204,7 @@ class Port(_Ops):
         self._int4 = self._l.fn("int4_gemv_rowscale", [_p, _p, _p, _p, _i64, _i64], None)
         self._int4t = self._l.fn("int4_gemv", [_p, _f, _p, _p, _i64, _i64], None)
         self._dec = self._l.fn("gpt2_decode", [_p, _p, _i64, _i64, _p, _p])
+        self._declm = self._l.fn("gpt2_decode_lm", [_p, _p, _p, _i64, _i64, _p, _p])
         self._argmax = self._l.fn("argmax", [_p, _i64], _i64)
 
     def int4_gemv_rowscale(self, w, scales, x):
@@ -232,6 +233,16 @@ class Port(_Ops):
                               ptr(toks), ptr(margins)))
         return toks, margins
 
+    def gpt2_decode_lm(self, wstruct, lm_head, prompt, max_tokens):
+        """Greedy decode with a separate LM head [vocab, hidden]."""
+        prompt = np.ascontiguousarray(prompt, np.int64)
+        lm_head = np.ascontiguousarray(lm_head, np.float32)
+        toks = np.empty(max_tokens, np.int64)
+        margins = np.empty(max_tokens, np.float32)
+        self._check(self._declm(ctypes.byref(wstruct), ptr(lm_head), ptr(prompt), prompt.size,
+                                max_tokens, ptr(toks), ptr(margins)))
+        return toks, margins
+
 
 class Ref(_Ops):
     kind = "reference"
@@ -240,6 +251,7 @@ class Ref(_Ops):
         self._l = _Lib(path, "ref_")
         _bind(self, self._l)
         self._dec = self._l.fn("gpt2_decode", [_p, _p, _i64, _i64, _p, _p, _p])
+        self._declm = self._l.fn("gpt2_decode_lm", [_p, _p, _p, _i64, _i64, _p, _p, _p])
         self._err = self._l.fn("last_error", [], ctypes.c_char_p)
 
     def _check(self, rc):
@@ -254,4 +266,16 @@ class Ref(_Ops):
         ms = ctypes.c_double(0.0)
         self._check(self._dec(ctypes.byref(wstruct), ptr(prompt), prompt.size, max_tokens,
                               ptr(toks), ptr(margins), ctypes.byref(ms)))
+        return toks, margins, ms.value
+
+    def gpt2_decode_lm(self, wstruct, lm_head, prompt, max_tokens):
+        """Greedy decode with a separate LM head [vocab, hidden]; returns
+        (tokens, margins, mean step ms)."""
+        prompt = np.ascontiguousarray(prompt, np.int64)
+        lm_head = np.ascontiguousarray(lm_head, np.float32)
+        toks = np.empty(max_tokens, np.int64)
+        margins = np.empty(max_tokens, np.float32)
+        ms = ctypes.c_double(0.0)
+        self._check(self._declm(ctypes.byref(wstruct), ptr(lm_head), ptr(prompt), prompt.size,
+                                max_tokens, ptr(toks), ptr(margins), ctypes.byref(ms)))
         return toks, margins, ms.value

@@ -184,6 +184,7 @@ namespace {
 
 struct Gpt2Ref {
   const InfercGpt2Weights* w;
+  const float* lm_head;  // [vocab, hidden]: wte (tied) or its int4 round trip
   std::vector<Tensor> past_k, past_v;  // [1, nH, L, hd] per layer
 
   // One graph run over n tokens at positions [pos0, pos0+n). Returns the
@@ -252,7 +253,7 @@ struct Gpt2Ref {
   Tensor lm_;
   const Tensor& Lm() {
     if (lm_.shape().empty())
-      lm_ = rt::Transpose(F32({w->vocab, w->hidden}, w->wte), {1, 0}).Contiguous();
+      lm_ = rt::Transpose(F32({w->vocab, w->hidden}, lm_head), {1, 0}).Contiguous();
     return lm_;
   }
 };
@@ -276,11 +277,13 @@ int64_t ArgmaxFirst(const float* p, int64_t n, float* margin) {
 // Greedy decode through the reference kernels. step_ms_out (may be NULL)
 // receives the mean wall-clock ms of the max_tokens-1 single-token steps, the
 // number `inferc decode` reports (main.cpp:862-868, :903-909).
-int ref_gpt2_decode(const InfercGpt2Weights* w, const int64_t* prompt,
-                    int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
-                    float* margins_out, double* step_ms_out) {
+// lm: the LM head [vocab, hidden] (the tied wte; its int4 round trip for the
+// weight-only int4 decoder).
+int ref_gpt2_decode_lm(const InfercGpt2Weights* w, const float* lm, const int64_t* prompt,
+                       int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
+                       float* margins_out, double* step_ms_out) {
   return Guard([&] {
-    Gpt2Ref g{w, {}, {}, Tensor()};
+    Gpt2Ref g{w, lm, {}, {}, Tensor()};
     g.Lm();
     std::vector<int64_t> p(prompt, prompt + n_prompt);
     Tensor lg = g.Run(p, 0).Contiguous();
@@ -297,6 +300,13 @@ int ref_gpt2_decode(const InfercGpt2Weights* w, const int64_t* prompt,
     }
     if (step_ms_out) *step_ms_out = max_tokens > 1 ? total / double(max_tokens - 1) : 0.0;
   });
+}
+
+int ref_gpt2_decode(const InfercGpt2Weights* w, const int64_t* prompt,
+                    int64_t n_prompt, int64_t max_tokens, int64_t* tokens_out,
+                    float* margins_out, double* step_ms_out) {
+  return ref_gpt2_decode_lm(w, w->wte, prompt, n_prompt, max_tokens, tokens_out, margins_out,
+                            step_ms_out);
 }
 
 }  // extern "C"

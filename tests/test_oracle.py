@@ -207,3 +207,28 @@ def test_port_matches_reference_build_random(port):
     gm = rng.standard_normal(300, dtype=np.float32)
     np.testing.assert_allclose(port.layernorm(x, gm, gm, 1e-5), ref.layernorm(x, gm, gm, 1e-5),
                                atol=2e-6)
+
+
+def test_int4_round_trip_properties():
+    rng = np.random.default_rng(4)
+    w = (rng.standard_normal((96, 40)) * 0.02).astype(np.float32)
+    w[:, 3] = 0.0  # an all-zero output row gets scale 1
+    m = synth.quantize_int4_rowscale(w)
+    assert m.w.shape == (40, 48) and m.scales[3] == 1.0
+    dq = synth.dequantize_int4_rowscale(m)
+    assert dq.shape == w.shape
+    s = np.abs(w).max(0) / np.float32(7)
+    s[3] = 1
+    assert (np.abs(dq - w) <= s / 2 + 1e-9).all()  # round to nearest
+    wt = synth.dequantize_int4_rowscale(synth.quantize_int4_rowscale(w.T.copy(), trans=True),
+                                        trans=True)
+    np.testing.assert_array_equal(wt, dq.T)
+
+
+def test_port_int4_decode_matches_reference_golden(port):
+    g = np.load(os.path.join(GOLD, "decode_int4.npz"))
+    cfg = synth.Gpt2Config(**make_golden.SMALL_GPT2)
+    dq = synth.gpt2_weights_int4_dequantized(cfg, synth.gpt2_weights(cfg, seed=8))
+    toks, _ = port.gpt2_decode_lm(structs.gpt2_struct(cfg, dq), dq["lm_head"], g["small_prompt"],
+                                  len(g["small_tokens"]))
+    np.testing.assert_array_equal(toks, g["small_tokens"])
