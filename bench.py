@@ -261,7 +261,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["decode", "int4", "sweep", "c0", "executor"],
+    ap.add_argument("--only", choices=["decode", "int4", "sweep", "c0", "executor", "decode_int4"],
                     help="run one sub-benchmark alone and print its object (small cases for ncu)")
     ap.add_argument("--roofline-only", action="store_true",
                     help="time only the dominant kernel (FFN1 split-fp16 GEMM, B=256 S=128) "
@@ -281,7 +281,8 @@ def main():
     dev = torch.device("cuda", local)
     if args.only:
         fn = {"decode": decode_bench, "int4": int4_bench, "sweep": sweep_bench,
-              "c0": encoder_c0_bench, "executor": executor_bench}[args.only]
+              "c0": encoder_c0_bench, "executor": executor_bench,
+              "decode_int4": decode_int4_bench}[args.only]
         print(json.dumps(fn(dev)), flush=True)
         return
     if args.roofline_only:
@@ -418,6 +419,7 @@ def main():
     if rank == 0 and not args.no_decode:
         result["encoder_c0"] = encoder_c0_bench(dev)
         result["decode"] = decode_bench(dev)
+        result["decode_int4"] = decode_int4_bench(dev)
         result["int4_gemv"] = int4_bench(dev)
         result["qkv_attention_sweep"] = sweep_bench(dev)
         result["plan_executor"] = executor_bench(dev, plan_seq_s=e2e_value)
@@ -546,6 +548,43 @@ def decode_bench(dev):
                     "path": "inferc_dev_decode wall time (host prompt in, prefill + 127 "
                             "steps, host token ids out) / 128 tokens; a step is one decode"},
             "cpu_baseline": _decode_cpu(cfg, w, prompt)}
+
+
+def decode_int4_bench(dev):
+    """Weight-only int4 GPT-2-small greedy decode (inferc_dev_decoder_create_int4),
+    prompt 32 + 128 new tokens: mean device ms per single-token step and the
+    int4 weight stream's HBM fraction; tokens against the reference kernels
+    decoding the same (dequantised) model."""
+    from inferc_b200 import plans, synth
+    cfg = synth.Gpt2Config()
+    w = synth.gpt2_weights(cfg, seed=0)
+    gold = np.load(os.path.join(ROOT, "tests", "golden", "decode_int4.npz"))
+    p = plans.DecoderPlan(cfg, w, max_len=1024, int4=True)
+    p.decode(gold["c1_prompt"], 128)
+    runs, walls = [], []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        runs.append(p.decode(gold["c1_prompt"], 128))
+        walls.append(time.perf_counter() - t0)
+    toks = runs[-1][0]
+    ms = statistics.median(r[1] for r in runs)
+    H, F = cfg.hidden, cfg.ffn
+    rows = cfg.layers * (3 * H + H + F + H) + cfg.vocab
+    wbytes = cfg.layers * (H * 3 * H + H * H + 2 * H * F) // 2 + cfg.vocab * H // 2 + 4 * rows
+    pk, basis = peaks()
+    gbs = wbytes / (ms / 1e3) / 1e9
+    return {"metric": "GPT-2-small int4 weight-only decode ms/token", "value": ms,
+            "unit": "ms/token", "higher_is_better": False,
+            "config": {"workload": "BASELINE config 1 with the layer matrices and LM head "
+                                   "per-row int4 (config 3's format), prompt 32 + 128"},
+            "tokens_match_reference": bool((toks == gold["c1_tokens"]).all()),
+            "weight_bytes_per_token": int(wbytes), "achieved_gbs": gbs,
+            "hbm_frac": gbs / pk["hbm_gbs"], "peak_basis": basis,
+            "kernel": "int4_row_gemv_kernel x 49 + decode attention x 12 per step, CUDA graph",
+            "e2e": {"value": statistics.median(walls) * 1e3 / 128, "unit": "ms/token",
+                    "h2d_bytes_per_step": int(gold["c1_prompt"].nbytes),
+                    "d2h_bytes_per_step": 8 * 128,
+                    "path": "inferc_dev_decode wall time / 128 (prompt and tokens via host)"}}
 
 
 def _decode_cpu(cfg, w, prompt):

@@ -232,6 +232,33 @@ __device__ void prefetch_panels(const MegaPanels& m, int pair, uint8_t* slots, S
   }
 }
 
+// L2 prefetch (no shared-memory destination, nothing to wait for): the
+// next layer's panels of this CTA are requested from HBM while the current
+// layer computes and waits at its barriers, so the later bulk copies into the
+// slots read L2. Addresses and sizes are multiples of 16 bytes (panels and
+// LM-head rows are).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Lanes of warp 0 issue this CTA's panels of layer L, 16 KiB per request.
+__device__ void prefetch_layer_l2(const MegaArgs& a, const MegaLayer& L) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  int q = 0;  // running request index, spread over the lanes
+  auto panel = [&](const MegaPanels& m, int p) {
+    if (p >= m.npanels) return;
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(m.data + (size_t)p * m.K * m.P);
+    const uint32_t bytes = (uint32_t)m.K * m.P * 4;
+    for (uint32_t off = 0; off < bytes; off += 16384, ++q)
+      if ((q & 31) == lane) prefetch_l2(src + off, min(16384u, bytes - off));
+  };
+  for (int j = 0; j < 2; ++j) panel(L.attn, blockIdx.x + j * gridDim.x);
+  if (blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) panel(L.proj, blockIdx.x);
+  for (int j = 0; j < 2; ++j) panel(L.fc, blockIdx.x + j * gridDim.x);
+  for (int j = 0; j < 2; ++j) panel(L.fp, blockIdx.x + j * gridDim.x);
+}
+
 // Waits for slot s; all threads; false on timeout.
 __device__ bool wait_slot(int s, Smem& sm, const MegaArgs& a) {
   const bool ok = __syncthreads_and(mb_wait(&sm.bar[s], sm.uses[s] & 1)) != 0;
@@ -838,6 +865,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
     for (int l = 0; l < a.layers; ++l) {
       const MegaLayer& L = a.layer[l];  // read on use (keeps registers free)
       const bool last = l + 1 == a.layers;
+      if (a.l2_prefetch) {
+        if (!last) prefetch_layer_l2(a, a.layer[l + 1]);
+        else if (tid < 32) {  // the first chunks of this CTA's LM-head rows
+          for (int ch = 4 + tid; ch < min(lm_nchunks, 4 + a.lm_prefetch_chunks); ch += 32) {
+            const int ra = lm_r0 + ch * lm_crow, rb = min(lm_r1, ra + lm_crow);
+            prefetch_l2(a.wte + (size_t)ra * H, (uint32_t)(rb - ra) * H * 4);
+          }
+        }
+      }
       // ---- QKV (pair 0; W_proj is in slot 2, LN1's gamma / beta in sm.lnp)
       const EpiIn e_qkv = gemv_preload(L.attn, L.attn_b, nullptr);
       const float *g1, *b1, *unused;
@@ -923,6 +959,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
         }
         __syncthreads();  // slot s fully consumed
         issue(ch + kSlots);
+        if (a.l2_prefetch && tid == 0) {
+          const int pc = ch + 4 + a.lm_prefetch_chunks;
+          if (pc < nchunks) {
+            const int ra = r0 + pc * crow, rb = min(r1, ra + crow);
+            prefetch_l2(a.wte + (size_t)ra * H, (uint32_t)(rb - ra) * H * 4);
+          }
+        }
+        if (a.l2_prefetch && ch == 0 && step + 1 < a.nsteps) prefetch_layer_l2(a, a.layer[0]);
       }
       if (lane == 0) { sm.bv[wid] = bv; sm.bi[wid] = bi; }
       __syncthreads();
