@@ -38,6 +38,8 @@
 
 #include "gemm_epi.cuh"
 #include "kernels.cuh"
+#include <cstdlib>
+
 #include "tc_ptx.cuh"
 
 namespace inferc_dev {
@@ -69,6 +71,8 @@ struct F16Shape {
   static constexpr uint32_t B_BYTES = BN * BK * 2;  // one fp16 plane
   static constexpr uint32_t STAGE_BYTES = A_F32_BYTES + 2 * B_BYTES;
   static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  // two accumulators of BN columns; TMEM is allocated in powers of two
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
   static_assert(BK == 32 || BK == 64, "BK must be 32 or 64");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32,256]");
   static __device__ __forceinline__ uint32_t chunk_swz(int r) {
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
   if (warp == 1) {  // two accumulators of BN columns each
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&tmem_base_sh)),
-                 "r"((uint32_t)(2 * BN)));
+                 "r"(S::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -419,7 +423,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"((uint32_t)(2 * BN)));
+                 "r"(S::TMEM_COLS));
   }
 }
 
@@ -529,18 +533,41 @@ void launch_f16s_width(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl
                        const float* inv_scale, int* range_flag, float* C, int64_t ldc,
                        const SplitOut& so, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
                        cudaStream_t st) {
-  // BN = 256 when there are enough 128 x 256 tiles to fill the SMs, else 128.
-  // Pre-split A with K <= 1024: BK = 64 (128-byte TMA rows, 2 stages of
-  // 96 KB) — measured 7-9 % faster than BK = 32 at K = 768, where the
-  // 64-byte rows of BK = 32 limit the TMA request rate; longer K keeps
-  // BK = 32 (4 stages), which is ahead there.
-  const int64_t tiles256 = ((N + 255) / 256) * ((M + BM - 1) / BM);
-  if (tiles256 >= sm_count_f16() / 2) {
-    if (AS && K <= 1024)
+  // Tile width by wave quantisation: of BN = 256, 192 and 128 the one whose
+  // tile count fills the SMs' last wave best (a larger BN on a tie, for
+  // operand reuse). N = 768 at M = 4096 (a rank's share of the batch-256
+  // encoder on 8 GPUs) gets 128 tiles of 192 columns in one 86 % wave
+  // instead of 96 tiles of 256 (65 %). INFERC_GEMM_BN forces a width.
+  // Pre-split A with K <= 1024: BK = 64 (128-byte TMA rows, 2 stages) —
+  // measured 7-9 % faster than BK = 32 at K = 768, where the 64-byte rows of
+  // BK = 32 limit the TMA request rate; longer K keeps BK = 32 (4 stages).
+  const int64_t sms = sm_count_f16();
+  auto util = [&](int64_t bn) {
+    const int64_t t = ((N + bn - 1) / bn) * ((M + BM - 1) / BM);
+    return (double)t / (double)(((t + sms - 1) / sms) * sms);
+  };
+  int bn = 256;
+  for (int cand : {192, 128})
+    if (util(cand) > util(bn) + 1e-9) bn = cand;
+  static const int forced = [] {
+    const char* e = std::getenv("INFERC_GEMM_BN");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced == 128 || forced == 192 || forced == 256) bn = forced;
+  const bool bk64 = AS && K <= 1024;
+  if (bn == 256) {
+    if (bk64)
       launch_f16s<256, 64, 2, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
                                              N, K, ep, st);
     else
       launch_f16s<256, 32, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
+                                             N, K, ep, st);
+  } else if (bn == 192) {
+    if (bk64)
+      launch_f16s<192, 64, 2, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
+                                             N, K, ep, st);
+    else
+      launch_f16s<192, 32, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
                                              N, K, ep, st);
   } else {
     launch_f16s<128, 32, 6, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,

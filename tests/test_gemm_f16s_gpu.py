@@ -147,7 +147,8 @@ def test_f16s_planes_chain():
 
 
 @pytest.mark.parametrize("M,K,N", [(512, 768, 256), (1000, 768, 2304), (4096, 3072, 768),
-                                   (777, 96, 300), (32768, 768, 3072)])
+                                   (777, 96, 300), (32768, 768, 3072), (4096, 768, 768),
+                                   (8192, 768, 768), (4000, 3072, 768), (32768, 3072, 768)])
 def test_f16s_planes_shapes(M, K, N):
     """A as fp16 planes (the plan's form) with the bias + residual epilogue
     (fp32 out), ragged M / N / K included: whole 256-column tiles take the
