@@ -263,6 +263,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["decode", "int4", "sweep", "c0", "executor", "decode_int4"],
                     help="run one sub-benchmark alone and print its object (small cases for ncu)")
+    ap.add_argument("--gemm-sweep", action="store_true",
+                    help="time the split-fp16 GEMM of the N=768 projections (A planes in, bias + "
+                         "residual, fp32 out) at M = 4096 .. 32768, K = 768 and 3072, with the "
+                         "tile width INFERC_GEMM_BN selects (default: by wave quantisation)")
+    ap.add_argument("--attention-only", action="store_true",
+                    help="time only the split-fp16 attention kernels at the plan's shape "
+                         "(B=256, S=128) and the flash form (B=8, S=512); the small case "
+                         "for their ncu captures")
     ap.add_argument("--roofline-only", action="store_true",
                     help="time only the dominant kernel (FFN1 split-fp16 GEMM, B=256 S=128) "
                          "and print its roofline; the small case for ncu captures")
@@ -284,6 +292,12 @@ def main():
               "c0": encoder_c0_bench, "executor": executor_bench,
               "decode_int4": decode_int4_bench}[args.only]
         print(json.dumps(fn(dev)), flush=True)
+        return
+    if args.gemm_sweep:
+        print(json.dumps(gemm_sweep(dev)), flush=True)
+        return
+    if args.attention_only:
+        print(json.dumps(attention_probe(dev, max(args.steps, 3))), flush=True)
         return
     if args.roofline_only:
         cfg = synth.EncoderConfig()
@@ -770,6 +784,103 @@ def executor_bench(dev, plan_seq_s=None):
                    "path": "prefill + with-past plans, present.* fed back as "
                            "past_key_values.* each step (Concat-growing cache, as the "
                            "reference's graphs do)"}}
+
+
+def gemm_sweep(dev):
+    """The output projection / FFN2 GEMM of the encoder (N = 768, fp32 out with
+    bias + residual, A as fp16 planes) at the per-rank M of 1/2/4/8 GPUs
+    (32768 / 16384 / 8192 / 4096) and K = 768 (out-proj) or 3072 (FFN2):
+    device us per launch (20 back-to-back launches, CUDA events) and TFLOP/s."""
+    import torch
+
+    from inferc_b200 import lib as _lib
+    L = _lib.load()
+    res = {"bn": os.environ.get("INFERC_GEMM_BN", "auto")}
+    sptr = torch.cuda.current_stream().cuda_stream
+    for K in (768, 3072):
+        N = 768
+        w = torch.randn(K, N, device=dev) * 0.02
+        kp = L.inferc_dev_f16_kp(K)
+        hi, lo = (torch.empty(N, kp, dtype=torch.int16, device=dev) for _ in range(2))
+        sc = torch.empty(2, device=dev)
+        _lib.check(L.inferc_dev_f16_split(w.data_ptr(), K, N, N, hi.data_ptr(), lo.data_ptr(),
+                                          sc.data_ptr(), sptr))
+        b = torch.randn(N, device=dev)
+        for M in (4096, 8192, 16384, 32768):
+            a = torch.randn(M, K, device=dev)
+            ah, al = (torch.empty(M, kp, dtype=torch.int16, device=dev) for _ in range(2))
+            _lib.check(L.inferc_dev_f16_split_rows(a.data_ptr(), M, K, K, ah.data_ptr(),
+                                                   al.data_ptr(), kp, sptr))
+            r = torch.randn(M, N, device=dev)
+            y = torch.empty(M, N, device=dev)
+
+            def f():
+                _lib.check(L.inferc_dev_gemm_f16s_planes(
+                    ah.data_ptr(), al.data_ptr(), kp, hi.data_ptr(), lo.data_ptr(),
+                    sc.data_ptr(), b.data_ptr(), r.data_ptr(), N, y.data_ptr(), None, None, N, M,
+                    N, K, 0, sptr))
+            for _ in range(5):
+                f()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                f()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / 20
+            res[f"K{K}_M{M}"] = {"us": ms * 1e3, "tflops": 2 * M * N * K / ms / 1e9}
+    return res
+
+
+def attention_probe(dev, reps):
+    """FusedAttention as the encoder plan runs it (attention_f16_kernel: q, k,
+    v as fp16 hi / lo planes cut from one [B*S, 3H] pair, the padding mask of
+    the bench workload) at B=256, S=128, and the flash form
+    (attention_f16_flash_kernel) at B=8, S=512; both through
+    inferc_dev_fused_attention_planes with fp32 output. Per case: device us per launch (CUDA events) and
+    the algorithmic bytes (q, k, v planes read once, output written once)."""
+    import torch
+
+    from inferc_b200 import lib as _lib
+    from inferc_b200 import synth
+    L = _lib.load()
+    H = 768
+    out = {}
+    for B, S in ((256, 128), (8, 512)):
+        rng = np.random.default_rng(B + S)
+        qkv = torch.from_numpy(rng.standard_normal((B * S, 3 * H), dtype=np.float32)).to(dev)
+        hi, lo = (torch.empty((B * S, 3 * H), dtype=torch.int16, device=dev) for _ in range(2))
+        _lib.check(L.inferc_dev_f16_split_rows(qkv.data_ptr(), B * S, 3 * H, 3 * H, hi.data_ptr(),
+                                               lo.data_ptr(), 3 * H, None))
+        if S == 128:
+            _, mask = synth.encoder_inputs(B, S, seed=7, variable_lengths=True)
+            km = torch.from_numpy((mask == 0).astype(np.uint8)).to(dev)
+        else:
+            _, _, lens = synth.attention_sweep_inputs(B, S)
+            km = torch.from_numpy((np.arange(S)[None, :] >= lens[:, None]).astype(np.uint8)).to(dev)
+        o = torch.empty((B, S, H), device=dev)
+        e = 2
+
+        def run():
+            _lib.check(L.inferc_dev_fused_attention_planes(
+                hi.data_ptr(), lo.data_ptr(), hi.data_ptr() + H * e, lo.data_ptr() + H * e,
+                hi.data_ptr() + 2 * H * e, lo.data_ptr() + 2 * H * e, 3 * H, km.data_ptr(), B, S,
+                12, -3.4028234663852886e38, o.data_ptr(), None))
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        nbytes = B * S * 3 * H * 2 * 2 + B * S * H * 4 + B * S
+        out[f"B{B}_S{S}"] = {"us_per_launch": us, "algorithmic_bytes": nbytes,
+                             "gbs": nbytes / (us / 1e6) / 1e9}
+    return out
 
 
 def sweep_bench(dev):

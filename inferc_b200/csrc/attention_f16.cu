@@ -333,7 +333,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_expect_tx(&bar_q, 2 * kTile);
     tma_load_4d(sm + FL_Q, &tQh, &bar_q, 0, h, qb * kRows, b);
     tma_load_4d(sm + FL_Q + kTile, &tQl, &bar_q, 0, h, qb * kRows, b);
-    load_kv(0);
   }
   const bool mask_bcast = a.mask && a.ms[2] == 0;
   uint8_t* mrow_s = sm + FL_MASK;
@@ -341,6 +340,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint8_t* mb = a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1];
     for (int j = tid; j < a.S; j += kThreads) mrow_s[j] = mb[(int64_t)j * a.ms[3]];
   }
+  // Key blocks to visit. With a per-key mask and a fill so negative that
+  // exp(fill - m) is exactly 0 in fp32, a block whose keys are all masked
+  // adds exact zeros to the row sums and leaves the running maximum of any
+  // row with a visible key unchanged, so skipping it gives the same bits. A
+  // sequence with no visible key keeps every block (the reference then
+  // weighs all keys equally).
+  uint32_t live = nkb >= 32 ? 0xffffffffu : (1u << nkb) - 1u;
+  if (mask_bcast && a.fill <= -1.0e30f) {
+    __syncthreads();
+    uint32_t lv = 0;
+    for (int kb = 0; kb < nkb; ++kb) {
+      bool vis = false;
+      for (int j = kb * kRows + tid; j < min(a.S, (kb + 1) * kRows); j += kThreads)
+        vis |= mrow_s[j] == 0;
+      if (__syncthreads_or(vis)) lv |= 1u << kb;
+    }
+    if (lv) live = lv;
+  }
+  auto next_live = [&](int kb) {  // first live block after kb (nkb when none)
+    const uint32_t rest = kb + 1 >= 32 ? 0u : live >> (kb + 1);
+    return rest ? kb + 1 + __ffs(rest) - 1 : nkb;
+  };
+  const int kb_first = next_live(-1);
+  if (tid == 0) load_kv(kb_first);
   const uint8_t* mrow_g =
       (a.mask && !mask_bcast && row < a.S)
           ? a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)row * a.ms[2]
@@ -350,8 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   float o_acc[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) o_acc[i] = 0.f;
-  for (int kb = 0; kb < nkb && ok; ++kb) {
-    ok = __syncthreads_and(mbar_wait(&bar_kv, kb & 1)) != 0;
+  for (int kb = kb_first, it = 0; kb < nkb && ok; kb = next_live(kb), ++it) {
+    ok = __syncthreads_and(mbar_wait(&bar_kv, it & 1)) != 0;
     if (!ok) break;
     if (tid == 0) {  // S_blk = Q K_blk^T
       tc_fence_after();
@@ -368,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(&bar_s);
     }
-    ok = __syncthreads_and(mbar_wait(&bar_s, kb & 1)) != 0;
+    ok = __syncthreads_and(mbar_wait(&bar_s, it & 1)) != 0;
     if (!ok) break;
     tc_fence_after();
     float s[64];
@@ -440,9 +463,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(&bar_o);
     }
-    ok = __syncthreads_and(mbar_wait(&bar_o, kb & 1)) != 0;
+    ok = __syncthreads_and(mbar_wait(&bar_o, it & 1)) != 0;
     if (!ok) break;
-    if (tid == 0 && kb + 1 < nkb) load_kv(kb + 1);  // K, V and P are free again
+    if (tid == 0 && next_live(kb) < nkb) load_kv(next_live(kb));  // K, V and P are free again
     tc_fence_after();
 #pragma unroll
     for (int c0 = 0; c0 < 32; c0 += 16) {

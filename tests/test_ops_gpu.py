@@ -360,6 +360,33 @@ def test_fused_attention_planes(port, B, S):
     np.testing.assert_allclose(host(out), ref, atol=2e-5)
 
 
+@pytest.mark.parametrize("S,lens", [(300, [0, 5, 300]), (512, [1, 129, 256, 257]),
+                                    (700, [700, 0, 64])])
+def test_fused_attention_planes_masked_blocks(port, S, lens):
+    """The flash form skips key blocks whose keys are all masked (exact zeros
+    in the sums); a sequence with no visible key keeps every block and gets
+    the reference's uniform weights."""
+    from inferc_b200 import lib
+    L = lib.load()
+    H, B = 768, len(lens)
+    q, k, v, m = _attn_case(B, S, H, 64, np.array(lens), S + 11)
+    qkv = np.concatenate([q, k, v], axis=2).reshape(B * S, 3 * H)
+    x = T(qkv)
+    hi, lo = (torch.empty((B * S, 3 * H), dtype=torch.int16, device=DEV) for _ in range(2))
+    lib.check(L.inferc_dev_f16_split_rows(x.data_ptr(), B * S, 3 * H, 3 * H, hi.data_ptr(),
+                                          lo.data_ptr(), 3 * H, None))
+    out = torch.empty((B, S, H), device=DEV)
+    km = T(m.reshape(B, S))
+    e = 2
+    lib.check(L.inferc_dev_fused_attention_planes(
+        hi.data_ptr(), lo.data_ptr(), hi.data_ptr() + H * e, lo.data_ptr() + H * e,
+        hi.data_ptr() + 2 * H * e, lo.data_ptr() + 2 * H * e, 3 * H, km.data_ptr(), B, S, 12,
+        -3.4028234663852886e38, out.data_ptr(), None))
+    lib.check(L.inferc_dev_stream_synchronize(None))
+    ref = port.fused_attention(q, k, v, m, 64, -3.4028234663852886e38)
+    np.testing.assert_allclose(host(out), ref, atol=2e-5)
+
+
 @pytest.mark.parametrize("B,S", [(2, 128), (1, 512), (3, 40)])
 def test_qkv_attention_f16(port, B, S):
     """inferc_dev_qkv_attention_f16 (split-fp16 weights, planes end to end) ==
