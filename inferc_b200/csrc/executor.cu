@@ -51,6 +51,17 @@ void launch_gemm_op(const float* A, int64_t lda, bool ta, const float* B, int64_
                     float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
                     cudaStream_t st);
 void weight_cache_evict_range(const void* base, size_t bytes);
+struct PreparedWeight {
+  uint16_t* hi;
+  uint16_t* lo;
+  float* scale2;
+  int64_t kp;
+  float* samples;
+  int* stale_host;
+  int* stale_dev;
+};
+PreparedWeight prepared_weight(const float* W, int64_t K, int64_t N, int64_t ldw, bool trans,
+                               cudaStream_t st);
 }  // namespace inferc_dev
 
 namespace {
@@ -86,6 +97,13 @@ struct T {
   std::shared_ptr<DevBuf> dev;                  // device storage (contiguous)
   size_t off = 0;                               // byte offset into dev
   std::shared_ptr<std::vector<uint8_t>> host;   // host values, when known there
+  // fp16 hi / lo planes of an fp32 tensor (row stride = last dim; hi, then
+  // lo), written by producers whose readers take them (split-fp16 GEMMs and
+  // attention); f32 false = only the planes exist.
+  std::shared_ptr<DevBuf> pl;
+  bool f32 = true;
+  uint16_t* phi() const { return static_cast<uint16_t*>(pl->p); }
+  uint16_t* plo() const { return phi() + numel(); }
   int64_t numel() const { return numel_of(shape); }
   size_t nbytes() const { return (size_t)(numel() * ox::dtype_bytes(dt)); }
   int64_t esize() const { return ox::dtype_bytes(dt); }
@@ -176,6 +194,12 @@ struct Step {
   // name the fused result is stored under
   bool fused_gemm = false;
   std::string bias, resid, out;
+  // FusedQKV whose three outputs feed only the next node, a FusedAttention:
+  // one QKV GEMM over the concatenated weights (wcat / bcat, made at load)
+  // writing fp16 planes, then the split-fp16 attention on them.
+  bool qkv_attn = false;
+  std::string wcat, bcat;
+  const ox::Node* attn = nullptr;
   std::vector<std::string> reads;  // every tensor name the step reads
 };
 
@@ -192,6 +216,13 @@ struct InfercGraph {
   std::unordered_map<std::string, size_t> last_use;
   std::set<std::string> graph_outputs;
   int* err = nullptr;
+  // Split-fp16 planes between fused ops: which tensors get them, and whether
+  // only the planes are needed. A run that meets a value fp16 cannot carry
+  // (the range flag) is rerun without planes, on the fp32 operands.
+  std::set<std::string> want_planes, planes_only;
+  bool use_planes = true;
+  int* range = nullptr;
+  int64_t range_reruns = 0;
   cudaStream_t st = nullptr;  // the stream of the current run
 
   ~InfercGraph() {
@@ -201,6 +232,7 @@ struct InfercGraph {
       if (kv.second.dev) weight_cache_evict_range(kv.second.dev->p, kv.second.nbytes() + 1);
     inits.clear();
     if (err) cudaFree(err);
+    if (range) cudaFree(range);
   }
 
   // ------------------------------------------------------------- tensors
@@ -220,6 +252,26 @@ struct InfercGraph {
     t.dev->pooled = true;
     t.dev->st = st;
     return t;
+  }
+  void alloc_planes(T& t) {
+    T p = alloc(ox::kInt32, {t.numel()});  // 2 x numel uint16 = numel words of 4 bytes
+    t.pl = p.dev;
+  }
+  SplitOut planes_out(T& t) {
+    alloc_planes(t);
+    SplitOut so;
+    so.hi = t.phi();
+    so.lo = t.plo();
+    so.ld = t.shape.empty() ? 1 : t.shape.back();
+    so.range = range;
+    return so;
+  }
+  static F16GemmA planes_a(const T& x) {
+    F16GemmA a;
+    a.hi = x.phi();
+    a.lo = x.plo();
+    a.ld = x.shape.back();
+    return a;
   }
   T host_tensor(int32_t dt, std::vector<int64_t> shape) {
     T t;
@@ -295,8 +347,33 @@ struct InfercGraph {
       init_names.insert(tp.name);
     }
     for (const auto& vi : g.outputs) graph_outputs.insert(vi.name);
+    IDEV_CUDA(cudaMalloc(&range, sizeof(int)));
+    IDEV_CUDA(cudaMemset(range, 0, sizeof(int)));
     fold_constant_transposes();
     plan_steps();
+    prepare_weights();
+  }
+
+  // The split-fp16 planes of every GEMM weight the steps read, made once here
+  // (the op-level weight cache), and the concatenated QKV weights.
+  void prepare_weights() {
+    IDEV_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    auto prep = [&](const std::string& name) {
+      const T& w = inits[name];
+      prepared_weight(w.d<float>(), w.shape[0], w.shape[1], w.shape[1], false, st);
+    };
+    for (const Step& s : steps) {
+      const ox::Node& n = *s.node;
+      if (s.fused_gemm) prep(n.inputs[1]);
+      else if (s.qkv_attn) prep(s.wcat);
+      else if (n.op_type == "FusedMatMulAddGELU" && is_2d_f32_init(n.inputs[1])) prep(n.inputs[1]);
+      else if (n.op_type == "FusedQKV")
+        for (int i = 1; i <= 5; i += 2)
+          if (is_2d_f32_init(n.inputs[i])) prep(n.inputs[i]);
+    }
+    IDEV_CUDA(cudaStreamSynchronize(st));
+    cudaStreamDestroy(st);
+    st = nullptr;
   }
 
   // Transpose of an initializer is computed once here and becomes an
@@ -344,6 +421,37 @@ struct InfercGraph {
       Step s;
       s.node = &nodes[i];
       const ox::Node& n = nodes[i];
+      // FusedQKV -> FusedAttention(q, k, v[, mask])
+      if (n.op_type == "FusedQKV" && i + 1 < nodes.size() && n.outputs.size() == 3 &&
+          n.inputs.size() == 7) {
+        const ox::Node& at = nodes[i + 1];
+        bool ok = at.op_type == "FusedAttention" && at.inputs.size() >= 3 &&
+                  at.attr_int("head_dim", 64) == 64;
+        for (int j = 0; ok && j < 3; ++j)
+          ok = at.inputs[j] == n.outputs[j] && single(n.outputs[j]) &&
+               is_2d_f32_init(n.inputs[1 + 2 * j]) && is_bias_any(n.inputs[2 + 2 * j]);
+        if (ok) {
+          const T& w0 = inits[n.inputs[1]];
+          const int64_t K = w0.shape[0], N = w0.shape[1];
+          for (int j = 1; ok && j < 3; ++j)
+            ok = inits[n.inputs[1 + 2 * j]].shape == w0.shape &&
+                 inits[n.inputs[2 + 2 * j]].numel() == N;
+          ok = ok && inits[n.inputs[2]].numel() == N && N % 64 == 0 && K % 8 == 0;
+          if (ok) {
+            s.qkv_attn = true;
+            s.attn = &at;
+            s.out = at.outputs[0];
+            s.wcat = n.name + "/wqkv";
+            s.bcat = n.name + "/bqkv";
+            concat_qkv(n, K, N, s.wcat, s.bcat);
+            s.reads = {n.inputs[0]};
+            if (at.inputs.size() >= 4 && !at.inputs[3].empty()) s.reads.push_back(at.inputs[3]);
+            steps.push_back(s);
+            ++i;
+            continue;
+          }
+        }
+      }
       // MatMul(x, W) -> Add(., b) [-> Add(., r)]
       if (n.op_type == "MatMul" && n.inputs.size() == 2 && is_2d_f32_init(n.inputs[1]) &&
           i + 1 < nodes.size() && single(n.outputs[0])) {
@@ -377,6 +485,50 @@ struct InfercGraph {
     }
     for (size_t k = 0; k < steps.size(); ++k)
       for (const auto& r : steps[k].reads) last_use[r] = k;
+    // readers that take split-fp16 planes for their A operand
+    std::unordered_map<std::string, int> plane_reads, all_reads;
+    for (const Step& st_ : steps) {
+      for (const auto& r : st_.reads) ++all_reads[r];
+      const ox::Node& n = *st_.node;
+      const bool planes_a =
+          st_.fused_gemm || st_.qkv_attn ||
+          (n.op_type == "FusedMatMulAddGELU" && is_2d_f32_init(n.inputs[1]) &&
+           inits[n.inputs[1]].shape[0] % 8 == 0);
+      if (planes_a) ++plane_reads[n.inputs[0]];
+    }
+    for (const auto& kv : plane_reads) {
+      want_planes.insert(kv.first);
+      if (kv.second == all_reads[kv.first] && !graph_outputs.count(kv.first))
+        planes_only.insert(kv.first);
+    }
+  }
+  bool is_bias_any(const std::string& name) {
+    auto it = inits.find(name);
+    return it != inits.end() && it->second.dt == ox::kFloat && it->second.shape.size() == 1;
+  }
+  // [K, 3N] = [Wq | Wk | Wv] and [3N] = [bq | bk | bv] as new initializers.
+  void concat_qkv(const ox::Node& n, int64_t K, int64_t N, const std::string& wname,
+                  const std::string& bname) {
+    T w, b;
+    w.dt = b.dt = ox::kFloat;
+    w.shape = {K, 3 * N};
+    b.shape = {3 * N};
+    w.dev = std::make_shared<DevBuf>();
+    b.dev = std::make_shared<DevBuf>();
+    IDEV_CUDA(cudaMalloc(&w.dev->p, w.nbytes()));
+    IDEV_CUDA(cudaMalloc(&b.dev->p, b.nbytes()));
+    for (int j = 0; j < 3; ++j) {
+      const T& wj = inits[n.inputs[1 + 2 * j]];
+      const T& bj = inits[n.inputs[2 + 2 * j]];
+      IDEV_CUDA(cudaMemcpy2D(w.d<float>() + j * N, 3 * N * sizeof(float), wj.d<float>(),
+                             N * sizeof(float), N * sizeof(float), K, cudaMemcpyDeviceToDevice));
+      IDEV_CUDA(cudaMemcpy(b.d<float>() + j * N, bj.d<float>(), N * sizeof(float),
+                           cudaMemcpyDeviceToDevice));
+    }
+    inits[wname] = w;
+    inits[bname] = b;
+    init_names.insert(wname);
+    init_names.insert(bname);
   }
   bool is_2d_f32_init(const std::string& name) {
     auto it = inits.find(name);
@@ -397,6 +549,21 @@ struct InfercGraph {
 
   // ----------------------------------------------------------------- run
   void run(cudaStream_t stream) {
+    use_planes = true;
+    IDEV_CUDA(cudaMemsetAsync(range, 0, sizeof(int), stream));
+    run_once(stream);
+    int hr = 0;
+    IDEV_CUDA(cudaMemcpyAsync(&hr, range, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    IDEV_CUDA(cudaStreamSynchronize(stream));
+    if (hr) {  // a value fp16 cannot carry: the same run on the fp32 operands
+      ++range_reruns;
+      use_planes = false;
+      run_once(stream);
+      use_planes = true;
+    }
+  }
+
+  void run_once(cudaStream_t stream) {
     st = stream;
     outputs.clear();
     static const bool trace = [] {
@@ -418,6 +585,7 @@ struct InfercGraph {
       const ox::Node& n = *s.node;
       try {
         if (s.fused_gemm) run_fused_gemm(s, get, tape);
+        else if (s.qkv_attn) run_qkv_attention(s, get, tape);
         else run_node(n, get, tape);
       } catch (const Error& e) {
         throw Error(e.code, std::string(e.what()) + " (node " + n.name + ", " + n.op_type + ")");
@@ -465,20 +633,29 @@ struct InfercGraph {
     if (x.dt != ox::kFloat || x.shape.empty()) fail("MatMul: only float32 supported in v1");
     const int64_t K = w.shape[0], N = w.shape[1];
     if (x.shape.back() != K) fail("MatMul: inner dim mismatch (K!=K)");
-    to_dev(x);
+    const bool planes = use_planes && x.pl;
+    if (!planes) to_dev(x);
     std::vector<int64_t> os = x.shape;
     os.back() = N;
     const int64_t M = x.numel() / K;
     Epilogue ep;
     ep.bias = b.d<float>();
     ep.bias_mode = 1;
+    auto gemm = [&](const Epilogue& e, float* y) {
+      if (planes) {
+        const PreparedWeight p = prepared_weight(w.d<float>(), K, N, N, false, st);
+        launch_gemm_f16s(planes_a(x), p.hi, p.lo, p.kp, p.scale2, range, y, N, SplitOut(), M, N,
+                         K, e, st);
+      } else {
+        launch_gemm_op(x.d<float>(), K, false, w.d<float>(), N, false, y, N, M, N, K, e, st);
+      }
+    };
     T r;
     if (!s.resid.empty()) {
       r = get(s.resid);
       if (r.dt != ox::kFloat || r.shape != os) {  // not a plain residual: no fusion of it
         T y = alloc(ox::kFloat, os);
-        launch_gemm_op(x.d<float>(), K, false, w.d<float>(), N, false, y.d<float>(), N, M, N, K,
-                       ep, st);
+        gemm(ep, y.d<float>());
         tape[s.out] = binary(GLUE_ADD, y, r);
         return;
       }
@@ -487,9 +664,97 @@ struct InfercGraph {
       ep.ldr = N;
     }
     T y = alloc(ox::kFloat, os);
-    launch_gemm_op(x.d<float>(), K, false, w.d<float>(), N, false, y.d<float>(), N, M, N, K, ep,
-                   st);
+    gemm(ep, y.d<float>());
     tape[s.out] = y;
+  }
+
+  // FusedQKV + FusedAttention: x's planes (its producer's, or split here) ->
+  // one QKV GEMM over [Wq | Wk | Wv] writing q, k, v as fp16 planes of one
+  // [M, 3N] pair -> split-fp16 attention reading them in place. Without
+  // planes (a range rerun, or shapes the fp16 kernels do not take) the two
+  // nodes run as they are.
+  template <typename Get>
+  void run_qkv_attention(const Step& s, Get& get, std::unordered_map<std::string, T>& tape) {
+    const ox::Node& n = *s.node;
+    const ox::Node& at = *s.attn;
+    T x = get(n.inputs[0]);
+    const T& w = inits[s.wcat];
+    const T& bc = inits[s.bcat];
+    const int64_t K = w.shape[0], N3 = w.shape[1], N = N3 / 3;
+    T m;
+    const bool has_mask = at.inputs.size() >= 4 && !at.inputs[3].empty();
+    if (has_mask) m = get(at.inputs[3]);
+    bool ok = use_planes && x.dt == ox::kFloat && x.shape.size() == 3 && x.shape[2] == K &&
+              (!has_mask || (m.dt == ox::kBool && m.shape.size() <= 4));
+    AttnF16Args af{};
+    T qkv, o;
+    if (ok) {
+      const int64_t B = x.shape[0], S = x.shape[1], M = B * S;
+      af.ld = N3;
+      af.bstride = S * N3;
+      af.B = B;
+      af.S = S;
+      af.nH = N / 64;
+      af.scale = 0.125f;
+      af.fill = at.attr_float("fill", -3.0e38f);
+      af.ldo = N;
+      af.bstride_o = S * N;
+      if (has_mask) {  // right-aligned broadcast strides over [B, nH, S, S] (attention.cc:17-29)
+        const int64_t full[4] = {B, af.nH, S, S};
+        const int r = (int)m.shape.size();
+        int64_t stride = 1;
+        for (int i = r - 1; i >= 0 && ok; --i) {
+          const int od = 4 - (r - i);
+          ok = m.shape[i] == 1 || m.shape[i] == full[od];
+          af.ms[od] = m.shape[i] == 1 ? 0 : stride;
+          stride *= m.shape[i];
+        }
+      }
+      qkv.dt = ox::kFloat;
+      qkv.shape = {M, N3};
+      alloc_planes(qkv);
+      af.qh = qkv.phi(); af.ql = qkv.plo();
+      af.kh = af.qh + N; af.kl = af.ql + N;
+      af.vh = af.qh + 2 * N; af.vl = af.ql + 2 * N;
+      o.dt = ox::kFloat;
+      o.shape = x.shape;
+      o.shape[2] = N;
+      if (planes_only.count(s.out)) {
+        af.so = planes_out(o);
+        o.f32 = false;
+      } else {
+        o = alloc(ox::kFloat, o.shape);
+        af.out = o.d<float>();
+      }
+      ok = ok && attention_f16_supported(af);
+      if (ok) {
+        if (!x.pl) {  // split x here
+          to_dev(x);
+          alloc_planes(x);
+          launch_split_rows_f16(x.d<float>(), M, K, K, x.phi(), x.plo(), K, range, st);
+        }
+        if (has_mask) {
+          to_dev(m);
+          af.mask = m.d<uint8_t>();
+        }
+        const PreparedWeight p = prepared_weight(w.d<float>(), K, N3, N3, false, st);
+        Epilogue ep;
+        ep.bias = bc.d<float>();
+        ep.bias_mode = 1;
+        SplitOut so;
+        so.hi = qkv.phi();
+        so.lo = qkv.plo();
+        so.ld = N3;
+        so.range = range;
+        launch_gemm_f16s(planes_a(x), p.hi, p.lo, p.kp, p.scale2, range, nullptr, N3, so, M, N3, K,
+                         ep, st);
+        launch_attention_f16(af, st);
+        tape[s.out] = o;
+        return;
+      }
+    }
+    run_node(n, get, tape);
+    run_node(at, get, tape);
   }
 
   // ------------------------------------------------------------ elementwise
@@ -970,7 +1235,10 @@ struct InfercGraph {
     const std::string& op = n.op_type;
     auto in = [&](size_t i) -> T& {
       if (i >= n.inputs.size() || n.inputs[i].empty()) fail(op + ": missing input " + std::to_string(i));
-      return get(n.inputs[i]);
+      T& t = get(n.inputs[i]);
+      if (!t.f32 && !(op == "FusedMatMulAddGELU" && i == 0 && use_planes))
+        fail("executor: '" + n.inputs[i] + "' exists only as fp16 planes");
+      return t;
     };
     auto set = [&](T t) {
       if (!n.outputs.empty()) tape[n.outputs[0]] = std::move(t);
@@ -1053,17 +1321,33 @@ struct InfercGraph {
       const int64_t K = w.shape[0], N = w.shape[1];
       if (x.shape.empty() || x.shape.back() != K) fail("FusedMatMulAddGELU: K mismatch");
       if (b.numel() != N) fail("FusedMatMulAddGELU: bias length mismatch");
-      to_dev(x);
       to_dev(w);
       to_dev(b);
       std::vector<int64_t> os = x.shape;
       os.back() = N;
-      T o = alloc(ox::kFloat, os);
       Epilogue ep;
       ep.bias = b.d<float>();
       ep.bias_mode = 1;
       ep.act = ACT_GELU_ERF;
       const int64_t M = x.numel() / K;
+      if (use_planes && x.pl && init_names.count(n.inputs[1]) && K % 8 == 0) {
+        const PreparedWeight p = prepared_weight(w.d<float>(), K, N, N, false, st);
+        T o;
+        o.dt = ox::kFloat;
+        o.shape = os;
+        SplitOut so;
+        if (planes_only.count(n.outputs[0]) && N % 16 == 0) {
+          so = planes_out(o);  // the next GEMM's A; no fp32 copy is stored
+          o.f32 = false;
+        } else {
+          o = alloc(ox::kFloat, os);
+        }
+        launch_gemm_f16s(planes_a(x), p.hi, p.lo, p.kp, p.scale2, range,
+                         o.f32 ? o.d<float>() : nullptr, N, so, M, N, K, ep, st);
+        return set(o);
+      }
+      to_dev(x);
+      T o = alloc(ox::kFloat, os);
       if (init_names.count(n.inputs[1]))
         launch_gemm_op(x.d<float>(), K, false, w.d<float>(), N, false, o.d<float>(), N, M, N, K, ep, st);
       else
@@ -1079,8 +1363,11 @@ struct InfercGraph {
       to_dev(g);
       to_dev(b);
       T o = alloc(ox::kFloat, x.shape);
+      SplitOut sp;  // also the fp16 planes when a split-fp16 GEMM reads the result
+      if (use_planes && want_planes.count(n.outputs[0]) && feat % 128 == 0 && feat <= 1024)
+        sp = planes_out(o);
       launch_layernorm(x.d<float>(), g.d<float>(), b.d<float>(), o.d<float>(),
-                       feat ? x.numel() / feat : 0, feat, n.attr_float("epsilon", 1e-5f), st);
+                       feat ? x.numel() / feat : 0, feat, n.attr_float("epsilon", 1e-5f), st, sp);
       return set(o);
     }
     if (op == "FusedAttention") {  // attention.cc:32-100, executor.cc:218-224

@@ -59,6 +59,23 @@ def test_distilbert_plan_full_config_c0_c4_and_rerun():
     np.testing.assert_allclose(got, e["c0_logits"], atol=LOGIT_TOL, rtol=0)
 
 
+def test_distilbert_plan_fp16_range_rerun():
+    """Activations beyond fp16's range (embedding LayerNorm gamma 1e5): the
+    executor's split-fp16 planes raise the range flag and the run is redone
+    on the fp32 operands; the logits still match the reference."""
+    from inferc_b200 import structs
+    from oracle import oracle
+    cfg = synth.EncoderConfig(**make_golden.SMALL_ENC)
+    w = synth.encoder_weights(cfg, seed=9)
+    w["emb_ln_g"] = np.full_like(w["emb_ln_g"], 1e5)
+    ids, mask = synth.encoder_inputs(3, 32, seed=4, vocab=cfg.vocab, variable_lengths=True)
+    ref = oracle.port().encoder_forward(structs.encoder_struct(cfg, w), ids, mask, 2)
+    g = executor.Graph(plan_synth.distilbert_plan(cfg, w))
+    for _ in range(2):
+        got = g.run_host({"input_ids": ids, "attention_mask": mask}, ["logits"])["logits"]
+        np.testing.assert_allclose(got, ref, atol=LOGIT_TOL, rtol=1e-4)
+
+
 @pytest.mark.parametrize("full", [False, True], ids=["small", "gpt2-small"])
 def test_gpt2_plans_decode_tokens(full):
     d = np.load(os.path.join(GOLD, "decode.npz"))
