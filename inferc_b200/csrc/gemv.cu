@@ -397,22 +397,45 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ int64_t si[kWarps];
   __shared__ bool last;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t words = a.K / 8;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  auto wload = [&](int64_t r, int64_t wi) {
+    return (r < a.N && wi < words)
+               ? __ldg(reinterpret_cast<const uint32_t*>(a.w + r * (a.K / 2)) + wi)
+               : 0x88888888u;
+  };
+  // The weights do not depend on the previous kernel: the first row group's
+  // first kPre words per row are loaded before waiting on it.
+  constexpr int kPre = 4;
+  uint32_t pre[4][kPre];
+  {
+    const int64_t r0 = (int64_t)blockIdx.x * kWarps + wid;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int j = 0; j < kPre; ++j) pre[u][j] = wload(r0 + u * stride, lane + 32 * j);
+  }
   pdl_launch_dependents();
   pdl_wait();
   stage_x(a.x, a.ln_gamma, a.ln_beta, a.ln_eps, a.K, 0, a.K, xs, red);
-  const int64_t words = a.K / 8;
   const float4* x4 = reinterpret_cast<const float4*>(xs);
   float bv = -INFINITY;
   int64_t bi = INT64_MAX;
-  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  bool first = true;
   for (int64_t r0 = (int64_t)blockIdx.x * kWarps + wid; r0 < a.N; r0 += 4 * stride) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int64_t wi = lane; wi < words; wi += 32) {
+    int j = 0;
+    for (int64_t wi = lane; wi < words; wi += 32, ++j) {
       uint32_t wv[4];
+      if (first && j < kPre) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t r = r0 + u * stride;
-        wv[u] = r < a.N ? __ldg(reinterpret_cast<const uint32_t*>(a.w + r * (a.K / 2)) + wi) : 0x88888888u;
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int q = 0; q < kPre; ++q)
+            if (q == j) wv[u] = pre[u][q];
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) wv[u] = wload(r0 + u * stride, wi);
       }
       const float4 xa = x4[2 * wi], xb = x4[2 * wi + 1];
       const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -436,6 +459,7 @@ __global__ void __launch_bounds__(kThreads)
         if (better(v, r, bv, bi)) { bv = v; bi = r; }
       }
     }
+    first = false;
   }
   if (a.argmax_out == nullptr) return;
   if (lane == 0) { sv[wid] = bv; si[wid] = bi; }
