@@ -634,7 +634,7 @@ void launch_gemm_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl,
   if (ep.bias_mode == 1 && ep.act == ACT_NONE && ep.resid == nullptr) epi = EPI_BIAS;
   if (ep.bias_mode == 1 && ep.act == ACT_GELU_ERF && ep.resid == nullptr) epi = EPI_BIAS_GELU;
   if (ep.bias_mode == 1 && ep.act == ACT_NONE && ep.resid != nullptr) epi = EPI_BIAS_RESID;
-  if (as && gemm_f16s_2cta_usable(A, M, N, so.hi != nullptr) &&
+  if (as && gemm_f16s_2cta_usable(A, M, N, K, so.hi != nullptr) &&
       (!so.hi || ((epi == EPI_BIAS || epi == EPI_BIAS_GELU) && N % 16 == 0 && so.lo &&
                   so.range && aligned16(so.hi) && aligned16(so.lo) && so.ld % 8 == 0 &&
                   so.ld >= N && aligned16(ep.bias)))) {

@@ -417,19 +417,23 @@ int read_and_clear_f16_2cta_error() {
   return v;
 }
 
-bool gemm_f16s_2cta_usable(const F16GemmA& A, int64_t M, int64_t N, bool split_out) {
-  // Measured on the encoder's GEMMs (M = 32768), with the staged epilogues:
-  // ahead of the one-SM kernel where the result is written as fp16 planes
-  // (FFN1 358 vs 367 us, QKV 254 vs 264 us), behind it for the fp32
-  // residual epilogue (117 vs 113 us at K = 768). So by default it takes the
-  // split-output GEMMs; INFERC_GEMM_2CTA=1 uses it for every eligible GEMM,
-  // =0 for none.
+bool gemm_f16s_2cta_usable(const F16GemmA& A, int64_t M, int64_t N, int64_t K,
+                           bool split_out) {
+  // Measured on the encoder's GEMMs, with the staged epilogues: ahead of the
+  // one-SM kernel where the result is written as fp16 planes (FFN1 358 vs
+  // 367 us, QKV 254 vs 264 us at M = 32768); for the fp32 residual epilogue
+  // ahead only with a long K at large M (FFN2, K = 3072: 356 vs 365 us at
+  // M = 32768, level at 16384) and behind at K = 768 (113 vs 108 us) and at
+  // small M, where the one-SM kernel's tile width follows the wave count
+  // (M = 4096: 64 vs 50 us). So by default it takes the split-output GEMMs
+  // and fp32-output GEMMs with K >= 2048 and M >= 32768;
+  // INFERC_GEMM_2CTA=1 uses it for every eligible GEMM, =0 for none.
   static const int mode = [] {
     const char* e = std::getenv("INFERC_GEMM_2CTA");
     return e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
   }();
   if (A.a32 != nullptr || M < 512 || N < 256) return false;
-  return mode == 1 || (mode == -1 && split_out);
+  return mode == 1 || (mode == -1 && (split_out || (K >= 2048 && M >= 32768)));
 }
 
 void launch_gemm_f16s_2cta(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,

@@ -77,7 +77,7 @@ int read_and_clear_f16_range();
 // Two-SM (cta_group::2, 256-row) form of the split-fp16 GEMM for pre-split A
 // (gemm_f16s_2cta.cu): used for split-plane outputs unless INFERC_GEMM_2CTA=0
 // (=1: for every eligible GEMM).
-bool gemm_f16s_2cta_usable(const F16GemmA& A, int64_t M, int64_t N, bool split_out);
+bool gemm_f16s_2cta_usable(const F16GemmA& A, int64_t M, int64_t N, int64_t K, bool split_out);
 void launch_gemm_f16s_2cta(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,
                            const float* scale2, float* C, int64_t ldc, const SplitOut& so,
                            int64_t M, int64_t N, int64_t K, int epi, const Epilogue& ep,
