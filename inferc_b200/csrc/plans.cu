@@ -145,6 +145,69 @@ std::unique_ptr<Graph> capture(cudaStream_t st, Fn&& body) {
   return out;
 }
 
+// Sets the conditional of an IF node from a device flag (non-zero = run the
+// body), and counts the times it did.
+__global__ void set_if_from_flag(cudaGraphConditionalHandle h, const int* flag, int64_t* count) {
+  const int v = *reinterpret_cast<const volatile int*>(flag);
+  cudaGraphSetConditional(h, v != 0 ? 1u : 0u);
+  if (v != 0) ++*count;
+}
+
+// One graph that runs `main` and then, only when the device flag `flag` is
+// set by it, `fallback` (an IF conditional node whose body is captured on
+// `st2`): the choice is made on the device, with no host round trip.
+template <typename Main, typename Fallback>
+std::unique_ptr<Graph> capture_guarded(cudaStream_t st, cudaStream_t st2, int* flag,
+                                       int64_t* count, Main&& main, Fallback&& fallback) {
+  IDEV_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  cudaGraph_t g = nullptr;
+  bool in_body = false;
+  try {
+    cudaStreamCaptureStatus status;
+    const cudaGraphNode_t* deps = nullptr;
+    size_t nd = 0;
+    IDEV_CUDA(cudaStreamGetCaptureInfo(st, &status, nullptr, &g, &deps, &nd));
+    cudaGraphConditionalHandle h;
+    IDEV_CUDA(cudaGraphConditionalHandleCreate(&h, g, 0, 0));
+    IDEV_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), st));
+    main(st);
+    set_if_from_flag<<<1, 1, 0, st>>>(h, flag, count);
+    IDEV_LAUNCHED();
+    IDEV_CUDA(cudaStreamGetCaptureInfo(st, &status, nullptr, nullptr, &deps, &nd));
+    cudaGraphNodeParams cp = {};
+    cp.type = cudaGraphNodeTypeConditional;
+    cp.conditional.handle = h;
+    cp.conditional.type = cudaGraphCondTypeIf;
+    cp.conditional.size = 1;
+    cudaGraphNode_t cn;
+    IDEV_CUDA(cudaGraphAddNode(&cn, g, deps, nd, &cp));
+    IDEV_CUDA(cudaStreamUpdateCaptureDependencies(st, &cn, 1, cudaStreamSetCaptureDependencies));
+    cudaGraph_t body = cp.conditional.phGraph_out[0];
+    IDEV_CUDA(cudaStreamBeginCaptureToGraph(st2, body, nullptr, nullptr, 0,
+                                            cudaStreamCaptureModeThreadLocal));
+    in_body = true;
+    fallback(st2);
+    in_body = false;
+    IDEV_CUDA(cudaStreamEndCapture(st2, &body));
+  } catch (...) {
+    if (in_body) {
+      cudaGraph_t b = nullptr;
+      cudaStreamEndCapture(st2, &b);
+    }
+    cudaGraph_t gg = nullptr;
+    cudaStreamEndCapture(st, &gg);
+    if (gg) cudaGraphDestroy(gg);
+    cudaGetLastError();
+    throw;
+  }
+  IDEV_CUDA(cudaStreamEndCapture(st, &g));
+  auto out = std::make_unique<Graph>();
+  const cudaError_t e = cudaGraphInstantiate(&out->exec, g, 0);
+  cudaGraphDestroy(g);
+  IDEV_CUDA(e);
+  return out;
+}
+
 }  // namespace
 
 // ======================================================================
@@ -179,10 +242,19 @@ struct InfercEncoderPlan {
   int* f16_range = nullptr;
   int* range_host = nullptr;  // pinned
   std::map<std::tuple<int64_t, int64_t, bool>, std::unique_ptr<Graph>> graphs;
-  int64_t range_fallbacks = 0;  // batches rerun on the 3xTF32 graph
+  // (B, S) -> split-fp16 forward with the 3xTF32 rerun as a device-side IF
+  // node (no host round trip per batch); empty when conditional nodes are
+  // unavailable and the host checks the flag instead.
+  std::map<std::pair<int64_t, int64_t>, std::unique_ptr<Graph>> guarded;
+  bool guarded_ok = true;
+  cudaStream_t stream2 = nullptr;     // captures the IF body
+  int64_t* fallback_count = nullptr;  // device: batches rerun by the IF body
+  int64_t range_fallbacks = 0;  // batches rerun on the 3xTF32 graph (host-checked path)
 
   ~InfercEncoderPlan() {
     graphs.clear();
+    guarded.clear();
+    if (stream2) cudaStreamDestroy(stream2);
     if (stream) cudaStreamDestroy(stream);
     if (range_host) cudaFreeHost(range_host);
   }
@@ -343,13 +415,36 @@ struct InfercEncoderPlan {
   }
 
   // Inputs already in plan buffers `ids`, `mask`; runs on `st` after the plan
-  // stream's previous work.
-  // With the split-fp16 path this waits for the batch on `st`, to check the
-  // range flag (and rerun the batch on the 3xTF32 path when it is set).
+  // stream's previous work. With the split-fp16 path, one graph per (B, S)
+  // holds the split-fp16 forward and, as a device-side IF node on the range
+  // flag, the 3xTF32 rerun of the batch, so nothing waits on the host. Where
+  // conditional nodes cannot be built, this waits for the batch on `st` to
+  // check the flag instead.
   void run_graph(int64_t B, int64_t S, cudaStream_t st) {
     if (!f16) {
       IDEV_CUDA(cudaGraphLaunch(graph_for(B, S, false).exec, st));
       return;
+    }
+    if (guarded_ok) {
+      auto key = std::make_pair(B, S);
+      auto it = guarded.find(key);
+      if (it == guarded.end()) {
+        graph_for(B, S, true);  // eager runs configure both forms' kernels
+        graph_for(B, S, false);
+        IDEV_CUDA(cudaStreamSynchronize(stream));
+        try {
+          it = guarded.emplace(key, capture_guarded(stream, stream2, f16_range, fallback_count,
+                                                    [&](cudaStream_t s1) { forward(B, S, s1, true); },
+                                                    [&](cudaStream_t s2) { forward(B, S, s2, false); }))
+                   .first;
+        } catch (const Error&) {
+          guarded_ok = false;  // conditional nodes unavailable: check on the host
+        }
+      }
+      if (guarded_ok) {
+        IDEV_CUDA(cudaGraphLaunch(it->second->exec, st));
+        return;
+      }
     }
     Graph& g = graph_for(B, S, true);
     IDEV_CUDA(cudaMemsetAsync(f16_range, 0, sizeof(int), st));
@@ -442,6 +537,9 @@ static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t 
     p->f16_range = m.alloc<int>(1);
     IDEV_CUDA(cudaMemset(p->f16_range, 0, sizeof(int)));
     IDEV_CUDA(cudaMallocHost(&p->range_host, sizeof(int)));
+    p->fallback_count = m.alloc<int64_t>(1);
+    IDEV_CUDA(cudaMemset(p->fallback_count, 0, sizeof(int64_t)));
+    IDEV_CUDA(cudaStreamCreateWithFlags(&p->stream2, cudaStreamNonBlocking));
   }
   IDEV_CUDA(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
 }
@@ -926,7 +1024,15 @@ int inferc_dev_encoder_run_host(inferc_encoder_t p, const int64_t* ids, const in
 }
 
 int64_t inferc_dev_encoder_range_fallbacks(inferc_encoder_t p) {
-  return p ? p->range_fallbacks : -1;
+  if (!p) return -1;
+  int64_t dev_count = 0;
+  if (p->fallback_count &&
+      cudaMemcpy(&dev_count, p->fallback_count, sizeof(int64_t), cudaMemcpyDeviceToHost) !=
+          cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return p->range_fallbacks + dev_count;
 }
 
 void inferc_dev_encoder_destroy(inferc_encoder_t p) { delete p; }

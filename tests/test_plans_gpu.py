@@ -104,6 +104,8 @@ def test_encoder_fp16_range_fallback():
     for _ in range(2):
         got = p.run_host(ids, mask)
         np.testing.assert_allclose(got, ref, atol=LOGIT_TOL, rtol=1e-4)
+    from inferc_b200 import lib
+    assert lib.load().inferc_dev_encoder_range_fallbacks(p._h) == 2
 
 
 def test_encoder_errors(full_encoder, enc_gold):
