@@ -549,11 +549,15 @@ void launch_f16s_width(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl
   int bn = 256;
   for (int cand : {192, 128})
     if (util(cand) > util(bn) + 1e-9) bn = cand;
+  // Small M (a handful of tiles): narrower tiles spread the weight stream over
+  // more SMs (config 0's M = 128 GEMMs).
+  const int64_t tiles128 = ((N + 127) / 128) * ((M + BM - 1) / BM);
+  if (tiles128 * 4 <= sms) bn = (tiles128 * 8 <= sms && N >= 32) ? 32 : 64;
   static const int forced = [] {
     const char* e = std::getenv("INFERC_GEMM_BN");
     return e ? std::atoi(e) : 0;
   }();
-  if (forced == 128 || forced == 192 || forced == 256) bn = forced;
+  if (forced == 32 || forced == 64 || forced == 128 || forced == 192 || forced == 256) bn = forced;
   const bool bk64 = AS && K <= 1024;
   if (bn == 256) {
     if (bk64)
@@ -569,9 +573,15 @@ void launch_f16s_width(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl
     else
       launch_f16s<192, 32, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
                                              N, K, ep, st);
-  } else {
+  } else if (bn == 128) {
     launch_f16s<128, 32, 6, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
                                            N, K, ep, st);
+  } else if (bn == 64) {
+    launch_f16s<64, 32, 8, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
+                                          N, K, ep, st);
+  } else {
+    launch_f16s<32, 32, 8, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
+                                          N, K, ep, st);
   }
 }
 

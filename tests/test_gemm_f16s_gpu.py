@@ -148,7 +148,9 @@ def test_f16s_planes_chain():
 
 @pytest.mark.parametrize("M,K,N", [(512, 768, 256), (1000, 768, 2304), (4096, 3072, 768),
                                    (777, 96, 300), (32768, 768, 3072), (4096, 768, 768),
-                                   (8192, 768, 768), (4000, 3072, 768), (32768, 3072, 768)])
+                                   (8192, 768, 768), (4000, 3072, 768), (32768, 3072, 768),
+                                   (128, 768, 768), (128, 3072, 768), (100, 768, 3072),
+                                   (1, 768, 2)])
 def test_f16s_planes_shapes(M, K, N):
     """A as fp16 planes (the plan's form) with the bias + residual epilogue
     (fp32 out), ragged M / N / K included: whole 256-column tiles take the
@@ -176,7 +178,8 @@ def test_f16s_planes_shapes(M, K, N):
 
 
 @pytest.mark.parametrize("M,K,N,act", [(777, 768, 784, 1), (1000, 768, 2304, 0),
-                                       (513, 3072, 272, 1)])
+                                       (513, 3072, 272, 1), (128, 768, 2304, 0),
+                                       (128, 768, 3072, 1), (77, 768, 48, 1)])
 def test_f16s_split_out_shapes(M, K, N, act):
     """Split-plane output (bias, or bias + GELU) with ragged M and an N whose
     last 256-column tile is partial (staged and per-row epilogues in one
