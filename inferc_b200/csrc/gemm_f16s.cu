@@ -577,11 +577,20 @@ void launch_f16s_width(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl
     launch_f16s<128, 32, 6, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
                                            N, K, ep, st);
   } else if (bn == 64) {
-    launch_f16s<64, 32, 8, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                          N, K, ep, st);
+    // narrow tiles stream mostly A: 128-byte TMA rows (BK = 64) for the planes
+    if (AS)
+      launch_f16s<64, 64, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
+                                            N, K, ep, st);
+    else
+      launch_f16s<64, 32, 8, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
+                                            N, K, ep, st);
   } else {
-    launch_f16s<32, 32, 8, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                          N, K, ep, st);
+    if (AS)
+      launch_f16s<32, 64, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
+                                            N, K, ep, st);
+    else
+      launch_f16s<32, 32, 8, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
+                                            N, K, ep, st);
   }
 }
 

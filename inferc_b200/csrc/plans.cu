@@ -246,7 +246,12 @@ struct InfercEncoderPlan {
   // node (no host round trip per batch); empty when conditional nodes are
   // unavailable and the host checks the flag instead.
   std::map<std::pair<int64_t, int64_t>, std::unique_ptr<Graph>> guarded;
-  bool guarded_ok = true;
+  // INFERC_ENCODER_GUARD=0: host-checked flag instead (ncu profiles kernel
+  // nodes only in graphs without conditional nodes)
+  bool guarded_ok = [] {
+    const char* e = std::getenv("INFERC_ENCODER_GUARD");
+    return !(e && e[0] == '0');
+  }();
   cudaStream_t stream2 = nullptr;     // captures the IF body
   int64_t* fallback_count = nullptr;  // device: batches rerun by the IF body
   int64_t range_fallbacks = 0;  // batches rerun on the 3xTF32 graph (host-checked path)
