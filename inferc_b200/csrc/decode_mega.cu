@@ -19,10 +19,25 @@
 // keeps streaming across barriers. Each output column is produced by exactly
 // one CTA with a fixed summation order (deterministic).
 //
-// Data produced inside the kernel (x, qkv, ctx, f, the per-CTA bests) is read
-// with L2-coherent loads (__ldcg), never through L1. Grid barriers and
-// mbarrier waits are bounded: on a timeout the kernel sets an error flag,
-// every CTA leaves at its next barrier, and the host reports the failure.
+// Inside a step the phases are not separated by grid barriers. Activations
+// (x, qkv, the projection partials, f) travel as tagged 64-bit words,
+// (tag << 32) | fp32 bits, each word written once per phase instance with a
+// tag unique to that instance; a reader loads the words it needs and re-reads
+// any whose tag is not yet the expected one. The load is the wait, so a phase
+// starts as soon as its own inputs have landed, with no release fence and no
+// extra L2 round trip for a barrier. Only the end of a step keeps a grid
+// barrier: the argmax needs every CTA's best, and it orders the step's
+// KV-cache appends before the next step's reads.
+//
+// Overwrites are safe without double buffers because every CTA takes part
+// in the FC and FP phases: a buffer is rewritten only by a phase whose inputs
+// depend (through tagged words) on every CTA having finished the phase that
+// read it. The layer input alternates between two buffers for the same
+// reason. A reader that sees a newer tag than it expects reports an error.
+// All data produced inside the kernel is read from L2, never through L1.
+// Every wait (tags, mbarriers, the grid barrier) is bounded: on a timeout the
+// kernel sets an error flag, every CTA leaves at its next check, and the host
+// reports the failure.
 #include <cuda.h>
 
 #include <cfloat>
@@ -115,6 +130,55 @@ struct Smem {
   unsigned nbar;  // barriers passed (thread 0)
 };
 
+// ---- tagged activation words
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p));
+  return w;
+}
+
+__device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t tag) {
+  const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ float word_f(uint64_t w) { return __uint_as_float((uint32_t)w); }
+
+// Waits until every word of w[0:N) (first loads already issued by the
+// caller; a slot that needs no word is preset to tag << 32) carries `tag`:
+// each round re-reads all stale words at once, so a batch that was loaded
+// too early costs one L2 round trip per round, not one per word. Bounded: a
+// newer tag (an ordering fault), a timeout or an error raised elsewhere sets
+// the error flags, zeroes the values and returns false.
+template <int N, typename Addr>
+__device__ __forceinline__ bool settle(uint64_t (&w)[N], uint32_t tag, Addr addr,
+                                       const MegaArgs& a, Smem& sm) {
+  unsigned long long t0 = 0;
+  for (uint32_t round = 0;; ++round) {
+    bool ready = true, newer = false;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const uint32_t wt = (uint32_t)(w[i] >> 32);
+      ready = ready && wt == tag;
+      newer = newer || (int)(wt - tag) > 0;
+    }
+    if (ready) return true;
+    bool fail = newer;
+    if (round == 0) t0 = gclock();
+    else if ((round & 15) == 0) fail = fail || gclock() - t0 > kMegaWaitNs || *(volatile int*)a.err;
+    if (fail) {
+      atomicExch(a.err, 1);
+      sm.abort_flag = 1;
+#pragma unroll
+      for (int i = 0; i < N; ++i) w[i] = (uint64_t)tag << 32;
+      return false;
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if ((uint32_t)(w[i] >> 32) != tag) w[i] = ld_word(addr(i));
+  }
+}
+
 #ifdef INFERC_DECODE_PROFILE
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
@@ -123,8 +187,6 @@ __device__ __forceinline__ unsigned long long gtimer() {
 }
 #endif
 
-// Grid-wide barrier (all CTAs co-resident: cooperative launch). Returns
-// false when the kernel must stop (timeout here or elsewhere).
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -136,11 +198,7 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 // stop (timeout here or an error flagged elsewhere).
 // Split in two so that thread 0 can issue the next copies between its
 // arrival and its wait.
-__device__ void grid_arrive(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
-#ifdef INFERC_DECODE_PROFILE
-  if (a.prof && step == 1 && blockIdx.x == 0 && threadIdx.x == 0 && tag >= 0)
-    a.prof[2 * tag] = gtimer();
-#endif
+__device__ void grid_arrive(const MegaArgs& a, Smem& sm) {
   __syncthreads();  // the CTA's outputs of the phase precede the release below
   if (threadIdx.x == 0) {
     sm.target = (++sm.nbar) * gridDim.x;
@@ -148,7 +206,7 @@ __device__ void grid_arrive(const MegaArgs& a, Smem& sm, int tag = -1, int step 
   }
 }
 
-__device__ bool grid_wait(const MegaArgs& a, Smem& sm, int tag = -1, int step = -1) {
+__device__ bool grid_wait(const MegaArgs& a, Smem& sm) {
   if (threadIdx.x == 0) {
     const unsigned target = sm.target;
     uint32_t i = 0;
@@ -160,11 +218,21 @@ __device__ bool grid_wait(const MegaArgs& a, Smem& sm, int tag = -1, int step = 
       }
     }
     sm.abort_flag = *(volatile int*)a.err;
-#ifdef INFERC_DECODE_PROFILE
-    if (a.prof && step == 1 && blockIdx.x == 0 && tag >= 0) a.prof[2 * tag + 1] = gtimer();
-#endif
   }
   __syncthreads();
+  return sm.abort_flag == 0;
+}
+
+// End of a phase of this CTA: all threads are past their reads of the slots
+// and their writes; false when a wait of the phase failed. With
+// -DINFERC_DECODE_PROFILE, CTA 0 stamps the global timer at phase q of step 1.
+__device__ __forceinline__ bool phase_end(const MegaArgs& a, Smem& sm, int q, int step) {
+  __syncthreads();
+#ifdef INFERC_DECODE_PROFILE
+  if (a.prof && step == 1 && blockIdx.x == 0 && threadIdx.x == 0) a.prof[q + 1] = gtimer();
+#else
+  (void)a; (void)q; (void)step;
+#endif
   return sm.abort_flag == 0;
 }
 
@@ -288,23 +356,28 @@ __device__ void drain(Smem& sm) {
   __syncthreads();
 }
 
-// Stages x (global, written in this kernel) into sm.xs, normalised with
-// (g, b) when g != null (two-pass mean / biased variance, as rt::LayerNorm).
-__device__ void stage_input(const float* x, int K, const float* g, const float* b, float eps,
-                            Smem& sm) {
+// Stages x (tagged words written in this kernel with `tag`) into sm.xs,
+// normalised with (g, b) when g != null (two-pass mean / biased variance, as
+// rt::LayerNorm).
+__device__ void stage_input(const uint64_t* x, uint32_t tag, int K, const float* g,
+                            const float* b, float eps, Smem& sm, const MegaArgs& a) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   // K <= 3072: at most 12 elements per thread; x, gamma and beta loads are
   // all issued before any is used.
+  uint64_t xw[12];
   float v[12], gv[12], bv[12];
 #pragma unroll
   for (int i = 0; i < 12; ++i) {
     const int k = tid + i * kMegaThreads;
-    v[i] = k < K ? __ldcg(x + k) : 0.f;
+    xw[i] = k < K ? ld_word(x + k) : (uint64_t)tag << 32;
     if (g != nullptr) {  // shared (prefetched) or global
       gv[i] = k < K ? g[k] : 0.f;
       bv[i] = k < K ? b[k] : 0.f;
     }
   }
+  settle(xw, tag, [&](int i) { return x + tid + i * kMegaThreads; }, a, sm);
+#pragma unroll
+  for (int i = 0; i < 12; ++i) v[i] = word_f(xw[i]);
   if (g == nullptr) {
 #pragma unroll
     for (int i = 0; i < 12; ++i) {
@@ -385,7 +458,8 @@ struct EpiIn {
 };
 
 __device__ __forceinline__ EpiIn gemv_preload(const MegaPanels& m, const float* bias,
-                                              const float* resid) {
+                                              const uint64_t* resid, uint32_t rtag,
+                                              const MegaArgs& a, Smem& sm) {
   EpiIn e{{0.f, 0.f}};
   const int tid = threadIdx.x;
   if (tid < m.P) {
@@ -395,7 +469,11 @@ __device__ __forceinline__ EpiIn gemv_preload(const MegaPanels& m, const float* 
       const int col = p * m.P + tid;
       if (p < m.npanels && col < m.N) {
         float v = __ldg(bias + col);
-        if (resid) v += __ldcg(resid + col);
+        if (resid) {
+          uint64_t rw[1] = {ld_word(resid + col)};
+          settle(rw, rtag, [&](int) { return resid + col; }, a, sm);
+          v += word_f(rw[0]);
+        }
         e.add[j] = v;
       }
     }
@@ -404,10 +482,10 @@ __device__ __forceinline__ EpiIn gemv_preload(const MegaPanels& m, const float* 
 }
 
 // y[col] = act(xs . panel[:, c] + bias[col] (+ resid[col])) for this CTA's
-// panels (slots 2*pair, 2*pair+1), both panels in one pass. resid may alias
-// y (each column is read and written by one thread).
+// panels (slots 2*pair, 2*pair+1), both panels in one pass; y is written as
+// tagged words with `ytag`.
 __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, const EpiIn& e,
-                           float* y, int act, Smem& sm, const MegaArgs& a, int ptag = -1) {
+                           uint64_t* y, uint32_t ytag, int act, Smem& sm, const MegaArgs& a) {
   const int tid = threadIdx.x;
   const int P = m.P, K = m.K;
   const int P4 = P / 4;                  // float4 columns per row
@@ -470,7 +548,7 @@ __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, 
       float t = 0.f;
       for (int q = 0; q < nw; ++q) t += sm.red[(j * nw + q) * P + tid];
       const int col = (blockIdx.x + j * gridDim.x) * P + tid;
-      if (col < m.N) y[col] = apply_act(t + e.add[j], act);
+      if (col < m.N) st_word(y + col, apply_act(t + e.add[j], act), ytag);
     }
   }
   __syncthreads();
@@ -481,7 +559,7 @@ __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, 
 // token at position pos, then out = softmax(q.k_j / sqrt(hd)) v over j <= pos.
 // Loads are issued in independent batches (the cache is read from L2).
 __device__ void attention_head(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
-                               Smem& sm, int h, bool append, float* ctx_out) {
+                               Smem& sm, int h, bool append, float* ctx_out, uint32_t qtag) {
 
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, hd = a.hd, H = a.H;
   float* qs = scr;             // [hd]
@@ -492,9 +570,12 @@ __device__ void attention_head(const MegaArgs& a, const MegaLayer& L, int64_t po
   float* kh = L.kc + (size_t)h * a.max_len * hd;
   float* vh = L.vc + (size_t)h * a.max_len * hd;
   if (tid < hd) {
-    qs[tid] = __ldcg(a.qkv + h * hd + tid);
-    kn[tid] = __ldcg(a.qkv + H + h * hd + tid);
-    vn[tid] = __ldcg(a.qkv + 2 * H + h * hd + tid);
+    const uint64_t* qp = a.tqkv + h * hd + tid;
+    uint64_t w3[3] = {ld_word(qp), ld_word(qp + H), ld_word(qp + 2 * H)};
+    settle(w3, qtag, [&](int i) { return qp + i * H; }, a, sm);
+    qs[tid] = word_f(w3[0]);
+    kn[tid] = word_f(w3[1]);
+    vn[tid] = word_f(w3[2]);
     if (append) {
       kh[pos * hd + tid] = kn[tid];
       vh[pos * hd + tid] = vn[tid];
@@ -596,8 +677,9 @@ __device__ void attention_head(const MegaArgs& a, const MegaLayer& L, int64_t po
 // tid + 256, ...; loads the K and V rows together (one L2 round trip per
 // key batch), keeps an online-softmax partial (m, l, o[64]); partials are
 // merged with a block max and shuffle sums.
-__device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
-                                 Smem& sm, int h, bool append, float* ctx_out) {
+__device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t pos,
+                                              float* scr, Smem& sm, int h, bool append,
+                                              float* ctx_out, uint32_t qtag) {
   constexpr int HD = 64;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, H = a.H;
   constexpr int nw = kMegaThreads / 32;
@@ -608,9 +690,12 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
   float* kh = L.kc + (size_t)h * a.max_len * HD;
   float* vh = L.vc + (size_t)h * a.max_len * HD;
   if (tid < HD) {
-    qs[tid] = __ldcg(a.qkv + h * HD + tid);
-    kn[tid] = __ldcg(a.qkv + H + h * HD + tid);
-    vn[tid] = __ldcg(a.qkv + 2 * H + h * HD + tid);
+    const uint64_t* qp = a.tqkv + h * HD + tid;
+    uint64_t w3[3] = {ld_word(qp), ld_word(qp + H), ld_word(qp + 2 * H)};
+    settle(w3, qtag, [&](int i) { return qp + i * H; }, a, sm);
+    qs[tid] = word_f(w3[0]);
+    kn[tid] = word_f(w3[1]);
+    vn[tid] = word_f(w3[2]);
     if (append) {
       kh[pos * HD + tid] = kn[tid];
       vh[pos * HD + tid] = vn[tid];
@@ -711,42 +796,56 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
 }
 
 // FC-phase input: xm = xa + b_proj + sum_h part[h] (heads in order); CTA 0
-// publishes xm (the FP residual); then LN2 in place.
+// publishes xm (the FP residual, tagged xm_tag); then LN2 in place.
 __device__ void stage_attn_residual(const MegaArgs& a, const float* proj_b, const float* g,
-                                    const float* b, const float* xa, float* xm, Smem& sm) {
+                                    const float* b, const uint64_t* xa, uint32_t xa_tag,
+                                    uint32_t part_tag, uint32_t xm_tag, Smem& sm) {
   const int tid = threadIdx.x, H = a.H;
   // All loads of the thread (up to 3 k's x 12 heads + x) are issued before
   // any is used: one L2 round trip, not one per k.
   constexpr int kK = 3, kHeads = 16;
-  float p[kK][kHeads], xv[kK], bp[kK];
+  uint64_t p[kK * kHeads], xw[kK];  // p[i * kHeads + h]: head h at k = tid + 256 i
+  float bp[kK];
 #pragma unroll
   for (int i = 0; i < kK; ++i) {
     const int k = tid + i * kMegaThreads;
     const bool in = k < H;
 #pragma unroll
     for (int h = 0; h < kHeads; ++h)
-      p[i][h] = (in && h < a.heads) ? __ldcg(a.part + (size_t)h * H + k) : 0.f;
-    xv[i] = in ? __ldcg(xa + k) : 0.f;
+      p[i * kHeads + h] = (in && h < a.heads) ? ld_word(a.tpart + (size_t)h * H + k)
+                                              : (uint64_t)part_tag << 32;
+    xw[i] = in ? ld_word(xa + k) : (uint64_t)xa_tag << 32;
     bp[i] = in ? proj_b[k] : 0.f;
   }
+  settle(p, part_tag, [&](int j) {
+    return a.tpart + (size_t)(j % kHeads) * H + tid + (j / kHeads) * kMegaThreads;
+  }, a, sm);
+  settle(xw, xa_tag, [&](int i) { return xa + tid + i * kMegaThreads; }, a, sm);
 #pragma unroll
   for (int i = 0; i < kK; ++i) {
     const int k = tid + i * kMegaThreads;
     if (k >= H) continue;
     float t = 0.f;
 #pragma unroll
-    for (int h = 0; h < kHeads; ++h) t += p[i][h];
-    const float v = xv[i] + (t + bp[i]);
+    for (int h = 0; h < kHeads; ++h) t += word_f(p[i * kHeads + h]);
+    const float v = word_f(xw[i]) + (t + bp[i]);
     sm.xs[k] = v;
-    if (blockIdx.x == 0) xm[k] = v;
+    if (blockIdx.x == 0) st_word(a.txm + k, v, xm_tag);
   }
   // wider rows than kK * kMegaThreads (not GPT-2-small): the remainder
   for (int k = tid + kK * kMegaThreads; k < H; k += kMegaThreads) {
     float t = 0.f;
-    for (int h = 0; h < a.heads; ++h) t += __ldcg(a.part + (size_t)h * H + k);
-    const float v = __ldcg(xa + k) + (t + proj_b[k]);
+    for (int h = 0; h < a.heads; ++h) {
+      const uint64_t* pp = a.tpart + (size_t)h * H + k;
+      uint64_t pw[1] = {ld_word(pp)};
+      settle(pw, part_tag, [&](int) { return pp; }, a, sm);
+      t += word_f(pw[0]);
+    }
+    uint64_t rw[1] = {ld_word(xa + k)};
+    settle(rw, xa_tag, [&](int) { return xa + k; }, a, sm);
+    const float v = word_f(rw[0]) + (t + proj_b[k]);
     sm.xs[k] = v;
-    if (blockIdx.x == 0) xm[k] = v;
+    if (blockIdx.x == 0) st_word(a.txm + k, v, xm_tag);
   }
   __syncthreads();
   stage_smem_ln(H, g, b, a.eps, sm);
@@ -759,16 +858,17 @@ __device__ void stage_attn_residual(const MegaArgs& a, const float* proj_b, cons
 // [hd][Wc] panel in slot `slot`. The partials are summed (fixed order) by
 // the next phase.
 __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
-                                const uint8_t* slots, int slot, Smem& sm) {
+                                const uint8_t* slots, int slot, Smem& sm, uint32_t qtag,
+                                uint32_t part_tag) {
   const int chunks = a.proj_chunks;
   const int c = blockIdx.x;
   if (c >= a.heads * chunks) return true;
   const int h = c / chunks, cc = c % chunks;
   float* ctx = scr + 384 + a.max_len + 4 + (kMegaThreads / 32) * 128;  // [hd]
   if (a.hd == 64)
-    attention_head64(a, L, pos, scr, sm, h, cc == 0, ctx);
+    attention_head64(a, L, pos, scr, sm, h, cc == 0, ctx, qtag);
   else
-    attention_head(a, L, pos, scr, sm, h, cc == 0, ctx);
+    attention_head(a, L, pos, scr, sm, h, cc == 0, ctx, qtag);
   if (!wait_slot(slot, sm, a)) return false;
   const MegaPanels& m = L.proj;  // K = hd, P = chunk width
   const float* w = reinterpret_cast<const float*>(slots + (size_t)slot * kSlotBytes);
@@ -786,7 +886,7 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
     float t = 0.f;
     for (int q = 0; q < slices; ++q) t += sm.red[q * Wc + tid];
     const int gcol = cc * Wc + tid;
-    if (gcol < a.H) a.part[(size_t)h * a.H + gcol] = t;
+    if (gcol < a.H) st_word(a.tpart + (size_t)h * a.H + gcol, t, part_tag);
   }
   __syncthreads();
   return true;
@@ -816,10 +916,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
   __syncthreads();
   const int H = a.H;
   float* scr = reinterpret_cast<float*>(slots + (size_t)kSlots * kSlotBytes);
-  // Residual stream: xa = layer input / FP output, xm = after the attention
-  // block (written by CTA 0 in the FC phase).
-  float* xa = a.x;
-  float* xm = a.x + H;
+  // Tags of one step, increasing in the order the words are written (every
+  // buffer sees only growing tags): the embedding (layer 0's input) is
+  // tag_step + 1; phase ph (0 QKV, 1 projection partials, 2 FC / xm, 3 FP) of
+  // layer l is tag_step + 4 l + ph + 2, so layer l's input is tag_step + 4 l + 1.
+  const uint32_t tags_per_step = 4u * (uint32_t)a.layers + 1u;
 
   int64_t tok = *a.tok;
   // Copies are issued one phase ahead, by thread 0 between its arrival at a
@@ -862,9 +963,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       drain(sm);
       return;
     }
+    const uint32_t tag_step = a.tag_base + (uint32_t)step * tags_per_step;
+#ifdef INFERC_DECODE_PROFILE
+    if (a.prof && step == 1 && blockIdx.x == 0 && tid == 0) a.prof[0] = gtimer();
+#endif
     for (int l = 0; l < a.layers; ++l) {
       const MegaLayer& L = a.layer[l];  // read on use (keeps registers free)
       const bool last = l + 1 == a.layers;
+      const uint32_t tag_in = tag_step + 4u * (uint32_t)l + 1u;  // this layer's input
+      const uint32_t tag_l = tag_in;  // phase ph writes tag_l + ph + 1
+      const uint64_t* xin = a.tx + (size_t)(l & 1) * H;
       if (a.l2_prefetch) {
         if (!last) prefetch_layer_l2(a, a.layer[l + 1]);
         else if (tid < 32) {  // the first chunks of this CTA's LM-head rows
@@ -875,7 +983,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
         }
       }
       // ---- QKV (pair 0; W_proj is in slot 2, LN1's gamma / beta in sm.lnp)
-      const EpiIn e_qkv = gemv_preload(L.attn, L.attn_b, nullptr);
+      const EpiIn e_qkv = gemv_preload(L.attn, L.attn_b, nullptr, 0u, a, sm);
       const float *g1, *b1, *unused;
       if (!ln_params(L.ln1_g, L.ln1_b, nullptr, H, sm, a, &g1, &b1, &unused)) { drain(sm); return; }
       if (l == 0) {
@@ -884,53 +992,52 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
         for (int k = tid; k < H; k += kMegaThreads) {
           const float v = __ldg(a.wte + tok * H + k) + __ldg(a.wpe + pos * H + k);
           sm.xs[k] = v;
-          if (blockIdx.x == 0) xa[k] = v;
+          if (blockIdx.x == 0) st_word(a.tx + k, v, tag_in);
         }
         __syncthreads();
         stage_smem_ln(H, g1, b1, a.eps, sm);
       } else {
-        stage_input(xa, H, g1, b1, a.eps, sm);
+        stage_input(xin, tag_in, H, g1, b1, a.eps, sm, a);
       }
-      if (!gemv_phase(L.attn, 0, slots, e_qkv, a.qkv, ACT_NONE, sm, a)) { drain(sm); return; }
-      grid_arrive(a, sm, 4 * l + 0, step);
+      if (!gemv_phase(L.attn, 0, slots, e_qkv, a.tqkv, tag_l + 1u, ACT_NONE, sm, a) ||
+          !phase_end(a, sm, 4 * l + 0, step)) { drain(sm); return; }
       prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);  // LN1's copy consumed
       prefetch_panels(L.fc, 0, slots, sm);  // pair 0 consumed
-      if (!grid_wait(a, sm, 4 * l + 0, step)) { drain(sm); return; }
       // ---- attention + output projection partials (slot 2)
-      if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm)) { drain(sm); return; }
-      grid_arrive(a, sm, 4 * l + 1, step);
+      if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm, tag_l + 1u, tag_l + 2u) ||
+          !phase_end(a, sm, 4 * l + 1, step)) { drain(sm); return; }
       prefetch_panels(L.fp, 1, slots, sm);  // slot 2 consumed, slot 3 free
-      if (!grid_wait(a, sm, 4 * l + 1, step)) { drain(sm); return; }
       // ---- FC (pair 0): xm = xa + b_proj + sum_h part[h]; f = gelu(LN2(xm) W + b).
-      const EpiIn e_fc = gemv_preload(L.fc, L.fc_b, nullptr);
+      const EpiIn e_fc = gemv_preload(L.fc, L.fc_b, nullptr, 0u, a, sm);
       const float *g2, *b2, *pb;
       if (!ln_params(L.ln2_g, L.ln2_b, L.proj_b, H, sm, a, &g2, &b2, &pb)) { drain(sm); return; }
-      stage_attn_residual(a, pb, g2, b2, xa, xm, sm);
-      if (!gemv_phase(L.fc, 0, slots, e_fc, a.f, ACT_GELU_TANH, sm, a)) { drain(sm); return; }
-      grid_arrive(a, sm, 4 * l + 2, step);
+      stage_attn_residual(a, pb, g2, b2, xin, tag_in, tag_l + 2u, tag_l + 3u, sm);
+      if (!gemv_phase(L.fc, 0, slots, e_fc, a.tf, tag_l + 3u, ACT_GELU_TANH, sm, a) ||
+          !phase_end(a, sm, 4 * l + 2, step)) { drain(sm); return; }
       // LN2's copy consumed: the next LayerNorm's vectors (small, first)
       if (!last) prefetch_ln(a.layer[l + 1].ln1_g, a.layer[l + 1].ln1_b, nullptr, H, sm);
       else prefetch_ln(a.lnf_g, a.lnf_b, nullptr, H, sm);
       if (!last) prefetch_panels(a.layer[l + 1].attn, 0, slots, sm);  // pair 0 consumed
-      if (!grid_wait(a, sm, 4 * l + 2, step)) { drain(sm); return; }
-      // ---- FP (pair 1): xa = xm + f W + b
-      const EpiIn e_fp = gemv_preload(L.fp, L.fp_b, xm);
-      stage_input(a.f, a.F, nullptr, nullptr, 0.f, sm);
-      if (!gemv_phase(L.fp, 1, slots, e_fp, xa, ACT_NONE, sm, a)) { drain(sm); return; }
-      grid_arrive(a, sm, 4 * l + 3, step);
+      // ---- FP (pair 1): x_next = xm + f W + b
+      const EpiIn e_fp = gemv_preload(L.fp, L.fp_b, a.txm, tag_l + 3u, a, sm);
+      stage_input(a.tf, tag_l + 3u, a.F, nullptr, nullptr, 0.f, sm, a);
+      if (!gemv_phase(L.fp, 1, slots, e_fp, a.tx + (size_t)((l + 1) & 1) * H, tag_l + 4u,
+                      ACT_NONE, sm, a) ||
+          !phase_end(a, sm, 4 * l + 3, step)) { drain(sm); return; }
       if (!last) {
         issue_proj(a.layer[l + 1]);  // slot 2 consumed
       } else {
         for (int ch = 0; ch < kSlots; ++ch) issue_lm(ch);  // every slot consumed
       }
-      if (!grid_wait(a, sm, 4 * l + 3, step)) { drain(sm); return; }
     }
     // LM head: logits = LNf(x) . wte[r] for this CTA's row range, streamed
     // through all four slots (the first four chunks are already in flight).
     {
       const float *gf, *bf, *unused;
       if (!ln_params(a.lnf_g, a.lnf_b, nullptr, H, sm, a, &gf, &bf, &unused)) { drain(sm); return; }
-      stage_input(xa, H, gf, bf, a.eps, sm);
+      // the last layer's FP output, tagged tag_step + 4 layers + 1
+      stage_input(a.tx + (size_t)(a.layers & 1) * H, tag_step + tags_per_step, H, gf, bf,
+                  a.eps, sm, a);
     }
     {
       const int r0 = lm_r0, r1 = lm_r1, crow = lm_crow, nchunks = lm_nchunks;
@@ -980,13 +1087,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       }
     }
     // Next step's first weights stream while the argmax is finalised.
-    grid_arrive(a, sm, 4 * a.layers, step);
+    if (!phase_end(a, sm, 4 * a.layers, step)) { drain(sm); return; }
+    grid_arrive(a, sm);
     if (step + 1 < a.nsteps) {
       prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
       prefetch_panels(a.layer[0].attn, 0, slots, sm);
       issue_proj(a.layer[0]);
     }
-    if (!grid_wait(a, sm, 4 * a.layers, step)) { drain(sm); return; }
+    if (!grid_wait(a, sm)) { drain(sm); return; }
     // Every CTA reduces the per-CTA bests in the same order (first max wins).
     if (wid == 0) {
       float v = -INFINITY;

@@ -23,14 +23,23 @@ struct MegaArgs {
   int layers, H, heads, hd, F, V, max_len, max_pos;
   float eps;
   const float *wte, *wpe, *lnf_g, *lnf_b;
-  // state / scratch (device)
-  float *x, *qkv, *ctx, *f, *logits;  // x: [2][H] residual buffers
-  float* part;      // [heads][H] output-projection partials
+  // Activations passed between CTAs inside a step. Every 64-bit word holds
+  // (tag << 32) | fp32 bits and is written once per phase instance with that
+  // instance's tag, so a reader's load is also its wait: it re-reads a word
+  // until the tag it expects is there (a single-copy-atomic 8-byte access
+  // carries the value and its tag together). Tags run tag_base + 1 ...
+  // tag_base + nsteps * (4 * layers + 1) over a launch.
+  uint64_t* tx;     // [2][H] layer inputs: layer l reads tx[l & 1]
+  uint64_t* txm;    // [H] residual stream after the attention block
+  uint64_t* tqkv;   // [3H]
+  uint64_t* tpart;  // [heads][H] output-projection partials
+  uint64_t* tf;     // [F] FC output
+  uint32_t tag_base;
+  float* logits;
   int proj_chunks;  // column chunks per head in the attention block
   float* best_v;
   int64_t* best_i;
-  unsigned int* bar_count;
-  unsigned int* bar_gen;
+  unsigned int* bar_count;  // end-of-step grid barrier (zeroed before each launch)
   int* err;
   int64_t* tok;        // in: current token; out: last generated token
   int64_t* token_log;  // token_log[log_offset + s] = token generated at step s

@@ -18,6 +18,7 @@
 // tanh-GELU, proj GEMV + residual], LN-prologue LM-head GEMV with fused
 // argmax. The step reads its position and token from device memory and
 // advances them itself, so successive replays need no host work.
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <cstdio>
@@ -578,8 +579,9 @@ struct InfercDecoderPlan {
   float* best_v = nullptr;
   int64_t* best_i = nullptr;
   unsigned int* bar = nullptr;  // [count, generation]
-  float* mega_x = nullptr;      // [2][H] residual buffers
-  float* mega_part = nullptr;   // [heads][H]
+  uint64_t* mega_tags = nullptr;  // tagged activation words: x [2][H], xm, qkv, partials, f
+  size_t mega_tag_words = 0;
+  uint32_t mega_tag_next = 0;     // tag base of the next launch
   int mega_chunks = 0;
   unsigned long long* prof_buf = nullptr;  // -DINFERC_DECODE_PROFILE builds only
   // Weight-only int4 mode (inferc_dev_decoder_create_int4): the four layer
@@ -782,9 +784,23 @@ struct InfercDecoderPlan {
       a.layers = (int)L; a.H = (int)H; a.heads = (int)nH; a.hd = (int)hd; a.F = (int)F;
       a.V = (int)V; a.max_len = (int)max_len; a.max_pos = (int)P; a.eps = eps;
       a.wte = wte; a.wpe = wpe; a.lnf_g = lnf_g; a.lnf_b = lnf_b;
-      a.x = mega_x; a.qkv = qkv; a.ctx = ctx; a.f = f; a.logits = logits;
-      a.part = mega_part; a.proj_chunks = mega_chunks;
-      a.best_v = best_v; a.best_i = best_i; a.bar_count = bar; a.bar_gen = bar + 1;
+      a.tx = mega_tags;
+      a.txm = a.tx + 2 * H;
+      a.tqkv = a.txm + H;
+      a.tpart = a.tqkv + 3 * H;
+      a.tf = a.tpart + nH * H;
+      // Tags only grow within [1, 2^31): when a launch would pass that, the
+      // words are cleared and the tags start again.
+      const uint64_t span = (uint64_t)(max_tokens - 1) * (4 * (uint64_t)L + 1);
+      if ((uint64_t)mega_tag_next + span >= (1ull << 31)) {
+        IDEV_CUDA(cudaMemsetAsync(mega_tags, 0, mega_tag_words * sizeof(uint64_t), st));
+        mega_tag_next = 0;
+      }
+      a.tag_base = mega_tag_next;
+      mega_tag_next += (uint32_t)span;
+      a.logits = logits;
+      a.proj_chunks = mega_chunks;
+      a.best_v = best_v; a.best_i = best_i; a.bar_count = bar;
       a.err = err; a.tok = tok; a.token_log = token_log; a.log_offset = 1;
       a.pos0 = n; a.nsteps = (int)(max_tokens - 1);
       // INFERC_DECODE_L2=1 requests each layer's panels into L2 one layer
@@ -798,7 +814,7 @@ struct InfercDecoderPlan {
       a.prof = nullptr;
 #ifdef INFERC_DECODE_PROFILE
       // Development build only (-DINFERC_DECODE_PROFILE): CTA 0 stamps the
-      // global timer at each grid barrier of step 1 into a per-plan buffer.
+      // global timer at the end of each phase of step 1 into a per-plan buffer.
       if (!prof_buf) prof_buf = mem.alloc<unsigned long long>(2048);
       a.prof = prof_buf;
 #endif
@@ -808,14 +824,13 @@ struct InfercDecoderPlan {
       IDEV_CUDA(cudaEventRecord(ev1, st));
 #ifdef INFERC_DECODE_PROFILE
       {
-        std::vector<unsigned long long> t(2 * (4 * L + 1));
+        std::vector<unsigned long long> t(4 * L + 2);
         IDEV_CUDA(cudaMemcpyAsync(t.data(), prof_buf, t.size() * 8, cudaMemcpyDeviceToHost, st));
         IDEV_CUDA(cudaStreamSynchronize(st));
         const char* names[4] = {"qkv", "attn+proj", "fc", "fp"};
-        for (int q = 1; q <= 4 * L; ++q)
-          fprintf(stderr, "phase %-9s work %6.2f us  barrier %5.2f us\n",
-                  q == 4 * L ? "lm" : names[q % 4], (t[2 * q] - t[2 * q - 1]) / 1e3,
-                  (t[2 * q + 1] - t[2 * q]) / 1e3);
+        for (int q = 0; q <= 4 * L; ++q)  // phase q ends at stamp q + 1
+          fprintf(stderr, "layer %2d phase %-9s %6.2f us\n", (int)(q / 4),
+                  q == 4 * L ? "lm" : names[q % 4], (t[q + 1] - t[q]) / 1e3);
       }
 #endif
     } else if (max_tokens > 1) {
@@ -864,8 +879,26 @@ static void setup_mega(InfercDecoderPlan* p) {
   if (H > 3072 || F > 3072 || H % 16 || F % 16 || p->hd % 4 || 256 % p->hd || p->hd > 128 ||
       (H * 4) > 48 * 1024 || p->L < 1 || p->nH > 16)
     return;
-  const int grid = mega_max_grid((int)p->max_len);
-  if (grid < 1) return;
+  int grid = mega_max_grid((int)p->max_len);
+  // Panel count of a [K, N] GEMV: the narrowest P (4, 8 or 16; the most
+  // panels, so the most CTAs streaming) with a panel <= 48 KiB and at most two
+  // panels per CTA; 0 when none fits.
+  auto panel_width = [](int K, int N, int g) -> int {
+    for (int P : {4, 8, 16})
+      if ((size_t)K * P * 4 <= 48 * 1024 && (N + P - 1) / P <= 2 * g) return P;
+    return 0;
+  };
+  // Every CTA must own an FC and an FP panel: the kernel's tagged-word
+  // ordering relies on each phase depending on every CTA (a smaller model
+  // runs on fewer CTAs).
+  for (;;) {
+    const int pfc = panel_width(H, F, grid), pfp = panel_width(F, H, grid);
+    if (grid < 1 || !pfc || !pfp) return;
+    const int g = std::min({grid, (F + pfc - 1) / pfc, (H + pfp - 1) / pfp});
+    if (g == grid) break;
+    grid = g;
+  }
+  if (grid < (int)p->nH) return;
   // attention block: heads x chunks CTAs, chunk width Wc (multiple of 4)
   int chunks = std::min<int>(grid / (int)p->nH, H / 4);
   if (const char* e = std::getenv("INFERC_DECODE_CHUNKS")) chunks = std::max(1, std::min(chunks, std::atoi(e)));
@@ -873,17 +906,12 @@ static void setup_mega(InfercDecoderPlan* p) {
   const int Wc = ((H + chunks - 1) / chunks + 3) / 4 * 4;
   if (Wc > 256 || (size_t)p->hd * Wc * 4 > 48 * 1024) return;
   auto panels = [&](const float* w, int K, int N) -> MegaPanels {
-    // narrowest P (4, 8 or 16; the most panels, so the most CTAs streaming)
-    // with a panel <= 48 KiB and at most two panels per CTA
-    for (int P : {4, 8, 16}) {
-      const int np = (N + P - 1) / P;
-      if ((size_t)K * P * 4 <= 48 * 1024 && np <= 2 * grid && P <= 256) {
-        float* d = p->mem.alloc<float>((size_t)np * K * P);
-        launch_panelize(w, d, K, N, P, np, nullptr);
-        return MegaPanels{d, K, N, P, np};
-      }
-    }
-    return MegaPanels{nullptr, K, N, 0, 0};
+    const int P = panel_width(K, N, grid);
+    if (!P) return MegaPanels{nullptr, K, N, 0, 0};
+    const int np = (N + P - 1) / P;
+    float* d = p->mem.alloc<float>((size_t)np * K * P);
+    launch_panelize(w, d, K, N, P, np, nullptr);
+    return MegaPanels{d, K, N, P, np};
   };
   std::vector<MegaLayer> layers((size_t)p->L);
   for (int64_t l = 0; l < p->L; ++l) {
@@ -908,8 +936,9 @@ static void setup_mega(InfercDecoderPlan* p) {
   p->best_v = p->mem.alloc<float>(grid);
   p->best_i = p->mem.alloc<int64_t>(grid);
   p->bar = p->mem.alloc<unsigned int>(2);
-  p->mega_x = p->mem.alloc<float>(2 * (size_t)H);
-  p->mega_part = p->mem.alloc<float>((size_t)p->nH * H);
+  p->mega_tag_words = (size_t)(6 + p->nH) * H + (size_t)F;
+  p->mega_tags = p->mem.alloc<uint64_t>(p->mega_tag_words);
+  IDEV_CUDA(cudaMemset(p->mega_tags, 0, p->mega_tag_words * sizeof(uint64_t)));
   p->mega_chunks = chunks;
   IDEV_CUDA(cudaMemset(p->bar, 0, 2 * sizeof(unsigned int)));
   IDEV_CUDA(cudaDeviceSynchronize());
