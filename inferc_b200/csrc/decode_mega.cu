@@ -104,6 +104,19 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// Bulk copy of streamed weights: read once per token, so marked first to be
+// evicted from L2, which keeps the KV cache and the activations resident.
+__device__ __forceinline__ void bulk_load_stream(void* dst, const void* src, uint32_t bytes,
+                                                 uint64_t* bar) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+      : "memory");
+}
+
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -223,6 +236,16 @@ __device__ bool grid_wait(const MegaArgs& a, Smem& sm) {
   return sm.abort_flag == 0;
 }
 
+// Development builds (-DINFERC_DECODE_PROFILE): every CTA stamps event e
+// of layer 5 of step 1 into prof[64 + 16 * cta + e].
+__device__ __forceinline__ void stamp_event(const MegaArgs& a, bool on, int e) {
+#ifdef INFERC_DECODE_PROFILE
+  if (a.prof && on && threadIdx.x == 0) a.prof[64 + 16 * blockIdx.x + e] = gtimer();
+#else
+  (void)a; (void)on; (void)e;
+#endif
+}
+
 // End of a phase of this CTA: all threads are past their reads of the slots
 // and their writes; false when a wait of the phase failed. With
 // -DINFERC_DECODE_PROFILE, CTA 0 stamps the global timer at phase q of step 1.
@@ -295,8 +318,8 @@ __device__ void prefetch_panels(const MegaPanels& m, int pair, uint8_t* slots, S
     mb_expect_tx(&sm.bar[s], bytes);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(m.data + (size_t)p * m.K * m.P);
     for (uint32_t off = 0; off < bytes; off += 16384)
-      bulk_load(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
-                &sm.bar[s]);
+      bulk_load_stream(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
+                       &sm.bar[s]);
   }
 }
 
@@ -679,7 +702,15 @@ __device__ void attention_head(const MegaArgs& a, const MegaLayer& L, int64_t po
 // merged with a block max and shuffle sums.
 __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer& L, int64_t pos,
                                               float* scr, Smem& sm, int h, bool append,
-                                              float* ctx_out, uint32_t qtag) {
+                                              float* ctx_out, uint32_t qtag, bool pe) {
+  stamp_event(a, pe, 7);
+#ifdef INFERC_DECODE_PROFILE
+  if (a.prof && pe && threadIdx.x == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    a.prof[64 + 16 * blockIdx.x + 15] = smid;
+  }
+#endif
   constexpr int HD = 64;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, H = a.H;
   constexpr int nw = kMegaThreads / 32;
@@ -689,6 +720,28 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
   float* part = scr + 384 + a.max_len + 4;  // [8][65]
   float* kh = L.kc + (size_t)h * a.max_len * HD;
   float* vh = L.vc + (size_t)h * a.max_len * HD;
+  const int half = tid & 1;  // thread pair (2i, 2i+1) shares key i: each lane holds half the dims
+  // Cached keys / values (positions < pos) of one pass of 128 keys; the new
+  // key at pos comes from shared memory below, the rest are zero.
+  auto load_kv = [&](int64_t base, float4 (&kr)[8], float4 (&vr)[8]) {
+    const int64_t j = base + (tid >> 1);
+    if (j < pos) {
+      const float4* kg = reinterpret_cast<const float4*>(kh + j * HD + 32 * half);
+      const float4* vg = reinterpret_cast<const float4*>(vh + j * HD + 32 * half);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        kr[d] = __ldcg(kg + d);
+        vr[d] = __ldcg(vg + d);
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < 8; ++d) kr[d] = vr[d] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  // The first pass's cached rows do not depend on this step's q / k / v:
+  // their loads are in flight while this CTA waits for its head's q / k / v.
+  float4 kr[8], vr[8];
+  load_kv(0, kr, vr);
   if (tid < HD) {
     const uint64_t* qp = a.tqkv + h * HD + tid;
     uint64_t w3[3] = {ld_word(qp), ld_word(qp + H), ld_word(qp + 2 * H)};
@@ -702,10 +755,9 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
     }
   }
   __syncthreads();
+  stamp_event(a, pe, 8);
   const int64_t Lk = pos + 1;
   const float sq = sqrtf((float)HD);
-  // thread pair (2i, 2i+1) shares key i: each lane holds half the dims.
-  const int half = tid & 1;
   float m = -INFINITY, l = 0.f, o[32];
 #pragma unroll
   for (int d = 0; d < 32; ++d) o[d] = 0.f;
@@ -716,24 +768,13 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
   for (int64_t base = 0; base < Lk; base += kMegaThreads / 2) {
     const int64_t j = base + (tid >> 1);
     const bool valid = j < Lk;
-    float4 kr[8], vr[8];
+    if (base > 0) load_kv(base, kr, vr);
     if (j == pos) {
 #pragma unroll
       for (int d = 0; d < 8; ++d) {
         kr[d] = reinterpret_cast<const float4*>(kn + 32 * half)[d];
         vr[d] = reinterpret_cast<const float4*>(vn + 32 * half)[d];
       }
-    } else if (valid) {
-      const float4* kg = reinterpret_cast<const float4*>(kh + j * HD + 32 * half);
-      const float4* vg = reinterpret_cast<const float4*>(vh + j * HD + 32 * half);
-#pragma unroll
-      for (int d = 0; d < 8; ++d) {
-        kr[d] = __ldcg(kg + d);
-        vr[d] = __ldcg(vg + d);
-      }
-    } else {
-#pragma unroll
-      for (int d = 0; d < 8; ++d) kr[d] = vr[d] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float dot = 0.f;
 #pragma unroll
@@ -761,10 +802,12 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
     }
     m = mn;
   }
+  stamp_event(a, pe, 11);
   // block max of m
   float mx = warp_max(m);
   if (lane == 0) sm.red[wid] = mx;
   __syncthreads();
+  stamp_event(a, pe, 12);
   float M = sm.red[0];
 #pragma unroll
   for (int w = 1; w < nw; ++w) M = fmaxf(M, sm.red[w]);
@@ -773,16 +816,27 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
 #pragma unroll
   for (int d = 0; d < 32; ++d) o[d] *= scale;
   l = warp_sum(l);
+  // Sum o over the 16 lanes of each half (lane bit 0) by reduce-scatter:
+  // each round a lane keeps half of its values and adds its partner's copy
+  // of them (30 shuffles, not 128). Afterwards lane holds dims
+  // 32 half + (lane & 30) + {0, 1} in o[0], o[1].
 #pragma unroll
-  for (int off = 2; off < 32; off <<= 1)
+  for (int r = 0; r < 4; ++r) {
+    const int off = 16 >> r;  // also the number of values passed on
+    const bool up = (lane & off) != 0;
 #pragma unroll
-    for (int d = 0; d < 32; ++d) o[d] += __shfl_xor_sync(0xffffffffu, o[d], off);
-  if (lane < 2) {
-#pragma unroll
-    for (int d = 0; d < 32; ++d) part[wid * 65 + 32 * lane + d] = o[d];
-    if (lane == 0) part[wid * 65 + 64] = l;
+    for (int i = 0; i < 16; ++i) {
+      if (i >= off) break;
+      const float send = up ? o[i] : o[i + off];
+      const float keep = up ? o[i + off] : o[i];
+      o[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
   }
+  part[wid * 65 + 32 * half + (lane & 30)] = o[0];
+  part[wid * 65 + 32 * half + (lane & 30) + 1] = o[1];
+  if (lane == 0) part[wid * 65 + 64] = l;
   __syncthreads();
+  stamp_event(a, pe, 13);
   if (tid < HD) {
     float r = 0.f, t = 0.f;
 #pragma unroll
@@ -859,17 +913,19 @@ __device__ void stage_attn_residual(const MegaArgs& a, const float* proj_b, cons
 // the next phase.
 __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
                                 const uint8_t* slots, int slot, Smem& sm, uint32_t qtag,
-                                uint32_t part_tag) {
+                                uint32_t part_tag, bool pe) {
   const int chunks = a.proj_chunks;
   const int c = blockIdx.x;
   if (c >= a.heads * chunks) return true;
   const int h = c / chunks, cc = c % chunks;
   float* ctx = scr + 384 + a.max_len + 4 + (kMegaThreads / 32) * 128;  // [hd]
   if (a.hd == 64)
-    attention_head64(a, L, pos, scr, sm, h, cc == 0, ctx, qtag);
+    attention_head64(a, L, pos, scr, sm, h, cc == 0, ctx, qtag, pe);
   else
     attention_head(a, L, pos, scr, sm, h, cc == 0, ctx, qtag);
+  stamp_event(a, pe, 9);
   if (!wait_slot(slot, sm, a)) return false;
+  stamp_event(a, pe, 10);
   const MegaPanels& m = L.proj;  // K = hd, P = chunk width
   const float* w = reinterpret_cast<const float*>(slots + (size_t)slot * kSlotBytes);
   const int tid = threadIdx.x;
@@ -931,8 +987,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       const uint32_t bytes = (uint32_t)Lx.proj.K * Lx.proj.P * 4;
       sm.issued[2]++;
       mb_expect_tx(&sm.bar[2], bytes);
-      bulk_load(slots + 2 * (size_t)kSlotBytes,
-                Lx.proj.data + (size_t)blockIdx.x * Lx.proj.K * Lx.proj.P, bytes, &sm.bar[2]);
+      bulk_load_stream(slots + 2 * (size_t)kSlotBytes,
+                       Lx.proj.data + (size_t)blockIdx.x * Lx.proj.K * Lx.proj.P, bytes,
+                       &sm.bar[2]);
     }
   };
   // LM head chunks: 16 rows of wte (48 KiB) per chunk, this CTA's row range.
@@ -950,8 +1007,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
     mb_expect_tx(&sm.bar[s], bytes);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wte + (size_t)ra * H);
     for (uint32_t off = 0; off < bytes; off += 16384)
-      bulk_load(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
-                &sm.bar[s]);
+      bulk_load_stream(slots + (size_t)s * kSlotBytes + off, src + off,
+                       min(16384u, bytes - off), &sm.bar[s]);
   };
   prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
   prefetch_panels(a.layer[0].attn, 0, slots, sm);
@@ -999,21 +1056,27 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       } else {
         stage_input(xin, tag_in, H, g1, b1, a.eps, sm, a);
       }
+      stamp_event(a, step == 1 && l == 5, 0);
       if (!gemv_phase(L.attn, 0, slots, e_qkv, a.tqkv, tag_l + 1u, ACT_NONE, sm, a) ||
           !phase_end(a, sm, 4 * l + 0, step)) { drain(sm); return; }
+      stamp_event(a, step == 1 && l == 5, 1);
       prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);  // LN1's copy consumed
       prefetch_panels(L.fc, 0, slots, sm);  // pair 0 consumed
       // ---- attention + output projection partials (slot 2)
-      if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm, tag_l + 1u, tag_l + 2u) ||
+      if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm, tag_l + 1u, tag_l + 2u,
+                           step == 1 && l == 5) ||
           !phase_end(a, sm, 4 * l + 1, step)) { drain(sm); return; }
+      stamp_event(a, step == 1 && l == 5, 2);
       prefetch_panels(L.fp, 1, slots, sm);  // slot 2 consumed, slot 3 free
       // ---- FC (pair 0): xm = xa + b_proj + sum_h part[h]; f = gelu(LN2(xm) W + b).
       const EpiIn e_fc = gemv_preload(L.fc, L.fc_b, nullptr, 0u, a, sm);
       const float *g2, *b2, *pb;
       if (!ln_params(L.ln2_g, L.ln2_b, L.proj_b, H, sm, a, &g2, &b2, &pb)) { drain(sm); return; }
       stage_attn_residual(a, pb, g2, b2, xin, tag_in, tag_l + 2u, tag_l + 3u, sm);
+      stamp_event(a, step == 1 && l == 5, 3);
       if (!gemv_phase(L.fc, 0, slots, e_fc, a.tf, tag_l + 3u, ACT_GELU_TANH, sm, a) ||
           !phase_end(a, sm, 4 * l + 2, step)) { drain(sm); return; }
+      stamp_event(a, step == 1 && l == 5, 4);
       // LN2's copy consumed: the next LayerNorm's vectors (small, first)
       if (!last) prefetch_ln(a.layer[l + 1].ln1_g, a.layer[l + 1].ln1_b, nullptr, H, sm);
       else prefetch_ln(a.lnf_g, a.lnf_b, nullptr, H, sm);
@@ -1021,9 +1084,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       // ---- FP (pair 1): x_next = xm + f W + b
       const EpiIn e_fp = gemv_preload(L.fp, L.fp_b, a.txm, tag_l + 3u, a, sm);
       stage_input(a.tf, tag_l + 3u, a.F, nullptr, nullptr, 0.f, sm, a);
+      stamp_event(a, step == 1 && l == 5, 5);
       if (!gemv_phase(L.fp, 1, slots, e_fp, a.tx + (size_t)((l + 1) & 1) * H, tag_l + 4u,
                       ACT_NONE, sm, a) ||
           !phase_end(a, sm, 4 * l + 3, step)) { drain(sm); return; }
+      stamp_event(a, step == 1 && l == 5, 6);
       if (!last) {
         issue_proj(a.layer[l + 1]);  // slot 2 consumed
       } else {

@@ -815,7 +815,7 @@ struct InfercDecoderPlan {
 #ifdef INFERC_DECODE_PROFILE
       // Development build only (-DINFERC_DECODE_PROFILE): CTA 0 stamps the
       // global timer at the end of each phase of step 1 into a per-plan buffer.
-      if (!prof_buf) prof_buf = mem.alloc<unsigned long long>(2048);
+      if (!prof_buf) prof_buf = mem.alloc<unsigned long long>(4096);
       a.prof = prof_buf;
 #endif
       IDEV_CUDA(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned int), st));
@@ -831,6 +831,32 @@ struct InfercDecoderPlan {
         for (int q = 0; q <= 4 * L; ++q)  // phase q ends at stamp q + 1
           fprintf(stderr, "layer %2d phase %-9s %6.2f us\n", (int)(q / 4),
                   q == 4 * L ? "lm" : names[q % 4], (t[q + 1] - t[q]) / 1e3);
+        // per-CTA events of layer 5: min / median / max over CTAs, us after
+        // the earliest event
+        std::vector<unsigned long long> ev((size_t)mega_grid * 16);
+        IDEV_CUDA(cudaMemcpy(ev.data(), prof_buf + 64, ev.size() * 8, cudaMemcpyDeviceToHost));
+        unsigned long long t0 = ~0ull;
+        for (int c = 0; c < mega_grid; ++c)
+          for (int e = 0; e < 7; ++e) t0 = std::min(t0, ev[(size_t)c * 16 + e]);
+        const char* en[14] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
+                              "fc end", "fp input staged", "fp end", "attn enter",
+                              "attn qkv ready", "attn ctx done", "attn panel ready",
+                              "attn keys done", "attn max synced", "attn o reduced"};
+        for (int e = 0; e < 14; ++e) {
+          const int n = e < 7 ? mega_grid : (int)(nH * mega_chunks);  // attention CTAs only
+          std::vector<double> v;
+          for (int c = 0; c < n; ++c) v.push_back((ev[(size_t)c * 16 + e] - t0) / 1e3);
+          std::vector<int> ids(n);
+          for (int c = 0; c < n; ++c) ids[c] = c;
+          std::sort(ids.begin(), ids.end(), [&](int x, int y) { return v[x] > v[y]; });
+          fprintf(stderr, "  slowest CTAs:");
+          for (int c = 0; c < std::min(n, 8); ++c)
+            fprintf(stderr, " %d/sm%llu(%.2f)", ids[c], ev[(size_t)ids[c] * 16 + 15], v[ids[c]]);
+          fprintf(stderr, "\n");
+          std::sort(v.begin(), v.end());
+          fprintf(stderr, "event %-17s min %6.2f  med %6.2f  max %6.2f us\n", en[e], v.front(),
+                  v[v.size() / 2], v.back());
+        }
       }
 #endif
     } else if (max_tokens > 1) {
