@@ -51,6 +51,11 @@ namespace inferc_dev {
 namespace {
 
 constexpr int kMegaThreads = 256;
+// The thread that issues the bulk copies: lane 0 of the last warp, not thread
+// 0, which leads every CTA reduction. An issue can stall for a microsecond or
+// more while the whole grid requests its next panels at once; in this warp
+// the stall overlaps the next phase's wait for its inputs.
+constexpr int kIssuer = kMegaThreads - 32;
 constexpr int kSlotBytes = 48 * 1024;
 constexpr int kSlots = 4;
 constexpr unsigned long long kMegaWaitNs = 50ull * 1000 * 1000;  // 50 ms per wait
@@ -273,7 +278,7 @@ __device__ __forceinline__ bool ln_prefetchable(const float* g, const float* b,
 
 __device__ void prefetch_ln(const float* g, const float* b, const float* extra, int K,
                             Smem& sm) {
-  if (threadIdx.x != 0 || !ln_prefetchable(g, b, extra, K)) return;
+  if (threadIdx.x != kIssuer || !ln_prefetchable(g, b, extra, K)) return;
   const uint32_t bytes = (uint32_t)K * 4;
   sm.ln_issued++;
   mb_expect_tx(&sm.ln_bar, (extra ? 3 : 2) * bytes);
@@ -307,8 +312,9 @@ __device__ bool ln_params(const float* g, const float* b, const float* extra, in
 }
 
 // Issue this CTA's panels of a GEMV phase into slot pair `pair`.
-__device__ void prefetch_panels(const MegaPanels& m, int pair, uint8_t* slots, Smem& sm) {
-  if (threadIdx.x != 0) return;
+__device__ void prefetch_panels(const MegaPanels& m, int pair, uint8_t* slots, Smem& sm,
+                                uint32_t piece) {
+  if (threadIdx.x != kIssuer) return;
   for (int j = 0; j < 2; ++j) {
     const int p = blockIdx.x + j * gridDim.x;
     if (p >= m.npanels) break;
@@ -317,8 +323,8 @@ __device__ void prefetch_panels(const MegaPanels& m, int pair, uint8_t* slots, S
     sm.issued[s]++;
     mb_expect_tx(&sm.bar[s], bytes);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(m.data + (size_t)p * m.K * m.P);
-    for (uint32_t off = 0; off < bytes; off += 16384)
-      bulk_load_stream(slots + (size_t)s * kSlotBytes + off, src + off, min(16384u, bytes - off),
+    for (uint32_t off = 0; off < bytes; off += piece)
+      bulk_load_stream(slots + (size_t)s * kSlotBytes + off, src + off, min(piece, bytes - off),
                        &sm.bar[s]);
   }
 }
@@ -983,7 +989,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
   // grid barrier and its wait there: a slot pair is refilled as soon as this
   // CTA has consumed it, off the critical path of the next phase.
   auto issue_proj = [&](const MegaLayer& Lx) {  // W_proj panel -> slot 2
-    if (tid == 0 && blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) {
+    if (tid == kIssuer && blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) {
       const uint32_t bytes = (uint32_t)Lx.proj.K * Lx.proj.P * 4;
       sm.issued[2]++;
       mb_expect_tx(&sm.bar[2], bytes);
@@ -999,19 +1005,19 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
   const int lm_crow = kSlotBytes / (H * 4);
   const int lm_nchunks = lm_r1 > lm_r0 ? (lm_r1 - lm_r0 + lm_crow - 1) / lm_crow : 0;
   auto issue_lm = [&](int ch) {
-    if (tid != 0 || ch >= lm_nchunks) return;
+    if (tid != kIssuer || ch >= lm_nchunks) return;
     const int s = ch % kSlots;
     const int ra = lm_r0 + ch * lm_crow, rb = min(lm_r1, ra + lm_crow);
     const uint32_t bytes = (uint32_t)(rb - ra) * H * 4;
     sm.issued[s]++;
     mb_expect_tx(&sm.bar[s], bytes);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wte + (size_t)ra * H);
-    for (uint32_t off = 0; off < bytes; off += 16384)
+    for (uint32_t off = 0; off < bytes; off += a.piece)
       bulk_load_stream(slots + (size_t)s * kSlotBytes + off, src + off,
-                       min(16384u, bytes - off), &sm.bar[s]);
+                       min(a.piece, bytes - off), &sm.bar[s]);
   };
   prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
-  prefetch_panels(a.layer[0].attn, 0, slots, sm);
+  prefetch_panels(a.layer[0].attn, 0, slots, sm, a.piece);
   issue_proj(a.layer[0]);
   for (int step = 0; step < a.nsteps; ++step) {
     const int64_t pos = a.pos0 + step;
@@ -1061,13 +1067,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
           !phase_end(a, sm, 4 * l + 0, step)) { drain(sm); return; }
       stamp_event(a, step == 1 && l == 5, 1);
       prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);  // LN1's copy consumed
-      prefetch_panels(L.fc, 0, slots, sm);  // pair 0 consumed
+      prefetch_panels(L.fc, 0, slots, sm, a.piece);  // pair 0 consumed
+      stamp_event(a, step == 1 && l == 5, 14);
       // ---- attention + output projection partials (slot 2)
       if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm, tag_l + 1u, tag_l + 2u,
                            step == 1 && l == 5) ||
           !phase_end(a, sm, 4 * l + 1, step)) { drain(sm); return; }
       stamp_event(a, step == 1 && l == 5, 2);
-      prefetch_panels(L.fp, 1, slots, sm);  // slot 2 consumed, slot 3 free
+      prefetch_panels(L.fp, 1, slots, sm, a.piece);  // slot 2 consumed, slot 3 free
       // ---- FC (pair 0): xm = xa + b_proj + sum_h part[h]; f = gelu(LN2(xm) W + b).
       const EpiIn e_fc = gemv_preload(L.fc, L.fc_b, nullptr, 0u, a, sm);
       const float *g2, *b2, *pb;
@@ -1080,7 +1087,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       // LN2's copy consumed: the next LayerNorm's vectors (small, first)
       if (!last) prefetch_ln(a.layer[l + 1].ln1_g, a.layer[l + 1].ln1_b, nullptr, H, sm);
       else prefetch_ln(a.lnf_g, a.lnf_b, nullptr, H, sm);
-      if (!last) prefetch_panels(a.layer[l + 1].attn, 0, slots, sm);  // pair 0 consumed
+      if (!last) prefetch_panels(a.layer[l + 1].attn, 0, slots, sm, a.piece);  // pair 0 consumed
       // ---- FP (pair 1): x_next = xm + f W + b
       const EpiIn e_fp = gemv_preload(L.fp, L.fp_b, a.txm, tag_l + 3u, a, sm);
       stage_input(a.tf, tag_l + 3u, a.F, nullptr, nullptr, 0.f, sm, a);
@@ -1131,7 +1138,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
         }
         __syncthreads();  // slot s fully consumed
         issue(ch + kSlots);
-        if (a.l2_prefetch && tid == 0) {
+        if (a.l2_prefetch && tid == kIssuer) {
           const int pc = ch + 4 + a.lm_prefetch_chunks;
           if (pc < nchunks) {
             const int ra = r0 + pc * crow, rb = min(r1, ra + crow);
@@ -1156,7 +1163,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
     grid_arrive(a, sm);
     if (step + 1 < a.nsteps) {
       prefetch_ln(a.layer[0].ln1_g, a.layer[0].ln1_b, nullptr, H, sm);
-      prefetch_panels(a.layer[0].attn, 0, slots, sm);
+      prefetch_panels(a.layer[0].attn, 0, slots, sm, a.piece);
       issue_proj(a.layer[0]);
     }
     if (!grid_wait(a, sm)) { drain(sm); return; }

@@ -35,6 +35,7 @@ struct MegaArgs {
   uint64_t* tpart;  // [heads][H] output-projection partials
   uint64_t* tf;     // [F] FC output
   uint32_t tag_base;
+  uint32_t piece;  // bytes per bulk copy of a weight panel or LM-head chunk (multiple of 16)
   float* logits;
   int proj_chunks;  // column chunks per head in the attention block
   float* best_v;

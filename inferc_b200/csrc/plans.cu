@@ -797,6 +797,8 @@ struct InfercDecoderPlan {
         mega_tag_next = 0;
       }
       a.tag_base = mega_tag_next;
+      const char* pc = std::getenv("INFERC_DECODE_PIECE");
+      a.piece = pc ? (uint32_t)std::max(16, std::atoi(pc) / 16 * 16) : 49152u;
       mega_tag_next += (uint32_t)span;
       a.logits = logits;
       a.proj_chunks = mega_chunks;
@@ -838,12 +840,13 @@ struct InfercDecoderPlan {
         unsigned long long t0 = ~0ull;
         for (int c = 0; c < mega_grid; ++c)
           for (int e = 0; e < 7; ++e) t0 = std::min(t0, ev[(size_t)c * 16 + e]);
-        const char* en[14] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
+        const char* en[15] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
                               "fc end", "fp input staged", "fp end", "attn enter",
                               "attn qkv ready", "attn ctx done", "attn panel ready",
-                              "attn keys done", "attn max synced", "attn o reduced"};
-        for (int e = 0; e < 14; ++e) {
-          const int n = e < 7 ? mega_grid : (int)(nH * mega_chunks);  // attention CTAs only
+                              "attn keys done", "attn max synced", "attn o reduced",
+                              "fc copies issued"};
+        for (int e = 0; e < 15; ++e) {
+          const int n = (e < 7 || e == 14) ? mega_grid : (int)(nH * mega_chunks);  // attention CTAs only
           std::vector<double> v;
           for (int c = 0; c < n; ++c) v.push_back((ev[(size_t)c * 16 + e] - t0) / 1e3);
           std::vector<int> ids(n);
