@@ -56,6 +56,8 @@ constexpr int kMegaThreads = 256;
 // more while the whole grid requests its next panels at once; in this warp
 // the stall overlaps the next phase's wait for its inputs.
 constexpr int kIssuer = kMegaThreads - 32;
+// LM head: warps 0..kLmWarps-1 compute rows; the issuer's warp only refills.
+constexpr int kLmWarps = kMegaThreads / 32 - 1;
 constexpr int kSlotBytes = 48 * 1024;
 constexpr int kSlots = 4;
 constexpr unsigned long long kMegaWaitNs = 50ull * 1000 * 1000;  // 50 ms per wait
@@ -72,6 +74,10 @@ __device__ __forceinline__ void mb_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
                "r"(bytes)
                : "memory");
+}
+
+__device__ __forceinline__ void mb_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long gclock() {
@@ -133,6 +139,8 @@ constexpr int kLnMax = 800;  // LayerNorm width whose gamma / beta (+ a bias) ar
 
 struct Smem {
   uint64_t bar[kSlots];
+  uint64_t empty[kSlots];   // LM head: slot consumed by the kLmWarps row warps
+  uint32_t empty_uses[kSlots];  // completed waits on empty[] (issuer only)
   uint32_t uses[kSlots];    // completed waits per slot (parity tracking)
   uint32_t issued[kSlots];  // issued fills per slot (thread 0 only)
   uint64_t ln_bar;          // gamma / beta of the next LayerNorm phase
@@ -327,33 +335,6 @@ __device__ void prefetch_panels(const MegaPanels& m, int pair, uint8_t* slots, S
       bulk_load_stream(slots + (size_t)s * kSlotBytes + off, src + off, min(piece, bytes - off),
                        &sm.bar[s]);
   }
-}
-
-// L2 prefetch (no shared-memory destination, nothing to wait for): the
-// next layer's panels of this CTA are requested from HBM while the current
-// layer computes and waits at its barriers, so the later bulk copies into the
-// slots read L2. Addresses and sizes are multiples of 16 bytes (panels and
-// LM-head rows are).
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// Lanes of warp 0 issue this CTA's panels of layer L, 16 KiB per request.
-__device__ void prefetch_layer_l2(const MegaArgs& a, const MegaLayer& L) {
-  if (threadIdx.x >= 32) return;
-  const int lane = threadIdx.x;
-  int q = 0;  // running request index, spread over the lanes
-  auto panel = [&](const MegaPanels& m, int p) {
-    if (p >= m.npanels) return;
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(m.data + (size_t)p * m.K * m.P);
-    const uint32_t bytes = (uint32_t)m.K * m.P * 4;
-    for (uint32_t off = 0; off < bytes; off += 16384, ++q)
-      if ((q & 31) == lane) prefetch_l2(src + off, min(16384u, bytes - off));
-  };
-  for (int j = 0; j < 2; ++j) panel(L.attn, blockIdx.x + j * gridDim.x);
-  if (blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) panel(L.proj, blockIdx.x);
-  for (int j = 0; j < 2; ++j) panel(L.fc, blockIdx.x + j * gridDim.x);
-  for (int j = 0; j < 2; ++j) panel(L.fp, blockIdx.x + j * gridDim.x);
 }
 
 // Waits for slot s; all threads; false on timeout.
@@ -965,6 +946,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
   if (tid == 0) {
     for (int s = 0; s < kSlots; ++s) {
       mb_init(&sm.bar[s], 1);
+      mb_init(&sm.empty[s], kLmWarps);
+      sm.empty_uses[s] = 0;
       sm.uses[s] = 0;
       sm.issued[s] = 0;
     }
@@ -1036,15 +1019,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       const uint32_t tag_in = tag_step + 4u * (uint32_t)l + 1u;  // this layer's input
       const uint32_t tag_l = tag_in;  // phase ph writes tag_l + ph + 1
       const uint64_t* xin = a.tx + (size_t)(l & 1) * H;
-      if (a.l2_prefetch) {
-        if (!last) prefetch_layer_l2(a, a.layer[l + 1]);
-        else if (tid < 32) {  // the first chunks of this CTA's LM-head rows
-          for (int ch = 4 + tid; ch < min(lm_nchunks, 4 + a.lm_prefetch_chunks); ch += 32) {
-            const int ra = lm_r0 + ch * lm_crow, rb = min(lm_r1, ra + lm_crow);
-            prefetch_l2(a.wte + (size_t)ra * H, (uint32_t)(rb - ra) * H * 4);
-          }
-        }
-      }
       // ---- QKV (pair 0; W_proj is in slot 2, LN1's gamma / beta in sm.lnp)
       const EpiIn e_qkv = gemv_preload(L.attn, L.attn_b, nullptr, 0u, a, sm);
       const float *g1, *b1, *unused;
@@ -1112,44 +1086,64 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
                   a.eps, sm, a);
     }
     {
+      // A ring over the four slots without CTA barriers: row warps wait for a
+      // chunk's copy on its full barrier and release the slot on its empty
+      // barrier; the issuer refills a slot once all row warps released it.
       const int r0 = lm_r0, r1 = lm_r1, crow = lm_crow, nchunks = lm_nchunks;
-      auto issue = [&](int ch) { issue_lm(ch); };
       float bv = -INFINITY;
       int64_t bi = INT64_MAX;
-      for (int ch = 0; ch < nchunks; ++ch) {
-        const int s = ch % kSlots;
-        if (!wait_slot(s, sm, a)) { drain(sm); return; }
-        const float* w = reinterpret_cast<const float*>(slots + (size_t)s * kSlotBytes);
-        const int ra = r0 + ch * crow, rb = min(r1, ra + crow);
-        for (int r = ra + wid; r < rb; r += kMegaThreads / 32) {
-          const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(r - ra) * H);
-          const float4* x4 = reinterpret_cast<const float4*>(sm.xs);
-          float acc = 0.f;
-          for (int k = lane; k < H / 4; k += 32) {
-            const float4 wv = wr[k], xv = x4[k];
-            acc = fmaf(xv.x, wv.x, acc);
-            acc = fmaf(xv.y, wv.y, acc);
-            acc = fmaf(xv.z, wv.z, acc);
-            acc = fmaf(xv.w, wv.w, acc);
+      bool ok = true;
+      if (wid < kLmWarps) {
+        for (int ch = 0; ch < nchunks && ok; ++ch) {
+          const int s = ch % kSlots;
+          ok = mb_wait(&sm.bar[s], (sm.uses[s] + ch / kSlots) & 1);
+          if (!ok) break;
+          const float* w = reinterpret_cast<const float*>(slots + (size_t)s * kSlotBytes);
+          const int ra = r0 + ch * crow, rb = min(r1, ra + crow);
+          for (int r = ra + wid; r < rb; r += kLmWarps) {
+            const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(r - ra) * H);
+            const float4* x4 = reinterpret_cast<const float4*>(sm.xs);
+            float acc = 0.f;
+            for (int k = lane; k < H / 4; k += 32) {
+              const float4 wv = wr[k], xv = x4[k];
+              acc = fmaf(xv.x, wv.x, acc);
+              acc = fmaf(xv.y, wv.y, acc);
+              acc = fmaf(xv.z, wv.z, acc);
+              acc = fmaf(xv.w, wv.w, acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) a.logits[r] = acc;
+            if (acc > bv || (acc == bv && r < bi)) { bv = acc; bi = r; }
           }
-          acc = warp_sum(acc);
-          if (lane == 0) a.logits[r] = acc;
-          if (acc > bv || (acc == bv && r < bi)) { bv = acc; bi = r; }
+          __syncwarp();
+          if (lane == 0) mb_arrive(&sm.empty[s]);
         }
-        __syncthreads();  // slot s fully consumed
-        issue(ch + kSlots);
-        if (a.l2_prefetch && tid == kIssuer) {
-          const int pc = ch + 4 + a.lm_prefetch_chunks;
-          if (pc < nchunks) {
-            const int ra = r0 + pc * crow, rb = min(r1, ra + crow);
-            prefetch_l2(a.wte + (size_t)ra * H, (uint32_t)(rb - ra) * H * 4);
-          }
+      } else if (tid == kIssuer) {
+        // chunks 0..kSlots-1 were issued at the end of the last layer
+        for (int ch = 0; ch + kSlots < nchunks && ok; ++ch) {
+          const int s = ch % kSlots;
+          ok = mb_wait(&sm.empty[s], sm.empty_uses[s] & 1);
+          sm.empty_uses[s]++;
+          if (ok) issue_lm(ch + kSlots);
         }
-        if (a.l2_prefetch && ch == 0 && step + 1 < a.nsteps) prefetch_layer_l2(a, a.layer[0]);
+        // the last chunks' releases, so empty[] parity stays in step
+        for (int ch = max(0, nchunks - kSlots); ch < nchunks && ok; ++ch) {
+          const int s = ch % kSlots;
+          ok = mb_wait(&sm.empty[s], sm.empty_uses[s] & 1);
+          sm.empty_uses[s]++;
+        }
+      }
+      if (!ok) {
+        atomicExch(a.err, 1);
+        sm.abort_flag = 1;
       }
       if (lane == 0) { sm.bv[wid] = bv; sm.bi[wid] = bi; }
       __syncthreads();
       if (tid == 0) {
+        // completed waits of the row warps, per slot (after an abort the count
+        // stays short, so drain() waits, bounded, for every copy issued)
+        if (sm.abort_flag == 0)
+          for (int s = 0; s < kSlots; ++s) sm.uses[s] += (nchunks - s + kSlots - 1) / kSlots;
         float v = sm.bv[0];
         int64_t i = sm.bi[0];
         for (int w = 1; w < kMegaThreads / 32; ++w)

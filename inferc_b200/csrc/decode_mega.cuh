@@ -48,8 +48,6 @@ struct MegaArgs {
   int64_t pos0;        // position of the current token at the first step
   int nsteps;
   unsigned long long* prof;  // optional: phase timestamps of CTA 0, step 1
-  int l2_prefetch;           // 1: request the next layer's panels into L2 a layer ahead
-  int lm_prefetch_chunks;    // LM-head chunks (of 48 KiB) kept requested ahead
 };
 
 

@@ -805,14 +805,6 @@ struct InfercDecoderPlan {
       a.best_v = best_v; a.best_i = best_i; a.bar_count = bar;
       a.err = err; a.tok = tok; a.token_log = token_log; a.log_offset = 1;
       a.pos0 = n; a.nsteps = (int)(max_tokens - 1);
-      // INFERC_DECODE_L2=1 requests each layer's panels into L2 one layer
-      // ahead. Off by default: measured on a B200 it made decode slower
-      // (0.467 against 0.399 ms/token), the prefetches competing with the
-      // current phase's copies.
-      const char* l2 = std::getenv("INFERC_DECODE_L2");
-      a.l2_prefetch = l2 && l2[0] == '1';
-      const char* lmc = std::getenv("INFERC_DECODE_LM_AHEAD");
-      a.lm_prefetch_chunks = lmc ? std::atoi(lmc) : 8;
       a.prof = nullptr;
 #ifdef INFERC_DECODE_PROFILE
       // Development build only (-DINFERC_DECODE_PROFILE): CTA 0 stamps the
