@@ -250,10 +250,10 @@ __device__ bool grid_wait(const MegaArgs& a, Smem& sm) {
 }
 
 // Development builds (-DINFERC_DECODE_PROFILE): every CTA stamps event e
-// of layer 5 of step 1 into prof[64 + 16 * cta + e].
+// of layer 5 of step 1 into prof[64 + 32 * cta + e].
 __device__ __forceinline__ void stamp_event(const MegaArgs& a, bool on, int e) {
 #ifdef INFERC_DECODE_PROFILE
-  if (a.prof && on && threadIdx.x == 0) a.prof[64 + 16 * blockIdx.x + e] = gtimer();
+  if (a.prof && on && threadIdx.x == 0) a.prof[64 + 32 * blockIdx.x + e] = gtimer();
 #else
   (void)a; (void)on; (void)e;
 #endif
@@ -695,7 +695,7 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
   if (a.prof && pe && threadIdx.x == 0) {
     unsigned smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    a.prof[64 + 16 * blockIdx.x + 15] = smid;
+    a.prof[64 + 32 * blockIdx.x + 15] = smid;
   }
 #endif
   constexpr int HD = 64;
@@ -925,12 +925,14 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
     for (int k = sl; k < hd; k += slices) acc = fmaf(ctx[k], w[k * Wc + col], acc);
   sm.red[tid] = acc;
   __syncthreads();
+  stamp_event(a, pe, 16);
   if (tid < Wc) {
     float t = 0.f;
     for (int q = 0; q < slices; ++q) t += sm.red[q * Wc + tid];
     const int gcol = cc * Wc + tid;
     if (gcol < a.H) st_word(a.tpart + (size_t)h * a.H + gcol, t, part_tag);
   }
+  stamp_event(a, pe, 17);
   __syncthreads();
   return true;
 }

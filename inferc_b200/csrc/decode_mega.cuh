@@ -18,8 +18,14 @@ struct MegaLayer {
   float *kc, *vc;  // [heads][max_len][hd]
 };
 
+constexpr int kMegaMaxLayers = 48;
+
 struct MegaArgs {
-  const MegaLayer* layer;  // [layers], device memory
+  // The layer records travel in the kernel parameters (constant bank): with
+  // the panel ring taking nearly all of shared memory little L1 is left, and
+  // from global memory every phase's first look at its record was an L2
+  // round trip on the critical path.
+  MegaLayer layer[kMegaMaxLayers];
   int layers, H, heads, hd, F, V, max_len, max_pos;
   float eps;
   const float *wte, *wpe, *lnf_g, *lnf_b;

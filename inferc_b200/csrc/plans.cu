@@ -575,7 +575,7 @@ struct InfercDecoderPlan {
   // persistent-kernel state
   bool use_mega = false;
   int mega_grid = 0;
-  MegaLayer* mega_layers = nullptr;  // device array [L]
+  std::vector<MegaLayer> mega_layers;  // per layer, copied into the launch parameters
   float* best_v = nullptr;
   int64_t* best_i = nullptr;
   unsigned int* bar = nullptr;  // [count, generation]
@@ -780,7 +780,7 @@ struct InfercDecoderPlan {
     if (max_tokens > 1 && use_mega) {
       // All max_tokens-1 single-token steps in one persistent launch.
       MegaArgs a{};
-      a.layer = mega_layers;
+      std::copy(mega_layers.begin(), mega_layers.end(), a.layer);
       a.layers = (int)L; a.H = (int)H; a.heads = (int)nH; a.hd = (int)hd; a.F = (int)F;
       a.V = (int)V; a.max_len = (int)max_len; a.max_pos = (int)P; a.eps = eps;
       a.wte = wte; a.wpe = wpe; a.lnf_g = lnf_g; a.lnf_b = lnf_b;
@@ -809,7 +809,7 @@ struct InfercDecoderPlan {
 #ifdef INFERC_DECODE_PROFILE
       // Development build only (-DINFERC_DECODE_PROFILE): CTA 0 stamps the
       // global timer at the end of each phase of step 1 into a per-plan buffer.
-      if (!prof_buf) prof_buf = mem.alloc<unsigned long long>(4096);
+      if (!prof_buf) prof_buf = mem.alloc<unsigned long long>(8192);
       a.prof = prof_buf;
 #endif
       IDEV_CUDA(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned int), st));
@@ -827,26 +827,27 @@ struct InfercDecoderPlan {
                   q == 4 * L ? "lm" : names[q % 4], (t[q + 1] - t[q]) / 1e3);
         // per-CTA events of layer 5: min / median / max over CTAs, us after
         // the earliest event
-        std::vector<unsigned long long> ev((size_t)mega_grid * 16);
+        std::vector<unsigned long long> ev((size_t)mega_grid * 32);
         IDEV_CUDA(cudaMemcpy(ev.data(), prof_buf + 64, ev.size() * 8, cudaMemcpyDeviceToHost));
         unsigned long long t0 = ~0ull;
         for (int c = 0; c < mega_grid; ++c)
-          for (int e = 0; e < 7; ++e) t0 = std::min(t0, ev[(size_t)c * 16 + e]);
-        const char* en[15] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
+          for (int e = 0; e < 7; ++e) t0 = std::min(t0, ev[(size_t)c * 32 + e]);
+        const char* en[18] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
                               "fc end", "fp input staged", "fp end", "attn enter",
                               "attn qkv ready", "attn ctx done", "attn panel ready",
                               "attn keys done", "attn max synced", "attn o reduced",
-                              "fc copies issued"};
-        for (int e = 0; e < 15; ++e) {
+                              "fc copies issued", "smid", "proj summed", "proj stored"};
+        for (int e = 0; e < 18; ++e) {
+          if (e == 15) continue;
           const int n = (e < 7 || e == 14) ? mega_grid : (int)(nH * mega_chunks);  // attention CTAs only
           std::vector<double> v;
-          for (int c = 0; c < n; ++c) v.push_back((ev[(size_t)c * 16 + e] - t0) / 1e3);
+          for (int c = 0; c < n; ++c) v.push_back((ev[(size_t)c * 32 + e] - t0) / 1e3);
           std::vector<int> ids(n);
           for (int c = 0; c < n; ++c) ids[c] = c;
           std::sort(ids.begin(), ids.end(), [&](int x, int y) { return v[x] > v[y]; });
           fprintf(stderr, "  slowest CTAs:");
           for (int c = 0; c < std::min(n, 8); ++c)
-            fprintf(stderr, " %d/sm%llu(%.2f)", ids[c], ev[(size_t)ids[c] * 16 + 15], v[ids[c]]);
+            fprintf(stderr, " %d/sm%llu(%.2f)", ids[c], ev[(size_t)ids[c] * 32 + 15], v[ids[c]]);
           fprintf(stderr, "\n");
           std::sort(v.begin(), v.end());
           fprintf(stderr, "event %-17s min %6.2f  med %6.2f  max %6.2f us\n", en[e], v.front(),
@@ -898,7 +899,7 @@ static void setup_mega(InfercDecoderPlan* p) {
   IDEV_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
   if (mega_smem_bytes((int)p->max_len) + 16 * 1024 > (size_t)optin) return;
   if (H > 3072 || F > 3072 || H % 16 || F % 16 || p->hd % 4 || 256 % p->hd || p->hd > 128 ||
-      (H * 4) > 48 * 1024 || p->L < 1 || p->nH > 16)
+      (H * 4) > 48 * 1024 || p->L < 1 || p->L > kMegaMaxLayers || p->nH > 16)
     return;
   int grid = mega_max_grid((int)p->max_len);
   // Panel count of a [K, N] GEMV: the narrowest P (4, 8 or 16; the most
@@ -951,9 +952,9 @@ static void setup_mega(InfercDecoderPlan* p) {
     m.ln1_g = p->ln1g[l]; m.ln1_b = p->ln1b[l]; m.ln2_g = p->ln2g[l]; m.ln2_b = p->ln2b[l];
     m.kc = p->kc[l]; m.vc = p->vc[l];
   }
-  p->mega_layers = p->mem.alloc<MegaLayer>(layers.size());
-  IDEV_CUDA(cudaMemcpy(p->mega_layers, layers.data(), layers.size() * sizeof(MegaLayer),
-                       cudaMemcpyHostToDevice));
+  if (std::getenv("INFERC_DIAG_SHARED_PANELS"))  // DIAGNOSTIC ONLY (temporary)
+    for (auto& m : layers) { m.attn = layers[0].attn; m.proj = layers[0].proj; m.fc = layers[0].fc; m.fp = layers[0].fp; }
+  p->mega_layers = layers;
   p->best_v = p->mem.alloc<float>(grid);
   p->best_i = p->mem.alloc<int64_t>(grid);
   p->bar = p->mem.alloc<unsigned int>(2);
