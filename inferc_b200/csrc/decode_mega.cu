@@ -251,11 +251,11 @@ __device__ bool grid_wait(const MegaArgs& a, Smem& sm) {
 
 // Development builds (-DINFERC_DECODE_PROFILE): every CTA stamps event e
 // of layer 5 of step 1 into prof[64 + 32 * cta + e].
-__device__ __forceinline__ void stamp_event(const MegaArgs& a, bool on, int e) {
+__device__ __forceinline__ void stamp_event(const MegaArgs& a, bool on, int e, int by = 0) {
 #ifdef INFERC_DECODE_PROFILE
-  if (a.prof && on && threadIdx.x == 0) a.prof[64 + 32 * blockIdx.x + e] = gtimer();
+  if (a.prof && on && threadIdx.x == by) a.prof[64 + 32 * blockIdx.x + e] = gtimer();
 #else
-  (void)a; (void)on; (void)e;
+  (void)a; (void)on; (void)e; (void)by;
 #endif
 }
 
@@ -1044,7 +1044,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       stamp_event(a, step == 1 && l == 5, 1);
       prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);  // LN1's copy consumed
       prefetch_panels(L.fc, 0, slots, sm, a.piece);  // pair 0 consumed
-      stamp_event(a, step == 1 && l == 5, 14);
+      stamp_event(a, step == 1 && l == 5, 14, kIssuer);
       // ---- attention + output projection partials (slot 2)
       if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm, tag_l + 1u, tag_l + 2u,
                            step == 1 && l == 5) ||

@@ -952,8 +952,6 @@ static void setup_mega(InfercDecoderPlan* p) {
     m.ln1_g = p->ln1g[l]; m.ln1_b = p->ln1b[l]; m.ln2_g = p->ln2g[l]; m.ln2_b = p->ln2b[l];
     m.kc = p->kc[l]; m.vc = p->vc[l];
   }
-  if (std::getenv("INFERC_DIAG_SHARED_PANELS"))  // DIAGNOSTIC ONLY (temporary)
-    for (auto& m : layers) { m.attn = layers[0].attn; m.proj = layers[0].proj; m.fc = layers[0].fc; m.fp = layers[0].fp; }
   p->mega_layers = layers;
   p->best_v = p->mem.alloc<float>(grid);
   p->best_i = p->mem.alloc<int64_t>(grid);
