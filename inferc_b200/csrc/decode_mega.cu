@@ -733,6 +733,7 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
     const uint64_t* qp = a.tqkv + h * HD + tid;
     uint64_t w3[3] = {ld_word(qp), ld_word(qp + H), ld_word(qp + 2 * H)};
     settle(w3, qtag, [&](int i) { return qp + i * H; }, a, sm);
+    stamp_event(a, pe, 18);
     qs[tid] = word_f(w3[0]);
     kn[tid] = word_f(w3[1]);
     vn[tid] = word_f(w3[2]);
@@ -920,10 +921,19 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
   // threads: (column, row-slice); Wc <= 256
   const int slices = kMegaThreads / Wc;
   const int col = tid % Wc, sl = tid / Wc;
-  float acc = 0.f;
-  if (sl < slices)
-    for (int k = sl; k < hd; k += slices) acc = fmaf(ctx[k], w[k * Wc + col], acc);
-  sm.red[tid] = acc;
+  // four independent partial sums (rows k, k + slices, ...) shorten the chain
+  float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+  if (sl < slices) {
+    int k = sl;
+    for (; k + 3 * slices < hd; k += 4 * slices) {
+      c0 = fmaf(ctx[k], w[k * Wc + col], c0);
+      c1 = fmaf(ctx[k + slices], w[(k + slices) * Wc + col], c1);
+      c2 = fmaf(ctx[k + 2 * slices], w[(k + 2 * slices) * Wc + col], c2);
+      c3 = fmaf(ctx[k + 3 * slices], w[(k + 3 * slices) * Wc + col], c3);
+    }
+    for (; k < hd; k += slices) c0 = fmaf(ctx[k], w[k * Wc + col], c0);
+  }
+  sm.red[tid] = (c0 + c1) + (c2 + c3);
   __syncthreads();
   stamp_event(a, pe, 16);
   if (tid < Wc) {

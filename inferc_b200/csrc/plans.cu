@@ -832,12 +832,13 @@ struct InfercDecoderPlan {
         unsigned long long t0 = ~0ull;
         for (int c = 0; c < mega_grid; ++c)
           for (int e = 0; e < 7; ++e) t0 = std::min(t0, ev[(size_t)c * 32 + e]);
-        const char* en[18] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
+        const char* en[19] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
                               "fc end", "fp input staged", "fp end", "attn enter",
                               "attn qkv ready", "attn ctx done", "attn panel ready",
                               "attn keys done", "attn max synced", "attn o reduced",
-                              "fc copies issued", "smid", "proj summed", "proj stored"};
-        for (int e = 0; e < 18; ++e) {
+                              "fc copies issued", "smid", "proj summed", "proj stored",
+                              "attn t0 qkv settled"};
+        for (int e = 0; e < 19; ++e) {
           if (e == 15) continue;
           const int n = (e < 7 || e == 14) ? mega_grid : (int)(nH * mega_chunks);  // attention CTAs only
           std::vector<double> v;
