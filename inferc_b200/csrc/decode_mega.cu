@@ -327,10 +327,10 @@ __device__ void prefetch_panels(const MegaPanels& m, int pair, uint8_t* slots, S
     const int p = blockIdx.x + j * gridDim.x;
     if (p >= m.npanels) break;
     const int s = 2 * pair + j;
-    const uint32_t bytes = (uint32_t)m.K * m.P * 4;
+    const uint32_t bytes = m.bytes;
     sm.issued[s]++;
     mb_expect_tx(&sm.bar[s], bytes);
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(m.data + (size_t)p * m.K * m.P);
+    const uint8_t* src = m.data + (size_t)p * m.bytes;
     for (uint32_t off = 0; off < bytes; off += piece)
       bulk_load_stream(slots + (size_t)s * kSlotBytes + off, src + off, min(piece, bytes - off),
                        &sm.bar[s]);
@@ -465,12 +465,13 @@ __device__ void stage_smem_ln(int K, const float* g, const float* b, float eps, 
 // staging so their latency overlaps it.
 struct EpiIn {
   float add[2];
+  float sc[2];  // int4: the columns' scales
 };
 
 __device__ __forceinline__ EpiIn gemv_preload(const MegaPanels& m, const float* bias,
                                               const uint64_t* resid, uint32_t rtag,
                                               const MegaArgs& a, Smem& sm) {
-  EpiIn e{{0.f, 0.f}};
+  EpiIn e{{0.f, 0.f}, {1.f, 1.f}};
   const int tid = threadIdx.x;
   if (tid < m.P) {
 #pragma unroll
@@ -478,6 +479,7 @@ __device__ __forceinline__ EpiIn gemv_preload(const MegaPanels& m, const float* 
       const int p = blockIdx.x + j * gridDim.x;
       const int col = p * m.P + tid;
       if (p < m.npanels && col < m.N) {
+        if (m.scale) e.sc[j] = __ldg(m.scale + col);
         float v = __ldg(bias + col);
         if (resid) {
           uint64_t rw[1] = {ld_word(resid + col)};
@@ -494,6 +496,7 @@ __device__ __forceinline__ EpiIn gemv_preload(const MegaPanels& m, const float* 
 // y[col] = act(xs . panel[:, c] + bias[col] (+ resid[col])) for this CTA's
 // panels (slots 2*pair, 2*pair+1), both panels in one pass; y is written as
 // tagged words with `ytag`.
+template <bool Q4>
 __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, const EpiIn& e,
                            uint64_t* y, uint32_t ytag, int act, Smem& sm, const MegaArgs& a) {
   const int tid = threadIdx.x;
@@ -518,7 +521,30 @@ __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, 
   float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
   const float4* w04 = reinterpret_cast<const float4*>(w0);
   const float4* w14 = reinterpret_cast<const float4*>(w1);
-  if (np == 2) {
+  if constexpr (Q4) {
+    // words (kg, c): 8 consecutive k of column c; a thread takes a column
+    // quad (one 16-byte load per panel) over k groups kg = sl, sl + slices, ...
+    const uint4* v0 = reinterpret_cast<const uint4*>(w0);
+    const uint4* v1 = reinterpret_cast<const uint4*>(w1);
+    const float4* x4 = reinterpret_cast<const float4*>(sm.xs);
+    auto dot8 = [](uint32_t q, const float (&xv)[8], float acc) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = fmaf((float)((int)((q >> (4 * i)) & 15u) - 8), xv[i], acc);
+      return acc;
+    };
+    for (int kg = sl; kg < K / 8; kg += slices) {
+      const float4 xa = x4[2 * kg], xb = x4[2 * kg + 1];
+      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      const uint4 u = v0[kg * P4 + c4];
+      a0.x = dot8(u.x, xv, a0.x); a0.y = dot8(u.y, xv, a0.y);
+      a0.z = dot8(u.z, xv, a0.z); a0.w = dot8(u.w, xv, a0.w);
+      if (np == 2) {
+        const uint4 t = v1[kg * P4 + c4];
+        a1.x = dot8(t.x, xv, a1.x); a1.y = dot8(t.y, xv, a1.y);
+        a1.z = dot8(t.z, xv, a1.z); a1.w = dot8(t.w, xv, a1.w);
+      }
+    }
+  } else if (np == 2) {
 #pragma unroll 4
     for (int k = sl; k < K; k += slices) {
       const float xv = sm.xs[k];
@@ -558,6 +584,7 @@ __device__ bool gemv_phase(const MegaPanels& m, int pair, const uint8_t* slots, 
       float t = 0.f;
       for (int q = 0; q < nw; ++q) t += sm.red[(j * nw + q) * P + tid];
       const int col = (blockIdx.x + j * gridDim.x) * P + tid;
+      if (Q4) t *= e.sc[j];
       if (col < m.N) st_word(y + col, apply_act(t + e.add[j], act), ytag);
     }
   }
@@ -899,6 +926,7 @@ __device__ void stage_attn_residual(const MegaArgs& a, const float* proj_b, cons
 // part[h][cols] = ctx_h . W_proj[h*hd:(h+1)*hd, cols] from its prefetched
 // [hd][Wc] panel in slot `slot`. The partials are summed (fixed order) by
 // the next phase.
+template <bool Q4>
 __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t pos, float* scr,
                                 const uint8_t* slots, int slot, Smem& sm, uint32_t qtag,
                                 uint32_t part_tag, bool pe) {
@@ -907,6 +935,11 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
   if (c >= a.heads * chunks) return true;
   const int h = c / chunks, cc = c % chunks;
   float* ctx = scr + 384 + a.max_len + 4 + (kMegaThreads / 32) * 128;  // [hd]
+  const int tid = threadIdx.x;
+  const int Wc = L.proj.P, hd = a.hd;
+  // int4: the chunk's column scales, loaded while the attention runs
+  float csc = 1.f;
+  if (Q4 && tid < Wc && cc * Wc + tid < a.H) csc = __ldg(L.proj.scale + cc * Wc + tid);
   if (a.hd == 64)
     attention_head64(a, L, pos, scr, sm, h, cc == 0, ctx, qtag, pe);
   else
@@ -914,16 +947,27 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
   stamp_event(a, pe, 9);
   if (!wait_slot(slot, sm, a)) return false;
   stamp_event(a, pe, 10);
-  const MegaPanels& m = L.proj;  // K = hd, P = chunk width
+  // L.proj: K = hd, P = chunk width
   const float* w = reinterpret_cast<const float*>(slots + (size_t)slot * kSlotBytes);
-  const int tid = threadIdx.x;
-  const int Wc = m.P, hd = a.hd;
   // threads: (column, row-slice); Wc <= 256
   const int slices = kMegaThreads / Wc;
   const int col = tid % Wc, sl = tid / Wc;
   // four independent partial sums (rows k, k + slices, ...) shorten the chain
   float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
-  if (sl < slices) {
+  if constexpr (Q4) {
+    // [hd/8][Wc] words: word (kg, c) = 8 consecutive k of column c
+    const uint32_t* wq = reinterpret_cast<const uint32_t*>(w);
+    for (int kg = sl; sl < slices && kg < hd / 8; kg += slices) {
+      const uint32_t q = wq[kg * Wc + col];
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        d0 = fmaf((float)((int)((q >> (4 * i)) & 15u) - 8), ctx[8 * kg + i], d0);
+        d1 = fmaf((float)((int)((q >> (4 * i + 4)) & 15u) - 8), ctx[8 * kg + i + 1], d1);
+      }
+      if (kg & 1) c1 += d0 + d1; else c0 += d0 + d1;
+    }
+  } else if (sl < slices) {
     int k = sl;
     for (; k + 3 * slices < hd; k += 4 * slices) {
       c0 = fmaf(ctx[k], w[k * Wc + col], c0);
@@ -940,6 +984,7 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
     float t = 0.f;
     for (int q = 0; q < slices; ++q) t += sm.red[q * Wc + tid];
     const int gcol = cc * Wc + tid;
+    if (Q4) t *= csc;
     if (gcol < a.H) st_word(a.tpart + (size_t)h * a.H + gcol, t, part_tag);
   }
   stamp_event(a, pe, 17);
@@ -949,6 +994,7 @@ __device__ bool attn_proj_phase(const MegaArgs& a, const MegaLayer& L, int64_t p
 
 }  // namespace
 
+template <bool Q4>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __grid_constant__ MegaArgs a) {
   extern __shared__ __align__(128) uint8_t mega_smem[];
   uint8_t* slots = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mega_smem) + 127) &
@@ -985,11 +1031,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
   // CTA has consumed it, off the critical path of the next phase.
   auto issue_proj = [&](const MegaLayer& Lx) {  // W_proj panel -> slot 2
     if (tid == kIssuer && blockIdx.x < (unsigned)(a.heads * a.proj_chunks)) {
-      const uint32_t bytes = (uint32_t)Lx.proj.K * Lx.proj.P * 4;
+      const uint32_t bytes = Lx.proj.bytes;
       sm.issued[2]++;
       mb_expect_tx(&sm.bar[2], bytes);
       bulk_load_stream(slots + 2 * (size_t)kSlotBytes,
-                       Lx.proj.data + (size_t)blockIdx.x * Lx.proj.K * Lx.proj.P, bytes,
+                       Lx.proj.data + (size_t)blockIdx.x * bytes, bytes,
                        &sm.bar[2]);
     }
   };
@@ -997,16 +1043,19 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
   const int lm_rows = (a.V + gridDim.x - 1) / gridDim.x;
   const int lm_r0 = blockIdx.x * lm_rows;
   const int lm_r1 = min(a.V, lm_r0 + lm_rows);
-  const int lm_crow = kSlotBytes / (H * 4);
+  // LM-head rows: fp32 wte [V][H] or the int4 head [V][H/2]
+  const int lm_row_bytes = Q4 ? H / 2 : H * 4;
+  const int lm_crow = kSlotBytes / lm_row_bytes;
   const int lm_nchunks = lm_r1 > lm_r0 ? (lm_r1 - lm_r0 + lm_crow - 1) / lm_crow : 0;
   auto issue_lm = [&](int ch) {
     if (tid != kIssuer || ch >= lm_nchunks) return;
     const int s = ch % kSlots;
     const int ra = lm_r0 + ch * lm_crow, rb = min(lm_r1, ra + lm_crow);
-    const uint32_t bytes = (uint32_t)(rb - ra) * H * 4;
+    const uint32_t bytes = (uint32_t)(rb - ra) * lm_row_bytes;
     sm.issued[s]++;
     mb_expect_tx(&sm.bar[s], bytes);
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wte + (size_t)ra * H);
+    const uint8_t* src = (Q4 ? a.lm_q : reinterpret_cast<const uint8_t*>(a.wte)) +
+                         (size_t)ra * lm_row_bytes;
     for (uint32_t off = 0; off < bytes; off += a.piece)
       bulk_load_stream(slots + (size_t)s * kSlotBytes + off, src + off,
                        min(a.piece, bytes - off), &sm.bar[s]);
@@ -1049,14 +1098,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
         stage_input(xin, tag_in, H, g1, b1, a.eps, sm, a);
       }
       stamp_event(a, step == 1 && l == 5, 0);
-      if (!gemv_phase(L.attn, 0, slots, e_qkv, a.tqkv, tag_l + 1u, ACT_NONE, sm, a) ||
+      if (!gemv_phase<Q4>(L.attn, 0, slots, e_qkv, a.tqkv, tag_l + 1u, ACT_NONE, sm, a) ||
           !phase_end(a, sm, 4 * l + 0, step)) { drain(sm); return; }
       stamp_event(a, step == 1 && l == 5, 1);
       prefetch_ln(L.ln2_g, L.ln2_b, L.proj_b, H, sm);  // LN1's copy consumed
       prefetch_panels(L.fc, 0, slots, sm, a.piece);  // pair 0 consumed
       stamp_event(a, step == 1 && l == 5, 14, kIssuer);
       // ---- attention + output projection partials (slot 2)
-      if (!attn_proj_phase(a, L, pos, scr, slots, 2, sm, tag_l + 1u, tag_l + 2u,
+      if (!attn_proj_phase<Q4>(a, L, pos, scr, slots, 2, sm, tag_l + 1u, tag_l + 2u,
                            step == 1 && l == 5) ||
           !phase_end(a, sm, 4 * l + 1, step)) { drain(sm); return; }
       stamp_event(a, step == 1 && l == 5, 2);
@@ -1067,7 +1116,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       if (!ln_params(L.ln2_g, L.ln2_b, L.proj_b, H, sm, a, &g2, &b2, &pb)) { drain(sm); return; }
       stage_attn_residual(a, pb, g2, b2, xin, tag_in, tag_l + 2u, tag_l + 3u, sm);
       stamp_event(a, step == 1 && l == 5, 3);
-      if (!gemv_phase(L.fc, 0, slots, e_fc, a.tf, tag_l + 3u, ACT_GELU_TANH, sm, a) ||
+      if (!gemv_phase<Q4>(L.fc, 0, slots, e_fc, a.tf, tag_l + 3u, ACT_GELU_TANH, sm, a) ||
           !phase_end(a, sm, 4 * l + 2, step)) { drain(sm); return; }
       stamp_event(a, step == 1 && l == 5, 4);
       // LN2's copy consumed: the next LayerNorm's vectors (small, first)
@@ -1078,7 +1127,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       const EpiIn e_fp = gemv_preload(L.fp, L.fp_b, a.txm, tag_l + 3u, a, sm);
       stage_input(a.tf, tag_l + 3u, a.F, nullptr, nullptr, 0.f, sm, a);
       stamp_event(a, step == 1 && l == 5, 5);
-      if (!gemv_phase(L.fp, 1, slots, e_fp, a.tx + (size_t)((l + 1) & 1) * H, tag_l + 4u,
+      if (!gemv_phase<Q4>(L.fp, 1, slots, e_fp, a.tx + (size_t)((l + 1) & 1) * H, tag_l + 4u,
                       ACT_NONE, sm, a) ||
           !phase_end(a, sm, 4 * l + 3, step)) { drain(sm); return; }
       stamp_event(a, step == 1 && l == 5, 6);
@@ -1110,20 +1159,35 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
           const int s = ch % kSlots;
           ok = mb_wait(&sm.bar[s], (sm.uses[s] + ch / kSlots) & 1);
           if (!ok) break;
-          const float* w = reinterpret_cast<const float*>(slots + (size_t)s * kSlotBytes);
+          const uint8_t* w = slots + (size_t)s * kSlotBytes;
           const int ra = r0 + ch * crow, rb = min(r1, ra + crow);
           for (int r = ra + wid; r < rb; r += kLmWarps) {
-            const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(r - ra) * H);
             const float4* x4 = reinterpret_cast<const float4*>(sm.xs);
             float acc = 0.f;
-            for (int k = lane; k < H / 4; k += 32) {
-              const float4 wv = wr[k], xv = x4[k];
-              acc = fmaf(xv.x, wv.x, acc);
-              acc = fmaf(xv.y, wv.y, acc);
-              acc = fmaf(xv.z, wv.z, acc);
-              acc = fmaf(xv.w, wv.w, acc);
+            if constexpr (Q4) {
+              // row of H/8 words (8 consecutive k each, low nibble first)
+              const float rs = __ldg(a.lm_s + r);
+              const uint32_t* wr = reinterpret_cast<const uint32_t*>(w + (size_t)(r - ra) * (H / 2));
+              for (int k = lane; k < H / 8; k += 32) {
+                const uint32_t q = wr[k];
+                const float4 xa = x4[2 * k], xb = x4[2 * k + 1];
+                const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  acc = fmaf((float)((int)((q >> (4 * i)) & 15u) - 8), xv[i], acc);
+              }
+              acc = warp_sum(acc) * rs;
+            } else {
+              const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(r - ra) * H * 4);
+              for (int k = lane; k < H / 4; k += 32) {
+                const float4 wv = wr[k], xv = x4[k];
+                acc = fmaf(xv.x, wv.x, acc);
+                acc = fmaf(xv.y, wv.y, acc);
+                acc = fmaf(xv.z, wv.z, acc);
+                acc = fmaf(xv.w, wv.w, acc);
+              }
+              acc = warp_sum(acc);
             }
-            acc = warp_sum(acc);
             if (lane == 0) a.logits[r] = acc;
             if (acc > bv || (acc == bv && r < bi)) { bv = acc; bi = r; }
           }
@@ -1206,22 +1270,20 @@ size_t mega_smem_bytes(int max_len) {
          (size_t)(384 + max_len + 4 + (kMegaThreads / 32) * 128 + 128) * sizeof(float);
 }
 
-void launch_decode_mega(const MegaArgs& a, int grid, cudaStream_t st) {
+void launch_decode_mega(const MegaArgs& a, int grid, bool q4, cudaStream_t st) {
   const size_t smem = mega_smem_bytes(a.max_len);
-  IDEV_CUDA(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
+  const void* fn = q4 ? (const void*)decode_mega_kernel<true> : (const void*)decode_mega_kernel<false>;
+  IDEV_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* args[] = {const_cast<MegaArgs*>(&a)};
-  IDEV_CUDA(cudaLaunchCooperativeKernel((const void*)decode_mega_kernel, dim3(grid),
-                                        dim3(kMegaThreads), args, smem, st));
+  IDEV_CUDA(cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kMegaThreads), args, smem, st));
 }
 
-int mega_max_grid(int max_len) {
+int mega_max_grid(int max_len, bool q4) {
   const size_t smem = mega_smem_bytes(max_len);
-  IDEV_CUDA(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
+  const void* fn = q4 ? (const void*)decode_mega_kernel<true> : (const void*)decode_mega_kernel<false>;
+  IDEV_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0, dev = 0, sms = 0;
-  IDEV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mega_kernel,
-                                                          kMegaThreads, smem));
+  IDEV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kMegaThreads, smem));
   IDEV_CUDA(cudaGetDevice(&dev));
   IDEV_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   return std::min(per_sm, 1) * sms;
@@ -1261,6 +1323,54 @@ __global__ void panelize_proj_kernel(const float* __restrict__ w, float* __restr
 void launch_panelize_proj(const float* w, float* out, int H, int hd, int heads, int chunks, int Wc,
                           cudaStream_t st) {
   panelize_proj_kernel<<<148 * 8, 256, 0, st>>>(w, out, H, hd, heads, chunks, Wc);
+  IDEV_LAUNCHED();
+}
+
+// int4 [N, K/2] (row n: K/8 words, 8 consecutive k each) -> panels
+// [npanels][K/8][P] words; columns past N get 8s (q - 8 = 0).
+__global__ void panelize_q4_kernel(const uint8_t* __restrict__ q, uint32_t* __restrict__ out,
+                                   int K, int N, int P, int npanels) {
+  const int KG = K / 8;
+  const int64_t total = (int64_t)npanels * KG * P;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(e % P);
+    const int kg = (int)((e / P) % KG);
+    const int p = (int)(e / ((int64_t)P * KG));
+    const int n = p * P + c;
+    out[e] = n < N ? reinterpret_cast<const uint32_t*>(q + (int64_t)n * (K / 2))[kg] : 0x88888888u;
+  }
+}
+
+// int4 W_proj [H (out), H/2] -> [heads][chunks][hd/8][Wc] words: k groups of
+// head h, columns of chunk cc (8s past H).
+__global__ void panelize_proj_q4_kernel(const uint8_t* __restrict__ q, uint32_t* __restrict__ out,
+                                        int H, int hd, int heads, int chunks, int Wc) {
+  const int KG = hd / 8;
+  const int64_t total = (int64_t)heads * chunks * KG * Wc;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(e % Wc);
+    const int kg = (int)((e / Wc) % KG);
+    const int cc = (int)((e / ((int64_t)Wc * KG)) % chunks);
+    const int h = (int)(e / ((int64_t)Wc * KG * chunks));
+    const int n = cc * Wc + c;
+    out[e] = n < H ? reinterpret_cast<const uint32_t*>(q + (int64_t)n * (H / 2))[h * KG + kg]
+                   : 0x88888888u;
+  }
+}
+
+void launch_panelize_q4(const uint8_t* q, uint32_t* out, int K, int N, int P, int npanels,
+                        cudaStream_t st) {
+  const int64_t total = (int64_t)npanels * (K / 8) * P;
+  panelize_q4_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16), 256, 0, st>>>(
+      q, out, K, N, P, npanels);
+  IDEV_LAUNCHED();
+}
+
+void launch_panelize_proj_q4(const uint8_t* q, uint32_t* out, int H, int hd, int heads,
+                             int chunks, int Wc, cudaStream_t st) {
+  panelize_proj_q4_kernel<<<148 * 8, 256, 0, st>>>(q, out, H, hd, heads, chunks, Wc);
   IDEV_LAUNCHED();
 }
 

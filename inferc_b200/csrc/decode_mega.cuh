@@ -6,9 +6,16 @@
 namespace inferc_dev {
 
 // ------------------------------------------------------------ parameters
+// Column panels of one weight matrix, contiguous per panel:
+//  - fp32: [npanels][K][P] floats;
+//  - int4 (per-output-column scale): [npanels][K/8][P] 32-bit words, word
+//    (kg, c) holding q[n][8 kg .. 8 kg + 7] of column n = p P + c in the
+//    reference's nibble order (low nibble first); columns past N hold 8s.
 struct MegaPanels {
-  const float* data;  // [npanels][K][P]
+  const uint8_t* data;
   int K, N, P, npanels;
+  uint32_t bytes;      // one panel
+  const float* scale;  // int4: s[n] per output column; fp32: null
 };
 
 struct MegaLayer {
@@ -29,6 +36,8 @@ struct MegaArgs {
   int layers, H, heads, hd, F, V, max_len, max_pos;
   float eps;
   const float *wte, *wpe, *lnf_g, *lnf_b;
+  const uint8_t* lm_q;  // int4 LM head [V][H/2] (rows contiguous) and its scales [V]
+  const float* lm_s;
   // Activations passed between CTAs inside a step. Every 64-bit word holds
   // (tag << 32) | fp32 bits and is written once per phase instance with that
   // instance's tag, so a reader's load is also its wait: it re-reads a word
@@ -59,12 +68,18 @@ struct MegaArgs {
 
 // Dynamic shared memory the kernel needs for a cache of max_len positions.
 size_t mega_smem_bytes(int max_len);
-// CTAs that can be co-resident (0 when the kernel does not fit).
-int mega_max_grid(int max_len);
-void launch_decode_mega(const MegaArgs& a, int grid, cudaStream_t st);
+// CTAs that can be co-resident (0 when the kernel does not fit); q4 selects
+// the int4-weight form of the kernel.
+int mega_max_grid(int max_len, bool q4);
+void launch_decode_mega(const MegaArgs& a, int grid, bool q4, cudaStream_t st);
 void launch_panelize(const float* w, float* out, int K, int N, int P, int npanels,
                      cudaStream_t st);
 void launch_panelize_proj(const float* w, float* out, int H, int hd, int heads, int chunks, int Wc,
                           cudaStream_t st);
+// int4 [N, K/2] per-row-scale weights (the reference's layout) into panels.
+void launch_panelize_q4(const uint8_t* q, uint32_t* out, int K, int N, int P, int npanels,
+                        cudaStream_t st);
+void launch_panelize_proj_q4(const uint8_t* q, uint32_t* out, int H, int hd, int heads,
+                             int chunks, int Wc, cudaStream_t st);
 
 }  // namespace inferc_dev

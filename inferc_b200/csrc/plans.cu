@@ -745,9 +745,15 @@ struct InfercDecoderPlan {
       IDEV_CUDA(cudaMemcpyAsync(tok, ids + i, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
       IDEV_CUDA(cudaGraphLaunch(int4_graph->exec, st));
     }
-    IDEV_CUDA(cudaEventRecord(ev0, st));
-    for (int64_t s = 1; s < max_tokens; ++s) IDEV_CUDA(cudaGraphLaunch(int4_graph->exec, st));
-    IDEV_CUDA(cudaEventRecord(ev1, st));
+    if (max_tokens > 1 && use_mega) {
+      // the generated tokens: the persistent kernel on the int4 panels, from
+      // the first generated token (token_log[n], in `tok`) at position n
+      run_mega(n, n + 1, max_tokens - 1, st);
+    } else {
+      IDEV_CUDA(cudaEventRecord(ev0, st));
+      for (int64_t s = 1; s < max_tokens; ++s) IDEV_CUDA(cudaGraphLaunch(int4_graph->exec, st));
+      IDEV_CUDA(cudaEventRecord(ev1, st));
+    }
     IDEV_CUDA(cudaMemcpyAsync(out, token_log + n, max_tokens * sizeof(int64_t),
                               cudaMemcpyDeviceToHost, st));
     int herr = 0;
@@ -764,6 +770,89 @@ struct InfercDecoderPlan {
     }
   }
 
+  // nsteps single-token steps in one persistent launch: the token in `tok`
+  // at position pos0 first; step s logs its token at token_log[log_offset + s].
+  void run_mega(int64_t pos0, int64_t log_offset, int64_t nsteps, cudaStream_t st) {
+    MegaArgs a{};
+    std::copy(mega_layers.begin(), mega_layers.end(), a.layer);
+    a.layers = (int)L; a.H = (int)H; a.heads = (int)nH; a.hd = (int)hd; a.F = (int)F;
+    a.V = (int)V; a.max_len = (int)max_len; a.max_pos = (int)P; a.eps = eps;
+    a.wte = wte; a.wpe = wpe; a.lnf_g = lnf_g; a.lnf_b = lnf_b;
+    a.tx = mega_tags;
+    a.txm = a.tx + 2 * H;
+    a.tqkv = a.txm + H;
+    a.tpart = a.tqkv + 3 * H;
+    a.tf = a.tpart + nH * H;
+    // Tags only grow within [1, 2^31): when a launch would pass that, the
+    // words are cleared and the tags start again.
+    const uint64_t span = (uint64_t)nsteps * (4 * (uint64_t)L + 1);
+    if ((uint64_t)mega_tag_next + span >= (1ull << 31)) {
+      IDEV_CUDA(cudaMemsetAsync(mega_tags, 0, mega_tag_words * sizeof(uint64_t), st));
+      mega_tag_next = 0;
+    }
+    a.tag_base = mega_tag_next;
+    const char* pc = std::getenv("INFERC_DECODE_PIECE");
+    a.piece = pc ? (uint32_t)std::max(16, std::atoi(pc) / 16 * 16) : 49152u;
+    mega_tag_next += (uint32_t)span;
+    a.logits = logits;
+    a.proj_chunks = mega_chunks;
+    a.best_v = best_v; a.best_i = best_i; a.bar_count = bar;
+    a.err = err; a.tok = tok; a.token_log = token_log; a.log_offset = log_offset;
+    a.pos0 = pos0; a.nsteps = (int)nsteps;
+    if (int4) { a.lm_q = q_lm; a.lm_s = s_lm; }
+    a.prof = nullptr;
+#ifdef INFERC_DECODE_PROFILE
+    // Development build only (-DINFERC_DECODE_PROFILE): CTA 0 stamps the
+    // global timer at the end of each phase of step 1 into a per-plan buffer.
+    if (!prof_buf) prof_buf = mem.alloc<unsigned long long>(8192);
+    a.prof = prof_buf;
+#endif
+    IDEV_CUDA(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned int), st));
+    IDEV_CUDA(cudaEventRecord(ev0, st));
+    launch_decode_mega(a, mega_grid, int4, st);
+    IDEV_CUDA(cudaEventRecord(ev1, st));
+#ifdef INFERC_DECODE_PROFILE
+    {
+      std::vector<unsigned long long> t(4 * L + 2);
+      IDEV_CUDA(cudaMemcpyAsync(t.data(), prof_buf, t.size() * 8, cudaMemcpyDeviceToHost, st));
+      IDEV_CUDA(cudaStreamSynchronize(st));
+      const char* names[4] = {"qkv", "attn+proj", "fc", "fp"};
+      for (int q = 0; q <= 4 * L; ++q)  // phase q ends at stamp q + 1
+        fprintf(stderr, "layer %2d phase %-9s %6.2f us\n", (int)(q / 4),
+                q == 4 * L ? "lm" : names[q % 4], (t[q + 1] - t[q]) / 1e3);
+      // per-CTA events of layer 5: min / median / max over CTAs, us after
+      // the earliest event
+      std::vector<unsigned long long> ev((size_t)mega_grid * 32);
+      IDEV_CUDA(cudaMemcpy(ev.data(), prof_buf + 64, ev.size() * 8, cudaMemcpyDeviceToHost));
+      unsigned long long t0 = ~0ull;
+      for (int c = 0; c < mega_grid; ++c)
+        for (int e = 0; e < 7; ++e) t0 = std::min(t0, ev[(size_t)c * 32 + e]);
+      const char* en[19] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
+                            "fc end", "fp input staged", "fp end", "attn enter",
+                            "attn qkv ready", "attn ctx done", "attn panel ready",
+                            "attn keys done", "attn max synced", "attn o reduced",
+                            "fc copies issued", "smid", "proj summed", "proj stored",
+                            "attn t0 qkv settled"};
+      for (int e = 0; e < 19; ++e) {
+        if (e == 15) continue;
+        const int n = (e < 7 || e == 14) ? mega_grid : (int)(nH * mega_chunks);  // attention CTAs only
+        std::vector<double> v;
+        for (int c = 0; c < n; ++c) v.push_back((ev[(size_t)c * 32 + e] - t0) / 1e3);
+        std::vector<int> ids(n);
+        for (int c = 0; c < n; ++c) ids[c] = c;
+        std::sort(ids.begin(), ids.end(), [&](int x, int y) { return v[x] > v[y]; });
+        fprintf(stderr, "  slowest CTAs:");
+        for (int c = 0; c < std::min(n, 8); ++c)
+          fprintf(stderr, " %d/sm%llu(%.2f)", ids[c], ev[(size_t)ids[c] * 32 + 15], v[ids[c]]);
+        fprintf(stderr, "\n");
+        std::sort(v.begin(), v.end());
+        fprintf(stderr, "event %-17s min %6.2f  med %6.2f  max %6.2f us\n", en[e], v.front(),
+                v[v.size() / 2], v.back());
+      }
+    }
+#endif
+  }
+
   void decode(const int64_t* prompt, int64_t n, int64_t max_tokens, int64_t* out,
               double* step_ms) {
     IDEV_CHECK_ARG(prompt != nullptr && out != nullptr, "decode: null prompt or output");
@@ -778,84 +867,7 @@ struct InfercDecoderPlan {
     n_host_scratch = n;
     prefill(n, st);
     if (max_tokens > 1 && use_mega) {
-      // All max_tokens-1 single-token steps in one persistent launch.
-      MegaArgs a{};
-      std::copy(mega_layers.begin(), mega_layers.end(), a.layer);
-      a.layers = (int)L; a.H = (int)H; a.heads = (int)nH; a.hd = (int)hd; a.F = (int)F;
-      a.V = (int)V; a.max_len = (int)max_len; a.max_pos = (int)P; a.eps = eps;
-      a.wte = wte; a.wpe = wpe; a.lnf_g = lnf_g; a.lnf_b = lnf_b;
-      a.tx = mega_tags;
-      a.txm = a.tx + 2 * H;
-      a.tqkv = a.txm + H;
-      a.tpart = a.tqkv + 3 * H;
-      a.tf = a.tpart + nH * H;
-      // Tags only grow within [1, 2^31): when a launch would pass that, the
-      // words are cleared and the tags start again.
-      const uint64_t span = (uint64_t)(max_tokens - 1) * (4 * (uint64_t)L + 1);
-      if ((uint64_t)mega_tag_next + span >= (1ull << 31)) {
-        IDEV_CUDA(cudaMemsetAsync(mega_tags, 0, mega_tag_words * sizeof(uint64_t), st));
-        mega_tag_next = 0;
-      }
-      a.tag_base = mega_tag_next;
-      const char* pc = std::getenv("INFERC_DECODE_PIECE");
-      a.piece = pc ? (uint32_t)std::max(16, std::atoi(pc) / 16 * 16) : 49152u;
-      mega_tag_next += (uint32_t)span;
-      a.logits = logits;
-      a.proj_chunks = mega_chunks;
-      a.best_v = best_v; a.best_i = best_i; a.bar_count = bar;
-      a.err = err; a.tok = tok; a.token_log = token_log; a.log_offset = 1;
-      a.pos0 = n; a.nsteps = (int)(max_tokens - 1);
-      a.prof = nullptr;
-#ifdef INFERC_DECODE_PROFILE
-      // Development build only (-DINFERC_DECODE_PROFILE): CTA 0 stamps the
-      // global timer at the end of each phase of step 1 into a per-plan buffer.
-      if (!prof_buf) prof_buf = mem.alloc<unsigned long long>(8192);
-      a.prof = prof_buf;
-#endif
-      IDEV_CUDA(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned int), st));
-      IDEV_CUDA(cudaEventRecord(ev0, st));
-      launch_decode_mega(a, mega_grid, st);
-      IDEV_CUDA(cudaEventRecord(ev1, st));
-#ifdef INFERC_DECODE_PROFILE
-      {
-        std::vector<unsigned long long> t(4 * L + 2);
-        IDEV_CUDA(cudaMemcpyAsync(t.data(), prof_buf, t.size() * 8, cudaMemcpyDeviceToHost, st));
-        IDEV_CUDA(cudaStreamSynchronize(st));
-        const char* names[4] = {"qkv", "attn+proj", "fc", "fp"};
-        for (int q = 0; q <= 4 * L; ++q)  // phase q ends at stamp q + 1
-          fprintf(stderr, "layer %2d phase %-9s %6.2f us\n", (int)(q / 4),
-                  q == 4 * L ? "lm" : names[q % 4], (t[q + 1] - t[q]) / 1e3);
-        // per-CTA events of layer 5: min / median / max over CTAs, us after
-        // the earliest event
-        std::vector<unsigned long long> ev((size_t)mega_grid * 32);
-        IDEV_CUDA(cudaMemcpy(ev.data(), prof_buf + 64, ev.size() * 8, cudaMemcpyDeviceToHost));
-        unsigned long long t0 = ~0ull;
-        for (int c = 0; c < mega_grid; ++c)
-          for (int e = 0; e < 7; ++e) t0 = std::min(t0, ev[(size_t)c * 32 + e]);
-        const char* en[19] = {"qkv input staged", "qkv end", "attn end", "fc input staged",
-                              "fc end", "fp input staged", "fp end", "attn enter",
-                              "attn qkv ready", "attn ctx done", "attn panel ready",
-                              "attn keys done", "attn max synced", "attn o reduced",
-                              "fc copies issued", "smid", "proj summed", "proj stored",
-                              "attn t0 qkv settled"};
-        for (int e = 0; e < 19; ++e) {
-          if (e == 15) continue;
-          const int n = (e < 7 || e == 14) ? mega_grid : (int)(nH * mega_chunks);  // attention CTAs only
-          std::vector<double> v;
-          for (int c = 0; c < n; ++c) v.push_back((ev[(size_t)c * 32 + e] - t0) / 1e3);
-          std::vector<int> ids(n);
-          for (int c = 0; c < n; ++c) ids[c] = c;
-          std::sort(ids.begin(), ids.end(), [&](int x, int y) { return v[x] > v[y]; });
-          fprintf(stderr, "  slowest CTAs:");
-          for (int c = 0; c < std::min(n, 8); ++c)
-            fprintf(stderr, " %d/sm%llu(%.2f)", ids[c], ev[(size_t)ids[c] * 32 + 15], v[ids[c]]);
-          fprintf(stderr, "\n");
-          std::sort(v.begin(), v.end());
-          fprintf(stderr, "event %-17s min %6.2f  med %6.2f  max %6.2f us\n", en[e], v.front(),
-                  v[v.size() / 2], v.back());
-        }
-      }
-#endif
+      run_mega(n, 1, max_tokens - 1, st);
     } else if (max_tokens > 1) {
       if (!step_graph || log_base != n) {
         // The graph bakes log_base; (re)capture when the prompt length
@@ -891,7 +903,7 @@ struct InfercDecoderPlan {
 // column panels of 48 KiB at most, at most two panels per CTA, hidden and
 // FFN widths the shared staging buffer holds. Otherwise (or with
 // INFERC_DECODE_GRAPH=1) decode runs the per-kernel CUDA-graph step.
-static void setup_mega(InfercDecoderPlan* p) {
+static void setup_mega(InfercDecoderPlan* p, bool q4) {
   const char* force = std::getenv("INFERC_DECODE_GRAPH");
   if (force && std::strcmp(force, "1") == 0) return;
   const int H = (int)p->H, F = (int)p->F;
@@ -902,13 +914,17 @@ static void setup_mega(InfercDecoderPlan* p) {
   if (H > 3072 || F > 3072 || H % 16 || F % 16 || p->hd % 4 || 256 % p->hd || p->hd > 128 ||
       (H * 4) > 48 * 1024 || p->L < 1 || p->L > kMegaMaxLayers || p->nH > 16)
     return;
-  int grid = mega_max_grid((int)p->max_len);
+  // int4: words of 8 k (hd too), LM-head rows of H/2 bytes on 16-byte bounds
+  if (q4 && (H % 32 || p->hd % 8)) return;
+  int grid = mega_max_grid((int)p->max_len, q4);
+  // bytes of a K x P panel
+  auto panel_bytes = [q4](int K, int P) -> size_t { return q4 ? (size_t)K * P / 2 : (size_t)K * P * 4; };
   // Panel count of a [K, N] GEMV: the narrowest P (4, 8 or 16; the most
   // panels, so the most CTAs streaming) with a panel <= 48 KiB and at most two
   // panels per CTA; 0 when none fits.
-  auto panel_width = [](int K, int N, int g) -> int {
+  auto panel_width = [&](int K, int N, int g) -> int {
     for (int P : {4, 8, 16})
-      if ((size_t)K * P * 4 <= 48 * 1024 && (N + P - 1) / P <= 2 * g) return P;
+      if (panel_bytes(K, P) <= 48 * 1024 && (N + P - 1) / P <= 2 * g) return P;
     return 0;
   };
   // Every CTA must own an FC and an FP panel: the kernel's tagged-word
@@ -927,27 +943,42 @@ static void setup_mega(InfercDecoderPlan* p) {
   if (const char* e = std::getenv("INFERC_DECODE_CHUNKS")) chunks = std::max(1, std::min(chunks, std::atoi(e)));
   if (chunks < 1) return;
   const int Wc = ((H + chunks - 1) / chunks + 3) / 4 * 4;
-  if (Wc > 256 || (size_t)p->hd * Wc * 4 > 48 * 1024) return;
-  auto panels = [&](const float* w, int K, int N) -> MegaPanels {
+  if (Wc > 256 || panel_bytes((int)p->hd, Wc) > 48 * 1024) return;
+  // fp32 W [K, N] or int4 q [N, K/2] (+ scales [N]) into column panels
+  auto panels = [&](const float* w, const uint8_t* q, const float* sc, int K, int N) -> MegaPanels {
     const int P = panel_width(K, N, grid);
-    if (!P) return MegaPanels{nullptr, K, N, 0, 0};
+    if (!P) return MegaPanels{nullptr, K, N, 0, 0, 0, nullptr};
     const int np = (N + P - 1) / P;
-    float* d = p->mem.alloc<float>((size_t)np * K * P);
-    launch_panelize(w, d, K, N, P, np, nullptr);
-    return MegaPanels{d, K, N, P, np};
+    const uint32_t bytes = (uint32_t)panel_bytes(K, P);
+    uint8_t* d = p->mem.alloc<uint8_t>((size_t)np * bytes);
+    if (q4)
+      launch_panelize_q4(q, reinterpret_cast<uint32_t*>(d), K, N, P, np, nullptr);
+    else
+      launch_panelize(w, reinterpret_cast<float*>(d), K, N, P, np, nullptr);
+    return MegaPanels{d, K, N, P, np, bytes, q4 ? sc : nullptr};
   };
   std::vector<MegaLayer> layers((size_t)p->L);
   for (int64_t l = 0; l < p->L; ++l) {
     MegaLayer& m = layers[(size_t)l];
-    m.attn = panels(p->attn_w[l], H, 3 * H);
+    const size_t li = (size_t)l;
+    m.attn = q4 ? panels(nullptr, p->q_attn[li], p->s_attn[li], H, 3 * H)
+                : panels(p->attn_w[l], nullptr, nullptr, H, 3 * H);
     {
       const int np = (int)p->nH * chunks;
-      float* d = p->mem.alloc<float>((size_t)np * p->hd * Wc);
-      launch_panelize_proj(p->proj_w[l], d, H, (int)p->hd, (int)p->nH, chunks, Wc, nullptr);
-      m.proj = MegaPanels{d, (int)p->hd, H, Wc, np};
+      const uint32_t bytes = (uint32_t)panel_bytes((int)p->hd, Wc);
+      uint8_t* d = p->mem.alloc<uint8_t>((size_t)np * bytes);
+      if (q4)
+        launch_panelize_proj_q4(p->q_proj[li], reinterpret_cast<uint32_t*>(d), H, (int)p->hd,
+                                (int)p->nH, chunks, Wc, nullptr);
+      else
+        launch_panelize_proj(p->proj_w[l], reinterpret_cast<float*>(d), H, (int)p->hd,
+                             (int)p->nH, chunks, Wc, nullptr);
+      m.proj = MegaPanels{d, (int)p->hd, H, Wc, np, bytes, q4 ? p->s_proj[li] : nullptr};
     }
-    m.fc = panels(p->fc_w[l], H, F);
-    m.fp = panels(p->fp_w[l], F, H);
+    m.fc = q4 ? panels(nullptr, p->q_fc[li], p->s_fc[li], H, F)
+              : panels(p->fc_w[l], nullptr, nullptr, H, F);
+    m.fp = q4 ? panels(nullptr, p->q_fp[li], p->s_fp[li], F, H)
+              : panels(p->fp_w[l], nullptr, nullptr, F, H);
     if (!m.attn.data || !m.proj.data || !m.fc.data || !m.fp.data) return;
     m.attn_b = p->attn_b[l]; m.proj_b = p->proj_b[l]; m.fc_b = p->fc_b[l]; m.fp_b = p->fp_b[l];
     m.ln1_g = p->ln1g[l]; m.ln1_b = p->ln1b[l]; m.ln2_g = p->ln2g[l]; m.ln2_b = p->ln2b[l];
@@ -967,7 +998,10 @@ static void setup_mega(InfercDecoderPlan* p) {
   p->use_mega = true;
 }
 
-static void decoder_create(const InfercGpt2Weights* w, int64_t max_len, InfercDecoderPlan* p) {
+// int4: the persistent kernel is prepared on the int4 panels once they are
+// packed (inferc_dev_decoder_create_int4), not on the fp32 weights.
+static void decoder_create(const InfercGpt2Weights* w, int64_t max_len, InfercDecoderPlan* p,
+                           bool int4 = false) {
   IDEV_CHECK_ARG(w != nullptr, "decoder_create: null weights");
   IDEV_CHECK_ARG(w->layers >= 1 && w->layers <= INFERC_MAX_LAYERS, "decoder: bad layer count");
   IDEV_CHECK_ARG(w->hidden > 0 && w->heads > 0 && w->hidden % w->heads == 0,
@@ -1015,7 +1049,7 @@ static void decoder_create(const InfercGpt2Weights* w, int64_t max_len, InfercDe
   IDEV_CUDA(cudaMemset(p->err, 0, sizeof(int)));
   p->ws.allocate(size_t(1) << 20, 1024);
   IDEV_CUDA(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
-  setup_mega(p);
+  if (!int4) setup_mega(p, false);
   IDEV_CUDA(cudaEventCreate(&p->ev0));
   IDEV_CUDA(cudaEventCreate(&p->ev1));
 }
@@ -1111,7 +1145,7 @@ int inferc_dev_decoder_create_int4(const InfercGpt2Weights* w, int64_t max_len,
                        w->hidden <= 8192 && w->ffn <= 8192,
                    "decoder_create_int4: hidden and ffn must be multiples of 8, at most 8192");
     auto p = std::make_unique<InfercDecoderPlan>();
-    decoder_create(w, max_len, p.get());
+    decoder_create(w, max_len, p.get(), /*int4=*/true);
     InfercDecoderPlan& d = *p;
     const int64_t H = d.H, F = d.F;
     auto pack = [&](const float* src, int64_t K, int64_t N, bool trans, std::vector<uint8_t*>* qv,
@@ -1131,6 +1165,7 @@ int inferc_dev_decoder_create_int4(const InfercGpt2Weights* w, int64_t max_len,
     pack(d.wte, H, d.V, true, nullptr, nullptr, &d.q_lm, &d.s_lm);
     IDEV_CUDA(cudaDeviceSynchronize());
     d.int4 = true;
+    setup_mega(&d, true);
     *out = p.release();
   });
 }

@@ -36,8 +36,13 @@ def test_packer_matches_numpy(K, N, trans):
     np.testing.assert_array_equal(s.cpu().numpy(), want.scales)
 
 
+@pytest.mark.parametrize("graph", [False, True], ids=["persistent", "step-graph"])
 @pytest.mark.parametrize("full", [False, True], ids=["small", "gpt2-small"])
-def test_int4_decode_tokens(full):
+def test_int4_decode_tokens(full, graph, monkeypatch):
+    """Generated tokens from the persistent kernel on int4 panels, and from
+    the per-kernel step graph (INFERC_DECODE_GRAPH=1, read at plan creation)."""
+    if graph:
+        monkeypatch.setenv("INFERC_DECODE_GRAPH", "1")
     g = np.load(os.path.join(GOLD, "decode_int4.npz"))
     if full:
         cfg, seed, tag = synth.Gpt2Config(), 0, "c1"
