@@ -33,6 +33,7 @@
 // (128-byte rows of 64 fp16, 8-row atoms of 1 KiB).
 // Every mbarrier wait is bounded; on a timeout the CTA flags g_f16_error,
 // stops issuing work, frees its TMEM and exits.
+#include <algorithm>
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -127,7 +128,8 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
                      const __grid_constant__ CUtensorMap tmBh,
                      const __grid_constant__ CUtensorMap tmBl, const float* __restrict__ b_inv_scale,
                      int* __restrict__ range_flag, float* __restrict__ C, int64_t ldc, int M, int N,
-                     int K, Epilogue ep, SplitOut so) {
+                     int K, Epilogue ep, SplitOut so, int splits, int kper,
+                     float* __restrict__ part, unsigned* __restrict__ cnt) {
   using S = F16Shape<BN, BK, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -141,6 +143,12 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
   const int ktiles = (K + BK - 1) / BK;
   const int tiles_n = (N + BN - 1) / BN;
   const int total = ((M + BM - 1) / BM) * tiles_n;
+  // work units: (tile, k split); unit u covers k tiles [kb0, kb1) of tile u / splits
+  const int units = total * splits;
+  auto krange = [&](int u, int& kb0, int& kb1) {
+    kb0 = (u % splits) * kper;
+    kb1 = min(ktiles, kb0 + kper);
+  };
   auto stage_a = [&](int s) { return smem + (size_t)s * S::STAGE_BYTES; };
   auto stage_bh = [&](int s) { return stage_a(s) + S::A_F32_BYTES; };
   auto stage_bl = [&](int s) { return stage_a(s) + S::A_F32_BYTES + S::B_BYTES; };
@@ -177,9 +185,12 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
   if (warp == 0) {
     if (lane == 0) {  // ---------------- TMA producer
       int g = 0;
-      for (int tile = blockIdx.x; tile < total && !abort_sh; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < units && !abort_sh; u += gridDim.x) {
+        const int tile = u / splits;
         const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
-        for (int it = 0; it < ktiles && !abort_sh; ++it, ++g) {
+        int kb0, kb1;
+        krange(u, kb0, kb1);
+        for (int it = kb0; it < kb1 && !abort_sh; ++it, ++g) {
           const int s = g % STAGES, r = g / STAGES;
           if (g >= STAGES && !mbar_wait(&empty_bar[s], (r - 1) & 1)) {
             fail();
@@ -205,7 +216,9 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
     if (lane == 0) {  // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_f16(BM, BN);
       int g = 0, tl = 0;
-      for (int tile = blockIdx.x; tile < total && !abort_sh; tile += gridDim.x, ++tl) {
+      for (int u = blockIdx.x; u < units && !abort_sh; u += gridDim.x, ++tl) {
+        int kb0, kb1;
+        krange(u, kb0, kb1);
         const int acc = tl & 1;
         if (tl >= 2 && !mbar_wait(&tempty_bar[acc], ((tl >> 1) - 1) & 1)) {
           fail();
@@ -213,7 +226,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * BN);
-        for (int it = 0; it < ktiles && !abort_sh; ++it, ++g) {
+        for (int it = kb0; it < kb1 && !abort_sh; ++it, ++g) {
           const int s = g % STAGES, r = g / STAGES;
           if (!mbar_wait(AS ? &full_bar[s] : &conv_bar[s], r & 1)) {
             fail();
@@ -228,7 +241,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
             const uint64_t dal = smem_desc(al + j * 32, 16, S::SBO, S::LAYOUT);
             const uint64_t dbh = smem_desc(bh + j * 32, 16, S::SBO, S::LAYOUT);
             const uint64_t dbl = smem_desc(bl + j * 32, 16, S::SBO, S::LAYOUT);
-            mma_f16(d, dal, dbh, idesc, (it | j) != 0);
+            mma_f16(d, dal, dbh, idesc, (it != kb0 || j != 0) ? 1u : 0u);
             mma_f16(d, dah, dbl, idesc, 1);
             mma_f16(d, dah, dbh, idesc, 1);
           }
@@ -245,8 +258,10 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
     const uint32_t sw = S::chunk_swz(r);
     int g = 0;
     bool bad = false, stop = false;
-    for (int tile = blockIdx.x; tile < total && !stop; tile += gridDim.x) {
-      for (int it = 0; it < ktiles; ++it, ++g) {
+    for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
+      int kb0, kb1;
+      krange(u, kb0, kb1);
+      for (int it = kb0; it < kb1; ++it, ++g) {
         const int s = g % STAGES, rr = g / STAGES;
         const bool ok = mbar_wait(&full_bar[s], rr & 1);
         if (!ok) fail();
@@ -302,7 +317,13 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
     const float sc = __ldg(b_inv_scale);
     bool bad = false;
     int tl = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tl) {
+    // staging rows of the fp32-residual and split-plane fast paths
+    __shared__ __align__(16) float stage[kEpiThreads / 32][32 * 20];
+    __shared__ int last_sh;
+    const int et = threadIdx.x - 64 - kConvThreads;  // 0 .. kEpiThreads-1
+    auto epi_sync = [] { asm volatile("bar.sync 2, %0;" ::"r"(kEpiThreads) : "memory"); };
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
+      const int tile = u / splits;
       const int acc = tl & 1;
       const bool ok = !abort_sh && mbar_wait(&tfull_bar[acc], (tl >> 1) & 1);
       if (!ok) {
@@ -316,105 +337,151 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
       // whole-tile fast paths below (warp-uniform); split outputs have
       // aligned planes and bias by the dispatcher's checks
       const bool staged = (SOUT || vec_ok) && n0 + BN <= N;
+      // the epilogue of 16 accumulator columns c0.. of this thread's row
+      auto finish = [&](int c0, float (&v)[16]) {
+          if constexpr (EPI == EPI_BIAS_RESID && !SOUT) {
+            if (staged) {
+              // fp32 + residual, staged through shared memory: the warp's
+              // 32 rows x 16 columns are written row per lane (rows padded to
+              // 20 floats: conflict-free float4 stores) and read back as
+              // float4s that cover 8 rows x 64 contiguous bytes per warp
+              // instruction, so the residual loads and C stores use whole
+              // 32-byte sectors. Arithmetic as in epilogue16<EPI_BIAS_RESID>.
+              float* wb = stage[warp - 2 - kConvThreads / 32];
+  #pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<float4*>(wb + lane * 20)[j] =
+                    make_float4(v[4 * j] * sc, v[4 * j + 1] * sc, v[4 * j + 2] * sc,
+                                v[4 * j + 3] * sc);
+              __syncwarp();
+              const int c4 = (lane & 3) * 4;
+              const int64_t col = (int64_t)n0 + c0 + c4;
+              const float4 bb = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+              float4 rr[4];
+  #pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int64_t grow = m0 + 32 * q + (lane >> 2) + 8 * k;
+                rr[k] = grow < M ? *reinterpret_cast<const float4*>(ep.resid + grow * ep.ldr + col)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+  #pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int rl = (lane >> 2) + 8 * k;
+                const int64_t grow = m0 + 32 * q + rl;
+                if (grow >= M) continue;
+                const float4 x = *reinterpret_cast<const float4*>(wb + rl * 20 + c4);
+                float4 o;
+                o.x = ep.alpha * x.x + ep.beta * bb.x; o.x += rr[k].x;
+                o.y = ep.alpha * x.y + ep.beta * bb.y; o.y += rr[k].y;
+                o.z = ep.alpha * x.z + ep.beta * bb.z; o.z += rr[k].z;
+                o.w = ep.alpha * x.w + ep.beta * bb.w; o.w += rr[k].w;
+                *reinterpret_cast<float4*>(C + grow * ldc + col) = o;
+              }
+              __syncwarp();
+              return;
+            }
+          }
+          if constexpr (SOUT && (EPI == EPI_BIAS || EPI == EPI_BIAS_GELU)) {
+            if (staged) {
+              // fp16 hi / lo planes, staged the same way: each lane finishes 4
+              // columns of a row and writes 8 contiguous bytes to each plane
+              // (8 rows x 32 bytes per warp instruction). Arithmetic as in
+              // epilogue16_split<EPI>.
+              float* wb = stage[warp - 2 - kConvThreads / 32];
+  #pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<float4*>(wb + lane * 20)[j] =
+                    make_float4(v[4 * j] * sc, v[4 * j + 1] * sc, v[4 * j + 2] * sc,
+                                v[4 * j + 3] * sc);
+              __syncwarp();
+              const int c4 = (lane & 3) * 4;
+              const int64_t col = (int64_t)n0 + c0 + c4;
+              const float4 bb = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+  #pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int rl = (lane >> 2) + 8 * k;
+                const int64_t grow = m0 + 32 * q + rl;
+                if (grow >= M) continue;
+                const float4 x = *reinterpret_cast<const float4*>(wb + rl * 20 + c4);
+                float o[4] = {ep.alpha * x.x + ep.beta * bb.x, ep.alpha * x.y + ep.beta * bb.y,
+                              ep.alpha * x.z + ep.beta * bb.z, ep.alpha * x.w + ep.beta * bb.w};
+                if (EPI == EPI_BIAS_GELU) {
+  #pragma unroll
+                  for (int i = 0; i < 4; ++i) o[i] = gelu_erf(o[i]);
+                }
+                uint32_t l0, l1;
+                const uint32_t h0 = split_pair(o[0], o[1], l0, bad);
+                const uint32_t h1 = split_pair(o[2], o[3], l1, bad);
+                *reinterpret_cast<uint2*>(so.hi + grow * so.ld + col) = make_uint2(h0, h1);
+                *reinterpret_cast<uint2*>(so.lo + grow * so.ld + col) = make_uint2(l0, l1);
+              }
+              __syncwarp();
+              return;
+            }
+          }
+          if (row >= M) return;
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] *= sc;
+          const int64_t col0 = (int64_t)n0 + c0;
+          if (SOUT) {
+            // N % 16 == 0 for split outputs: a chunk is wholly inside or outside
+            if (col0 < N) epilogue16_split<EPI>(ep, v, row, col0, so, bad);
+          } else {
+            epilogue16<EPI>(ep, v, row, col0, N, C + row * ldc + col0, vec_ok);
+          }
+      };
+      if (splits == 1) {
+#pragma unroll 1
+        for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
+          float v[16];
+          tmem_ld16(base + (uint32_t)c0, v);
+          finish(c0, v);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[acc]);
+        continue;
+      }
+      // Split K: this unit's raw partial tile to the scratch, the accumulator
+      // released, then the CTA that completes the tile's count sums the
+      // partials in split order and finishes the tile.
+      float* pu = part + ((size_t)u * BM + 32 * q + lane) * BN;
 #pragma unroll 1
       for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
         float v[16];
         tmem_ld16(base + (uint32_t)c0, v);
-        if constexpr (EPI == EPI_BIAS_RESID && !SOUT) {
-          if (staged) {
-            // fp32 + residual, staged through shared memory: the warp's
-            // 32 rows x 16 columns are written row per lane (rows padded to
-            // 20 floats: conflict-free float4 stores) and read back as
-            // float4s that cover 8 rows x 64 contiguous bytes per warp
-            // instruction, so the residual loads and C stores use whole
-            // 32-byte sectors. Arithmetic as in epilogue16<EPI_BIAS_RESID>.
-            __shared__ __align__(16) float stage[kEpiThreads / 32][32 * 20];
-            float* wb = stage[warp - 2 - kConvThreads / 32];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              reinterpret_cast<float4*>(wb + lane * 20)[j] =
-                  make_float4(v[4 * j] * sc, v[4 * j + 1] * sc, v[4 * j + 2] * sc,
-                              v[4 * j + 3] * sc);
-            __syncwarp();
-            const int c4 = (lane & 3) * 4;
-            const int64_t col = (int64_t)n0 + c0 + c4;
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
-            float4 rr[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int64_t grow = m0 + 32 * q + (lane >> 2) + 8 * k;
-              rr[k] = grow < M ? *reinterpret_cast<const float4*>(ep.resid + grow * ep.ldr + col)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int rl = (lane >> 2) + 8 * k;
-              const int64_t grow = m0 + 32 * q + rl;
-              if (grow >= M) continue;
-              const float4 x = *reinterpret_cast<const float4*>(wb + rl * 20 + c4);
-              float4 o;
-              o.x = ep.alpha * x.x + ep.beta * bb.x; o.x += rr[k].x;
-              o.y = ep.alpha * x.y + ep.beta * bb.y; o.y += rr[k].y;
-              o.z = ep.alpha * x.z + ep.beta * bb.z; o.z += rr[k].z;
-              o.w = ep.alpha * x.w + ep.beta * bb.w; o.w += rr[k].w;
-              *reinterpret_cast<float4*>(C + grow * ldc + col) = o;
-            }
-            __syncwarp();
-            continue;
-          }
-        }
-        if constexpr (SOUT && (EPI == EPI_BIAS || EPI == EPI_BIAS_GELU)) {
-          if (staged) {
-            // fp16 hi / lo planes, staged the same way: each lane finishes 4
-            // columns of a row and writes 8 contiguous bytes to each plane
-            // (8 rows x 32 bytes per warp instruction). Arithmetic as in
-            // epilogue16_split<EPI>.
-            __shared__ __align__(16) float stage[kEpiThreads / 32][32 * 20];
-            float* wb = stage[warp - 2 - kConvThreads / 32];
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              reinterpret_cast<float4*>(wb + lane * 20)[j] =
-                  make_float4(v[4 * j] * sc, v[4 * j + 1] * sc, v[4 * j + 2] * sc,
-                              v[4 * j + 3] * sc);
-            __syncwarp();
-            const int c4 = (lane & 3) * 4;
-            const int64_t col = (int64_t)n0 + c0 + c4;
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int rl = (lane >> 2) + 8 * k;
-              const int64_t grow = m0 + 32 * q + rl;
-              if (grow >= M) continue;
-              const float4 x = *reinterpret_cast<const float4*>(wb + rl * 20 + c4);
-              float o[4] = {ep.alpha * x.x + ep.beta * bb.x, ep.alpha * x.y + ep.beta * bb.y,
-                            ep.alpha * x.z + ep.beta * bb.z, ep.alpha * x.w + ep.beta * bb.w};
-              if (EPI == EPI_BIAS_GELU) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) o[i] = gelu_erf(o[i]);
-              }
-              uint32_t l0, l1;
-              const uint32_t h0 = split_pair(o[0], o[1], l0, bad);
-              const uint32_t h1 = split_pair(o[2], o[3], l1, bad);
-              *reinterpret_cast<uint2*>(so.hi + grow * so.ld + col) = make_uint2(h0, h1);
-              *reinterpret_cast<uint2*>(so.lo + grow * so.ld + col) = make_uint2(l0, l1);
-            }
-            __syncwarp();
-            continue;
-          }
-        }
-        if (row >= M) continue;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] *= sc;
-        const int64_t col0 = (int64_t)n0 + c0;
-        if (SOUT) {
-          // N % 16 == 0 for split outputs: a chunk is wholly inside or outside
-          if (col0 < N) epilogue16_split<EPI>(ep, v, row, col0, so, bad);
-        } else {
-          epilogue16<EPI>(ep, v, row, col0, N, C + row * ldc + col0, vec_ok);
-        }
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<float4*>(pu + c0)[i] =
+              make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
+      __threadfence();
+      epi_sync();
+      if (et == 0) last_sh = atomicAdd(cnt + tile, 1u) == (unsigned)(splits - 1);
+      epi_sync();
+      if (!last_sh) continue;
+      __threadfence();
+      const float* pt = part + ((size_t)tile * splits * BM + 32 * q + lane) * BN;
+#pragma unroll 1
+      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        for (int k = 0; k < splits; ++k) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 w =
+                __ldcg(reinterpret_cast<const float4*>(pt + (size_t)k * BM * BN + c0) + i);
+            v[4 * i] += w.x;
+            v[4 * i + 1] += w.y;
+            v[4 * i + 2] += w.z;
+            v[4 * i + 3] += w.w;
+          }
+        }
+        finish(c0, v);
+      }
+      if (et == 0) cnt[tile] = 0u;  // zero at rest for the next call on this stream
     }
     if (SOUT && bad) atomicExch(so.range, 1);
   }
@@ -504,7 +571,7 @@ template <int BN, int BK, int STAGES, int EPI, bool AS, bool SOUT>
 void launch_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,
                  const float* inv_scale, int* range_flag, float* C, int64_t ldc,
                  const SplitOut& so, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
-                 cudaStream_t st) {
+                 cudaStream_t st, const SplitK& sk) {
   using S = F16Shape<BN, BK, STAGES>;
   const CUtensorMapSwizzle hswz = BK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUtensorMap ta, tal;
@@ -522,9 +589,22 @@ void launch_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int6
   IDEV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::SMEM_BYTES));
   const int64_t tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM);
-  dim3 grid((unsigned)std::min<int64_t>(tiles, sm_count_f16()));
+  const int64_t sms = sm_count_f16();
+  const int64_t ktiles = (K + BK - 1) / BK;
+  // Split K when the tiles leave most SMs idle: at least 8 k tiles per split
+  // (the partial-tile fix-up costs a few microseconds, so at K = 768 a split
+  // measured slower: FFN1 at M = 128 14.5 -> 20.6 us with 4 k tiles per
+  // split), as many splits as the SMs and the caller's scratch allow.
+  int64_t splits = 1;
+  if (sk.part && sk.cnt && tiles * 2 <= sms && tiles <= sk.cnt_n)
+    splits = std::max<int64_t>(1, std::min({sms / tiles, ktiles / 8,
+                                            sk.part_floats / (tiles * BM * BN)}));
+  const int64_t kper = (ktiles + splits - 1) / splits;
+  splits = (ktiles + kper - 1) / kper;  // no empty split
+  dim3 grid((unsigned)std::min<int64_t>(tiles * splits, sms));
   kern<<<grid, kThreadsF16, S::SMEM_BYTES, st>>>(ta, tal, tbh, tbl, inv_scale, range_flag, C, ldc,
-                                                  (int)M, (int)N, (int)K, ep, so);
+                                                  (int)M, (int)N, (int)K, ep, so, (int)splits,
+                                                  (int)kper, sk.part, sk.cnt);
   IDEV_LAUNCHED();
 }
 
@@ -532,7 +612,7 @@ template <int EPI, bool AS, bool SOUT>
 void launch_f16s_width(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,
                        const float* inv_scale, int* range_flag, float* C, int64_t ldc,
                        const SplitOut& so, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
-                       cudaStream_t st) {
+                       cudaStream_t st, const SplitK& sk) {
   // Tile width by wave quantisation: of BN = 256, 192 and 128 the one whose
   // tile count fills the SMs' last wave best (a larger BN on a tie, for
   // operand reuse). N = 768 at M = 4096 (a rank's share of the batch-256
@@ -562,35 +642,35 @@ void launch_f16s_width(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl
   if (bn == 256) {
     if (bk64)
       launch_f16s<256, 64, 2, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                             N, K, ep, st);
+                                             N, K, ep, st, sk);
     else
       launch_f16s<256, 32, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                             N, K, ep, st);
+                                             N, K, ep, st, sk);
   } else if (bn == 192) {
     if (bk64)
       launch_f16s<192, 64, 2, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                             N, K, ep, st);
+                                             N, K, ep, st, sk);
     else
       launch_f16s<192, 32, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                             N, K, ep, st);
+                                             N, K, ep, st, sk);
   } else if (bn == 128) {
     launch_f16s<128, 32, 6, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                           N, K, ep, st);
+                                           N, K, ep, st, sk);
   } else if (bn == 64) {
     // narrow tiles stream mostly A: 128-byte TMA rows (BK = 64) for the planes
     if (AS)
       launch_f16s<64, 64, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                            N, K, ep, st);
+                                            N, K, ep, st, sk);
     else
       launch_f16s<64, 32, 8, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                            N, K, ep, st);
+                                            N, K, ep, st, sk);
   } else {
     if (AS)
       launch_f16s<32, 64, 4, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                            N, K, ep, st);
+                                            N, K, ep, st, sk);
     else
       launch_f16s<32, 32, 8, EPI, AS, SOUT>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                            N, K, ep, st);
+                                            N, K, ep, st, sk);
   }
 }
 
@@ -634,7 +714,7 @@ bool gemm_f16s_supported(const float* A, int64_t lda, int64_t M, int64_t N, int6
 void launch_gemm_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,
                       const float* scale2, int* range_flag, float* C, int64_t ldc,
                       const SplitOut& so, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
-                      cudaStream_t st) {
+                      cudaStream_t st, const SplitK& sk) {
   const float* inv_scale = scale2 + 1;
   if (!range_flag)  // the current device's copy of the module-wide flag
     IDEV_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&range_flag), g_f16_range));
@@ -668,20 +748,20 @@ void launch_gemm_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl,
                    "N % 16 == 0 and aligned planes");
     if (epi == EPI_BIAS)
       launch_f16s_width<EPI_BIAS, true, true>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,
-                                              N, K, ep, st);
+                                              N, K, ep, st, sk);
     else
       launch_f16s_width<EPI_BIAS_GELU, true, true>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc,
-                                                   so, M, N, K, ep, st);
+                                                   so, M, N, K, ep, st, sk);
     return;
   }
 #define IDEV_F16(EPIK)                                                                          \
   do {                                                                                          \
     if (as)                                                                                     \
       launch_f16s_width<EPIK, true, false>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M,  \
-                                           N, K, ep, st);                                       \
+                                           N, K, ep, st, sk);                                       \
     else                                                                                        \
       launch_f16s_width<EPIK, false, false>(A, Bh, Bl, kp, inv_scale, range_flag, C, ldc, so, M, \
-                                            N, K, ep, st);                                      \
+                                            N, K, ep, st, sk);                                      \
   } while (0)
   switch (epi) {
     case EPI_BIAS: IDEV_F16(EPI_BIAS); break;

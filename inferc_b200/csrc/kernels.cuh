@@ -67,12 +67,24 @@ struct F16GemmA {
   const uint16_t* lo = nullptr;
   int64_t ld = 0;
 };
+// Split-K scratch of the one-SM split-fp16 GEMM, owned by the caller and
+// used by one stream at a time: when the output has too few tiles to fill
+// the SMs, K is split over CTAs that store raw partial tiles in `part`
+// (part_floats floats); the CTA that completes a tile's counter (cnt, cnt_n
+// words, zero at rest and left zero) sums the partials in split order and
+// runs the epilogue. Null part: no split.
+struct SplitK {
+  float* part = nullptr;
+  int64_t part_floats = 0;
+  unsigned* cnt = nullptr;
+  int cnt_n = 0;
+};
 // General form: so.hi set = write the result's fp16 split instead of C
 // (pre-split A, bias or bias+GELU epilogue only).
 void launch_gemm_f16s(const F16GemmA& A, const uint16_t* Bh, const uint16_t* Bl, int64_t kp,
                       const float* scale2, int* range_flag, float* C, int64_t ldc,
                       const SplitOut& so, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
-                      cudaStream_t st);
+                      cudaStream_t st, const SplitK& sk = SplitK());
 int read_and_clear_f16_range();
 // Two-SM (cta_group::2, 256-row) form of the split-fp16 GEMM for pre-split A
 // (gemm_f16s_2cta.cu): used for split-plane outputs unless INFERC_GEMM_2CTA=0

@@ -226,6 +226,10 @@ struct InfercEncoderPlan {
   std::vector<float*> bqkv, bo, ln1g, ln1b, b1, b2, ln2g, ln2b;
   std::vector<SplitWeight> wqkv, wo, w1, w2;
   float *pre_w, *pre_b, *cls_w, *cls_b;
+  // [K, N] copies of the classifier head for one-sequence batches, run as
+  // split-K GEMVs (a 128-row tensor-core tile for one row measured 17-20 us)
+  float *pre_wt = nullptr, *cls_wt = nullptr;
+  Workspace head_ws;
   // activations
   int64_t *ids, *mask;
   uint8_t* cond;
@@ -241,6 +245,7 @@ struct InfercEncoderPlan {
   uint16_t *qkv_hi = nullptr, *qkv_lo = nullptr;  // fp16 planes of qkv (S <= 128)
   SplitWeight pre16, cls16;
   int* f16_range = nullptr;
+  SplitK splitk;  // split-K scratch of the small-M GEMMs (this plan's stream only)
   int* range_host = nullptr;  // pinned
   std::map<std::tuple<int64_t, int64_t, bool>, std::unique_ptr<Graph>> graphs;
   // (B, S) -> split-fp16 forward with the 3xTF32 rerun as a device-side IF
@@ -258,6 +263,7 @@ struct InfercEncoderPlan {
   int64_t range_fallbacks = 0;  // batches rerun on the 3xTF32 graph (host-checked path)
 
   ~InfercEncoderPlan() {
+    head_ws.release();
     graphs.clear();
     guarded.clear();
     if (stream2) cudaStreamDestroy(stream2);
@@ -295,7 +301,8 @@ struct InfercEncoderPlan {
   }
   void gemm16(const F16GemmA& A, const SplitWeight& w, float* C, int64_t ldc, const SplitOut& so,
               int64_t M, int64_t N, int64_t K, const Epilogue& ep, cudaStream_t st) {
-    launch_gemm_f16s(A, w.hi, w.lo, w.kp, w.scale2, f16_range, C, ldc, so, M, N, K, ep, st);
+    launch_gemm_f16s(A, w.hi, w.lo, w.kp, w.scale2, f16_range, C, ldc, so, M, N, K, ep, st,
+                     splitk);
   }
 
   void forward(int64_t B, int64_t S, cudaStream_t st, bool use_f16) {
@@ -391,7 +398,17 @@ struct InfercEncoderPlan {
     Epilogue e_c;
     e_c.bias = cls_b;
     e_c.bias_mode = 1;
-    if (use_f16) {
+    if (B == 1) {
+      GemvArgs g{};
+      g.ws = &head_ws;
+      g.x = x;  // the CLS row
+      g.w = pre_wt; g.bias = pre_b; g.y = pre; g.K = H; g.N = H;
+      g.alpha = 1.f; g.beta = 1.f; g.act = ACT_RELU;
+      launch_gemv(g, st);
+      g.x = pre;
+      g.w = cls_wt; g.bias = cls_b; g.y = logits; g.N = C; g.act = ACT_NONE;
+      launch_gemv(g, st);
+    } else if (use_f16) {
       gemm16(fp32_a(x, S * H), pre16, pre, H, SplitOut(), B, H, H, e_p, st);
       gemm16(fp32_a(pre, H), cls16, logits, C, SplitOut(), B, C, H, e_c, st);
     } else {
@@ -511,6 +528,17 @@ static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t 
   p->pre_b = m.upload(w->pre_b, H, "pre_b");
   p->cls_w = m.upload(w->cls_w, (size_t)p->C * H, "cls_w");
   p->cls_b = m.upload(w->cls_b, p->C, "cls_b");
+  {
+    auto transpose = [](const float* a, int64_t rows, int64_t cols) {  // [rows, cols] -> [cols, rows]
+      std::vector<float> t((size_t)rows * cols);
+      for (int64_t r = 0; r < rows; ++r)
+        for (int64_t c = 0; c < cols; ++c) t[(size_t)c * rows + r] = a[(size_t)r * cols + c];
+      return t;
+    };
+    p->pre_wt = m.upload(transpose(w->pre_w, H, H).data(), (size_t)H * H, "pre_w");
+    p->cls_wt = m.upload(transpose(w->cls_w, p->C, H).data(), (size_t)p->C * H, "cls_w");
+    p->head_ws.allocate(size_t(1) << 16, 256);
+  }
   p->ids = m.alloc<int64_t>(M);
   p->mask = m.alloc<int64_t>(M);
   p->cond = m.alloc<uint8_t>(M);
@@ -542,6 +570,13 @@ static void encoder_create(const InfercEncoderWeights* w, int64_t maxB, int64_t 
     p->cls16 = split_weight_t(m, p->cls_w, H, p->C);
     p->f16_range = m.alloc<int>(1);
     IDEV_CUDA(cudaMemset(p->f16_range, 0, sizeof(int)));
+    // 8 MB of partial tiles covers every split GEMM of a batch-1 forward
+    // (at most ~1.2 M floats); the counters are zero at rest.
+    p->splitk.part_floats = (int64_t)2 << 20;
+    p->splitk.part = m.alloc<float>((size_t)p->splitk.part_floats);
+    p->splitk.cnt_n = 4096;
+    p->splitk.cnt = m.alloc<unsigned>((size_t)p->splitk.cnt_n);
+    IDEV_CUDA(cudaMemset(p->splitk.cnt, 0, (size_t)p->splitk.cnt_n * sizeof(unsigned)));
     IDEV_CUDA(cudaMallocHost(&p->range_host, sizeof(int)));
     p->fallback_count = m.alloc<int64_t>(1);
     IDEV_CUDA(cudaMemset(p->fallback_count, 0, sizeof(int64_t)));
