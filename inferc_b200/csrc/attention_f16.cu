@@ -118,6 +118,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_sh;
+  // Dependents may launch once every CTA holds its TMEM (none can take TMEM
+  // this grid still needs); q/k/v come from the previous kernel.
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (tid == 0) {
     mbar_expect_tx(&bar_load, 6 * kTile);
@@ -580,7 +584,8 @@ void launch_attention_f16(const AttnF16Args& a, cudaStream_t st) {
     IDEV_CUDA(cudaFuncSetAttribute(attention_f16_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     dim3 grid(1, (unsigned)nH, (unsigned)B);
-    attention_f16_kernel<<<grid, kThreads, kSmemBytes, st>>>(tqh, tql, tkh, tkl, tvh, tvl, k);
+    launch_pdl(attention_f16_kernel, grid, dim3(kThreads), kSmemBytes, st, tqh, tql, tkh, tkl, tvh,
+               tvl, k);
   } else {
     IDEV_CUDA(cudaFuncSetAttribute(attention_f16_flash_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlashSmem));

@@ -62,6 +62,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     layernorm_warp_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                           const float* __restrict__ beta, float* y, int64_t rows, float eps,
                           SplitOut sp) {
+  pdl_launch_dependents();
+  pdl_wait();  // x comes from the previous kernel
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -115,8 +117,8 @@ template <int VPT>
 void launch_warp(const float* x, const float* g, const float* b, float* y, int64_t rows,
                  float eps, const SplitOut& sp, cudaStream_t st) {
   const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  layernorm_warp_kernel<VPT><<<(unsigned)blocks, kWarpsPerBlock * 32, 0, st>>>(x, g, b, y, rows,
-                                                                                  eps, sp);
+  launch_pdl(layernorm_warp_kernel<VPT>, dim3((unsigned)blocks), dim3(kWarpsPerBlock * 32), 0, st,
+             x, g, b, y, rows, eps, sp);
 }
 
 // Encoder embedding + LayerNorm: one warp per token.
@@ -127,6 +129,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
                     const float* __restrict__ gamma, const float* __restrict__ beta,
                     float* __restrict__ y, uint8_t* __restrict__ cond, int64_t BS, int64_t S,
                     float eps, int* err_flag, SplitOut sp) {
+  pdl_launch_dependents();
+  pdl_wait();  // y may still be read by the previous kernel
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   if (t >= BS) return;
@@ -192,8 +196,8 @@ void launch_embed_layernorm(const int64_t* ids, const int64_t* mask, const float
   const int64_t BS = B * S;
   const unsigned blocks = (unsigned)((BS + kWarpsPerBlock - 1) / kWarpsPerBlock);
 #define IDEV_EMB(V)                                                                         \
-  embed_ln_kernel<V><<<blocks, kWarpsPerBlock * 32, 0, st>>>(ids, mask, word, pos, vocab, g, \
-                                                             b, y, cond, BS, S, eps, err_flag, sp)
+  launch_pdl(embed_ln_kernel<V>, dim3(blocks), dim3(kWarpsPerBlock * 32), 0, st, ids, mask, word, \
+             pos, vocab, g, b, y, cond, BS, S, eps, err_flag, sp)
   switch (H / 128) {
     case 1: IDEV_EMB(1); break;
     case 2: IDEV_EMB(2); break;
