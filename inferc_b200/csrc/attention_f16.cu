@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bar_load, bar_s, bar_o;
+  __shared__ __align__(8) uint64_t bar_load, bar_v, bar_s, bar_o;  // bar_load: q and k
   __shared__ uint32_t tmem_sh;
   __shared__ float red_max[2][kRows], red_sum[2][kRows];
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (tid == 0) {
     mbar_init(&bar_load, 1);
+    mbar_init(&bar_v, 1);
     mbar_init(&bar_s, 1);
     mbar_init(&bar_o, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -124,13 +125,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   pdl_wait();
 
   if (tid == 0) {
-    mbar_expect_tx(&bar_load, 6 * kTile);
+    // v on its own barrier: QK^T and the softmax overlap its load
+    mbar_expect_tx(&bar_load, 4 * kTile);
     tma_load_4d(sm + OFF_QH, &tQh, &bar_load, 0, h, 0, b);
     tma_load_4d(sm + OFF_QL, &tQl, &bar_load, 0, h, 0, b);
     tma_load_4d(sm + OFF_KH, &tKh, &bar_load, 0, h, 0, b);
     tma_load_4d(sm + OFF_KL, &tKl, &bar_load, 0, h, 0, b);
-    tma_load_4d(sm + OFF_VH, &tVh, &bar_load, 0, h, 0, b);
-    tma_load_4d(sm + OFF_VL, &tVl, &bar_load, 0, h, 0, b);
+    mbar_expect_tx(&bar_v, 2 * kTile);
+    tma_load_4d(sm + OFF_VH, &tVh, &bar_v, 0, h, 0, b);
+    tma_load_4d(sm + OFF_VL, &tVl, &bar_v, 0, h, 0, b);
   }
   // A mask that broadcasts over query rows is staged once (one row).
   const bool mask_bcast = a.mask && a.ms[2] == 0;
@@ -140,6 +143,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = tid; j < kRows; j += kThreads) mrow_s[j] = j < a.S ? mb[(int64_t)j * a.ms[3]] : 0;
   }
   bool ok = __syncthreads_and(mbar_wait(&bar_load, 0)) != 0;
+  bool v_waited = false;
   if (ok) {
     if (tid == 0) {
       tc_fence_after();
@@ -215,8 +219,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     fence_proxy_async();
     tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
+    ok = __syncthreads_and(mbar_wait(&bar_v, 0)) != 0;
+    v_waited = true;
+    if (ok && tid == 0) {
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16(kRows, kHd, true);
       const uint32_t ph0 = smem_u32(sm + OFF_PH), pl0 = smem_u32(sm + OFF_PL);
@@ -235,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       mma_commit(&bar_o);
     }
-    ok = __syncthreads_and(mbar_wait(&bar_o, 0)) != 0;
+    if (ok) ok = __syncthreads_and(mbar_wait(&bar_o, 0)) != 0;
   }
   if (ok) {
     tc_fence_after();
@@ -267,6 +272,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (tid == 0) {
     atomicExch(&g_attn_f16_error, 1);
   }
+  // after an early failure, v may still be landing: wait (bounded) before exit
+  if (!v_waited) mbar_wait(&bar_v, 0);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
