@@ -180,14 +180,19 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // Scalar fallback for odd N / unaligned pointers: one thread per column.
+// One warp per column (lanes take k = lane, lane + 32, ..., then a fixed-order
+// warp sum): a few columns, or a layout the vector kernel cannot take.
 __global__ void gemv_kn_scalar_kernel(GemvArgs a) {
   __shared__ float xs[kMaxK];
   __shared__ float red[kWarps];
   stage_x(a.x, a.ln_gamma, a.ln_beta, a.ln_eps, a.K, 0, a.K, xs, red);
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t c = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (c >= a.N) return;
   float acc = 0.f;
-  for (int64_t k = 0; k < a.K; ++k) acc = fmaf(xs[k], a.w[k * a.N + c], acc);
+  for (int64_t k = lane; k < a.K; k += 32) acc = fmaf(xs[k], a.w[k * a.N + c], acc);
+  acc = warp_sum(acc);
+  if (lane != 0) return;
   float v = a.alpha * acc;
   if (a.bias) v += a.beta * a.bias[c];
   if (a.resid) v += a.resid[c];
@@ -552,7 +557,7 @@ void launch_gemv(const GemvArgs& g, cudaStream_t st) {
   Workspace& ws = g.ws ? *g.ws : workspace_for_current_device();
   const bool vec = g.N % 4 == 0 && aligned16(g.w);
   if (!vec) {
-    gemv_kn_scalar_kernel<<<(unsigned)((g.N + kThreads - 1) / kThreads), kThreads, 0, st>>>(g);
+    gemv_kn_scalar_kernel<<<(unsigned)((g.N + kWarps - 1) / kWarps), kThreads, 0, st>>>(g);
     IDEV_LAUNCHED();
     return;
   }
@@ -700,7 +705,7 @@ extern "C" int inferc_dev_gemv_noalloc(const float* x, const float* w, const flo
     g.x = x; g.w = w; g.bias = b; g.resid = resid; g.y = y; g.K = K; g.N = N;
     g.alpha = 1.0f; g.beta = 1.0f; g.act = act;
     if (!(N % 4 == 0 && aligned16(w))) {  // scalar path: needs no scratch
-      gemv_kn_scalar_kernel<<<(unsigned)((N + kThreads - 1) / kThreads), kThreads, 0, st>>>(g);
+      gemv_kn_scalar_kernel<<<(unsigned)((N + kWarps - 1) / kWarps), kThreads, 0, st>>>(g);
       IDEV_LAUNCHED();
       return;
     }
