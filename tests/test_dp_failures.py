@@ -90,6 +90,9 @@ def _dier(rank, world, port, q):
         q.put(("no error", time.monotonic() - t0))
     except Exception as e:  # gloo: connection closed or timeout
         q.put((type(e).__name__, time.monotonic() - t0))
+    # os._exit skips the queue's feeder thread: flush the result first
+    q.close()
+    q.join_thread()
     os._exit(0)
 
 
