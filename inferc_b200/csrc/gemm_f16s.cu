@@ -327,10 +327,25 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
     __shared__ int last_sh;
     const int et = threadIdx.x - 64 - kConvThreads;  // 0 .. kEpiThreads-1
     auto epi_sync = [] { asm volatile("bar.sync 2, %0;" ::"r"(kEpiThreads) : "memory"); };
+    // AND over the epilogue threads (barrier 2): with split K they meet at
+    // epi_sync, so all must leave the loop together
+    auto epi_all = [](bool v) {
+      uint32_t r;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.u32 p, %1, 0;\n\t"
+          "bar.red.and.pred q, 2, %2, p;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(r)
+          : "r"((uint32_t)v), "r"(kEpiThreads)
+          : "memory");
+      return r != 0;
+    };
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++tl) {
       const int tile = u / splits;
       const int acc = tl & 1;
-      const bool ok = !abort_sh && mbar_wait(&tfull_bar[acc], (tl >> 1) & 1);
+      bool ok = !abort_sh && mbar_wait(&tfull_bar[acc], (tl >> 1) & 1);
+      if (splits > 1) ok = epi_all(ok);
       if (!ok) {
         fail();
         break;

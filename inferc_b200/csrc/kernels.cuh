@@ -72,7 +72,8 @@ struct F16GemmA {
 // the SMs, K is split over CTAs that store raw partial tiles in `part`
 // (part_floats floats); the CTA that completes a tile's counter (cnt, cnt_n
 // words, zero at rest and left zero) sums the partials in split order and
-// runs the epilogue. Null part: no split.
+// runs the epilogue. Null part: no split. A call that reports a timeout can
+// leave counters non-zero: the owner must clear them (or be recreated).
 struct SplitK {
   float* part = nullptr;
   int64_t part_floats = 0;
