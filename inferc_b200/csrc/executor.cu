@@ -210,6 +210,8 @@ struct InfercGraph {
   int device = 0;
   std::unordered_map<std::string, T> inits;
   std::set<std::string> init_names;
+  // folded Transpose(perm = [1, 0]) of a 2-D initializer -> that initializer
+  std::map<std::string, std::string> transposed_of;
   std::unordered_map<std::string, T> inputs;
   std::unordered_map<std::string, T> outputs;
   std::vector<Step> steps;
@@ -400,6 +402,9 @@ struct InfercGraph {
       if (owned.numel() <= kFoldElems) owned.host = t.host;
       inits[n.outputs[0]] = owned;
       init_names.insert(n.outputs[0]);
+      const std::vector<int64_t> perm = n.attr_ints("perm");
+      if (t.shape.size() == 2 && perm.size() == 2 && perm[0] == 1 && perm[1] == 0)
+        transposed_of[n.outputs[0]] = n.inputs[0];
       folded.insert(&n);
     }
     IDEV_CUDA(cudaStreamSynchronize(st));
@@ -1146,7 +1151,16 @@ struct InfercGraph {
     const int64_t batch = numel_of(ob);
     const bool b_is_init = init_names.count(b_name) && bb.empty();
     Epilogue ep;
-    if (batch == 1 && M == 1 && K <= 8192) {  // a row vector: the split-K GEMV
+    const auto tr = transposed_of.find(b_name);
+    if (batch == 1 && M == 1 && K <= 8192 && (N % 4 != 0 || !aligned16(b.d<float>())) &&
+        tr != transposed_of.end() && bb.empty()) {
+      // a row vector by a folded W^T whose rows the vector GEMV cannot read
+      // (the tied LM head: N = vocab): the row GEMV over W itself, [N, K]
+      RowGemvArgs r{};
+      r.x = a.d<float>(); r.w = inits[tr->second].d<float>(); r.y = o.d<float>();
+      r.K = K; r.N = N;
+      launch_row_gemv(r, st);
+    } else if (batch == 1 && M == 1 && K <= 8192) {  // a row vector: the split-K GEMV
       GemvArgs gv{};
       gv.x = a.d<float>(); gv.w = b.d<float>(); gv.y = o.d<float>(); gv.K = K; gv.N = N;
       gv.alpha = 1.f; gv.beta = 1.f; gv.act = ACT_NONE;
@@ -1163,6 +1177,26 @@ struct InfercGraph {
       bcast_strides(ab, ob, sa);
       bcast_strides(bb, ob, sb);
       const int br = (int)ob.size();
+      if (M <= kGlueBmmMaxM && batch <= 65535 && br <= kGlueMaxRank) {
+        // a few rows per matrix (decode attention: one query row per head):
+        // every matrix of the batch in one launch
+        GlueShape g;
+        g.rank = br;
+        g.n = batch;
+        for (int d = 0; d < br; ++d) {
+          g.shape[d] = ob[d];
+          g.s0[d] = sa[d];
+          g.s1[d] = sb[d];
+        }
+        launch_glue_bmm_small(a.d<float>(), b.d<float>(), o.d<float>(), M, K, N, g, st);
+        if (a1 || b1) {
+          std::vector<int64_t> s2 = ob;
+          if (!a1) s2.push_back(M);
+          if (!b1) s2.push_back(N);
+          o.shape = s2;
+        }
+        return o;
+      }
       for (int64_t i = 0; i < batch; ++i) {
         int64_t rem = i, ia = 0, ib = 0;
         for (int d = br - 1; d >= 0; --d) {

@@ -388,4 +388,56 @@ void launch_glue_fill(int elem_bytes, void* out, const void* value, int64_t n, c
   IDEV_LAUNCHED();
 }
 
+
+// One CTA per (32 output columns, matrix): lane = column (coalesced rows of
+// B), warp = k slice (k = warp, warp + 8, ...); the 8 slices' partial sums
+// are added in slice order.
+__global__ void __launch_bounds__(256) bmm_small_kernel(const float* __restrict__ a,
+                                                        const float* __restrict__ b,
+                                                        float* __restrict__ out, int M, int64_t K,
+                                                        int64_t N, GlueShape g) {
+  __shared__ float red[8][kGlueBmmMaxM][32];
+  const int64_t i = blockIdx.y;
+  int64_t rem = i, ia = 0, ib = 0;
+  for (int d = g.rank - 1; d >= 0; --d) {
+    const int64_t c = rem % g.shape[d];
+    rem /= g.shape[d];
+    ia += c * g.s0[d];
+    ib += c * g.s1[d];
+  }
+  const float* A = a + ia * M * K;
+  const float* B = b + ib * K * N;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t n = (int64_t)blockIdx.x * 32 + tx;
+  float acc[kGlueBmmMaxM];
+#pragma unroll
+  for (int m = 0; m < kGlueBmmMaxM; ++m) acc[m] = 0.f;
+  if (n < N)
+    for (int64_t k = ty; k < K; k += 8) {
+      const float bv = B[k * N + n];
+#pragma unroll
+      for (int m = 0; m < kGlueBmmMaxM; ++m)
+        if (m < M) acc[m] = fmaf(A[m * K + k], bv, acc[m]);
+    }
+#pragma unroll
+  for (int m = 0; m < kGlueBmmMaxM; ++m)
+    if (m < M) red[ty][m][tx] = acc[m];
+  __syncthreads();
+  if (ty < M && n < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int sl = 0; sl < 8; ++sl) t += red[sl][ty][tx];
+    out[(i * M + ty) * N + n] = t;
+  }
+}
+
+void launch_glue_bmm_small(const float* a, const float* b, float* out, int64_t M, int64_t K,
+                           int64_t N, const GlueShape& g, cudaStream_t st) {
+  if (g.n <= 0 || M <= 0 || N <= 0) return;
+  IDEV_CHECK_ARG(M <= kGlueBmmMaxM && g.n <= 65535, "batched small MatMul: M or batch too large");
+  dim3 grid((unsigned)((N + 31) / 32), (unsigned)g.n);
+  bmm_small_kernel<<<grid, 256, 0, st>>>(a, b, out, (int)M, K, N, g);
+  IDEV_LAUNCHED();
+}
+
 }  // namespace inferc_dev

@@ -51,4 +51,12 @@ void launch_glue_gather(int elem_bytes, const void* data, const void* idx, bool 
 void launch_glue_row_mean(const float* x, float* y, int64_t rows, int64_t cols, cudaStream_t st);
 void launch_glue_fill(int elem_bytes, void* out, const void* value, int64_t n, cudaStream_t st);
 
+// Batched MatMul with at most kGlueBmmMaxM rows per matrix: for each index i
+// of the batch shape g.shape (g.n matrices), out[i] (M x N) = A[i] (M x K)
+// B[i] (K x N), A[i] and B[i] found through the per-axis matrix strides g.s0
+// and g.s1 (0 on broadcast axes). Fixed summation order.
+constexpr int kGlueBmmMaxM = 8;
+void launch_glue_bmm_small(const float* a, const float* b, float* out, int64_t M, int64_t K,
+                           int64_t N, const GlueShape& g, cudaStream_t st);
+
 }  // namespace inferc_dev

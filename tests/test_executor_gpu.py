@@ -242,3 +242,23 @@ def test_errors_match_the_reference_messages():
         _run(lambda g: g.add("Add", ["x", g.init("b", _f(4))], outputs=["y"]), {"x": x})
     with pytest.raises(InfercError, match="Cast: unsupported dtype pair"):
         _run(lambda g: g.add("Cast", ["x"], outputs=["y"], to=9), {"x": x})
+
+
+def test_matmul_decode_shapes():
+    """The with-past decode graph's MatMuls: one query row per head against a
+    growing key block (batched, every matrix in one launch), and the tied LM
+    head, a row vector by the folded Transpose of an initializer whose width
+    is not a multiple of 4 (the row GEMV over the initializer itself)."""
+    q, kt = _f(1, 12, 1, 64), _f(1, 12, 64, 161)
+    p, v = _f(1, 12, 1, 161), _f(1, 12, 161, 64)
+    x, wte = _f(1, 96), _f(1003, 96)
+
+    def build(g):
+        g.init("wte", wte)
+        g.add("MatMul", ["q", "kt"], outputs=["s"])
+        g.add("MatMul", ["p", "v"], outputs=["o"])
+        g.add("MatMul", ["x", g.one("Transpose", ["wte"], perm=[1, 0])], outputs=["logits"])
+    r = _run(build, {"q": q, "kt": kt, "p": p, "v": v, "x": x}, ("s", "o", "logits"))
+    np.testing.assert_allclose(r["s"], np.matmul(q, kt), rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(r["o"], np.matmul(p, v), rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(r["logits"], x @ wte.T, rtol=1e-5, atol=1e-4)
