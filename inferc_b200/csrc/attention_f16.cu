@@ -2,23 +2,23 @@
 // fp32-level accuracy, for q, k and v given as the split-fp16 planes the
 // QKV GEMM writes (x = hi + lo, gemm_f16s.cu's representation).
 //
-// S <= 128: one CTA per (batch, head), as in attention_tc.cu, but:
+// S <= 128: persistent CTAs, two per SM, each walking (batch, head) items:
 //   * no split step: TMA loads the six hi / lo head tiles (96 KB) directly;
 //   * S = Q K^T and O = P V each take three kind::f16 MMAs per product
 //     (lo hi + hi lo + hi hi), at twice the tf32 rate;
 //   * P is written as fp16 hi / lo (P in [0, 1]: elements below 2^-14 keep
-//     an absolute error under 2^-25);
+//     an absolute error under 2^-25) into tensor memory over S, and the PV
+//     MMAs read it from there, so the Q / K tiles are free as soon as S is
+//     done and the next item's loads run under this item's softmax;
 //   * the mask is staged as one row (a mask that broadcasts over query rows,
 //     the padding mask of the encoder) or read per row from global memory.
-// That is ~98 KB of shared memory and 256 TMEM columns per CTA, so two CTAs
-// share an SM and one's softmax or epilogue overlaps the other's loads and
-// MMAs.
+// That is ~98 KB of shared memory and 256 TMEM columns per CTA.
 //
-// Steps: TMA -> S = QK^T (M=128 queries, N=128 keys, K=64) -> masked
+// Steps per item: TMA -> S = QK^T (M=128 queries, N=128 keys, K=64) -> masked
 // softmax (two threads per row, 64 keys each in registers; masked entries
 // are REPLACED by `fill`, keys past S get no weight, as rt::FusedAttention,
-// src/kernels/attention.cc:77-91) -> P planes over the spent Q / K tiles ->
-// O = P V (V MN-major, SWIZZLE_128B) -> O as fp32 or as fp16 planes.
+// src/kernels/attention.cc:77-91) -> P hi / lo into TMEM -> O = P V (V
+// MN-major, SWIZZLE_128B) -> O as fp32 or as fp16 planes.
 // Every mbarrier wait is bounded; a timeout sets g_attn_f16_error.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -40,11 +40,9 @@ constexpr int kRows = 128;
 constexpr int kHd = 64;
 constexpr int kThreads = 256;
 constexpr uint32_t kTile = 16384;  // [128 rows][128 B]: one fp16 plane of a head tile
-// Q hi, Q lo, K hi, K lo, V hi, V lo; P hi / lo (two 64-key atoms each)
-// reuse Q and K once S = QK^T is done.
+// Q hi, Q lo, K hi, K lo, V hi, V lo (P lives in tensor memory).
 constexpr uint32_t OFF_QH = 0, OFF_QL = kTile, OFF_KH = 2 * kTile, OFF_KL = 3 * kTile,
                    OFF_VH = 4 * kTile, OFF_VL = 5 * kTile;
-constexpr uint32_t OFF_PH = 0, OFF_PL = 2 * kTile;
 constexpr uint32_t OFF_MASK = 6 * kTile;  // one row of kRows bytes
 constexpr uint32_t kSmemBytes = 6 * kTile + kRows + 1024;
 
@@ -84,33 +82,88 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool b_mn) {
          ((uint32_t)(m >> 4) << 24);
 }
 
+// PV with A = P read from tensor memory: 128 lanes = query rows, each 32-bit
+// column two consecutive keys (the lower half the even key).
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// split_pair for values known to lie in [0, 1] (no range check): fp16 hi of
+// (a, b) packed, the fp16 of the remainders in lo_bits.
+__device__ __forceinline__ uint32_t split_unit_pair(float a, float b, uint32_t& lo_bits) {
+  uint32_t h, l;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  const float ha = __half2float(__ushort_as_half((unsigned short)(h & 0xFFFFu)));
+  const float hb = __half2float(__ushort_as_half((unsigned short)(h >> 16)));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(l) : "f"(b - hb), "f"(a - ha));
+  lo_bits = l;
+  return h;
+}
+
+// 16 consecutive 32-bit columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+// Persistent: CTA c takes the (batch, head) items c, c + grid, c + 2 grid, ...
+// (item = b * nH + h). Per item:
+//   S = QK^T (TMEM cols 0..127) -> the next item's Q / K load is issued at once
+//   (their tiles are free) -> masked softmax in registers, P written over S as
+//   fp16 hi (cols 0..63) / lo (cols 64..127) -> O = P V with A read from TMEM
+//   (cols 128..191) -> the next item's V load and S = QK^T are issued -> the
+//   epilogue of this item overlaps both.
+// So a CTA's loads run under its own softmax and epilogue, and two CTAs per SM
+// overlap each other's compute phases.
 __global__ void __launch_bounds__(kThreads, 2)
     attention_f16_kernel(const __grid_constant__ CUtensorMap tQh,
                          const __grid_constant__ CUtensorMap tQl,
                          const __grid_constant__ CUtensorMap tKh,
                          const __grid_constant__ CUtensorMap tKl,
                          const __grid_constant__ CUtensorMap tVh,
-                         const __grid_constant__ CUtensorMap tVl, const AttnF16Kern a) {
+                         const __grid_constant__ CUtensorMap tVl, const AttnF16Kern a,
+                         int n_items, int nH) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bar_load, bar_v, bar_s, bar_o;  // bar_load: q and k
+  __shared__ __align__(8) uint64_t bar_qk, bar_v, bar_s, bar_o, bar_drain;
   __shared__ uint32_t tmem_sh;
+  __shared__ int fail0;
   __shared__ float red_max[2][kRows], red_sum[2][kRows];
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int b = blockIdx.z, h = blockIdx.y;
   const int quad = warp & 3, half = warp >> 2;
   const int row = quad * 32 + (tid & 31), col0 = 64 * half;
   const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
 
   if (tid == 0) {
-    mbar_init(&bar_load, 1);
+    mbar_init(&bar_qk, 1);
     mbar_init(&bar_v, 1);
     mbar_init(&bar_s, 1);
     mbar_init(&bar_o, 1);
+    mbar_init(&bar_drain, 1);
+    fail0 = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // S: columns 0..127, O: 128..191
+  if (warp == 1) {  // S / P: columns 0..127, O: 128..191
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
         smem_u32(&tmem_sh)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -124,45 +177,71 @@ __global__ void __launch_bounds__(kThreads, 2)
   pdl_launch_dependents();
   pdl_wait();
 
-  if (tid == 0) {
-    // v on its own barrier: QK^T and the softmax overlap its load
-    mbar_expect_tx(&bar_load, 4 * kTile);
-    tma_load_4d(sm + OFF_QH, &tQh, &bar_load, 0, h, 0, b);
-    tma_load_4d(sm + OFF_QL, &tQl, &bar_load, 0, h, 0, b);
-    tma_load_4d(sm + OFF_KH, &tKh, &bar_load, 0, h, 0, b);
-    tma_load_4d(sm + OFF_KL, &tKl, &bar_load, 0, h, 0, b);
+  // Copies and MMAs are issued by thread 0 only; it counts what it issued
+  // and what it saw complete, so that the abort path can wait for the rest.
+  uint32_t qk_issued = 0, qk_seen = 0, v_issued = 0, v_seen = 0;
+  auto issue_qk = [&](int it) {
+    const int b = it / nH, h = it - (it / nH) * nH;
+    mbar_expect_tx(&bar_qk, 4 * kTile);
+    tma_load_4d(sm + OFF_QH, &tQh, &bar_qk, 0, h, 0, b);
+    tma_load_4d(sm + OFF_QL, &tQl, &bar_qk, 0, h, 0, b);
+    tma_load_4d(sm + OFF_KH, &tKh, &bar_qk, 0, h, 0, b);
+    tma_load_4d(sm + OFF_KL, &tKl, &bar_qk, 0, h, 0, b);
+    ++qk_issued;
+  };
+  auto issue_v = [&](int it) {
+    const int b = it / nH, h = it - (it / nH) * nH;
     mbar_expect_tx(&bar_v, 2 * kTile);
     tma_load_4d(sm + OFF_VH, &tVh, &bar_v, 0, h, 0, b);
     tma_load_4d(sm + OFF_VL, &tVl, &bar_v, 0, h, 0, b);
-  }
-  // A mask that broadcasts over query rows is staged once (one row).
+    ++v_issued;
+  };
+  auto issue_s = [&]() {  // S = Q K^T into columns 0..127
+    tc_fence_after();
+    constexpr uint32_t idesc = idesc_f16(kRows, kRows, false);
+    const uint32_t qh = smem_u32(sm + OFF_QH), ql = smem_u32(sm + OFF_QL);
+    const uint32_t kh = smem_u32(sm + OFF_KH), kl = smem_u32(sm + OFF_KL);
+#pragma unroll
+    for (int j = 0; j < kHd / 16; ++j) {  // 16 fp16 = 32 bytes per k-step
+      const uint64_t dqh = smem_desc(qh + j * 32, 16, 1024, 2), dql = smem_desc(ql + j * 32, 16, 1024, 2);
+      const uint64_t dkh = smem_desc(kh + j * 32, 16, 1024, 2), dkl = smem_desc(kl + j * 32, 16, 1024, 2);
+      mma_f16(tmem, dql, dkh, idesc, j != 0);
+      mma_f16(tmem, dqh, dkl, idesc, 1);
+      mma_f16(tmem, dqh, dkh, idesc, 1);
+    }
+    mma_commit(&bar_s);
+  };
+
   const bool mask_bcast = a.mask && a.ms[2] == 0;
   uint8_t* mrow_s = sm + OFF_MASK;
-  if (mask_bcast) {
-    const uint8_t* mb = a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1];
-    for (int j = tid; j < kRows; j += kThreads) mrow_s[j] = j < a.S ? mb[(int64_t)j * a.ms[3]] : 0;
+  bool ok = true;
+  if (tid == 0 && (int)blockIdx.x < n_items) {
+    issue_qk(blockIdx.x);
+    issue_v(blockIdx.x);
   }
-  bool ok = __syncthreads_and(mbar_wait(&bar_load, 0)) != 0;
-  bool v_waited = false;
-  if (ok) {
-    if (tid == 0) {
-      tc_fence_after();
-      constexpr uint32_t idesc = idesc_f16(kRows, kRows, false);
-      const uint32_t qh = smem_u32(sm + OFF_QH), ql = smem_u32(sm + OFF_QL);
-      const uint32_t kh = smem_u32(sm + OFF_KH), kl = smem_u32(sm + OFF_KL);
-#pragma unroll
-      for (int j = 0; j < kHd / 16; ++j) {  // 16 fp16 = 32 bytes per k-step
-        const uint64_t dqh = smem_desc(qh + j * 32, 16, 1024, 2), dql = smem_desc(ql + j * 32, 16, 1024, 2);
-        const uint64_t dkh = smem_desc(kh + j * 32, 16, 1024, 2), dkl = smem_desc(kl + j * 32, 16, 1024, 2);
-        mma_f16(tmem, dql, dkh, idesc, j != 0);
-        mma_f16(tmem, dqh, dkl, idesc, 1);
-        mma_f16(tmem, dqh, dkh, idesc, 1);
-      }
-      mma_commit(&bar_s);
+  uint32_t k = 0;  // this CTA's item count
+  for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+    const int b = it / nH, h = it - (it / nH) * nH;
+    const int next = it + (int)gridDim.x;
+    const uint32_t par = k & 1u;
+    // A mask that broadcasts over query rows is staged once per item (one
+    // row); the previous item's readers are past a CTA barrier.
+    if (mask_bcast) {
+      const uint8_t* mb = a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1];
+      for (int j = tid; j < kRows; j += kThreads) mrow_s[j] = j < a.S ? mb[(int64_t)j * a.ms[3]] : 0;
     }
-    ok = __syncthreads_and(mbar_wait(&bar_s, 0)) != 0;
-  }
-  if (ok) {
+    if (k == 0) {
+      ok = __syncthreads_and(mbar_wait(&bar_qk, 0)) != 0;
+      if (!ok) break;
+      if (tid == 0) {
+        ++qk_seen;
+        issue_s();
+      }
+    }
+    // S(it) landed: Q / K tiles are free for the next item
+    ok = __syncthreads_and(fail0 == 0 && mbar_wait(&bar_s, par)) != 0;
+    if (!ok) break;
+    if (tid == 0 && next < n_items) issue_qk(next);
     tc_fence_after();
     float s[64];
 #pragma unroll
@@ -176,81 +255,108 @@ __global__ void __launch_bounds__(kThreads, 2)
         (a.mask && !mask_bcast && row < a.S)
             ? a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)row * a.ms[2]
             : nullptr;
+    // scores: scale * s, masked entries replaced by fill, keys past S -inf
+    const int nvalid = a.S - col0;  // keys of this thread's half that exist
     float mx = -INFINITY;
+    if (mask_bcast) {
+      uint4 mw[4];  // this half's 64 mask bytes
 #pragma unroll
-    for (int q = 0; q < 64; ++q) {
-      const int j = col0 + q;
-      bool masked = false;
-      if (mask_bcast) masked = mrow_s[j] != 0;
-      else if (mrow_g && j < a.S) masked = mrow_g[(int64_t)j * a.ms[3]] != 0;
-      float v;
-      if (j >= a.S) v = -INFINITY;  // beyond the sequence: no weight at all
-      else if (masked) v = a.fill;
-      else v = a.scale * s[q];
-      s[q] = v;
-      mx = fmaxf(mx, v);
+      for (int i = 0; i < 4; ++i) mw[i] = reinterpret_cast<const uint4*>(mrow_s + col0)[i];
+#pragma unroll
+      for (int q = 0; q < 64; ++q) {
+        const uint4 w4 = mw[q >> 4];
+        const uint32_t w = (q & 15) < 4 ? w4.x : (q & 15) < 8 ? w4.y : (q & 15) < 12 ? w4.z : w4.w;
+        const bool masked = ((w >> (8 * (q & 3))) & 0xffu) != 0u;
+        float v = masked ? a.fill : a.scale * s[q];
+        if (q >= nvalid) v = -INFINITY;  // beyond the sequence: no weight at all
+        s[q] = v;
+        mx = fmaxf(mx, v);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 64; ++q) {
+        const bool masked = mrow_g && q < nvalid && mrow_g[(int64_t)(col0 + q) * a.ms[3]] != 0;
+        float v = masked ? a.fill : a.scale * s[q];
+        if (q >= nvalid) v = -INFINITY;
+        s[q] = v;
+        mx = fmaxf(mx, v);
+      }
     }
     red_max[half][row] = mx;
+    // every thread's S reads are complete (tcgen05.wait::ld) before this
+    // barrier, so P may overwrite the S columns after it
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
     mx = fmaxf(red_max[0][row], red_max[1][row]);
+    // P = exp(v - max), left unnormalised (in [0, 1]); the epilogue divides O
+    // by the row sum. exp(x) = 2^(x log2 e) on the SFU (ex2.approx, relative
+    // error ~2^-22, below the fp16 hi / lo split's resolution). A fully masked
+    // row has v = max = fill everywhere: v - max = 0, uniform weights, as in
+    // the reference; any other fill entry gives 2^-inf = 0.
+    // P hi: keys 2c, 2c + 1 -> column c (this thread's keys: columns
+    // 32 half .. 32 half + 31); P lo at 64 + the same column.
     float sum = 0.f;
 #pragma unroll
-    for (int q = 0; q < 64; ++q) {
-      s[q] = expf(s[q] - mx);
-      sum += s[q];
+    for (int c = 0; c < 2; ++c) {
+      uint32_t hw[16], lw[16];
+#pragma unroll
+      for (int p = 0; p < 16; ++p) {
+        const float e0 = ex2_approx((s[32 * c + 2 * p] - mx) * kLog2e);
+        const float e1 = ex2_approx((s[32 * c + 2 * p + 1] - mx) * kLog2e);
+        sum += e0 + e1;
+        hw[p] = split_unit_pair(e0, e1, lw[p]);
+      }
+      tmem_st16(tmem + lane_base + (uint32_t)(32 * half + 16 * c), hw);
+      tmem_st16(tmem + lane_base + (uint32_t)(64 + 32 * half + 16 * c), lw);
     }
     red_sum[half][row] = sum;
-    __syncthreads();
-    const float inv = 1.0f / (red_sum[0][row] + red_sum[1][row]);
-    // P planes: keys [0, 64) and [64, 128) are two K atoms of [128 rows][128 B];
-    // this thread's 64 keys are atom `half`, 8 chunks of 8 keys.
-    uint8_t* ph = sm + OFF_PH + half * kTile;
-    uint8_t* pl = sm + OFF_PL + half * kTile;
-    bool bad = false;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint32_t hw[4], lw[4];
-#pragma unroll
-      for (int p = 0; p < 4; ++p)
-        hw[p] = split_pair(s[8 * c + 2 * p] * inv, s[8 * c + 2 * p + 1] * inv, lw[p], bad);
-      const uint32_t off = (uint32_t)row * 128 + ((uint32_t)(c ^ (row & 7)) << 4);
-      *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    }
-    fence_proxy_async();
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     tc_fence_before();
-    ok = __syncthreads_and(mbar_wait(&bar_v, 0)) != 0;
-    v_waited = true;
-    if (ok && tid == 0) {
+    ok = __syncthreads_and(mbar_wait(&bar_v, par)) != 0;
+    if (!ok) break;
+    if (tid == 0) {
+      ++v_seen;
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16(kRows, kHd, true);
-      const uint32_t ph0 = smem_u32(sm + OFF_PH), pl0 = smem_u32(sm + OFF_PL);
       const uint32_t vh = smem_u32(sm + OFF_VH), vl = smem_u32(sm + OFF_VL);
 #pragma unroll
-      for (int j = 0; j < kRows / 16; ++j) {  // 16 keys per k-step
-        const uint32_t aoff = (j >> 2) * kTile + (j & 3) * 32;
-        const uint64_t dph = smem_desc(ph0 + aoff, 16, 1024, 2), dpl = smem_desc(pl0 + aoff, 16, 1024, 2);
+      for (int j = 0; j < kRows / 16; ++j) {  // 16 keys (8 P columns) per k-step
         // V: MN-major SWIZZLE_128B, rows of 64 d (128 B), 8-key groups 1 KiB
         // apart; a 16-key step advances 2 KiB. N = 64 is one atom wide.
         const uint64_t dvh = smem_desc(vh + j * 2048, 8192, 1024, 2);
         const uint64_t dvl = smem_desc(vl + j * 2048, 8192, 1024, 2);
-        mma_f16(tmem + kRows, dpl, dvh, idesc, j != 0);
-        mma_f16(tmem + kRows, dph, dvl, idesc, 1);
-        mma_f16(tmem + kRows, dph, dvh, idesc, 1);
+        const uint32_t ph = tmem + (uint32_t)(8 * j), pl = tmem + (uint32_t)(64 + 8 * j);
+        mma_f16_ta(tmem + kRows, pl, dvh, idesc, j != 0);
+        mma_f16_ta(tmem + kRows, ph, dvl, idesc, 1);
+        mma_f16_ta(tmem + kRows, ph, dvh, idesc, 1);
       }
       mma_commit(&bar_o);
     }
-    if (ok) ok = __syncthreads_and(mbar_wait(&bar_o, 0)) != 0;
-  }
-  if (ok) {
+    ok = __syncthreads_and(mbar_wait(&bar_o, par)) != 0;
+    if (!ok) break;
+    // P and V consumed: the next item's V load and S = QK^T run under this
+    // item's epilogue (S writes columns 0..127, the epilogue reads 128..191).
+    if (tid == 0 && next < n_items) {
+      issue_v(next);
+      if (mbar_wait(&bar_qk, (k + 1) & 1u)) {
+        ++qk_seen;
+        issue_s();
+      } else {
+        fail0 = 1;
+      }
+    }
     tc_fence_after();
     const int64_t col = h * kHd + 32 * half;
+    const float inv = 1.0f / (red_sum[0][row] + red_sum[1][row]);
     bool bad = false;
 #pragma unroll
     for (int c0 = 0; c0 < 32; c0 += 16) {
       float v[16];
       tmem_ld16(tmem + lane_base + kRows + (uint32_t)(32 * half + c0), v);
       if (row >= a.S) continue;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) v[q] *= inv;
       const int64_t o = (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + col + c0;
       if (a.so.hi) {
         uint32_t hw[8], lw[8];
@@ -269,11 +375,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     if (bad) atomicExch(a.so.range, 1);
-  } else if (tid == 0) {
-    atomicExch(&g_attn_f16_error, 1);
+    // O reads complete before the next item's PV may write O
+    tc_fence_before();
   }
-  // after an early failure, v may still be landing: wait (bounded) before exit
-  if (!v_waited) mbar_wait(&bar_v, 0);
+  if (!ok && tid == 0) atomicExch(&g_attn_f16_error, 1);
+  if (tid == 0) {
+    // Abort path: wait (bounded) for copies still landing in this CTA's
+    // shared memory and for every MMA this thread issued. On the normal path
+    // every copy was seen and the last MMA's commit was waited on.
+    for (; qk_seen < qk_issued; ++qk_seen) mbar_wait(&bar_qk, qk_seen & 1u);
+    for (; v_seen < v_issued; ++v_seen) mbar_wait(&bar_v, v_seen & 1u);
+    if (!ok) drain_mma(&bar_drain);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -281,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
   }
 }
+
 
 // ---------------------------------------------------------------- S > 128
 // Flash form: CTA (q-block, head, batch) holds its 128 query rows and loops
@@ -432,22 +546,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     red_max[half][lrow] = mx;
     __syncthreads();
     const float m_new = fmaxf(m_run, fmaxf(red_max[0][lrow], red_max[1][lrow]));
-    const float corr = expf(m_run - m_new);  // 0 on the first block (m_run = -inf)
+    const float corr = ex2_approx((m_run - m_new) * kLog2e);  // 0 on the first block (m_run = -inf)
     float sum = 0.f;
 #pragma unroll
     for (int q = 0; q < 64; ++q) {
-      s[q] = expf(s[q] - m_new);
+      s[q] = ex2_approx((s[q] - m_new) * kLog2e);
       sum += s[q];
     }
     red_sum[half][lrow] = sum;
     uint8_t* ph = sm + FL_P + half * kTile;
     uint8_t* pl = sm + FL_P + 2 * kTile + half * kTile;
-    bool bad = false;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint32_t hw[4], lw[4];
 #pragma unroll
-      for (int p = 0; p < 4; ++p) hw[p] = split_pair(s[8 * c + 2 * p], s[8 * c + 2 * p + 1], lw[p], bad);
+      for (int p = 0; p < 4; ++p) hw[p] = split_unit_pair(s[8 * c + 2 * p], s[8 * c + 2 * p + 1], lw[p]);
       const uint32_t off = (uint32_t)lrow * 128 + ((uint32_t)(c ^ (lrow & 7)) << 4);
       *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
@@ -590,9 +703,14 @@ void launch_attention_f16(const AttnF16Args& a, cudaStream_t st) {
   if (S <= kRows) {  // one key block: the two-CTAs-per-SM kernel
     IDEV_CUDA(cudaFuncSetAttribute(attention_f16_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    dim3 grid(1, (unsigned)nH, (unsigned)B);
-    launch_pdl(attention_f16_kernel, grid, dim3(kThreads), kSmemBytes, st, tqh, tql, tkh, tkl, tvh,
-               tvl, k);
+    // persistent: two CTAs per SM, each walking (batch, head) items
+    int dev = 0, sms = 0;
+    IDEV_CUDA(cudaGetDevice(&dev));
+    IDEV_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int items = B * nH;
+    const int grid = items < 2 * sms ? items : 2 * sms;
+    launch_pdl(attention_f16_kernel, dim3((unsigned)grid), dim3(kThreads), kSmemBytes, st, tqh,
+               tql, tkh, tkl, tvh, tvl, k, items, nH);
   } else {
     IDEV_CUDA(cudaFuncSetAttribute(attention_f16_flash_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlashSmem));

@@ -333,7 +333,8 @@ def test_qkv_attention_prepared(port, B, S):
 
 
 @pytest.mark.parametrize("B,S", [(1, 128), (8, 128), (3, 70), (1, 1), (2, 17), (4, 100),
-                                 (2, 512), (1, 300), (3, 257)])
+                                 (2, 512), (1, 300), (3, 257),
+                                 (64, 128), (31, 97)])
 def test_fused_attention_planes(port, B, S):
     """Split-fp16 tensor-core attention on q, k, v planes cut from one
     [B*S, 3H] pair (the encoder plan's layout), against the reference; S > 128
