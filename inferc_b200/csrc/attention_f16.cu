@@ -114,6 +114,27 @@ __device__ __forceinline__ uint32_t split_unit_pair(float a, float b, uint32_t& 
   return h;
 }
 
+// 32 consecutive 32-bit columns of this warp's 32 lanes, no wait: the
+// caller issues tcgen05.wait::ld once for a batch of loads.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, float (&v)[32]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // 16 consecutive 32-bit columns of this warp's 32 lanes.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -244,19 +265,24 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (tid == 0 && next < n_items) issue_qk(next);
     tc_fence_after();
     float s[64];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float v[16];
-      tmem_ld16(tmem + lane_base + (uint32_t)(col0 + 16 * c), v);
-#pragma unroll
-      for (int q = 0; q < 16; ++q) s[16 * c + q] = v[q];
+    {
+      float (&s0)[32] = *reinterpret_cast<float(*)[32]>(&s[0]);
+      float (&s1)[32] = *reinterpret_cast<float(*)[32]>(&s[32]);
+      tmem_ld32_async(tmem + lane_base + (uint32_t)col0, s0);
+      tmem_ld32_async(tmem + lane_base + (uint32_t)(col0 + 32), s1);
+      tmem_wait_ld();
     }
     const uint8_t* mrow_g =
         (a.mask && !mask_bcast && row < a.S)
             ? a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)row * a.ms[2]
             : nullptr;
-    // scores: scale * s, masked entries replaced by fill, keys past S -inf
+    // scores in the log2 domain: v = scale * s * log2(e); a masked entry is
+    // REPLACED by fill (clamped at -1e30, which gives the same weights: 0
+    // next to any visible key, uniform in a fully masked row); keys past S
+    // get -inf (no weight at all).
     const int nvalid = a.S - col0;  // keys of this thread's half that exist
+    const float sc2 = a.scale * kLog2e;
+    const float fill2 = fmaxf(a.fill, -1.0e30f) * kLog2e;
     float mx = -INFINITY;
     if (mask_bcast) {
       uint4 mw[4];  // this half's 64 mask bytes
@@ -266,20 +292,24 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int q = 0; q < 64; ++q) {
         const uint4 w4 = mw[q >> 4];
         const uint32_t w = (q & 15) < 4 ? w4.x : (q & 15) < 8 ? w4.y : (q & 15) < 12 ? w4.z : w4.w;
-        const bool masked = ((w >> (8 * (q & 3))) & 0xffu) != 0u;
-        float v = masked ? a.fill : a.scale * s[q];
-        if (q >= nvalid) v = -INFINITY;  // beyond the sequence: no weight at all
-        s[q] = v;
-        mx = fmaxf(mx, v);
+        const bool masked = (w & (0xffu << (8 * (q & 3)))) != 0u;
+        s[q] = masked ? fill2 : sc2 * s[q];
       }
     } else {
 #pragma unroll
       for (int q = 0; q < 64; ++q) {
         const bool masked = mrow_g && q < nvalid && mrow_g[(int64_t)(col0 + q) * a.ms[3]] != 0;
-        float v = masked ? a.fill : a.scale * s[q];
-        if (q >= nvalid) v = -INFINITY;
-        s[q] = v;
-        mx = fmaxf(mx, v);
+        s[q] = masked ? fill2 : sc2 * s[q];
+      }
+    }
+    if (nvalid >= 64) {
+#pragma unroll
+      for (int q = 0; q < 64; ++q) mx = fmaxf(mx, s[q]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 64; ++q) {
+        if (q >= nvalid) s[q] = -INFINITY;
+        mx = fmaxf(mx, s[q]);
       }
     }
     red_max[half][row] = mx;
@@ -289,11 +319,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     tc_fence_after();
     mx = fmaxf(red_max[0][row], red_max[1][row]);
-    // P = exp(v - max), left unnormalised (in [0, 1]); the epilogue divides O
-    // by the row sum. exp(x) = 2^(x log2 e) on the SFU (ex2.approx, relative
-    // error ~2^-22, below the fp16 hi / lo split's resolution). A fully masked
-    // row has v = max = fill everywhere: v - max = 0, uniform weights, as in
-    // the reference; any other fill entry gives 2^-inf = 0.
+    // P = exp(v - max) = 2^(v2 - max2) on the SFU (ex2.approx, relative error
+    // ~2^-22, below the fp16 hi / lo split's resolution), left unnormalised
+    // (in [0, 1]); the epilogue divides O by the row sum.
     // P hi: keys 2c, 2c + 1 -> column c (this thread's keys: columns
     // 32 half .. 32 half + 31); P lo at 64 + the same column.
     float sum = 0.f;
@@ -302,8 +330,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t hw[16], lw[16];
 #pragma unroll
       for (int p = 0; p < 16; ++p) {
-        const float e0 = ex2_approx((s[32 * c + 2 * p] - mx) * kLog2e);
-        const float e1 = ex2_approx((s[32 * c + 2 * p + 1] - mx) * kLog2e);
+        const float e0 = ex2_approx(s[32 * c + 2 * p] - mx);
+        const float e1 = ex2_approx(s[32 * c + 2 * p + 1] - mx);
         sum += e0 + e1;
         hw[p] = split_unit_pair(e0, e1, lw[p]);
       }
@@ -350,13 +378,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int64_t col = h * kHd + 32 * half;
     const float inv = 1.0f / (red_sum[0][row] + red_sum[1][row]);
     bool bad = false;
+    float ov[32];
+    tmem_ld32_async(tmem + lane_base + kRows + (uint32_t)(32 * half), ov);
+    tmem_wait_ld();
 #pragma unroll
     for (int c0 = 0; c0 < 32; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem + lane_base + kRows + (uint32_t)(32 * half + c0), v);
       if (row >= a.S) continue;
+      float v[16];
 #pragma unroll
-      for (int q = 0; q < 16; ++q) v[q] *= inv;
+      for (int q = 0; q < 16; ++q) v[q] = ov[c0 + q] * inv;
       const int64_t o = (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + col + c0;
       if (a.so.hi) {
         uint32_t hw[8], lw[8];
