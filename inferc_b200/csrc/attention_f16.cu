@@ -240,17 +240,23 @@ __global__ void __launch_bounds__(kThreads, 2)
     issue_qk(blockIdx.x);
     issue_v(blockIdx.x);
   }
+  // A mask that broadcasts over query rows is staged once per item (one row
+  // of kRows bytes, thread j < kRows holds byte j). The next item's bytes are
+  // loaded into a register during this item, so no load latency sits between
+  // two items.
+  auto mask_byte = [&](int itm) -> uint32_t {
+    if (!mask_bcast || tid >= kRows || tid >= a.S || itm >= n_items) return 0u;
+    const int bb = itm / nH, hh = itm - (itm / nH) * nH;
+    return a.mask[(int64_t)bb * a.ms[0] + (int64_t)hh * a.ms[1] + (int64_t)tid * a.ms[3]];
+  };
+  uint32_t mval = mask_byte(blockIdx.x);
   uint32_t k = 0;  // this CTA's item count
   for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
     const int b = it / nH, h = it - (it / nH) * nH;
     const int next = it + (int)gridDim.x;
     const uint32_t par = k & 1u;
-    // A mask that broadcasts over query rows is staged once per item (one
-    // row); the previous item's readers are past a CTA barrier.
-    if (mask_bcast) {
-      const uint8_t* mb = a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1];
-      for (int j = tid; j < kRows; j += kThreads) mrow_s[j] = j < a.S ? mb[(int64_t)j * a.ms[3]] : 0;
-    }
+    // the previous item's readers of the row are past a CTA barrier
+    if (mask_bcast && tid < kRows) mrow_s[tid] = (uint8_t)mval;
     if (k == 0) {
       ok = __syncthreads_and(mbar_wait(&bar_qk, 0)) != 0;
       if (!ok) break;
@@ -263,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     ok = __syncthreads_and(fail0 == 0 && mbar_wait(&bar_s, par)) != 0;
     if (!ok) break;
     if (tid == 0 && next < n_items) issue_qk(next);
+    mval = mask_byte(next);
     tc_fence_after();
     float s[64];
     {
