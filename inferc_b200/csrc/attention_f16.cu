@@ -436,18 +436,21 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------- S > 128
 // Flash form: CTA (q-block, head, batch) holds its 128 query rows and loops
 // over 128-key blocks with an online softmax. Per block: S_blk = Q K_blk^T
-// (TMEM), running row max m and sum l are updated (two threads per row,
-// 64 keys each), P_blk = exp(s - m) (in (0, 1], fp16 hi / lo) and
-// O_blk = P_blk V_blk (a fresh TMEM tile) is merged into the registers:
-// O = O c + O_blk with c = exp(m_old - m). The next block's K / V load is
-// issued as soon as this block's PV MMAs are done. O / l is stored at the end.
-// Shared memory: Q 32 KB, K 32 KB, V 32 KB, P 64 KB (one CTA per SM).
-constexpr uint32_t FL_Q = 0, FL_K = 2 * kTile, FL_V = 4 * kTile, FL_P = 6 * kTile;
-constexpr uint32_t FL_MASK = 10 * kTile;  // one mask row, up to kFlashMaxS bytes
+// (TMEM columns 0..127), running row max m and sum l are updated (two
+// threads per row, 64 keys each, in the log2 domain), P_blk = 2^(s - m) (in
+// (0, 1], fp16 hi / lo) is written over S_blk in TMEM, O_blk = P_blk V_blk
+// (TMEM columns 128..191, A read from TMEM) is merged into the registers:
+// O = O c + O_blk with c = 2^(m_old - m). O / l is stored at the end.
+// The next block's K load is issued as soon as S_blk is done (K free), its V
+// load and S = QK^T as soon as O_blk is done, so copies and MMAs run under
+// the softmax and the merge.
+// Shared memory: Q 32 KB, K 32 KB, V 32 KB, one mask row (one CTA per SM).
+constexpr uint32_t FL_Q = 0, FL_K = 2 * kTile, FL_V = 4 * kTile;
+constexpr uint32_t FL_MASK = 6 * kTile;  // one mask row, up to kFlashMaxS bytes
 constexpr int kFlashMaxS = 4096;
-constexpr uint32_t kFlashSmem = 10 * kTile + kFlashMaxS + 1024;
+constexpr uint32_t kFlashSmem = 6 * kTile + kFlashMaxS + 1024;
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     attention_f16_flash_kernel(const __grid_constant__ CUtensorMap tQh,
                                const __grid_constant__ CUtensorMap tQl,
                                const __grid_constant__ CUtensorMap tKh,
@@ -457,8 +460,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bar_q, bar_kv, bar_s, bar_o;
+  __shared__ __align__(8) uint64_t bar_q, bar_k, bar_v, bar_s, bar_o, bar_drain;
   __shared__ uint32_t tmem_sh;
+  __shared__ int fail0;
   __shared__ float red_max[2][kRows], red_sum[2][kRows];
   const int tid = threadIdx.x, warp = tid >> 5;
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -470,9 +474,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(&bar_q, 1);
-    mbar_init(&bar_kv, 1);
+    mbar_init(&bar_k, 1);
+    mbar_init(&bar_v, 1);
     mbar_init(&bar_s, 1);
     mbar_init(&bar_o, 1);
+    mbar_init(&bar_drain, 1);
+    fail0 = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -484,17 +491,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_sh;
-  auto load_kv = [&](int kb) {
-    mbar_expect_tx(&bar_kv, 4 * kTile);
-    tma_load_4d(sm + FL_K, &tKh, &bar_kv, 0, h, kb * kRows, b);
-    tma_load_4d(sm + FL_K + kTile, &tKl, &bar_kv, 0, h, kb * kRows, b);
-    tma_load_4d(sm + FL_V, &tVh, &bar_kv, 0, h, kb * kRows, b);
-    tma_load_4d(sm + FL_V + kTile, &tVl, &bar_kv, 0, h, kb * kRows, b);
+  // Copies and MMAs are issued by thread 0 only; it counts what it issued
+  // and what it saw complete, so that the abort path can wait for the rest.
+  uint32_t q_issued = 0, q_seen = 0, k_issued = 0, k_seen = 0, v_issued = 0, v_seen = 0;
+  auto load_k = [&](int kb) {
+    mbar_expect_tx(&bar_k, 2 * kTile);
+    tma_load_4d(sm + FL_K, &tKh, &bar_k, 0, h, kb * kRows, b);
+    tma_load_4d(sm + FL_K + kTile, &tKl, &bar_k, 0, h, kb * kRows, b);
+    ++k_issued;
+  };
+  auto load_v = [&](int kb) {
+    mbar_expect_tx(&bar_v, 2 * kTile);
+    tma_load_4d(sm + FL_V, &tVh, &bar_v, 0, h, kb * kRows, b);
+    tma_load_4d(sm + FL_V + kTile, &tVl, &bar_v, 0, h, kb * kRows, b);
+    ++v_issued;
+  };
+  auto issue_s = [&]() {  // S_blk = Q K_blk^T into columns 0..127
+    tc_fence_after();
+    constexpr uint32_t idesc = idesc_f16(kRows, kRows, false);
+    const uint32_t qh = smem_u32(sm + FL_Q), ql = qh + kTile;
+    const uint32_t kh = smem_u32(sm + FL_K), kl = kh + kTile;
+#pragma unroll
+    for (int j = 0; j < kHd / 16; ++j) {
+      const uint64_t dqh = smem_desc(qh + j * 32, 16, 1024, 2), dql = smem_desc(ql + j * 32, 16, 1024, 2);
+      const uint64_t dkh = smem_desc(kh + j * 32, 16, 1024, 2), dkl = smem_desc(kl + j * 32, 16, 1024, 2);
+      mma_f16(tmem, dql, dkh, idesc, j != 0);
+      mma_f16(tmem, dqh, dkl, idesc, 1);
+      mma_f16(tmem, dqh, dkh, idesc, 1);
+    }
+    mma_commit(&bar_s);
   };
   if (tid == 0) {
     mbar_expect_tx(&bar_q, 2 * kTile);
     tma_load_4d(sm + FL_Q, &tQh, &bar_q, 0, h, qb * kRows, b);
     tma_load_4d(sm + FL_Q + kTile, &tQl, &bar_q, 0, h, qb * kRows, b);
+    ++q_issued;
   }
   const bool mask_bcast = a.mask && a.ms[2] == 0;
   uint8_t* mrow_s = sm + FL_MASK;
@@ -525,117 +556,125 @@ __global__ void __launch_bounds__(kThreads, 1)
     return rest ? kb + 1 + __ffs(rest) - 1 : nkb;
   };
   const int kb_first = next_live(-1);
-  if (tid == 0) load_kv(kb_first);
+  if (tid == 0) {
+    load_k(kb_first);
+    load_v(kb_first);
+  }
   const uint8_t* mrow_g =
       (a.mask && !mask_bcast && row < a.S)
           ? a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)row * a.ms[2]
           : nullptr;
-  bool ok = __syncthreads_and(mbar_wait(&bar_q, 0)) != 0;
+  bool ok = __syncthreads_and(mbar_wait(&bar_q, 0) && mbar_wait(&bar_k, 0)) != 0;
+  if (ok && tid == 0) {
+    ++q_seen;
+    ++k_seen;
+    issue_s();
+  }
+  const float sc2 = a.scale * kLog2e;
+  const float fill2 = fmaxf(a.fill, -1.0e30f) * kLog2e;
   float m_run = -INFINITY, l_run = 0.f;
   float o_acc[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) o_acc[i] = 0.f;
-  for (int kb = kb_first, it = 0; kb < nkb && ok; kb = next_live(kb), ++it) {
-    ok = __syncthreads_and(mbar_wait(&bar_kv, it & 1)) != 0;
+  for (int kb = kb_first, it = 0; kb < nkb && ok; ++it) {
+    const int nxt = next_live(kb);
+    const uint32_t par = (uint32_t)it & 1u;
+    ok = __syncthreads_and(fail0 == 0 && mbar_wait(&bar_s, par)) != 0;
     if (!ok) break;
-    if (tid == 0) {  // S_blk = Q K_blk^T
-      tc_fence_after();
-      constexpr uint32_t idesc = idesc_f16(kRows, kRows, false);
-      const uint32_t qh = smem_u32(sm + FL_Q), ql = qh + kTile;
-      const uint32_t kh = smem_u32(sm + FL_K), kl = kh + kTile;
-#pragma unroll
-      for (int j = 0; j < kHd / 16; ++j) {
-        const uint64_t dqh = smem_desc(qh + j * 32, 16, 1024, 2), dql = smem_desc(ql + j * 32, 16, 1024, 2);
-        const uint64_t dkh = smem_desc(kh + j * 32, 16, 1024, 2), dkl = smem_desc(kl + j * 32, 16, 1024, 2);
-        mma_f16(tmem, dql, dkh, idesc, j != 0);
-        mma_f16(tmem, dqh, dkl, idesc, 1);
-        mma_f16(tmem, dqh, dkh, idesc, 1);
-      }
-      mma_commit(&bar_s);
-    }
-    ok = __syncthreads_and(mbar_wait(&bar_s, it & 1)) != 0;
-    if (!ok) break;
+    if (tid == 0 && nxt < nkb) load_k(nxt);  // K_blk consumed
     tc_fence_after();
     float s[64];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float v[16];
-      tmem_ld16(tmem + lane_base + (uint32_t)(col0 + 16 * c), v);
-#pragma unroll
-      for (int q = 0; q < 16; ++q) s[16 * c + q] = v[q];
+    {
+      float (&s0)[32] = *reinterpret_cast<float(*)[32]>(&s[0]);
+      float (&s1)[32] = *reinterpret_cast<float(*)[32]>(&s[32]);
+      tmem_ld32_async(tmem + lane_base + (uint32_t)col0, s0);
+      tmem_ld32_async(tmem + lane_base + (uint32_t)(col0 + 32), s1);
+      tmem_wait_ld();
     }
+    // log2-domain scores, as in the S <= 128 kernel: masked -> fill
+    // (clamped at -1e30), keys past S -> -inf
+    const int nvalid = a.S - kb * kRows - col0;
     float mx = -INFINITY;
 #pragma unroll
     for (int q = 0; q < 64; ++q) {
-      const int j = kb * kRows + col0 + q;
       bool masked = false;
-      if (j < a.S) {
-        if (mask_bcast) masked = mrow_s[j] != 0;
-        else if (mrow_g) masked = mrow_g[(int64_t)j * a.ms[3]] != 0;
+      if (q < nvalid) {
+        if (mask_bcast) masked = mrow_s[kb * kRows + col0 + q] != 0;
+        else if (mrow_g) masked = mrow_g[(int64_t)(kb * kRows + col0 + q) * a.ms[3]] != 0;
       }
-      float v;
-      if (j >= a.S) v = -INFINITY;
-      else if (masked) v = a.fill;
-      else v = a.scale * s[q];
+      float v = masked ? fill2 : sc2 * s[q];
+      if (q >= nvalid) v = -INFINITY;
       s[q] = v;
       mx = fmaxf(mx, v);
     }
     red_max[half][lrow] = mx;
-    __syncthreads();
-    const float m_new = fmaxf(m_run, fmaxf(red_max[0][lrow], red_max[1][lrow]));
-    const float corr = ex2_approx((m_run - m_new) * kLog2e);  // 0 on the first block (m_run = -inf)
-    float sum = 0.f;
-#pragma unroll
-    for (int q = 0; q < 64; ++q) {
-      s[q] = ex2_approx((s[q] - m_new) * kLog2e);
-      sum += s[q];
-    }
-    red_sum[half][lrow] = sum;
-    uint8_t* ph = sm + FL_P + half * kTile;
-    uint8_t* pl = sm + FL_P + 2 * kTile + half * kTile;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint32_t hw[4], lw[4];
-#pragma unroll
-      for (int p = 0; p < 4; ++p) hw[p] = split_unit_pair(s[8 * c + 2 * p], s[8 * c + 2 * p + 1], lw[p]);
-      const uint32_t off = (uint32_t)lrow * 128 + ((uint32_t)(c ^ (lrow & 7)) << 4);
-      *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    }
-    fence_proxy_async();
+    // every thread's S reads are complete before this barrier, so P may
+    // overwrite the S columns after it
     tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const float m_new = fmaxf(m_run, fmaxf(red_max[0][lrow], red_max[1][lrow]));
+    const float corr = ex2_approx(m_run - m_new);  // 0 on the first block (m_run = -inf)
+    float sum = 0.f;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      uint32_t hw[16], lw[16];
+#pragma unroll
+      for (int p = 0; p < 16; ++p) {
+        const float e0 = ex2_approx(s[32 * c + 2 * p] - m_new);
+        const float e1 = ex2_approx(s[32 * c + 2 * p + 1] - m_new);
+        sum += e0 + e1;
+        hw[p] = split_unit_pair(e0, e1, lw[p]);
+      }
+      tmem_st16(tmem + lane_base + (uint32_t)(32 * half + 16 * c), hw);
+      tmem_st16(tmem + lane_base + (uint32_t)(64 + 32 * half + 16 * c), lw);
+    }
+    red_sum[half][lrow] = sum;
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    tc_fence_before();
+    ok = __syncthreads_and(mbar_wait(&bar_v, par)) != 0;
+    if (!ok) break;
     l_run = l_run * corr + red_sum[0][lrow] + red_sum[1][lrow];
     m_run = m_new;
-    if (tid == 0) {  // O_blk = P_blk V_blk, then the next K / V block
+    if (tid == 0) {  // O_blk = P_blk V_blk
+      ++v_seen;
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16(kRows, kHd, true);
-      const uint32_t ph0 = smem_u32(sm + FL_P), pl0 = ph0 + 2 * kTile;
       const uint32_t vh = smem_u32(sm + FL_V), vl = vh + kTile;
 #pragma unroll
       for (int j = 0; j < kRows / 16; ++j) {
-        const uint32_t aoff = (j >> 2) * kTile + (j & 3) * 32;
-        const uint64_t dph = smem_desc(ph0 + aoff, 16, 1024, 2), dpl = smem_desc(pl0 + aoff, 16, 1024, 2);
         const uint64_t dvh = smem_desc(vh + j * 2048, 8192, 1024, 2);
         const uint64_t dvl = smem_desc(vl + j * 2048, 8192, 1024, 2);
-        mma_f16(tmem + kRows, dpl, dvh, idesc, j != 0);
-        mma_f16(tmem + kRows, dph, dvl, idesc, 1);
-        mma_f16(tmem + kRows, dph, dvh, idesc, 1);
+        const uint32_t ph = tmem + (uint32_t)(8 * j), pl = tmem + (uint32_t)(64 + 8 * j);
+        mma_f16_ta(tmem + kRows, pl, dvh, idesc, j != 0);
+        mma_f16_ta(tmem + kRows, ph, dvl, idesc, 1);
+        mma_f16_ta(tmem + kRows, ph, dvh, idesc, 1);
       }
       mma_commit(&bar_o);
     }
-    ok = __syncthreads_and(mbar_wait(&bar_o, it & 1)) != 0;
+    ok = __syncthreads_and(mbar_wait(&bar_o, par)) != 0;
     if (!ok) break;
-    if (tid == 0 && next_live(kb) < nkb) load_kv(next_live(kb));  // K, V and P are free again
-    tc_fence_after();
-#pragma unroll
-    for (int c0 = 0; c0 < 32; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem + lane_base + kRows + (uint32_t)(32 * half + c0), v);
-#pragma unroll
-      for (int q = 0; q < 16; ++q) o_acc[c0 + q] = o_acc[c0 + q] * corr + v[q];
+    // P_blk and V_blk consumed: the next block's V load and S run under the merge
+    if (tid == 0 && nxt < nkb) {
+      load_v(nxt);
+      if (mbar_wait(&bar_k, k_seen & 1u)) {
+        ++k_seen;
+        issue_s();
+      } else {
+        fail0 = 1;
+      }
     }
+    tc_fence_after();
+    {
+      float ov[32];
+      tmem_ld32_async(tmem + lane_base + kRows + (uint32_t)(32 * half), ov);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 32; ++q) o_acc[q] = o_acc[q] * corr + ov[q];
+    }
+    // O_blk reads complete before the next block's PV may write it
     tc_fence_before();
+    kb = nxt;
   }
   if (ok) {
     const float inv = 1.0f / l_run;
@@ -668,6 +707,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (tid == 0) {
     atomicExch(&g_attn_f16_error, 1);
+  }
+  if (tid == 0) {
+    // Abort path: wait (bounded) for copies still landing in this CTA's
+    // shared memory and for every MMA this thread issued.
+    for (; q_seen < q_issued; ++q_seen) mbar_wait(&bar_q, 0);
+    for (; k_seen < k_issued; ++k_seen) mbar_wait(&bar_k, k_seen & 1u);
+    for (; v_seen < v_issued; ++v_seen) mbar_wait(&bar_v, v_seen & 1u);
+    if (!ok) drain_mma(&bar_drain);
   }
   tc_fence_before();
   __syncthreads();
