@@ -19,7 +19,9 @@
 // are REPLACED by `fill`, keys past S get no weight, as rt::FusedAttention,
 // src/kernels/attention.cc:77-91) -> P hi / lo into TMEM -> O = P V (V
 // MN-major, SWIZZLE_128B) -> O as fp32 or as fp16 planes.
-// Every mbarrier wait is bounded; a timeout sets g_attn_f16_error.
+// Every mbarrier wait is bounded; a timeout sets g_attn_f16_error. Only warp
+// 0 polls a barrier; the other warps wait at the CTA barrier that follows,
+// which takes no issue slots from the other CTA on the SM.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -64,6 +66,36 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
       : "memory");
+}
+
+// Bulk tensor store shared -> global (coordinates start at 0 or above; the
+// map clips rows outside the tensor), tracked by the bulk async-group.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// the committed stores have read their shared-memory source
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// the committed stores are complete
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -161,7 +193,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                          const __grid_constant__ CUtensorMap tKh,
                          const __grid_constant__ CUtensorMap tKl,
                          const __grid_constant__ CUtensorMap tVh,
-                         const __grid_constant__ CUtensorMap tVl, const AttnF16Kern a,
+                         const __grid_constant__ CUtensorMap tVl,
+                         const __grid_constant__ CUtensorMap tOh,
+                         const __grid_constant__ CUtensorMap tOl, const AttnF16Kern a,
                          int n_items, int nH) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -258,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // the previous item's readers of the row are past a CTA barrier
     if (mask_bcast && tid < kRows) mrow_s[tid] = (uint8_t)mval;
     if (k == 0) {
-      ok = __syncthreads_and(mbar_wait(&bar_qk, 0)) != 0;
+      ok = __syncthreads_and(warp != 0 || (mbar_wait(&bar_qk, 0))) != 0;
       if (!ok) break;
       if (tid == 0) {
         ++qk_seen;
@@ -266,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     // S(it) landed: Q / K tiles are free for the next item
-    ok = __syncthreads_and(fail0 == 0 && mbar_wait(&bar_s, par)) != 0;
+    ok = __syncthreads_and(warp != 0 || (fail0 == 0 && mbar_wait(&bar_s, par))) != 0;
     if (!ok) break;
     if (tid == 0 && next < n_items) issue_qk(next);
     mval = mask_byte(next);
@@ -348,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     red_sum[half][row] = sum;
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     tc_fence_before();
-    ok = __syncthreads_and(mbar_wait(&bar_v, par)) != 0;
+    ok = __syncthreads_and(warp != 0 || (mbar_wait(&bar_v, par))) != 0;
     if (!ok) break;
     if (tid == 0) {
       ++v_seen;
@@ -368,12 +402,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       mma_commit(&bar_o);
     }
-    ok = __syncthreads_and(mbar_wait(&bar_o, par)) != 0;
+    ok = __syncthreads_and(warp != 0 || (mbar_wait(&bar_o, par))) != 0;
     if (!ok) break;
-    // P and V consumed: the next item's V load and S = QK^T run under this
-    // item's epilogue (S writes columns 0..127, the epilogue reads 128..191).
+    // P and V consumed: the next item's S = QK^T runs under this item's
+    // epilogue (S writes columns 0..127, the epilogue reads 128..191).
     if (tid == 0 && next < n_items) {
-      issue_v(next);
       if (mbar_wait(&bar_qk, (k + 1) & 1u)) {
         ++qk_seen;
         issue_s();
@@ -382,41 +415,60 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     tc_fence_after();
-    const int64_t col = h * kHd + 32 * half;
     const float inv = 1.0f / (red_sum[0][row] + red_sum[1][row]);
     bool bad = false;
     float ov[32];
     tmem_ld32_async(tmem + lane_base + kRows + (uint32_t)(32 * half), ov);
     tmem_wait_ld();
 #pragma unroll
-    for (int c0 = 0; c0 < 32; c0 += 16) {
-      if (row >= a.S) continue;
-      float v[16];
+    for (int q = 0; q < 32; ++q) ov[q] *= inv;
+    // O is staged in the spent V tiles in the output map's layout ([128 rows]
+    // [128 B], 16-byte chunk c of row r at c ^ (r & 7)) and written by bulk
+    // tensor stores: whole 128-byte row segments instead of one 16-byte
+    // piece per thread and row. Rows past S are clipped by the map.
+    const uint32_t swz = (uint32_t)(row & 7);
+    if (a.so.hi) {
+      // planes: hi tile at OFF_VH, lo at OFF_VL; this thread's 32 columns are
+      // chunks 4 half .. 4 half + 3
 #pragma unroll
-      for (int q = 0; q < 16; ++q) v[q] = ov[c0 + q] * inv;
-      const int64_t o = (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + col + c0;
-      if (a.so.hi) {
-        uint32_t hw[8], lw[8];
+      for (int c = 0; c < 4; ++c) {
+        uint32_t hw[4], lw[4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) hw[q] = split_pair(v[2 * q], v[2 * q + 1], lw[q], bad);
-        uint4* hp = reinterpret_cast<uint4*>(a.so.hi + o);
-        uint4* lp = reinterpret_cast<uint4*>(a.so.lo + o);
-        hp[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        hp[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-        lp[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        lp[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-      } else {
+        for (int q = 0; q < 4; ++q) hw[q] = split_pair(ov[8 * c + 2 * q], ov[8 * c + 2 * q + 1], lw[q], bad);
+        const uint32_t off = (uint32_t)row * 128 + (((uint32_t)(4 * half + c) ^ swz) << 4);
+        *reinterpret_cast<uint4*>(sm + OFF_VH + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(sm + OFF_VL + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
+    } else {
+      // fp32: columns 32 half .. 32 half + 31 are box `half` (128 B per row)
 #pragma unroll
-        for (int q = 0; q < 16; q += 4)
-          *reinterpret_cast<float4*>(a.out + o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t off = (uint32_t)half * kTile + (uint32_t)row * 128 + (((uint32_t)c ^ swz) << 4);
+        *reinterpret_cast<float4*>(sm + OFF_VH + off) =
+            make_float4(ov[4 * c], ov[4 * c + 1], ov[4 * c + 2], ov[4 * c + 3]);
       }
     }
     if (bad) atomicExch(a.so.range, 1);
+    fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      if (a.so.hi) {
+        tma_store_4d(&tOh, sm + OFF_VH, 0, h, 0, b);
+        tma_store_4d(&tOl, sm + OFF_VL, 0, h, 0, b);
+      } else {
+        tma_store_3d(&tOh, sm + OFF_VH, 64 * h, 0, b);
+        tma_store_3d(&tOh, sm + OFF_VH + kTile, 64 * h + 32, 0, b);
+      }
+      bulk_commit();
+      bulk_wait_read();  // the V tiles may be overwritten once the stores read them
+      if (next < n_items) issue_v(next);
+    }
     // O reads complete before the next item's PV may write O
     tc_fence_before();
   }
   if (!ok && tid == 0) atomicExch(&g_attn_f16_error, 1);
   if (tid == 0) {
+    bulk_wait_all();  // this CTA's output stores are complete
     // Abort path: wait (bounded) for copies still landing in this CTA's
     // shared memory and for every MMA this thread issued. On the normal path
     // every copy was seen and the last MMA's commit was waited on.
@@ -564,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       (a.mask && !mask_bcast && row < a.S)
           ? a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)row * a.ms[2]
           : nullptr;
-  bool ok = __syncthreads_and(mbar_wait(&bar_q, 0) && mbar_wait(&bar_k, 0)) != 0;
+  bool ok = __syncthreads_and(warp != 0 || (mbar_wait(&bar_q, 0) && mbar_wait(&bar_k, 0))) != 0;
   if (ok && tid == 0) {
     ++q_seen;
     ++k_seen;
@@ -579,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   for (int kb = kb_first, it = 0; kb < nkb && ok; ++it) {
     const int nxt = next_live(kb);
     const uint32_t par = (uint32_t)it & 1u;
-    ok = __syncthreads_and(fail0 == 0 && mbar_wait(&bar_s, par)) != 0;
+    ok = __syncthreads_and(warp != 0 || (fail0 == 0 && mbar_wait(&bar_s, par))) != 0;
     if (!ok) break;
     if (tid == 0 && nxt < nkb) load_k(nxt);  // K_blk consumed
     tc_fence_after();
@@ -632,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     red_sum[half][lrow] = sum;
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     tc_fence_before();
-    ok = __syncthreads_and(mbar_wait(&bar_v, par)) != 0;
+    ok = __syncthreads_and(warp != 0 || (mbar_wait(&bar_v, par))) != 0;
     if (!ok) break;
     l_run = l_run * corr + red_sum[0][lrow] + red_sum[1][lrow];
     m_run = m_new;
@@ -652,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       mma_commit(&bar_o);
     }
-    ok = __syncthreads_and(mbar_wait(&bar_o, par)) != 0;
+    ok = __syncthreads_and(warp != 0 || (mbar_wait(&bar_o, par))) != 0;
     if (!ok) break;
     // P_blk and V_blk consumed: the next block's V load and S run under the merge
     if (tid == 0 && nxt < nkb) {
@@ -743,6 +795,24 @@ CUtensorMap plane_map(const uint16_t* base, int nH, int S, int B, int64_t ld, in
   return m;
 }
 
+// 3-D map over an fp32 [B, S, ldo] output: dims (column: nH * 64, s: S,
+// b: B), box (32, 128, 1) = 128-byte rows, 128-byte swizzle.
+CUtensorMap out_f32_map(float* base, int nH, int S, int B, int64_t ldo, int64_t bstride) {
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {(cuuint64_t)nH * kHd, (cuuint64_t)S, (cuuint64_t)B};
+  const cuuint64_t strides[2] = {(cuuint64_t)ldo * 4, (cuuint64_t)bstride * 4};
+  const cuuint32_t box[3] = {32, (cuuint32_t)kRows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw Error(INFERC_ERR_CUDA, "cuTensorMapEncodeTiled (attention output) failed (" +
+                                     std::to_string((int)r) + ")");
+  return m;
+}
+
 }  // namespace
 
 int read_and_clear_attn_f16_error() {
@@ -758,7 +828,8 @@ int read_and_clear_attn_f16_error() {
 bool attention_f16_supported(const AttnF16Args& a) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const bool planes = al(a.qh) && al(a.ql) && al(a.kh) && al(a.kl) && al(a.vh) && al(a.vl);
-  const bool out_ok = a.so.hi ? (al(a.so.hi) && al(a.so.lo) && a.so.range != nullptr)
+  const bool out_ok = a.so.hi ? (al(a.so.hi) && al(a.so.lo) && a.so.range != nullptr &&
+                                 a.bstride_o % 8 == 0)
                               : (al(a.out) && a.ldo % 4 == 0 && a.bstride_o % 4 == 0);
   return a.S >= 1 && a.S <= kFlashMaxS && planes && out_ok && a.ld % 8 == 0 && a.bstride % 8 == 0 &&
          a.ld >= a.nH * kHd && a.bstride >= a.S * a.ld && a.ldo % 8 == 0 && a.B < 65536 &&
@@ -793,8 +864,15 @@ void launch_attention_f16(const AttnF16Args& a, cudaStream_t st) {
     IDEV_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int items = B * nH;
     const int grid = items < 2 * sms ? items : 2 * sms;
+    // output maps: the hi / lo planes, or the fp32 tensor
+    const CUtensorMap toh = a.so.hi ? plane_map(reinterpret_cast<const uint16_t*>(a.so.hi), nH, S,
+                                                B, a.ldo, a.bstride_o)
+                                    : out_f32_map(a.out, nH, S, B, a.ldo, a.bstride_o);
+    const CUtensorMap tol = a.so.hi ? plane_map(reinterpret_cast<const uint16_t*>(a.so.lo), nH, S,
+                                                B, a.ldo, a.bstride_o)
+                                    : toh;
     launch_pdl(attention_f16_kernel, dim3((unsigned)grid), dim3(kThreads), kSmemBytes, st, tqh,
-               tql, tkh, tkl, tvh, tvl, k, items, nH);
+               tql, tkh, tkl, tvh, tvl, toh, tol, k, items, nH);
   } else {
     IDEV_CUDA(cudaFuncSetAttribute(attention_f16_flash_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlashSmem));
