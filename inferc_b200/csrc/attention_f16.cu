@@ -508,7 +508,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                                const __grid_constant__ CUtensorMap tKh,
                                const __grid_constant__ CUtensorMap tKl,
                                const __grid_constant__ CUtensorMap tVh,
-                               const __grid_constant__ CUtensorMap tVl, const AttnF16Kern a) {
+                               const __grid_constant__ CUtensorMap tVl,
+                               const __grid_constant__ CUtensorMap tOh,
+                               const __grid_constant__ CUtensorMap tOl, const AttnF16Kern a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
@@ -729,33 +731,45 @@ __global__ void __launch_bounds__(kThreads, 2)
     kb = nxt;
   }
   if (ok) {
+    // O / l staged in the spent V tiles and written by bulk tensor stores, as
+    // in the S <= 128 kernel (rows past S are clipped by the map)
     const float inv = 1.0f / l_run;
-    if (row < a.S) {
-      const int64_t o = (int64_t)b * a.bstride_o + (int64_t)row * a.ldo + h * kHd + 32 * half;
-      bool bad = false;
+    const uint32_t swz = (uint32_t)(lrow & 7);
+    bool bad = false;
 #pragma unroll
-      for (int c0 = 0; c0 < 32; c0 += 16) {
-        float v[16];
+    for (int q = 0; q < 32; ++q) o_acc[q] *= inv;
+    if (a.so.hi) {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) v[q] = o_acc[c0 + q] * inv;
-        if (a.so.hi) {
-          uint32_t hw[8], lw[8];
+      for (int c = 0; c < 4; ++c) {
+        uint32_t hw[4], lw[4];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) hw[q] = split_pair(v[2 * q], v[2 * q + 1], lw[q], bad);
-          uint4* hp = reinterpret_cast<uint4*>(a.so.hi + o + c0);
-          uint4* lp = reinterpret_cast<uint4*>(a.so.lo + o + c0);
-          hp[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          hp[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-          lp[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-          lp[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 16; q += 4)
-            *reinterpret_cast<float4*>(a.out + o + c0 + q) =
-                make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-        }
+        for (int q = 0; q < 4; ++q)
+          hw[q] = split_pair(o_acc[8 * c + 2 * q], o_acc[8 * c + 2 * q + 1], lw[q], bad);
+        const uint32_t off = (uint32_t)lrow * 128 + (((uint32_t)(4 * half + c) ^ swz) << 4);
+        *reinterpret_cast<uint4*>(sm + FL_V + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(sm + FL_V + kTile + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
-      if (bad) atomicExch(a.so.range, 1);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t off = (uint32_t)half * kTile + (uint32_t)lrow * 128 + (((uint32_t)c ^ swz) << 4);
+        *reinterpret_cast<float4*>(sm + FL_V + off) =
+            make_float4(o_acc[4 * c], o_acc[4 * c + 1], o_acc[4 * c + 2], o_acc[4 * c + 3]);
+      }
+    }
+    if (bad) atomicExch(a.so.range, 1);
+    fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      if (a.so.hi) {
+        tma_store_4d(&tOh, sm + FL_V, 0, h, qb * kRows, b);
+        tma_store_4d(&tOl, sm + FL_V + kTile, 0, h, qb * kRows, b);
+      } else {
+        tma_store_3d(&tOh, sm + FL_V, 64 * h, qb * kRows, b);
+        tma_store_3d(&tOh, sm + FL_V + kTile, 64 * h + 32, qb * kRows, b);
+      }
+      bulk_commit();
+      bulk_wait_all();
     }
   } else if (tid == 0) {
     atomicExch(&g_attn_f16_error, 1);
@@ -855,7 +869,14 @@ void launch_attention_f16(const AttnF16Args& a, cudaStream_t st) {
   k.ldo = a.ldo;
   k.bstride_o = a.bstride_o;
   k.so = a.so;
-  if (S <= kRows) {  // one key block: the two-CTAs-per-SM kernel
+  // output maps: the hi / lo planes, or the fp32 tensor
+  const CUtensorMap toh = a.so.hi ? plane_map(reinterpret_cast<const uint16_t*>(a.so.hi), nH, S, B,
+                                              a.ldo, a.bstride_o)
+                                  : out_f32_map(a.out, nH, S, B, a.ldo, a.bstride_o);
+  const CUtensorMap tol = a.so.hi ? plane_map(reinterpret_cast<const uint16_t*>(a.so.lo), nH, S, B,
+                                              a.ldo, a.bstride_o)
+                                  : toh;
+  if (S <= kRows) {  // one key block: the persistent kernel
     IDEV_CUDA(cudaFuncSetAttribute(attention_f16_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     // persistent: two CTAs per SM, each walking (batch, head) items
@@ -864,13 +885,6 @@ void launch_attention_f16(const AttnF16Args& a, cudaStream_t st) {
     IDEV_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int items = B * nH;
     const int grid = items < 2 * sms ? items : 2 * sms;
-    // output maps: the hi / lo planes, or the fp32 tensor
-    const CUtensorMap toh = a.so.hi ? plane_map(reinterpret_cast<const uint16_t*>(a.so.hi), nH, S,
-                                                B, a.ldo, a.bstride_o)
-                                    : out_f32_map(a.out, nH, S, B, a.ldo, a.bstride_o);
-    const CUtensorMap tol = a.so.hi ? plane_map(reinterpret_cast<const uint16_t*>(a.so.lo), nH, S,
-                                                B, a.ldo, a.bstride_o)
-                                    : toh;
     launch_pdl(attention_f16_kernel, dim3((unsigned)grid), dim3(kThreads), kSmemBytes, st, tqh,
                tql, tkh, tkl, tvh, tvl, toh, tol, k, items, nH);
   } else {
@@ -878,7 +892,7 @@ void launch_attention_f16(const AttnF16Args& a, cudaStream_t st) {
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlashSmem));
     dim3 grid((unsigned)((S + kRows - 1) / kRows), (unsigned)nH, (unsigned)B);
     attention_f16_flash_kernel<<<grid, kThreads, kFlashSmem, st>>>(tqh, tql, tkh, tkl, tvh, tvl,
-                                                                   k);
+                                                                   toh, tol, k);
   }
   IDEV_LAUNCHED();
 }
