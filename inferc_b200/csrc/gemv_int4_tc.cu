@@ -38,11 +38,13 @@
 // GEMV warp roles (320 threads):
 //   warp 0      TMA producer: [128 rows x 128 bytes] slabs of W (2-D maps,
 //               unswizzled: measured 24 % faster than a 128-byte-swizzle map
-//               for these boxes; rows past N zero-filled) into a 9-stage
-//               ring (144 KB in flight per SM: loaded HBM latency is ~4 us)
+//               for these boxes; rows past N zero-filled) into a 5-stage
+//               ring (80 KB of weights in flight per SM)
 //   warp 1      TMEM allocation + MMA issuer
-//   warps 2..5  unpack: hi tile in place, lo tile into one of two buffers,
-//               both written at the SWIZZLE_128B positions the MMA reads
+//   warps 2..5  unpack: hi tile in place, lo tile into the stage's own lo
+//               buffer, both written at the SWIZZLE_128B positions the MMA
+//               reads (with two shared lo buffers, the unpack of slab g
+//               waited for the MMAs of slab g - 2: one slab per ~640 ns)
 //   warps 6..9  bulk copies of the digit tiles into a double buffer (the next
 //               matrix's tile lands while the current one streams), and
 //               the epilogue (tcgen05.ld of both accumulators, a row per
@@ -66,12 +68,17 @@ namespace {
 
 using namespace tc;
 
-constexpr int kStages = 9;
+#ifndef INT4_TC_STAGES
+#define INT4_TC_STAGES 5
+#endif
+// Each stage holds a slab (hi tile in place) and its own lo tile, so a stage
+// is released by one MMA commit and the unpack never waits on another slab.
+constexpr int kStages = INT4_TC_STAGES;
 constexpr uint32_t kSlab = 128 * 128;          // packed bytes of one slab (hi in place)
 constexpr int kMaxAtoms = 16;                  // K/2 <= 2048 bytes
 constexpr uint32_t kAtomB = 8 * 128;           // one 128-byte K atom of an 8-row B tile
 constexpr uint32_t kBTile = kMaxAtoms * kAtomB;
-constexpr uint32_t kSmem = kStages * kSlab + 2 * kSlab + 2 * kBTile + 1024;
+constexpr uint32_t kSmem = 2 * kStages * kSlab + 2 * kBTile + 1024;
 constexpr int kThreads = 320;
 constexpr int kEpi = 128;  // warps 6..9
 constexpr int kMaxMats = 64;  // ~11.5 KB of kernel parameters
@@ -262,8 +269,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* lobuf = smem + kStages * kSlab;  // two lo tiles
-  uint8_t* bplanes = lobuf + 2 * kSlab;     // digit tiles of two matrices (double buffer)
+  uint8_t* lobuf = smem + kStages * kSlab;       // the stages' lo tiles
+  uint8_t* bplanes = lobuf + kStages * kSlab;    // digit tiles of two matrices (double buffer)
   __shared__ __align__(8) uint64_t full_bar[kStages], conv_bar[kStages], empty_bar[kStages];
   __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], b_ready[2], b_free[2];
   __shared__ __align__(8) uint64_t drain_bar;
@@ -373,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t hi = smem_u32(smem + s * kSlab);
-          const uint32_t lo = smem_u32(lobuf + (g & 1) * kSlab);
+          const uint32_t lo = smem_u32(lobuf + s * kSlab);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {  // 32-byte K steps inside the 128-byte atom
             const uint32_t acc_in = (i | ks) != 0;
@@ -397,11 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           fail();
           break;
         }
-        // lo buffer g & 1 was last read by the MMAs of slab g - 2
-        if (g >= 2 && !mbar_wait(&empty_bar[(g - 2) % kStages], ((g - 2) / kStages) & 1)) {
-          fail();
-          break;
-        }
+        // The stage's lo tile was last read by the MMAs of the slab this
+        // stage held before, which completed before the producer refilled it.
         // The slab landed unswizzled (faster TMA). Eight consecutive lanes
         // take the eight 16-byte chunks of one row (a quarter-warp reads one
         // contiguous 128-byte row) and write hi in place and lo into the lo
@@ -409,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // a permutation inside the row, so the row's chunks are all loaded
         // (one warp, __syncwarp) before any is overwritten.
         uint4* p = reinterpret_cast<uint4*>(smem + s * kSlab);
-        uint4* q = reinterpret_cast<uint4*>(lobuf + (g & 1) * kSlab);
+        uint4* q = reinterpret_cast<uint4*>(lobuf + s * kSlab);
         uint4 v[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) v[k] = p[k * 128 + t];
