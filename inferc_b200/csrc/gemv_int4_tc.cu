@@ -708,6 +708,11 @@ void launch_gemv_int4_tc(const InfercInt4Gemv* const* ds, int n, cudaStream_t st
   }();
   IDEV_CUDA(cudaFuncSetAttribute(gemv_int4_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kSmem));
+  // The digits kernel asks for the GEMV's shared-memory carve-out, so an SM
+  // that ran a digits CTA need not change its L1 / shared split before it
+  // can take a GEMV CTA.
+  IDEV_CUDA(cudaFuncSetAttribute(int4_digits_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared));
   for (int base = 0; base < n; base += kMaxMats) {
     static thread_local Int4Params hp;  // built in place, then found in or added to the cache
     std::memset(&hp, 0, sizeof(hp));     // padding and unused entries compare equal
