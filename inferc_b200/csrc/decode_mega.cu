@@ -868,8 +868,28 @@ __device__ __noinline__ void attention_head64(const MegaArgs& a, const MegaLayer
 // publishes xm (the FP residual, tagged xm_tag); then LN2 in place.
 __device__ void stage_attn_residual(const MegaArgs& a, const float* proj_b, const float* g,
                                     const float* b, const uint64_t* xa, uint32_t xa_tag,
-                                    uint32_t part_tag, uint32_t xm_tag, Smem& sm) {
+                                    uint32_t part_tag, uint32_t xm_tag, int chunk_w, Smem& sm) {
   const int tid = threadIdx.x, H = a.H;
+  // Every CTA waits here for the attention CTAs, most of them from early in
+  // the layer. Until then only warp 0 polls, and only the first word of each
+  // (head, column chunk) partial (up to 64 words): the full read of all
+  // heads' partials (12 x 768 words per CTA in GPT-2-small) starts once
+  // every writer has been seen, so the grid's polling does not load L2
+  // while the attention CTAs read the KV cache.
+  if (tid < 32) {
+    const int nsent = a.heads * a.proj_chunks;
+    auto sent = [&](int j) {
+      return a.tpart + (size_t)(j / a.proj_chunks) * H + (size_t)(j % a.proj_chunks) * chunk_w;
+    };
+    uint64_t w[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int j = tid + 32 * i;
+      w[i] = j < nsent ? ld_word(sent(j)) : (uint64_t)part_tag << 32;
+    }
+    settle(w, part_tag, [&](int i) { return sent(tid + 32 * i); }, a, sm);
+  }
+  __syncthreads();
   // All loads of the thread (up to 3 k's x 12 heads + x) are issued before
   // any is used: one L2 round trip, not one per k.
   constexpr int kK = 3, kHeads = 16;
@@ -1114,7 +1134,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const __gr
       const EpiIn e_fc = gemv_preload(L.fc, L.fc_b, nullptr, 0u, a, sm);
       const float *g2, *b2, *pb;
       if (!ln_params(L.ln2_g, L.ln2_b, L.proj_b, H, sm, a, &g2, &b2, &pb)) { drain(sm); return; }
-      stage_attn_residual(a, pb, g2, b2, xin, tag_in, tag_l + 2u, tag_l + 3u, sm);
+      stage_attn_residual(a, pb, g2, b2, xin, tag_in, tag_l + 2u, tag_l + 3u, L.proj.P, sm);
       stamp_event(a, step == 1 && l == 5, 3);
       if (!gemv_phase<Q4>(L.fc, 0, slots, e_fc, a.tf, tag_l + 3u, ACT_GELU_TANH, sm, a) ||
           !phase_end(a, sm, 4 * l + 2, step)) { drain(sm); return; }
